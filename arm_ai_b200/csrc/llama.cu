@@ -1,0 +1,1019 @@
+// llama.cu — quantized-Llama model: GGUF load, decode step (PDL + CUDA graph),
+// prefill, greedy generate. C ABI in include/armai.h.
+#include <math.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gguf.h"
+#include "llama_kernels.cuh"
+
+using namespace armai;
+
+namespace {
+
+constexpr int PREFILL_TILE = 8;       // tokens per prefill matvec launch
+constexpr int ATTN_SPLITS = 16;       // split-K factor of the decode attention
+constexpr int ATTN_TOK_PER_LAUNCH = 64;
+constexpr uint32_t STAGE_MAX = 44 * 1024;
+constexpr size_t SMEM_LIMIT = 227 * 1024;   // hard per-CTA limit
+constexpr size_t SMEM_DECODE = 110 * 1024;  // decode kernels: two CTAs per SM for PDL overlap
+
+struct DevMat {
+  uint8_t* w = nullptr;
+  int type = 0;
+  int rows = 0, cols = 0;
+  int row_bytes = 0;
+  Seg seg() const { return Seg{w, type, rows, cols / QK_K, row_bytes}; }
+};
+
+struct Layer {
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  DevMat wq, wk, wv, wo, wg, wu, wd;
+};
+
+struct Plan {
+  int grid = 0, rows_per_cta = 0, chunk_rows = 0, ns = 0;
+  uint32_t stage_bytes = 0;
+  size_t smem = 0;
+};
+
+}  // namespace
+
+struct armai_llama {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  bool broken = false;
+  // hyper-parameters
+  int n_layer = 0, n_embd = 0, n_ff = 0, n_head = 0, n_head_kv = 0, head_dim = 0, rope_dim = 0;
+  int n_vocab = 0, max_seq = 4096, max_batch = 1, kv_f16 = 0;
+  float eps = 1e-5f, rope_base = 10000.f;
+  bool use_graph = true, use_pdl = true;
+  // weights
+  uint8_t* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<Layer> layers;
+  DevMat tok_embd, output;
+  float* out_norm = nullptr;
+  int64_t weight_bytes_per_token = 0;
+  // tables and caches
+  float* cos_t = nullptr;
+  float* sin_t = nullptr;
+  void* kc = nullptr;
+  void* vc = nullptr;
+  int64_t kv_seq_stride = 0, kv_layer_stride = 0;
+  // decode activations (max_batch rows)
+  float *x = nullptr, *q = nullptr, *y = nullptr, *h = nullptr, *logits = nullptr;
+  uint32_t* d_token = nullptr;
+  int* d_pos = nullptr;
+  uint32_t* d_err = nullptr;
+  float* attn_part = nullptr;
+  unsigned* attn_cnt = nullptr;
+  size_t attn_cap_tokens = 0;
+  float* am_val = nullptr;
+  int* am_idx = nullptr;
+  unsigned* am_cnt = nullptr;
+  // prefill buffers
+  int pf_cap = 0;
+  float *pX = nullptr, *pQ = nullptr, *pY = nullptr, *pH = nullptr;
+  int* p_pos = nullptr;
+  uint32_t* p_tok = nullptr;
+  // pinned host staging
+  uint32_t* h_tok = nullptr;   // ring of 8 token slots
+  int* h_misc = nullptr;       // small pinned scratch
+  uint32_t* h_prompt = nullptr;
+  size_t h_prompt_cap = 0;
+  // plans
+  Plan pl_qkv1, pl_wo1, pl_gu1, pl_down1, pl_head1;
+  Plan pl_qkvT, pl_woT, pl_guT, pl_downT;
+  size_t attn_smem = 0;
+  int n_kernels_step = 0;
+  cudaGraphExec_t graph = nullptr;
+  int kv_len = 0;  // positions currently in the cache (host mirror)
+  size_t device_bytes = 0;
+};
+
+namespace {
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                     bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Row plan for a k_matvec launch: contiguous row ranges per CTA, chunks that
+// fit a stage, a ring of up to 3 stages within the shared-memory budget.
+Plan make_plan(int total_rows, int unit, int row_bytes_per_unit_row, int rows_per_unit_in_stage,
+               int K, int NB, bool norm, int nsm, size_t budget) {
+  Plan p;
+  // rows of the virtual row space per CTA, rounded up to `unit`
+  int per = (total_rows + nsm - 1) / nsm;
+  per = ((per + unit - 1) / unit) * unit;
+  p.rows_per_cta = per;
+  p.grid = (total_rows + per - 1) / per;
+  const size_t act = mv_smem_layout(0, 0, K, NB, norm).total;
+  const size_t unit_bytes = (size_t)row_bytes_per_unit_row * rows_per_unit_in_stage;  // bytes per row of the chunk
+  const size_t room = budget > act + 1024 ? budget - act - 1024 : 0;
+  size_t stage_cap = std::min<size_t>(STAGE_MAX, room);
+  int chunk = (int)(stage_cap / unit_bytes);
+  chunk = (chunk / unit) * unit;
+  if (chunk < unit) chunk = unit;
+  if (chunk > per) chunk = per;
+  p.chunk_rows = chunk;
+  p.stage_bytes = (uint32_t)al16((size_t)chunk * unit_bytes);
+  const int nchunks = (per + chunk - 1) / chunk;
+  int ns = std::min(nchunks, 3);
+  while (ns > 1 && act + (size_t)ns * p.stage_bytes + 1024 > budget) ns--;
+  p.ns = ns;
+  p.smem = mv_smem_layout(ns, p.stage_bytes, K, NB, norm).total;
+  return p;
+}
+
+template <int MODE, int NB>
+int set_smem_attr(size_t smem) {
+  ARMAI_CUDA(cudaFuncSetAttribute(k_matvec<MODE, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+  return ARMAI_OK;
+}
+
+template <int MODE, int NB>
+cudaError_t launch_mv(armai_llama* m, const Plan& pl, const MvParams& p) {
+  return launch_k(k_matvec<MODE, NB>, dim3(pl.grid), dim3(MV_THREADS), pl.smem, m->stream,
+                  m->use_pdl, p);
+}
+
+MvParams base_params(armai_llama* m, const Plan& pl) {
+  MvParams p;
+  std::memset(&p, 0, sizeof p);
+  p.eps = m->eps;
+  p.rows_per_cta = pl.rows_per_cta;
+  p.chunk_rows = pl.chunk_rows;
+  p.ns = pl.ns;
+  p.stage_bytes = pl.stage_bytes;
+  p.err = m->d_err;
+  p.hd = m->head_dim;
+  p.max_seq = m->max_seq;
+  p.kv_f16 = m->kv_f16;
+  p.cos_t = m->cos_t;
+  p.sin_t = m->sin_t;
+  return p;
+}
+
+void* kv_layer_ptr(armai_llama* m, void* base, int l) {
+  const size_t es = m->kv_f16 ? 2 : 4;
+  return (uint8_t*)base + (size_t)l * m->kv_layer_stride * es;
+}
+
+// ---- one layer's launches for NB tokens whose activations live at x/q/y/h ----
+template <int NB>
+cudaError_t launch_qkv(armai_llama* m, const Plan& pl, int l, const float* x, float* q,
+                       const int* pos, int64_t kv_seq_stride, void* kc_override = nullptr,
+                       void* vc_override = nullptr) {
+  const Layer& L = m->layers[l];
+  MvParams p = base_params(m, pl);
+  p.x = x;
+  p.gamma = L.attn_norm;
+  p.K = m->n_embd;
+  p.nb = m->n_embd / QK_K;
+  p.seg[0] = L.wq.seg();
+  p.seg[1] = L.wk.seg();
+  p.seg[2] = L.wv.seg();
+  p.nseg = 3;
+  p.qn = L.wq.rows;
+  p.kn = L.wk.rows;
+  p.total_rows = L.wq.rows + L.wk.rows + L.wv.rows;
+  p.out = q;
+  p.out_stride = m->n_head * m->head_dim;
+  p.kc = kc_override ? kc_override : kv_layer_ptr(m, m->kc, l);
+  p.vc = vc_override ? vc_override : kv_layer_ptr(m, m->vc, l);
+  p.kv_seq_stride = kv_seq_stride;
+  p.pos = pos;
+  return launch_mv<MODE_QKV, NB>(m, pl, p);
+}
+
+template <int NB>
+cudaError_t launch_resid(armai_llama* m, const Plan& pl, const DevMat& w, const float* in,
+                         float* x) {
+  MvParams p = base_params(m, pl);
+  p.x = in;
+  p.gamma = nullptr;
+  p.K = w.cols;
+  p.nb = w.cols / QK_K;
+  p.seg[0] = w.seg();
+  p.nseg = 1;
+  p.total_rows = w.rows;
+  p.out = x;
+  p.out_stride = m->n_embd;
+  return launch_mv<MODE_RESID, NB>(m, pl, p);
+}
+
+template <int NB>
+cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x, float* h) {
+  const Layer& L = m->layers[l];
+  MvParams p = base_params(m, pl);
+  p.x = x;
+  p.gamma = L.ffn_norm;
+  p.K = m->n_embd;
+  p.nb = m->n_embd / QK_K;
+  p.seg[0] = L.wg.seg();
+  p.seg[1] = L.wu.seg();
+  p.nseg = 2;
+  p.total_rows = L.wg.rows;
+  p.out = h;
+  p.out_stride = m->n_ff;
+  return launch_mv<MODE_GATEUP, NB>(m, pl, p);
+}
+
+cudaError_t launch_head(armai_llama* m, const float* x, const int* pos, int* pos_out) {
+  const Plan& pl = m->pl_head1;
+  MvParams p = base_params(m, pl);
+  p.x = x;
+  p.gamma = m->out_norm;
+  p.K = m->n_embd;
+  p.nb = m->n_embd / QK_K;
+  p.seg[0] = m->output.seg();
+  p.nseg = 1;
+  p.total_rows = m->output.rows;
+  p.out = m->logits;
+  p.out_stride = m->n_vocab;
+  p.am_val = m->am_val;
+  p.am_idx = m->am_idx;
+  p.counter = m->am_cnt;
+  p.token = m->d_token;
+  p.pos = pos;
+  p.pos_out = pos_out;
+  return launch_mv<MODE_HEAD, 1>(m, pl, p);
+}
+
+cudaError_t launch_attn(armai_llama* m, int l, const float* q, float* y, const int* pos, int nb_tok,
+                        int64_t kv_seq_stride) {
+  AttnParams a;
+  a.q = q;
+  a.kc = kv_layer_ptr(m, m->kc, l);
+  a.vc = kv_layer_ptr(m, m->vc, l);
+  a.kv_seq_stride = kv_seq_stride;
+  a.kv_f16 = m->kv_f16;
+  a.pos = pos;
+  a.max_seq = m->max_seq;
+  a.hd = m->head_dim;
+  a.n_head = m->n_head;
+  a.n_kv = m->n_head_kv;
+  a.splits = ATTN_SPLITS;
+  a.max_chunk = (m->max_seq + ATTN_SPLITS - 1) / ATTN_SPLITS;
+  a.scale = (float)(1.0 / sqrt((double)m->head_dim));
+  a.part = m->attn_part;
+  a.counters = m->attn_cnt;
+  a.y = y;
+  a.err = m->d_err;
+  return launch_k(k_attn_decode, dim3(m->n_head_kv, ATTN_SPLITS, nb_tok), dim3(128), m->attn_smem,
+                  m->stream, m->use_pdl, a);
+}
+
+cudaError_t launch_embed(armai_llama* m, const uint32_t* tokens, float* x, int n) {
+  return launch_k(k_embed, dim3(n), dim3(256), 0, m->stream, m->use_pdl,
+                  (const uint8_t*)m->tok_embd.w, m->tok_embd.type, m->n_embd / QK_K,
+                  (int64_t)m->tok_embd.row_bytes, tokens, x, m->n_embd, m->n_vocab, m->d_err);
+}
+
+// The single-sequence decode step: token d_token at position d_pos.
+int enqueue_decode_step(armai_llama* m) {
+  ARMAI_CUDA(launch_embed(m, m->d_token, m->x, 1));
+  for (int l = 0; l < m->n_layer; l++) {
+    ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->x, m->q, m->d_pos, 0));
+    ARMAI_CUDA(launch_attn(m, l, m->q, m->y, m->d_pos, 1, 0));
+    ARMAI_CUDA(launch_resid<1>(m, m->pl_wo1, m->layers[l].wo, m->y, m->x));
+    ARMAI_CUDA(launch_gateup<1>(m, m->pl_gu1, l, m->x, m->h));
+    ARMAI_CUDA(launch_resid<1>(m, m->pl_down1, m->layers[l].wd, m->h, m->x));
+  }
+  ARMAI_CUDA(launch_head(m, m->x, m->d_pos, m->d_pos));
+  return ARMAI_OK;
+}
+
+int run_decode_step(armai_llama* m) {
+  if (m->graph) {
+    ARMAI_CUDA(cudaGraphLaunch(m->graph, m->stream));
+    return ARMAI_OK;
+  }
+  return enqueue_decode_step(m);
+}
+
+int check_device_error(armai_llama* m) {
+  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_CUDA(cudaMemcpy(m->h_misc, m->d_err, 4, cudaMemcpyDeviceToHost));
+  if (m->h_misc[0] != 0) {
+    m->broken = true;
+    return fail(ARMAI_E_DEVICE, "device error flag 0x" + std::to_string(m->h_misc[0]) +
+                                    " (bounded wait expired or bad token id); reload the model");
+  }
+  return ARMAI_OK;
+}
+
+int ensure_prefill(armai_llama* m, int S) {
+  if (S <= m->pf_cap) return ARMAI_OK;
+  int cap = std::max(S, 64);
+  cap = ((cap + PREFILL_TILE - 1) / PREFILL_TILE) * PREFILL_TILE;
+  cudaFree(m->pX); cudaFree(m->pQ); cudaFree(m->pY); cudaFree(m->pH);
+  cudaFree(m->p_pos); cudaFree(m->p_tok);
+  m->pX = m->pQ = m->pY = m->pH = nullptr;
+  m->pf_cap = 0;
+  const size_t qn = (size_t)m->n_head * m->head_dim;
+  ARMAI_CUDA(cudaMalloc(&m->pX, (size_t)cap * m->n_embd * 4));
+  ARMAI_CUDA(cudaMalloc(&m->pQ, (size_t)cap * qn * 4));
+  ARMAI_CUDA(cudaMalloc(&m->pY, (size_t)cap * qn * 4));
+  ARMAI_CUDA(cudaMalloc(&m->pH, (size_t)cap * m->n_ff * 4));
+  ARMAI_CUDA(cudaMalloc(&m->p_pos, (size_t)cap * 4));
+  ARMAI_CUDA(cudaMalloc(&m->p_tok, (size_t)cap * 4));
+  if ((size_t)cap > m->h_prompt_cap) {
+    if (m->h_prompt) cudaFreeHost(m->h_prompt);
+    m->h_prompt = nullptr;
+    ARMAI_CUDA(cudaMallocHost(&m->h_prompt, (size_t)cap * 2 * 4));
+    m->h_prompt_cap = cap;
+  }
+  m->pf_cap = cap;
+  return ARMAI_OK;
+}
+
+// Prefill of S >= 2 tokens at positions 0..S-1 (index_pos 0: fresh cache).
+// Integer path: the same Q8_K x Q4_K/Q6_K kernels as decode, over tiles of
+// PREFILL_TILE tokens (weights streamed once per tile), and the split-K
+// attention with per-token causal limits.
+int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S) {
+  ARMAI_TRY(ensure_prefill(m, S));
+  uint32_t* ht = m->h_prompt;
+  int* hp = reinterpret_cast<int*>(m->h_prompt + m->h_prompt_cap);
+  // The pinned staging may still be read by an earlier async copy.
+  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  for (int i = 0; i < S; i++) { ht[i] = tokens[i]; hp[i] = i; }
+  ARMAI_CUDA(cudaMemcpyAsync(m->p_tok, ht, (size_t)S * 4, cudaMemcpyHostToDevice, m->stream));
+  ARMAI_CUDA(cudaMemcpyAsync(m->p_pos, hp, (size_t)S * 4, cudaMemcpyHostToDevice, m->stream));
+  const size_t E = m->n_embd, QN = (size_t)m->n_head * m->head_dim, F = m->n_ff;
+  ARMAI_CUDA(launch_embed(m, m->p_tok, m->pX, S));
+  for (int l = 0; l < m->n_layer; l++) {
+    int t = 0;
+    for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
+      ARMAI_CUDA(launch_qkv<PREFILL_TILE>(m, m->pl_qkvT, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0));
+    for (; t < S; t++)
+      ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0));
+    for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
+      const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
+      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0));
+    }
+    t = 0;
+    for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
+      ARMAI_CUDA(launch_resid<PREFILL_TILE>(m, m->pl_woT, m->layers[l].wo, m->pY + t * QN, m->pX + t * E));
+    for (; t < S; t++)
+      ARMAI_CUDA(launch_resid<1>(m, m->pl_wo1, m->layers[l].wo, m->pY + t * QN, m->pX + t * E));
+    t = 0;
+    for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
+      ARMAI_CUDA(launch_gateup<PREFILL_TILE>(m, m->pl_guT, l, m->pX + t * E, m->pH + t * F));
+    for (; t < S; t++)
+      ARMAI_CUDA(launch_gateup<1>(m, m->pl_gu1, l, m->pX + t * E, m->pH + t * F));
+    t = 0;
+    for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
+      ARMAI_CUDA(launch_resid<PREFILL_TILE>(m, m->pl_downT, m->layers[l].wd, m->pH + t * F, m->pX + t * E));
+    for (; t < S; t++)
+      ARMAI_CUDA(launch_resid<1>(m, m->pl_down1, m->layers[l].wd, m->pH + t * F, m->pX + t * E));
+  }
+  ARMAI_CUDA(launch_head(m, m->pX + (size_t)(S - 1) * E, m->p_pos + (S - 1), m->d_pos));
+  return ARMAI_OK;
+}
+
+// Single token at position `pos` through the decode kernels.
+int enqueue_single(armai_llama* m, uint32_t token, int pos) {
+  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  m->h_misc[1] = (int)token;
+  m->h_misc[2] = pos;
+  ARMAI_CUDA(cudaMemcpyAsync(m->d_token, &m->h_misc[1], 4, cudaMemcpyHostToDevice, m->stream));
+  ARMAI_CUDA(cudaMemcpyAsync(m->d_pos, &m->h_misc[2], 4, cudaMemcpyHostToDevice, m->stream));
+  return run_decode_step(m);
+}
+
+// forward(tokens, index_pos) semantics shared by armai_llama_forward and generate.
+int forward_locked(armai_llama* m, const uint32_t* tokens, int n, int index_pos) {
+  if (n <= 0) return fail(ARMAI_E_INVALID, "forward: empty input");
+  for (int i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)m->n_vocab)
+      return fail(ARMAI_E_INVALID, "forward: token id " + std::to_string(tokens[i]) +
+                                       " out of range for vocab " + std::to_string(m->n_vocab));
+  if ((int64_t)index_pos + n > m->max_seq)
+    return fail(ARMAI_E_RANGE, "forward: positions " + std::to_string(index_pos) + ".." +
+                                   std::to_string(index_pos + n - 1) +
+                                   " exceed the rotary table (max_seq_len " +
+                                   std::to_string(m->max_seq) + ")");
+  if (index_pos == 0) m->kv_len = 0;
+  if (index_pos != m->kv_len)
+    return fail(ARMAI_E_INVALID, "forward: index_pos " + std::to_string(index_pos) +
+                                     " does not continue the cache (length " +
+                                     std::to_string(m->kv_len) + ")");
+  if (n > 1 && index_pos != 0)
+    return fail(ARMAI_E_INVALID,
+                "forward: a multi-token step after the prompt is not supported (the causal mask "
+                "covers only index_pos 0)");
+  if (n == 1) ARMAI_TRY(enqueue_single(m, tokens[0], index_pos));
+  else ARMAI_TRY(enqueue_prefill(m, tokens, n));
+  m->kv_len = index_pos + n;
+  return ARMAI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Loading.
+// ---------------------------------------------------------------------------
+bool md_u32(const GgufFile& g, const std::string& key, int64_t& out) {
+  auto it = g.kv.find(key);
+  if (it == g.kv.end()) return false;
+  if (it->second.kind != GgufValue::UINT && it->second.kind != GgufValue::INT) return false;
+  out = it->second.i;
+  return true;
+}
+bool md_f32(const GgufFile& g, const std::string& key, double& out) {
+  auto it = g.kv.find(key);
+  if (it == g.kv.end()) return false;
+  if (it->second.kind == GgufValue::ARRAY || it->second.kind == GgufValue::STRING) return false;
+  out = it->second.f;
+  return true;
+}
+
+struct TensorJob {
+  const GgufTensor* t;
+  DevMat* mat;      // for matrices
+  float** vec;      // for f32 vectors (norms)
+};
+
+int upload_tensors(armai_llama* m, const char* path, const GgufFile& g, std::vector<TensorJob>& jobs) {
+  FILE* f = fopen(path, "rb");
+  if (!f) return fail(ARMAI_E_IO, std::string("open ") + path + " failed");
+  const size_t STG = 64ull << 20;
+  uint8_t* stg[2] = {nullptr, nullptr};
+  uint8_t* rep = nullptr;
+  cudaEvent_t ev[2];
+  int rc = ARMAI_OK;
+  if (cudaMallocHost(&stg[0], STG) != cudaSuccess || cudaMallocHost(&stg[1], STG) != cudaSuccess) {
+    fclose(f);
+    if (stg[0]) cudaFreeHost(stg[0]);
+    return fail(ARMAI_E_NOMEM, "pinned staging allocation failed");
+  }
+  rep = (uint8_t*)malloc(STG);
+  cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming);
+  cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming);
+  cudaEventRecord(ev[0], m->stream);
+  cudaEventRecord(ev[1], m->stream);
+  int slot = 0;
+  for (TensorJob& j : jobs) {
+    const GgufTensor& t = *j.t;
+    const int64_t rows = t.rows(), cols = t.cols();
+    const int64_t raw_rb = ggml_row_bytes(t.type, cols);
+    int64_t rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)std::max<int64_t>(raw_rb, 1)));
+    if (j.mat && t.type == GGML_Q6_K) rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)dev_row_bytes(GGML_Q6_K, cols)));
+    if (fseeko(f, (off_t)(g.data_offset + t.offset), SEEK_SET) != 0) { rc = fail(ARMAI_E_IO, "seek failed"); break; }
+    uint8_t* dst = j.mat ? j.mat->w : (uint8_t*)*j.vec;
+    for (int64_t r0 = 0; r0 < rows && rc == ARMAI_OK; r0 += rows_per) {
+      const int64_t nr = std::min(rows_per, rows - r0);
+      cudaEventSynchronize(ev[slot]);
+      uint8_t* buf = stg[slot];
+      size_t bytes = (size_t)(nr * raw_rb);
+      if (fread(j.mat && t.type == GGML_Q6_K ? rep : buf, 1, bytes, f) != bytes) {
+        rc = fail(ARMAI_E_IO, "short read of tensor '" + t.name + "'");
+        break;
+      }
+      size_t out_bytes = bytes;
+      if (j.mat && t.type == GGML_Q6_K) {
+        repack_q6k_rows(rep, nr, cols, buf);
+        out_bytes = (size_t)(nr * dev_row_bytes(GGML_Q6_K, cols));
+      } else if (!j.mat && t.type == GGML_F16) {
+        // f16 vector -> f32 (candle dequantises norm weights at load)
+        float* tmp = (float*)rep;
+        const uint16_t* hsrc = (const uint16_t*)buf;
+        for (int64_t i = 0; i < nr * cols; i++) {
+          __half hv = __ushort_as_half(hsrc[i]);
+          tmp[i] = __half2float(hv);
+        }
+        memcpy(buf, tmp, (size_t)(nr * cols * 4));
+        out_bytes = (size_t)(nr * cols * 4);
+      }
+      const size_t drb = j.mat ? (size_t)j.mat->row_bytes : (size_t)cols * 4;
+      if (cudaMemcpyAsync(dst + (size_t)r0 * drb, buf, out_bytes, cudaMemcpyHostToDevice, m->stream) != cudaSuccess) {
+        rc = fail(ARMAI_E_CUDA, "upload of '" + t.name + "' failed");
+        break;
+      }
+      cudaEventRecord(ev[slot], m->stream);
+      slot ^= 1;
+    }
+    if (rc != ARMAI_OK) break;
+  }
+  cudaStreamSynchronize(m->stream);
+  cudaEventDestroy(ev[0]);
+  cudaEventDestroy(ev[1]);
+  cudaFreeHost(stg[0]);
+  cudaFreeHost(stg[1]);
+  free(rep);
+  fclose(f);
+  return rc;
+}
+
+void free_model(armai_llama* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->graph) cudaGraphExecDestroy(m->graph);
+  void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
+                   m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
+                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok};
+  for (void* p : dptrs)
+    if (p) cudaFree(p);
+  for (Layer& L : m->layers) { (void)L; }
+  if (m->h_tok) cudaFreeHost(m->h_tok);
+  if (m->h_misc) cudaFreeHost(m->h_misc);
+  if (m->h_prompt) cudaFreeHost(m->h_prompt);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out) {
+  GgufFile g;
+  ARMAI_TRY(gguf_read(path, g));
+  auto it = g.kv.find("general.architecture");
+  if (it != g.kv.end() && it->second.kind == GgufValue::STRING && it->second.s != "llama")
+    return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: unsupported architecture '" + it->second.s + "' (llama.* keys required)");
+  int64_t n_expert = 0;
+  if (md_u32(g, "llama.expert_count", n_expert) && n_expert > 1)
+    return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: mixture-of-experts models are not supported");
+  int64_t head_count, head_count_kv, block_count, embd, rope_dim;
+  double eps, freq_base = 10000.0;
+  const char* req[] = {"llama.attention.head_count", "llama.attention.head_count_kv", "llama.block_count",
+                       "llama.embedding_length", "llama.rope.dimension_count"};
+  int64_t* dst[] = {&head_count, &head_count_kv, &block_count, &embd, &rope_dim};
+  for (int i = 0; i < 5; i++)
+    if (!md_u32(g, req[i], *dst[i]))
+      return fail(ARMAI_E_FORMAT, std::string("ModelWeights::from_gguf failed: cannot find ") + req[i] + " in metadata");
+  if (!md_f32(g, "llama.attention.layer_norm_rms_epsilon", eps))
+    return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find llama.attention.layer_norm_rms_epsilon in metadata");
+  md_f32(g, "llama.rope.freq_base", freq_base);
+
+  auto* m = new armai_llama();
+  armai_llama_opts o;
+  armai_llama_default_opts(&o);
+  if (opts) o = *opts;
+  m->device = o.device;
+  m->max_seq = o.max_seq_len > 0 ? o.max_seq_len : 4096;
+  m->kv_f16 = o.kv_f16 ? 1 : 0;
+  m->max_batch = std::max(1, o.max_batch);
+  m->use_graph = o.use_graph != 0;
+  m->use_pdl = o.use_pdl != 0;
+  if (o.tp_size > 1) {
+    delete m;
+    return fail(ARMAI_E_INVALID, "tensor parallelism is not available in this build");
+  }
+  m->n_layer = (int)block_count;
+  m->n_embd = (int)embd;
+  m->n_head = (int)head_count;
+  m->n_head_kv = (int)head_count_kv;
+  m->head_dim = (int)(embd / head_count);
+  m->rope_dim = (int)rope_dim;
+  m->eps = (float)eps;
+  m->rope_base = (float)freq_base;
+  if (m->n_head <= 0 || m->n_head_kv <= 0 || m->n_head % m->n_head_kv || embd % head_count ||
+      m->rope_dim != m->head_dim || m->head_dim % 2 || m->n_embd % QK_K) {
+    delete m;
+    return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: unsupported head geometry");
+  }
+  if (m->n_head / m->n_head_kv > 8 || m->head_dim > 256) {
+    delete m;
+    return fail(ARMAI_E_FORMAT, "unsupported attention geometry (query heads per KV head > 8 or head_dim > 256)");
+  }
+
+  auto find = [&](const std::string& name) -> const GgufTensor* {
+    auto t = g.tensors.find(name);
+    return t == g.tensors.end() ? nullptr : &t->second;
+  };
+  std::vector<TensorJob> jobs;
+  size_t arena = 0;
+  int rc = ARMAI_OK;
+  auto add_mat = [&](const std::string& name, DevMat& dm, int64_t want_cols, int64_t want_rows) -> int {
+    const GgufTensor* t = find(name);
+    if (!t) return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find tensor info for " + name);
+    if (t->dims.size() != 2) return fail(ARMAI_E_FORMAT, "tensor " + name + " is not 2-D");
+    if (t->type != GGML_Q4_K && t->type != GGML_Q6_K)
+      return fail(ARMAI_E_FORMAT, std::string("tensor ") + name + " has type " + ggml_type_name(t->type) +
+                                      "; this build supports Q4_K and Q6_K matrices");
+    if ((want_cols > 0 && t->cols() != want_cols) || (want_rows > 0 && t->rows() != want_rows))
+      return fail(ARMAI_E_FORMAT, "tensor " + name + " has an unexpected shape");
+    dm.type = (int)t->type;
+    dm.rows = (int)t->rows();
+    dm.cols = (int)t->cols();
+    dm.row_bytes = (int)dev_row_bytes(dm.type, dm.cols);
+    dm.w = reinterpret_cast<uint8_t*>(arena);  // offset for now
+    arena += al16((size_t)dm.row_bytes * dm.rows + 255) & ~size_t(255);
+    m->weight_bytes_per_token += (int64_t)dm.row_bytes * dm.rows;
+    jobs.push_back(TensorJob{t, &dm, nullptr});
+    return ARMAI_OK;
+  };
+  std::vector<float*> vec_offsets;
+  auto add_vec = [&](const std::string& name, float*& dv, int64_t n) -> int {
+    const GgufTensor* t = find(name);
+    if (!t) return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find tensor info for " + name);
+    if (t->type != GGML_F32 && t->type != GGML_F16)
+      return fail(ARMAI_E_FORMAT, "norm tensor " + name + " must be F32 or F16");
+    if ((int64_t)(t->rows() * t->cols()) != n) return fail(ARMAI_E_FORMAT, "tensor " + name + " has an unexpected shape");
+    dv = reinterpret_cast<float*>(arena);
+    arena += (size_t)((n * 4 + 255) & ~int64_t(255));
+    m->weight_bytes_per_token += n * 4;
+    jobs.push_back(TensorJob{t, nullptr, &dv});
+    return ARMAI_OK;
+  };
+  const GgufTensor* te = find("token_embd.weight");
+  if (!te) { delete m; return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find tensor info for token_embd.weight"); }
+  m->n_vocab = (int)te->rows();
+  m->layers.resize(m->n_layer);
+  rc = add_mat("token_embd.weight", m->tok_embd, m->n_embd, -1);
+  // token_embd streams one row per token, not the whole table
+  if (rc == ARMAI_OK) m->weight_bytes_per_token -= (int64_t)m->tok_embd.row_bytes * (m->tok_embd.rows - 1);
+  if (rc == ARMAI_OK) rc = add_vec("output_norm.weight", m->out_norm, m->n_embd);
+  if (rc == ARMAI_OK) {
+    if (find("output.weight")) rc = add_mat("output.weight", m->output, m->n_embd, m->n_vocab);
+    else {
+      m->output = m->tok_embd;  // tied: candle falls back to token_embd
+      m->weight_bytes_per_token += (int64_t)m->output.row_bytes * (m->output.rows - 1);
+    }
+  }
+  const int64_t QN = (int64_t)m->n_head * m->head_dim, KN = (int64_t)m->n_head_kv * m->head_dim;
+  for (int l = 0; l < m->n_layer && rc == ARMAI_OK; l++) {
+    Layer& L = m->layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    rc = add_mat(p + "attn_q.weight", L.wq, m->n_embd, QN);
+    if (!rc) rc = add_mat(p + "attn_k.weight", L.wk, m->n_embd, KN);
+    if (!rc) rc = add_mat(p + "attn_v.weight", L.wv, m->n_embd, KN);
+    if (!rc) rc = add_mat(p + "attn_output.weight", L.wo, QN, m->n_embd);
+    if (!rc) rc = add_mat(p + "ffn_gate.weight", L.wg, m->n_embd, -1);
+    if (!rc) { m->n_ff = L.wg.rows; rc = add_mat(p + "ffn_up.weight", L.wu, m->n_embd, m->n_ff); }
+    if (!rc) rc = add_mat(p + "ffn_down.weight", L.wd, m->n_ff, m->n_embd);
+    if (!rc) rc = add_vec(p + "attn_norm.weight", L.attn_norm, m->n_embd);
+    if (!rc) rc = add_vec(p + "ffn_norm.weight", L.ffn_norm, m->n_embd);
+    if (!rc && (m->n_ff % QK_K)) rc = fail(ARMAI_E_FORMAT, "feed-forward length must be a multiple of 256");
+  }
+  if (rc != ARMAI_OK) { delete m; return rc; }
+
+  cudaError_t ce = cudaSetDevice(m->device);
+  if (ce != cudaSuccess) { delete m; return cuda_fail(ce, "cudaSetDevice", __FILE__, __LINE__); }
+#define LOAD_CUDA(call)                                                   \
+  do {                                                                    \
+    cudaError_t _e = (call);                                              \
+    if (_e != cudaSuccess) {                                              \
+      int _r = cuda_fail(_e, #call, __FILE__, __LINE__);                  \
+      free_model(m);                                                      \
+      return _r;                                                          \
+    }                                                                     \
+  } while (0)
+  LOAD_CUDA(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  m->arena_bytes = arena;
+  LOAD_CUDA(cudaMalloc(&m->arena, arena));
+  // rebase arena offsets to device pointers
+  auto rebase = [&](uint8_t*& p) { p = m->arena + reinterpret_cast<size_t>(p); };
+  for (TensorJob& j : jobs) {
+    if (j.mat) rebase(j.mat->w);
+    else { uint8_t* q = reinterpret_cast<uint8_t*>(*j.vec); rebase(q); *j.vec = reinterpret_cast<float*>(q); }
+  }
+  if (!find("output.weight")) m->output = m->tok_embd;
+  rc = upload_tensors(m, path, g, jobs);
+  if (rc != ARMAI_OK) { free_model(m); return rc; }
+
+  // rotary tables: precomput_freqs_cis of candle quantized_llama
+  {
+    const int half = m->rope_dim / 2;
+    std::vector<float> theta(half), c((size_t)m->max_seq * half), s((size_t)m->max_seq * half);
+    for (int i = 0; i < m->rope_dim; i += 2)
+      theta[i / 2] = 1.0f / powf(m->rope_base, (float)i / (float)m->rope_dim);
+    for (int p = 0; p < m->max_seq; p++)
+      for (int j = 0; j < half; j++) {
+        const float a = (float)p * theta[j];
+        c[(size_t)p * half + j] = cosf(a);
+        s[(size_t)p * half + j] = sinf(a);
+      }
+    LOAD_CUDA(cudaMalloc(&m->cos_t, c.size() * 4));
+    LOAD_CUDA(cudaMalloc(&m->sin_t, s.size() * 4));
+    LOAD_CUDA(cudaMemcpy(m->cos_t, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+    LOAD_CUDA(cudaMemcpy(m->sin_t, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+  }
+  // KV cache [layer][seq][kv_head][max_seq][head_dim]
+  m->kv_seq_stride = (int64_t)m->n_head_kv * m->max_seq * m->head_dim;
+  m->kv_layer_stride = m->kv_seq_stride * m->max_batch;
+  const size_t kv_bytes = (size_t)m->kv_layer_stride * m->n_layer * (m->kv_f16 ? 2 : 4);
+  LOAD_CUDA(cudaMalloc(&m->kc, kv_bytes));
+  LOAD_CUDA(cudaMalloc(&m->vc, kv_bytes));
+  LOAD_CUDA(cudaMemsetAsync(m->kc, 0, kv_bytes, m->stream));
+  LOAD_CUDA(cudaMemsetAsync(m->vc, 0, kv_bytes, m->stream));
+  const int B = m->max_batch;
+  LOAD_CUDA(cudaMalloc(&m->x, (size_t)B * m->n_embd * 4));
+  LOAD_CUDA(cudaMalloc(&m->q, (size_t)B * QN * 4));
+  LOAD_CUDA(cudaMalloc(&m->y, (size_t)B * QN * 4));
+  LOAD_CUDA(cudaMalloc(&m->h, (size_t)B * m->n_ff * 4));
+  LOAD_CUDA(cudaMalloc(&m->logits, (size_t)B * m->n_vocab * 4));
+  LOAD_CUDA(cudaMalloc(&m->d_token, (size_t)std::max(B, 8) * 4));
+  LOAD_CUDA(cudaMalloc(&m->d_pos, (size_t)std::max(B, 8) * 4));
+  LOAD_CUDA(cudaMalloc(&m->d_err, 64));
+  LOAD_CUDA(cudaMemsetAsync(m->d_err, 0, 64, m->stream));
+  LOAD_CUDA(cudaMemsetAsync(m->d_token, 0, (size_t)std::max(B, 8) * 4, m->stream));
+  LOAD_CUDA(cudaMemsetAsync(m->d_pos, 0, (size_t)std::max(B, 8) * 4, m->stream));
+  const int nrep = m->n_head / m->n_head_kv;
+  m->attn_cap_tokens = (size_t)std::max(B, ATTN_TOK_PER_LAUNCH);
+  LOAD_CUDA(cudaMalloc(&m->attn_part, m->attn_cap_tokens * m->n_head_kv * ATTN_SPLITS * nrep * (m->head_dim + 2) * 4));
+  LOAD_CUDA(cudaMalloc(&m->attn_cnt, m->attn_cap_tokens * m->n_head_kv * 4));
+  LOAD_CUDA(cudaMemsetAsync(m->attn_cnt, 0, m->attn_cap_tokens * m->n_head_kv * 4, m->stream));
+  const int nsm = sm_count();
+  LOAD_CUDA(cudaMalloc(&m->am_val, (size_t)B * nsm * 4));
+  LOAD_CUDA(cudaMalloc(&m->am_idx, (size_t)B * nsm * 4));
+  LOAD_CUDA(cudaMalloc(&m->am_cnt, 64));
+  LOAD_CUDA(cudaMemsetAsync(m->am_cnt, 0, 64, m->stream));
+  LOAD_CUDA(cudaMallocHost(&m->h_tok, 64));
+  LOAD_CUDA(cudaMallocHost(&m->h_misc, 64));
+
+  // launch plans
+  auto maxrb = [](const DevMat& a, const DevMat& b, const DevMat& c) {
+    return std::max(a.row_bytes, std::max(b.row_bytes, c.row_bytes));
+  };
+  const Layer& L0 = m->layers[0];
+  int qkv_rb = 0, gu_rb = 0, wo_rb = 0, dn_rb = 0;
+  for (const Layer& L : m->layers) {
+    qkv_rb = std::max(qkv_rb, maxrb(L.wq, L.wk, L.wv));
+    gu_rb = std::max(gu_rb, L.wg.row_bytes + L.wu.row_bytes);
+    wo_rb = std::max(wo_rb, L.wo.row_bytes);
+    dn_rb = std::max(dn_rb, L.wd.row_bytes);
+  }
+  const int qkv_rows = L0.wq.rows + L0.wk.rows + L0.wv.rows;
+  m->pl_qkv1 = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
+  m->pl_wo1 = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, 1, false, nsm, SMEM_DECODE);
+  m->pl_gu1 = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
+  m->pl_down1 = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, 1, false, nsm, SMEM_DECODE);
+  m->pl_head1 = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
+  m->pl_qkvT = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT);
+  m->pl_woT = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, PREFILL_TILE, false, nsm, SMEM_LIMIT);
+  m->pl_guT = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT);
+  m->pl_downT = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, PREFILL_TILE, false, nsm, SMEM_LIMIT);
+  for (const Plan* pl : {&m->pl_qkv1, &m->pl_wo1, &m->pl_gu1, &m->pl_down1, &m->pl_head1, &m->pl_qkvT,
+                         &m->pl_woT, &m->pl_guT, &m->pl_downT})
+    if (pl->smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "model rows too wide for shared memory"); }
+  int arc = set_smem_attr<MODE_QKV, 1>(m->pl_qkv1.smem);
+  if (!arc) arc = set_smem_attr<MODE_RESID, 1>(std::max(m->pl_wo1.smem, m->pl_down1.smem));
+  if (!arc) arc = set_smem_attr<MODE_GATEUP, 1>(m->pl_gu1.smem);
+  if (!arc) arc = set_smem_attr<MODE_HEAD, 1>(m->pl_head1.smem);
+  if (!arc) arc = set_smem_attr<MODE_QKV, PREFILL_TILE>(m->pl_qkvT.smem);
+  if (!arc) arc = set_smem_attr<MODE_RESID, PREFILL_TILE>(std::max(m->pl_woT.smem, m->pl_downT.smem));
+  if (!arc) arc = set_smem_attr<MODE_GATEUP, PREFILL_TILE>(m->pl_guT.smem);
+  if (arc) { free_model(m); return arc; }
+  const int max_chunk = (m->max_seq + ATTN_SPLITS - 1) / ATTN_SPLITS;
+  m->attn_smem = (size_t)(nrep * m->head_dim + nrep * max_chunk + 2 * nrep) * 4;
+  if (m->attn_smem > 48 * 1024)
+    LOAD_CUDA(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem));
+  if (m->attn_smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "max_seq_len too large for the attention kernel"); }
+  m->n_kernels_step = 2 + 5 * m->n_layer;
+  LOAD_CUDA(cudaStreamSynchronize(m->stream));
+
+  // capture the decode step
+  if (m->use_graph) {
+    cudaGraph_t gr = nullptr;
+    LOAD_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int erc = enqueue_decode_step(m);
+    cudaError_t ec = cudaStreamEndCapture(m->stream, &gr);
+    if (erc != ARMAI_OK || ec != cudaSuccess) {
+      if (gr) cudaGraphDestroy(gr);
+      int r = erc != ARMAI_OK ? erc : cuda_fail(ec, "cudaStreamEndCapture", __FILE__, __LINE__);
+      free_model(m);
+      return r;
+    }
+    ce = cudaGraphInstantiate(&m->graph, gr, 0);
+    cudaGraphDestroy(gr);
+    if (ce != cudaSuccess) { int r = cuda_fail(ce, "cudaGraphInstantiate", __FILE__, __LINE__); free_model(m); return r; }
+  }
+  size_t fb = 0, tb = 0;
+  cudaMemGetInfo(&fb, &tb);
+  m->device_bytes = arena + 2 * kv_bytes;
+  *out = m;
+  return ARMAI_OK;
+#undef LOAD_CUDA
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" void armai_llama_default_opts(armai_llama_opts* o) {
+  std::memset(o, 0, sizeof *o);
+  o->device = 0;
+  o->max_seq_len = 4096;
+  o->kv_f16 = 0;
+  o->max_batch = 1;
+  o->use_graph = 1;
+  o->use_pdl = 1;
+  o->tp_size = 1;
+  o->tp_rank = 0;
+}
+
+extern "C" int armai_llama_load(const char* path, const armai_llama_opts* opts, armai_llama** out) {
+  if (!out) return fail(ARMAI_E_INVALID, "load: null output handle");
+  *out = nullptr;
+  if (!path || !*path) return fail(ARMAI_E_IO, "open failed: empty path");
+  return load_model(path, opts, out);
+}
+
+extern "C" void armai_llama_free(armai_llama* m) { free_model(m); }
+
+extern "C" int armai_llama_get_info(const armai_llama* m, armai_llama_info* info) {
+  if (!m || !info) return fail(ARMAI_E_INVALID, "get_info: null argument");
+  info->n_layer = m->n_layer;
+  info->n_embd = m->n_embd;
+  info->n_ff = m->n_ff;
+  info->n_head = m->n_head;
+  info->n_head_kv = m->n_head_kv;
+  info->head_dim = m->head_dim;
+  info->n_vocab = m->n_vocab;
+  info->max_seq_len = m->max_seq;
+  info->rms_eps = m->eps;
+  info->rope_theta = m->rope_base;
+  info->weight_bytes = m->weight_bytes_per_token;
+  info->device_bytes = (int64_t)m->device_bytes;
+  info->n_kernels_per_step = m->n_kernels_step;
+  info->kv_f16 = m->kv_f16;
+  return ARMAI_OK;
+}
+
+extern "C" int armai_llama_forward(armai_llama* m, const uint32_t* tokens, size_t n, size_t index_pos,
+                                   float* logits, uint32_t* token) {
+  if (!m || (!tokens && n)) return fail(ARMAI_E_INVALID, "forward: null argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  ARMAI_TRY(forward_locked(m, tokens, (int)n, (int)index_pos));
+  if (logits)
+    ARMAI_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->n_vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+  ARMAI_CUDA(cudaMemcpyAsync(m->h_tok, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
+  ARMAI_TRY(check_device_error(m));
+  if (token) *token = m->h_tok[0];
+  return ARMAI_OK;
+}
+
+extern "C" int armai_llama_generate(armai_llama* m, const uint32_t* prompt, size_t n_prompt,
+                                    size_t max_new, const uint32_t* stop, size_t n_stop,
+                                    armai_token_cb on_token, void* user, uint32_t* out,
+                                    size_t* n_out, uint64_t* prefill_us, uint64_t* decode_us) {
+  if (!m || !n_out || !prefill_us || !decode_us) return fail(ARMAI_E_INVALID, "generate: null argument");
+  *n_out = 0;
+  *prefill_us = 0;
+  *decode_us = 0;
+  if (max_new == 0 || n_prompt == 0) return ARMAI_OK;  // llama_candle.rs:76-78
+  if (!prompt || !out) return fail(ARMAI_E_INVALID, "generate: null prompt or output buffer");
+  std::lock_guard<std::mutex> lk(m->mu);  // llama_candle.rs:80 (Mutex per model)
+  if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  if (n_prompt + max_new - 1 > (size_t)m->max_seq)
+    return fail(ARMAI_E_RANGE, "generate: prompt + max_new - 1 = " + std::to_string(n_prompt + max_new - 1) +
+                                   " positions exceed the rotary table (max_seq_len " + std::to_string(m->max_seq) + ")");
+  auto is_stop = [&](uint32_t t) {
+    for (size_t i = 0; i < n_stop; i++)
+      if (stop[i] == t) return true;
+    return false;
+  };
+  using clk = std::chrono::steady_clock;
+  const auto t0 = clk::now();
+  ARMAI_TRY(forward_locked(m, prompt, (int)n_prompt, 0));
+  ARMAI_CUDA(cudaMemcpyAsync(m->h_tok, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
+  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  *prefill_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(clk::now() - t0).count();
+  uint32_t next = m->h_tok[0];
+  size_t n = 0;
+  out[n++] = next;
+  if (on_token) on_token(user, next);
+  const auto t1 = clk::now();
+  // Decode: step i consumes token i-1 (already on the device) and produces
+  // token i. Step i+1 is enqueued before token i reaches the host, so the
+  // GPU never idles on the host round trip; its result is discarded if token
+  // i turns out to be a stop token (the reference stops before running it).
+  const int RING = 8;
+  cudaEvent_t ev[RING];
+  for (int i = 0; i < RING; i++) cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming);
+  int rc = ARMAI_OK;
+  auto launch_step = [&](size_t i) -> int {
+    ARMAI_TRY(run_decode_step(m));
+    ARMAI_CUDA(cudaMemcpyAsync(&m->h_tok[i % RING], m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
+    ARMAI_CUDA(cudaEventRecord(ev[i % RING], m->stream));
+    return ARMAI_OK;
+  };
+  if (max_new > 1 && !is_stop(next)) rc = launch_step(1);
+  for (size_t i = 1; i < max_new && rc == ARMAI_OK; i++) {
+    if (is_stop(next)) break;  // llama_candle.rs:110
+    if (i + 1 < max_new) {
+      rc = launch_step(i + 1);
+      if (rc) break;
+    }
+    cudaError_t e = cudaEventSynchronize(ev[i % RING]);
+    if (e != cudaSuccess) { rc = cuda_fail(e, "cudaEventSynchronize", __FILE__, __LINE__); break; }
+    next = m->h_tok[i % RING];
+    out[n++] = next;
+    if (on_token) on_token(user, next);
+  }
+  cudaStreamSynchronize(m->stream);
+  *decode_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(clk::now() - t1).count();
+  for (int i = 0; i < RING; i++) cudaEventDestroy(ev[i]);
+  m->kv_len = (int)(n_prompt + n - 1);
+  *n_out = n;
+  if (rc != ARMAI_OK) return rc;
+  return check_device_error(m);
+}
+
+extern "C" int armai_llama_generate_batch(armai_llama* m, const uint32_t* prompts, const size_t* n_prompt,
+                                          size_t n_seq, size_t max_new, const uint32_t* stop, size_t n_stop,
+                                          uint32_t* out, size_t* n_out, uint64_t* prefill_us,
+                                          uint64_t* decode_us) {
+  (void)m; (void)prompts; (void)n_prompt; (void)n_seq; (void)max_new; (void)stop; (void)n_stop;
+  (void)out; (void)n_out; (void)prefill_us; (void)decode_us;
+  return fail(ARMAI_E_INVALID, "generate_batch: not implemented yet");
+}
+
+extern "C" int armai_llama_bench_decode(armai_llama* m, int32_t n_steps, float* ms) {
+  if (!m || !ms || n_steps <= 0) return fail(ARMAI_E_INVALID, "bench_decode: bad argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  if (m->kv_len + n_steps > m->max_seq) return fail(ARMAI_E_RANGE, "bench_decode: steps exceed max_seq_len");
+  cudaEvent_t a, b;
+  ARMAI_CUDA(cudaEventCreate(&a));
+  ARMAI_CUDA(cudaEventCreate(&b));
+  ARMAI_CUDA(cudaEventRecord(a, m->stream));
+  for (int i = 0; i < n_steps; i++) ARMAI_TRY(run_decode_step(m));
+  ARMAI_CUDA(cudaEventRecord(b, m->stream));
+  ARMAI_CUDA(cudaEventSynchronize(b));
+  ARMAI_CUDA(cudaEventElapsedTime(ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  m->kv_len += n_steps;
+  return check_device_error(m);
+}
+
+extern "C" int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t rounds, float* ms_per_launch,
+                                        int64_t* bytes_per_launch) {
+  if (!m || !ms_per_launch || !bytes_per_launch || rounds <= 0 || kind < 0 || kind > 5)
+    return fail(ARMAI_E_INVALID, "bench_kernel: bad argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  const bool pdl = m->use_pdl;
+  m->use_pdl = false;
+  int64_t bytes = 0;
+  int launches = 0;
+  auto one = [&](int l) -> cudaError_t {
+    const Layer& L = m->layers[l];
+    switch (kind) {
+      case 0: bytes += (int64_t)L.wg.rows * L.wg.row_bytes + (int64_t)L.wu.rows * L.wu.row_bytes;
+              return launch_gateup<1>(m, m->pl_gu1, l, m->x, m->h);
+      case 1: bytes += (int64_t)L.wq.rows * L.wq.row_bytes + (int64_t)L.wk.rows * L.wk.row_bytes +
+                       (int64_t)L.wv.rows * L.wv.row_bytes;
+              return launch_qkv<1>(m, m->pl_qkv1, l, m->x, m->q, m->d_pos, 0);
+      case 2: bytes += (int64_t)L.wo.rows * L.wo.row_bytes;
+              return launch_resid<1>(m, m->pl_wo1, L.wo, m->y, m->x);
+      case 3: bytes += (int64_t)L.wd.rows * L.wd.row_bytes;
+              return launch_resid<1>(m, m->pl_down1, L.wd, m->h, m->x);
+      case 4: bytes += (int64_t)m->output.rows * m->output.row_bytes;
+              return launch_head(m, m->x, m->d_pos, nullptr);
+      default: return launch_attn(m, l, m->q, m->y, m->d_pos, 1, 0);
+    }
+  };
+  cudaEvent_t a, b;
+  ARMAI_CUDA(cudaEventCreate(&a));
+  ARMAI_CUDA(cudaEventCreate(&b));
+  int rc = ARMAI_OK;
+  for (int l = 0; l < m->n_layer && rc == ARMAI_OK; l++)  // warm-up round
+    if (one(l) != cudaSuccess) rc = fail(ARMAI_E_CUDA, "bench_kernel: launch failed");
+  bytes = 0;
+  cudaEventRecord(a, m->stream);
+  for (int r = 0; r < rounds && rc == ARMAI_OK; r++)
+    for (int l = 0; l < (kind == 4 ? 1 : m->n_layer) && rc == ARMAI_OK; l++) {
+      if (one(l) != cudaSuccess) rc = fail(ARMAI_E_CUDA, "bench_kernel: launch failed");
+      launches++;
+    }
+  cudaEventRecord(b, m->stream);
+  m->use_pdl = pdl;
+  if (rc != ARMAI_OK) { cudaEventDestroy(a); cudaEventDestroy(b); return rc; }
+  ARMAI_CUDA(cudaEventSynchronize(b));
+  float ms = 0.f;
+  ARMAI_CUDA(cudaEventElapsedTime(&ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  *ms_per_launch = ms / (float)launches;
+  *bytes_per_launch = bytes / launches;
+  return check_device_error(m);
+}

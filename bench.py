@@ -1,0 +1,310 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantized-Llama decode path (BASELINE.json metric).
+
+Workload (the configuration the metric is quoted
+on): TinyLlama-1.1B-architecture, Q4_K_M, batch 1, greedy; 32-token seeded
+prompt, 128 new tokens. A "step" is one generation's decode phase: 127
+single-token decode steps after the prompt's prefill.
+
+  value  decode tokens/s, device-timed (CUDA events around back-to-back CUDA
+         graph replays; the prompt's prefill between steps is not timed),
+         summed over ranks / max rank time.
+  e2e    the same metric through the C ABI call (armai_llama_generate) with
+         host buffers: prompt H2D, every token D2H to the host for the stop
+         check, measured the way the reference measures it
+         ((n_new - 1) / decode_us, llama_candle.rs:106-130, llama_candle.ex:99).
+
+N > 1 (torchrun): independent replicas, one per GPU (batch-1 TinyLlama does
+not shard; scaling "weak"). `--impl reference` times the reference's CPU
+path (the oracle restatement of candle's generic kernels, all host threads)
+on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tokens/s and weight-stream HBM GB/s (% peak), Q4_K_M Llama, b=1"
+ARCH = "tinyllama-1.1b"
+PROMPT, MAX_NEW = 32, 128
+PUBLISHED_TOK_S = 4.71  # TinyLlama 1.1B Q4_K_M b=1 decode (Snapdragon 632)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="armai", choices=["armai", "reference"])
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline sample")
+    p.add_argument("--no-clocks", action="store_true")
+    return p.parse_args()
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi samples (every 200 ms) during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev: int, enabled: bool):
+        self.dev, self.proc, self.lines = dev, None, []
+        self.enabled = enabled
+
+    def __enter__(self):
+        if self.enabled:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                     "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.th = threading.Thread(target=self._read, daemon=True)
+                self.th.start()
+            except Exception:
+                self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.lines:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 7:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def cpu_baseline_sample(path, prompt, max_new=6):
+    """The oracle (candle's generic kernels restated in C, OpenMP over output
+    columns as rayon does) on all host threads: decode tokens/s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref
+    cores = os.cpu_count() or 1
+    ref.set_threads(cores)
+    m = ref.OracleLlama(path)
+    t0 = time.time()
+    toks, pre_us, dec_us = m.generate(prompt, max_new)
+    wall = time.time() - t0
+    m.close()
+    v = (len(toks) - 1) * 1e6 / max(dec_us, 1)
+    return {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{ARCH} Q4_K_M b=1: {len(prompt)}-token prompt + {max_new} new tokens "
+                      f"(decode {len(toks) - 1} steps, {dec_us / 1e6:.1f} s; prefill {pre_us / 1e6:.1f} s; "
+                      f"wall {wall:.1f} s)"}
+
+
+def run_reference(args, d):
+    if d.rank != 0:
+        return
+    from arm_ai_b200 import synth
+    path = synth.model_path(ARCH, seed=0)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ref
+    cores = os.cpu_count() or 1
+    ref.set_threads(cores)
+    m = ref.OracleLlama(path)
+    prompt = synth.prompt_tokens(PROMPT, m.n_vocab, 1000)
+    per_step_new = 4  # bounded sample: 3 decode steps per step
+    for _ in range(args.warmup):
+        m.generate(prompt, per_step_new)
+    tok, dec = 0, 0
+    t0 = time.time()
+    for _ in range(args.steps):
+        toks, _, dec_us = m.generate(prompt, per_step_new)
+        tok += len(toks) - 1
+        dec += dec_us
+    wall = time.time() - t0
+    v = tok * 1e6 / max(dec, 1)
+    out = {"metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps,
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": v / PUBLISHED_TOK_S, "dtype": "int8",
+           "data": "synthetic (seeded random-init weights, Q4_K_M mix)",
+           "config": {"workload": f"{ARCH} Q4_K_M greedy decode b=1, {PROMPT}-token prompt; CPU sample of "
+                                  f"{per_step_new} new tokens per step"},
+           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"{args.steps} x ({PROMPT}-token prompt + {per_step_new} new tokens)"},
+           "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def run_armai(args, d):
+    from arm_ai_b200 import native, synth
+    if d.rank == 0:
+        path = synth.model_path(ARCH, seed=0)
+    d.barrier()
+    path = synth.model_path(ARCH, seed=0)
+    gpu = native.llama_candle_load_op(path, device=d.local)
+    info = gpu.info()
+    prompt = synth.prompt_tokens(PROMPT, info.n_vocab, 1000 + d.rank)
+    n_dec = MAX_NEW - 1
+
+    def decode_once():
+        native.llama_forward(gpu, prompt, 0, want_logits=False)  # prefill (not timed)
+        return native.llama_bench_decode(gpu, n_dec)
+
+    for _ in range(args.warmup):
+        decode_once()
+    with Clocks(d.local, not args.no_clocks) as clk:
+        d.barrier()
+        t_wall = time.time()
+        ms = [decode_once() for _ in range(args.steps)]
+        t_wall = time.time() - t_wall
+        d.barrier()
+    dev_s = sum(ms) / 1e3
+    max_s = d.max(dev_s)
+    total_tokens = d.sum(args.steps * n_dec)
+    value = total_tokens / max_s
+
+    # e2e: through the C ABI generate call, host prompt in, every token out
+    e2e_dec, e2e_tok, e2e_wall, pre_us_all = 0, 0, 0.0, 0
+    for _ in range(max(1, args.steps)):
+        t0 = time.time()
+        toks, pre_us, dec_us = native.llama_candle_generate_op(gpu, prompt, MAX_NEW, [])
+        e2e_wall += time.time() - t0
+        e2e_dec += dec_us
+        e2e_tok += len(toks) - 1
+        pre_us_all += pre_us
+    e2e_rank = e2e_tok * 1e6 / max(e2e_dec, 1)
+    e2e_total = d.sum(e2e_rank)
+
+    # roofline of the dominant kernel (gate/up matvec, cycled over the layers)
+    kern = {}
+    for kind in ("gateup", "ffn_down", "qkv", "attn_output", "head"):
+        kern[kind] = native.llama_bench_kernel(gpu, kind, rounds=5)
+    ms_k, bytes_k = kern["gateup"]
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_k / (ms_k * 1e-3) / 1e9
+    bytes_tok = info.weight_bytes
+    kv_bytes = 2 * info.n_layer * info.n_head_kv * info.head_dim * (2 if info.kv_f16 else 4) * \
+        (PROMPT + (PROMPT + n_dec)) / 2
+    ws_gbs = (bytes_tok + kv_bytes) * (value / d.world) / 1e9
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(path, prompt)
+    if d.rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": d.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_s * 1e3 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / d.world / PUBLISHED_TOK_S, "dtype": "int8",
+            "data": "synthetic (seeded random-init N(0,0.02) weights quantised Q4_K/Q6_K (Q4_K_M mix); "
+                    "prompt ids uniform in [3, 32000))",
+            "config": {"workload": f"{ARCH} Q4_K_M greedy decode b=1: {PROMPT}-token prompt + {MAX_NEW} new "
+                                   f"tokens ({n_dec} timed decode steps per step)",
+                       "arch": "22 layers, hidden 2048, FFN 5632, 32/4 heads, head_dim 64, vocab 32000",
+                       "l2": f"inputs larger than L2: {bytes_tok / 1e6:.0f} MB of weights streamed per token",
+                       "timed": "decode graph replays on device (CUDA events); prefill between steps untimed",
+                       "parallelism": f"replicas x{d.world}" if d.world > 1 else "1 GPU"},
+            "weight_stream": {"gb_s_per_gpu": ws_gbs, "frac_of_hbm": ws_gbs / peak,
+                              "bytes_per_token": bytes_tok + kv_bytes, "peak_gbs": peak, "peak_source": peak_kind},
+            "e2e": {"value": e2e_total, "unit": "tokens/s",
+                    "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": MAX_NEW * 4,
+                    "wall_tokens_per_s_incl_prefill": e2e_tok / max(e2e_wall, 1e-9) * d.world,
+                    "prefill_tokens_per_s": PROMPT * 1e6 / max(pre_us_all / max(1, args.steps), 1)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "kernel": "k_matvec<MODE_GATEUP,1>",
+                         "peak_source": peak_kind,
+                         "per_kernel_gbs": {k: b / (m_ * 1e-3) / 1e9 for k, (m_, b) in kern.items()},
+                         "per_kernel_us": {k: m_ * 1e3 for k, (m_, b) in kern.items()}},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": int(args.steps * n_dec * info.n_kernels_per_step * d.world),
+            "wall_s_timed_region": t_wall,
+        }
+        print(json.dumps(out), flush=True)
+    gpu.close()
+
+
+def main():
+    args = parse()
+    d = Dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, d)
+        else:
+            run_armai(args, d)
+    finally:
+        d.close()
+
+
+if __name__ == "__main__":
+    main()

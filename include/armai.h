@@ -1,0 +1,254 @@
+/*
+ * armai.h — C ABI of libarmai_cuda.so, the B200 (sm_100a) implementation of
+ * arm_ai's quantized-Llama decode path and its int8/int4 primitive NIFs.
+ *
+ * A Rust NIF shim (native/arm_ai_nif, feature "cuda") binds these entry
+ * points with `extern "C"` and keeps every NIF name and arity of the
+ * reference. Each entry point cites the reference function it replaces.
+ *
+ * Conventions
+ *   - Status: 0 = ok, negative = error (see ARMAI_E_*). The message of the
+ *     last failing call on the calling thread is armai_last_error().
+ *   - Host-pointer entry points take plain host buffers plus their lengths
+ *     (in elements), exactly the binaries a NIF receives, and write into a
+ *     caller-owned output buffer (the NIF's OwnedBinary). Length mismatches
+ *     are errors with the reference's wording.
+ *   - armai_dev_* entry points take device pointers and a cudaStream_t
+ *     (passed as void*) and do not synchronise.
+ *   - Every call sets its CUDA device on the calling thread first.
+ */
+#ifndef ARMAI_H
+#define ARMAI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ARMAI_API __attribute__((visibility("default")))
+#else
+#define ARMAI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ARMAI_OK 0
+#define ARMAI_E_INVALID -1     /* bad argument / length mismatch */
+#define ARMAI_E_IO -2          /* file open / read failure */
+#define ARMAI_E_FORMAT -3      /* malformed or unsupported GGUF content */
+#define ARMAI_E_CUDA -4        /* CUDA runtime error */
+#define ARMAI_E_NOMEM -5       /* device or host allocation failure */
+#define ARMAI_E_DEVICE -6      /* kernel-side error flag (bounded wait expired) */
+#define ARMAI_E_RANGE -7       /* position beyond the rotary table / KV capacity */
+
+/* ------------------------------------------------------------------ */
+/* Quantized Llama model                                                */
+/* ------------------------------------------------------------------ */
+typedef struct armai_llama armai_llama;
+
+typedef struct armai_llama_opts {
+  int32_t device;       /* CUDA device ordinal; default 0 */
+  int32_t max_seq_len;  /* rotary table length = KV capacity; default 4096
+                           (candle quantized_llama MAX_SEQ_LEN) */
+  int32_t kv_f16;       /* 0: f32 KV cache (as candle); 1: f16 KV cache */
+  int32_t max_batch;    /* sequences per batched decode step; default 1 */
+  int32_t use_graph;    /* capture the decode step as a CUDA graph; default 1 */
+  int32_t use_pdl;      /* programmatic dependent launch between kernels; default 1 */
+  int32_t tp_size;      /* tensor-parallel degree; default 1 */
+  int32_t tp_rank;      /* this process's rank in the TP group */
+  const void* tp_unique_id; /* ncclUniqueId bytes (128), same on every rank */
+  int32_t reserved[8];
+} armai_llama_opts;
+
+/* Fill `o` with the defaults above. */
+ARMAI_API void armai_llama_default_opts(armai_llama_opts* o);
+
+/* Replaces llama_candle::load_model (native/arm_ai_nif/src/llama_candle.rs:35-48)
+ * behind llama_candle_load_op (native/arm_ai_nif/src/lib.rs:1659-1665).
+ * Parses the GGUF file, uploads the Q4_K / Q6_K super-blocks to HBM,
+ * allocates the KV cache and captures the decode graph. `opts` may be NULL. */
+ARMAI_API int armai_llama_load(const char* path, const armai_llama_opts* opts, armai_llama** out);
+
+/* Releases every device and host resource of the model (the NIF resource's
+ * Drop; native/arm_ai_nif/src/lib.rs:2040-2043). NULL is a no-op. */
+ARMAI_API void armai_llama_free(armai_llama* m);
+
+typedef struct armai_llama_info {
+  int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, max_seq_len;
+  float rms_eps, rope_theta;
+  int64_t weight_bytes;      /* bytes of weights streamed per decode token */
+  int64_t device_bytes;      /* total device memory held by the model */
+  int32_t n_kernels_per_step;/* kernels launched per decode step */
+  int32_t kv_f16;
+} armai_llama_info;
+ARMAI_API int armai_llama_get_info(const armai_llama* m, armai_llama_info* info);
+
+/* Per-token callback: called on the generating thread as soon as each
+ * token's id has reached the host (llama_candle_stream_op sends
+ * {:llama_token, id} from this point; native/arm_ai_nif/src/lib.rs:1682-1699). */
+typedef void (*armai_token_cb)(void* user, uint32_t token);
+
+/* Replaces llama_candle::generate_greedy_with (llama_candle.rs:69-137)
+ * behind llama_candle_generate_op / llama_candle_stream_op
+ * (native/arm_ai_nif/src/lib.rs:1667-1699). Greedy decode: prefill at offset
+ * 0, then up to max_new-1 single-token steps, stopping after a token in
+ * `stop` (the stop token is included in `out`). max_new == 0 or n_prompt == 0
+ * yields no tokens and zero timings. `out` must hold max_new ids.
+ * prefill_us / decode_us are the reference's two wall-clock timers. */
+ARMAI_API int armai_llama_generate(armai_llama* m, const uint32_t* prompt, size_t n_prompt,
+                         size_t max_new, const uint32_t* stop, size_t n_stop,
+                         armai_token_cb on_token, void* user, uint32_t* out, size_t* n_out,
+                         uint64_t* prefill_us, uint64_t* decode_us);
+
+/* Batched greedy decode of n_seq independent sequences:
+ * prompts are concatenated in `prompts` with lengths in `n_prompt[n_seq]`.
+ * Each sequence behaves exactly like one armai_llama_generate call; decode
+ * steps of all live sequences run as one batched step. out is
+ * [n_seq][max_new], n_out[n_seq]. No reference counterpart (the reference
+ * holds one KV cache per handle, llama_candle.rs:27-29). */
+ARMAI_API int armai_llama_generate_batch(armai_llama* m, const uint32_t* prompts, const size_t* n_prompt,
+                               size_t n_seq, size_t max_new, const uint32_t* stop,
+                               size_t n_stop, uint32_t* out, size_t* n_out,
+                               uint64_t* prefill_us, uint64_t* decode_us);
+
+/* ModelWeights::forward(tokens[1, n], index_pos) (candle-transformers 0.8.4
+ * quantized_llama, called at llama_candle.rs:92-94 and :118-120): runs the
+ * tokens at positions index_pos.. (index_pos == 0 resets the KV cache) and
+ * writes the last position's f32 logits [n_vocab] to host `logits` (may be
+ * NULL) and its first-max argmax (llama_candle.rs:145-176) to *token. */
+ARMAI_API int armai_llama_forward(armai_llama* m, const uint32_t* tokens, size_t n, size_t index_pos,
+                        float* logits, uint32_t* token);
+
+/* Device-resident decode benchmark: runs `n_steps` greedy decode steps
+ * back to back from the current state (token and position already on the
+ * device after a forward/prefill), without host round trips, and returns the
+ * device time (CUDA events on the model's stream) in *ms. */
+ARMAI_API int armai_llama_bench_decode(armai_llama* m, int32_t n_steps, float* ms);
+
+/* Kernel-level timing for roofline figures: launches one kind of decode
+ * kernel (0 = gate/up matvec, 1 = q/k/v matvec, 2 = attn_output matvec,
+ * 3 = ffn_down matvec, 4 = output head + argmax, 5 = attention) once per
+ * layer, layer after layer, `rounds` times, back to back without PDL on the
+ * model's stream, and returns the average device time per launch (CUDA
+ * events) and the weight bytes one launch streams (layer average). The
+ * launches read whatever activations are resident; results are discarded. */
+ARMAI_API int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t rounds, float* ms_per_launch,
+                                       int64_t* bytes_per_launch);
+
+/* ------------------------------------------------------------------ */
+/* Primitive NIFs (nx_arm building blocks). Host buffers in, caller-owned  */
+/* host output buffer out; same argument order as the NIFs.                */
+/* ------------------------------------------------------------------ */
+
+/* int8_matmul_f32_op (native/arm_ai_nif/src/lib.rs:215-235 ->
+ * shape_ops.rs:1169-1211): out[M,N] = (f32)(sum_k a[m,k] w[n,k]) * act_scale * w_scales[n]. */
+ARMAI_API int armai_int8_matmul_f32(const int8_t* a, size_t a_len, const int8_t* w, size_t w_len,
+                          const float* w_scales, size_t w_scales_len, double act_scale,
+                          size_t m, size_t n, size_t k, float* out);
+
+/* int8_matmul_f32_per_token_op (lib.rs:239-264 -> shape_ops.rs:1222-1264). */
+ARMAI_API int armai_int8_matmul_f32_per_token(const int8_t* a, size_t a_len, const int8_t* w, size_t w_len,
+                                    const float* act_scales, size_t act_scales_len,
+                                    const float* w_scales, size_t w_scales_len, size_t m,
+                                    size_t n, size_t k, float* out);
+
+/* The s8 x s8 -> s32 GEMM underneath the two entry points above
+ * (shape_ops.rs:1364-1370 int8_dot per output). out[M,N] int32. */
+ARMAI_API int armai_int8_matmul_s32(const int8_t* a, size_t a_len, const int8_t* w, size_t w_len,
+                          size_t m, size_t n, size_t k, int32_t* out);
+
+/* quantize_int8_per_token_op (lib.rs:268-296 -> shape_ops.rs:1273-1292):
+ * q[M,K] int8, scales[M] f32. */
+ARMAI_API int armai_quantize_int8_per_token(const float* a, size_t a_len, size_t m, size_t k, int8_t* q,
+                                  float* scales);
+
+/* int4_matmul_f32_op (lib.rs:450-473 -> shape_ops.rs:3175-3236): a[M,K] f32,
+ * w_packed[N,K/2] (low nibble = even k, value-8), w_scales[N,K/32] f32. */
+ARMAI_API int armai_int4_matmul_f32(const float* a, size_t a_len, const uint8_t* w_packed,
+                          size_t w_packed_len, const float* w_scales, size_t w_scales_len,
+                          size_t m, size_t n, size_t k, float* out);
+
+/* int4_matmul_gemv_neon_op (lib.rs:427-446 -> shape_ops.rs:3059-3166): M = 1. */
+ARMAI_API int armai_int4_matmul_gemv(const float* a, size_t a_len, const uint8_t* w_packed,
+                           size_t w_packed_len, const float* w_scales, size_t w_scales_len,
+                           size_t n, size_t k, float* out);
+
+/* int4_matmul_gemv_q4_x_q8_neon_op (lib.rs:403-422 -> shape_ops.rs:2923-3028):
+ * activations quantised Q8_0-style per 32 values, integer group dots. */
+ARMAI_API int armai_int4_matmul_gemv_q4_x_q8(const float* a, size_t a_len, const uint8_t* w_packed,
+                                   size_t w_packed_len, const float* w_scales,
+                                   size_t w_scales_len, size_t n, size_t k, float* out);
+
+/* quantize_int4_q4_0_op (lib.rs:477-502 -> shape_ops.rs:3242-3275):
+ * packed[N,K/2], scales[N,K/32]. */
+ARMAI_API int armai_quantize_int4_q4_0(const float* w, size_t w_len, size_t n, size_t k, uint8_t* packed,
+                             float* scales);
+
+/* rmsnorm_f32_op (lib.rs:127-145 -> shape_ops.rs:976-1018). */
+ARMAI_API int armai_rmsnorm_f32(const float* input, size_t input_len, const float* gamma, size_t gamma_len,
+                      size_t n_outer, size_t inner, double epsilon, float* out);
+
+/* flash_attention_f32_op (lib.rs:743-764 -> shape_ops.rs:464-558):
+ * q[B,H,Sq,D], k/v[B,H,Sk,D] f32 -> out[B,H,Sq,D]. */
+ARMAI_API int armai_flash_attention_f32(const float* q, size_t q_len, const float* k, size_t k_len,
+                              const float* v, size_t v_len, double scale, size_t b, size_t h,
+                              size_t sq, size_t sk, size_t d, int causal, float* out);
+
+/* dequant_matmul_int8_f32_op (lib.rs:507-532 -> shape_ops.rs:1525-1582). */
+ARMAI_API int armai_dequant_matmul_int8_f32(const float* act, size_t act_len, const int8_t* w, size_t w_len,
+                                  const float* scales, size_t scales_len, size_t b, size_t m,
+                                  size_t n, size_t k, float* out);
+
+/* ------------------------------------------------------------------ */
+/* Device-pointer variants (benchmarks, and callers that keep tensors     */
+/* resident). `stream` is a cudaStream_t.                                   */
+/* ------------------------------------------------------------------ */
+ARMAI_API int armai_dev_int8_matmul_s32(const int8_t* a, const int8_t* w, int32_t* out, int64_t m,
+                              int64_t n, int64_t k, void* stream);
+ARMAI_API int armai_dev_int8_matmul_f32(const int8_t* a, const int8_t* w, const float* act_scales,
+                              int per_token, float act_scale, const float* w_scales, float* out,
+                              int64_t m, int64_t n, int64_t k, void* stream);
+ARMAI_API int armai_dev_int4_matmul_f32(const float* a, const uint8_t* w_packed, const float* w_scales,
+                              float* out, int64_t m, int64_t n, int64_t k, void* stream);
+ARMAI_API int armai_dev_int4_gemv_q4_x_q8(const float* a, const uint8_t* w_packed, const float* w_scales,
+                                float* out, int64_t n, int64_t k, void* stream);
+/* BASELINE config 5's int4 variant: per-32-group f16 scales [N,K/32]. */
+ARMAI_API int armai_dev_int4_gemv_f16s(const float* a, const uint8_t* w_packed, const uint16_t* w_scales,
+                             float* out, int64_t n, int64_t k, void* stream);
+ARMAI_API int armai_dev_rmsnorm_f32(const float* x, const float* gamma, float* out, int64_t n_outer,
+                          int64_t inner, float eps, void* stream);
+/* Causal/non-causal attention, f16 q/k/v [B,H,S,D] -> f32 out. */
+ARMAI_API int armai_dev_flash_attention_f16(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                  float* out, float scale, int64_t b, int64_t h, int64_t sq,
+                                  int64_t sk, int64_t d, int causal, void* stream);
+ARMAI_API int armai_dev_flash_attention_f32(const float* q, const float* k, const float* v, float* out,
+                                  float scale, int64_t b, int64_t h, int64_t sq, int64_t sk,
+                                  int64_t d, int causal, void* stream);
+
+/* ------------------------------------------------------------------ */
+/* k-quant building blocks, exposed for bit-exact parity tests.           */
+/* ------------------------------------------------------------------ */
+/* Q8_K quantisation of x[m, k] (candle BlockQ8K::from_float): writes
+ * blocks of {f32 d, int8 qs[256], int16 bsums[16]} (292 B) to host `out`. */
+ARMAI_API int armai_quantize_q8k(const float* x, size_t m, size_t k, void* out);
+/* Integer per-super-block dot products of weight rows w[n, k] (GGML type
+ * 12 = Q4_K or 14 = Q6_K, raw GGUF bytes) with Q8_K rows q8[m, k]:
+ * isum[m][n][k/256] = sum_j scale_j*<q_j, q8_j>; msum (Q4_K only) =
+ * sum_j min_j * bsum_j. The same device code the decode kernels use. */
+ARMAI_API int armai_kquant_block_dots(const void* w, int type, size_t n, size_t k, const void* q8,
+                            size_t m, int32_t* isum, int32_t* msum);
+/* QMatMul: out[m][n] = vec_dot(w row n, Q8_K(x row m)) through the decode
+ * (m == 1) or prefill (m > 1) matvec kernels. */
+ARMAI_API int armai_qmatmul(const void* w, int type, size_t n, size_t k, const float* x, size_t m,
+                  float* out);
+
+/* Thread-local message of the last failing call on this thread. */
+ARMAI_API const char* armai_last_error(void);
+/* Library version string. */
+ARMAI_API const char* armai_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,77 @@
+"""Bit-exact checks of the CUDA k-quant building blocks against the oracle.
+
+Integer work (Q8_K bytes and bsums, per-super-block integer dot products) must
+be identical; QMatMul's f32 output differs from candle's only in the order of
+the f32 combine of exact integers, so it is held to 2e-6 of the magnitude
+sum (sum_i |w_i x_i|).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import ref
+from arm_ai_b200 import kquant
+from arm_ai_b200._lib import load_synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _rows(qtype, rows, k, seed, std=0.02):
+    lib = load_synth()
+    bb = 144 if qtype == kquant.Q4_K else 210
+    out = np.empty((rows, (k // 256) * bb), dtype=np.uint8)
+    assert lib.synth_tensor(ctypes.c_uint64(seed), rows, k, ctypes.c_float(std), qtype,
+                            out.ctypes.data_as(ctypes.c_void_p)) == 0
+    return out
+
+
+def _activations(m, k, seed):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[0, :256] = 0.0                                   # all-zero block
+    if m > 1:
+        x[1, 256:512] = np.float32(0.75)               # every value ties on |x|
+        x[1, 300] = np.float32(-0.75)
+    if m > 2:
+        # max |x| = 2 -> iscale = 64; 64 * (i + 0.5)/64 = i + 0.5 exactly, so
+        # every value sits on a rounding tie (half away from zero).
+        x[2, 0] = np.float32(-2.0)
+        x[2, 1:256] = (np.arange(255, dtype=np.float32) - 127 + np.float32(0.5)) / np.float32(64.0)
+    return x
+
+
+@pytest.mark.parametrize("k", [256, 2048, 5632])
+def test_q8k_quantize_bit_exact(built, k):
+    x = _activations(5, k, k)
+    ours = kquant.quantize_q8k(x)
+    theirs = ref.quantize_q8k(x)
+    assert np.array_equal(ours["qs"], theirs["qs"])
+    assert np.array_equal(ours["bsums"], theirs["bsums"])
+    assert np.array_equal(ours["d"].view(np.uint32), theirs["d"].view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K])
+@pytest.mark.parametrize("k", [2048, 5632])
+def test_block_dots_bit_exact(built, qtype, k):
+    w = _rows(qtype, 37, k, seed=k + qtype)
+    q8 = ref.quantize_q8k(_activations(3, k, 7))
+    isum, msum = kquant.block_dots(qtype, w, k, q8)
+    risum, rmsum = ref.block_ints(qtype, w, q8, k)
+    assert np.array_equal(isum, risum)
+    if qtype == kquant.Q4_K:
+        assert np.array_equal(msum, rmsum)
+
+
+@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K])
+@pytest.mark.parametrize("k,n,m", [(2048, 2560, 1), (5632, 2048, 1), (2048, 300, 11)])
+def test_qmatmul_matches_oracle(built, qtype, k, n, m):
+    w = _rows(qtype, n, k, seed=n + k)
+    x = _activations(m, k, 3)
+    ours = kquant.qmatmul(qtype, w, k, x)
+    theirs = ref.qmatmul(qtype, w, k, x)
+    deq = ref.dequant_rows(qtype, w, k).astype(np.float64)
+    q8 = ref.quantize_q8k(x)
+    xq = (q8["qs"].astype(np.float64) * q8["d"][..., None]).reshape(m, k)
+    mag = np.abs(xq) @ np.abs(deq).T
+    assert np.all(np.abs(ours - theirs) <= 2e-6 * mag + 1e-12)
