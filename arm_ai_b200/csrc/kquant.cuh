@@ -227,6 +227,129 @@ __device__ __forceinline__ float row_dot(int type, const uint8_t* row, int nb, c
   return type == GGML_Q4_K ? q4k_row_dot(row, nb, a, lane) : q6k_row_dot(row, nb, a, lane);
 }
 
+// ---------------------------------------------------------------------------
+// Register-resident activation slices (the matvec kernels' inner loop).
+//
+// Lane l of a warp owns quarter t = l & 3 of super-block 8p + (l >> 2) in pass
+// p: values [64t, 64t+64) of that block. Its slice of the Q8_K activation —
+// 16 words of int8, the 4 bsums of those values and the block scale d — is
+// loaded once per pass and reused for every weight row of the chunk. Both
+// weight types are mapped onto the same slice:
+//   Q4_K: qs bytes [32t, 32t+32): low nibbles = sub-block 2t (words 0..7),
+//         high nibbles = sub-block 2t+1 (words 8..15); scales sc/m of 2t, 2t+1.
+//   Q6_K: with t = 2n + h, value 64t + i (i < 64) takes ql[64n + i] nibble h
+//         and qh[32n + (i & 31)] bits 4h + 2*(i >> 5); its 16-value scale is
+//         sc[4t + i/16] — the same index as its Q8_K bsum.
+// ---------------------------------------------------------------------------
+struct ActSlice {
+  uint32_t q[16];
+  int bs[4];
+  float dy;
+};
+
+__device__ __forceinline__ void load_slice(const ActQ8& a, int blk, int t, ActSlice& s) {
+  const int4* qv = reinterpret_cast<const int4*>(a.qs + (size_t)blk * QK_K + 64 * t);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int4 v = qv[i];
+    s.q[4 * i] = (uint32_t)v.x;
+    s.q[4 * i + 1] = (uint32_t)v.y;
+    s.q[4 * i + 2] = (uint32_t)v.z;
+    s.q[4 * i + 3] = (uint32_t)v.w;
+  }
+  const int4 b = *reinterpret_cast<const int4*>(a.bs + (size_t)blk * 16 + 4 * t);
+  s.bs[0] = b.x;
+  s.bs[1] = b.y;
+  s.bs[2] = b.z;
+  s.bs[3] = b.w;
+  s.dy = a.d[blk];
+}
+
+// Integers of one Q4_K quarter: isum = sc_2t*<q,q8> + sc_2t+1*<q,q8>,
+// msum = m_2t*bs + m_2t+1*bs; also returns the block's f16 d and dmin.
+__device__ __forceinline__ void q4k_quarter(const uint8_t* blk, int t, const ActSlice& A, int& isum,
+                                            int& msum, float& dx, float& dmx) {
+  const int4 hd = *reinterpret_cast<const int4*>(blk);
+  const int4 qa = *reinterpret_cast<const int4*>(blk + 16 + 32 * t);
+  const int4 qb = *reinterpret_cast<const int4*>(blk + 32 + 32 * t);
+  const uint32_t w[8] = {(uint32_t)qa.x, (uint32_t)qa.y, (uint32_t)qa.z, (uint32_t)qa.w,
+                         (uint32_t)qb.x, (uint32_t)qb.y, (uint32_t)qb.z, (uint32_t)qb.w};
+  int dlo = 0, dhi = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    dlo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), (int)A.q[i], dlo);
+    dhi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), (int)A.q[8 + i], dhi);
+  }
+  // 12 scale bytes s[0..11] live in words hd.y (s0..3), hd.z (s4..7), hd.w (s8..11)
+  const uint32_t s03 = (uint32_t)hd.y, s47 = (uint32_t)hd.z, s811 = (uint32_t)hd.w;
+  int sa, ma, sb, mb;
+  {
+    const int j = 2 * t, j1 = 2 * t + 1;
+    auto byte = [&](int i) -> uint32_t {
+      const uint32_t wd = i < 4 ? s03 : (i < 8 ? s47 : s811);
+      return (wd >> (8 * (i & 3))) & 0xffu;
+    };
+    if (t < 2) {
+      sa = byte(j) & 63;  ma = byte(j + 4) & 63;
+      sb = byte(j1) & 63; mb = byte(j1 + 4) & 63;
+    } else {
+      sa = (byte(j + 4) & 0xF) | ((byte(j - 4) >> 6) << 4);
+      ma = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+      sb = (byte(j1 + 4) & 0xF) | ((byte(j1 - 4) >> 6) << 4);
+      mb = (byte(j1 + 4) >> 4) | ((byte(j1) >> 6) << 4);
+    }
+  }
+  isum = sa * dlo + sb * dhi;
+  msum = ma * (A.bs[0] + A.bs[1]) + mb * (A.bs[2] + A.bs[3]);
+  dx = h2f((uint16_t)((uint32_t)hd.x & 0xffffu));
+  dmx = h2f((uint16_t)((uint32_t)hd.x >> 16));
+}
+
+// Integer of one Q6_K quarter: sum_g sc[4t+g] * <q6 - 32, q8> over the four
+// 16-value groups of the slice. `body` is the block's 208-byte body.
+__device__ __forceinline__ int q6k_quarter(const uint8_t* body, int t, const ActSlice& A) {
+  const int n = t >> 1, h = t & 1;
+  const int4* qlv = reinterpret_cast<const int4*>(body + 64 * n);
+  const int4* qhv = reinterpret_cast<const int4*>(body + 128 + 32 * n);
+  const int4 l0 = qlv[0], l1 = qlv[1], l2 = qlv[2], l3 = qlv[3];
+  const int4 h0 = qhv[0], h1 = qhv[1];
+  const uint32_t lw[16] = {(uint32_t)l0.x, (uint32_t)l0.y, (uint32_t)l0.z, (uint32_t)l0.w,
+                           (uint32_t)l1.x, (uint32_t)l1.y, (uint32_t)l1.z, (uint32_t)l1.w,
+                           (uint32_t)l2.x, (uint32_t)l2.y, (uint32_t)l2.z, (uint32_t)l2.w,
+                           (uint32_t)l3.x, (uint32_t)l3.y, (uint32_t)l3.z, (uint32_t)l3.w};
+  const uint32_t hw[8] = {(uint32_t)h0.x, (uint32_t)h0.y, (uint32_t)h0.z, (uint32_t)h0.w,
+                          (uint32_t)h1.x, (uint32_t)h1.y, (uint32_t)h1.z, (uint32_t)h1.w};
+  const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(body + 192 + 4 * t);
+  int tot = 0;
+#pragma unroll
+  for (int g = 0; g < 4; g++) {
+    int dot = 0;
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) {
+      const int w = 4 * g + w4;  // word w covers values 4w..4w+3 of the slice
+      const uint32_t lo = (lw[w] >> (4 * h)) & 0x0F0F0F0Fu;
+      const uint32_t hi = (hw[w & 7] >> (4 * h + 2 * (w >> 3))) & 0x03030303u;
+      dot = __dp4a((int)(lo | (hi << 4)), (int)A.q[w], dot);
+    }
+    const int sc = (int)(int8_t)((sc4 >> (8 * g)) & 0xffu);
+    tot += sc * (dot - 32 * A.bs[g]);
+  }
+  return tot;
+}
+
+// One lane's f32 share of <weight row, activation> over pass `pass`.
+__device__ __forceinline__ float quarter_dot(int type, const uint8_t* row, int nb, int blk, int t,
+                                             const ActSlice& A) {
+  if (type == GGML_Q4_K) {
+    int is, ms;
+    float dx, dmx;
+    q4k_quarter(row + (size_t)blk * Q4K_BLOCK_BYTES, t, A, is, ms, dx, dmx);
+    return __fmul_rn(dx, A.dy) * (float)is - __fmul_rn(dmx, A.dy) * (float)ms;
+  }
+  const uint16_t dh = reinterpret_cast<const uint16_t*>(row + (size_t)nb * Q6K_BODY_BYTES)[blk];
+  return __fmul_rn(h2f(dh), A.dy) * (float)q6k_quarter(row + (size_t)blk * Q6K_BODY_BYTES, t, A);
+}
+
 // BlockQ4K::to_float for one row, by one warp: y = (d*sc)*q - (dmin*m), with
 // each product and the difference rounded separately.
 __device__ __forceinline__ void q4k_dequant_row(const uint8_t* row, int nb, float* y, int lane) {

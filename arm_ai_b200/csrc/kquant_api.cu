@@ -48,11 +48,12 @@ __global__ void k_q8k_split(const BlockQ8K* in, int64_t nblocks, int8_t* qs, flo
   if (threadIdx.x == 0) d[b] = in[b].d;
 }
 
-// Per-(token, row, super-block) integers through q4k_quarter_ints /
-// q6k_unit_ints, the code the matvec kernels run.
+// Per-(token, row, super-block) integers through load_slice + q4k_quarter /
+// q6k_quarter, the exact code of the matvec kernels' inner loop (four lanes
+// per super-block, their quarter integers summed).
 __global__ void k_block_dots(const uint8_t* w, int type, int rows, int nb, int row_bytes,
-                             const int8_t* qs, const int32_t* bs, int m, int32_t* isum,
-                             int32_t* msum) {
+                             const int8_t* qs, const float* dq, const int32_t* bs, int m,
+                             int32_t* isum, int32_t* msum) {
   const int lane = threadIdx.x & 31;
   const int64_t job = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int64_t groups = (nb + 7) / 8;
@@ -64,10 +65,18 @@ __global__ void k_block_dots(const uint8_t* w, int type, int rows, int nb, int r
   int is = 0, ms = 0;
   if (b < nb) {
     const uint8_t* row = w + (int64_t)r * row_bytes;
-    const int8_t* q8 = qs + ((int64_t)t * nb + b) * QK_K;
-    const int32_t* bsb = bs + ((int64_t)t * nb + b) * 16;
-    if (type == GGML_Q4_K) q4k_quarter_ints(row + (int64_t)b * Q4K_BLOCK_BYTES, u, q8, bsb, is, ms);
-    else is = q6k_unit_ints(row + (int64_t)b * Q6K_BODY_BYTES, u, q8, bsb);
+    ActQ8 a;
+    a.qs = const_cast<int8_t*>(qs) + (int64_t)t * nb * QK_K;
+    a.d = const_cast<float*>(dq) + (int64_t)t * nb;
+    a.bs = const_cast<int32_t*>(bs) + (int64_t)t * nb * 16;
+    ActSlice A;
+    load_slice(a, b, u, A);
+    if (type == GGML_Q4_K) {
+      float dx, dmx;
+      q4k_quarter(row + (int64_t)b * Q4K_BLOCK_BYTES, u, A, is, ms, dx, dmx);
+    } else {
+      is = q6k_quarter(row + (int64_t)b * Q6K_BODY_BYTES, u, A);
+    }
   }
   is += __shfl_xor_sync(0xffffffffu, is, 1);
   is += __shfl_xor_sync(0xffffffffu, is, 2);
@@ -142,7 +151,7 @@ extern "C" int armai_kquant_block_dots(const void* w, int type, size_t n, size_t
   ARMAI_CUDA(cudaMalloc(&dm.p, outn * 4));
   const int64_t jobs = (int64_t)m * n * ((nb + 7) / 8);
   k_block_dots<<<(unsigned)((jobs + 7) / 8), 256>>>((const uint8_t*)dw.p, type, (int)n, nb, rb,
-                                                    (const int8_t*)dqs.p, (const int32_t*)dbs.p,
+                                                    (const int8_t*)dqs.p, (const float*)dd.p, (const int32_t*)dbs.p,
                                                     (int)m, (int32_t*)di.p,
                                                     type == GGML_Q4_K ? (int32_t*)dm.p : nullptr);
   ARMAI_CUDA(cudaGetLastError());

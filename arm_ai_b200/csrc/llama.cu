@@ -19,7 +19,7 @@ using namespace armai;
 namespace {
 
 constexpr int PREFILL_TILE = 8;       // tokens per prefill matvec launch
-constexpr int ATTN_SPLITS = 16;       // split-K factor of the decode attention
+
 constexpr int ATTN_TOK_PER_LAUNCH = 64;
 constexpr uint32_t STAGE_MAX = 44 * 1024;
 constexpr size_t SMEM_LIMIT = 227 * 1024;   // hard per-CTA limit
@@ -276,15 +276,17 @@ cudaError_t launch_attn(armai_llama* m, int l, const float* q, float* y, const i
   a.hd = m->head_dim;
   a.n_head = m->n_head;
   a.n_kv = m->n_head_kv;
-  a.splits = ATTN_SPLITS;
-  a.max_chunk = (m->max_seq + ATTN_SPLITS - 1) / ATTN_SPLITS;
   a.scale = (float)(1.0 / sqrt((double)m->head_dim));
   a.part = m->attn_part;
   a.counters = m->attn_cnt;
   a.y = y;
   a.err = m->d_err;
-  return launch_k(k_attn_decode, dim3(m->n_head_kv, ATTN_SPLITS, nb_tok), dim3(128), m->attn_smem,
-                  m->stream, m->use_pdl, a);
+  const dim3 grid(m->n_head_kv, ATT_SPLITS, nb_tok), block(ATT_THREADS);
+  if (m->head_dim == 64)
+    return m->kv_f16 ? launch_k(k_attn_decode<64, __half>, grid, block, m->attn_smem, m->stream, m->use_pdl, a)
+                     : launch_k(k_attn_decode<64, float>, grid, block, m->attn_smem, m->stream, m->use_pdl, a);
+  return m->kv_f16 ? launch_k(k_attn_decode<128, __half>, grid, block, m->attn_smem, m->stream, m->use_pdl, a)
+                   : launch_k(k_attn_decode<128, float>, grid, block, m->attn_smem, m->stream, m->use_pdl, a);
 }
 
 cudaError_t launch_embed(armai_llama* m, const uint32_t* tokens, float* x, int n) {
@@ -594,9 +596,9 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     delete m;
     return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: unsupported head geometry");
   }
-  if (m->n_head / m->n_head_kv > 8 || m->head_dim > 256) {
+  if (m->n_head / m->n_head_kv > ATT_MAX_REP || (m->head_dim != 64 && m->head_dim != 128)) {
     delete m;
-    return fail(ARMAI_E_FORMAT, "unsupported attention geometry (query heads per KV head > 8 or head_dim > 256)");
+    return fail(ARMAI_E_FORMAT, "unsupported attention geometry (query heads per KV head > 8, or head_dim not 64 or 128)");
   }
 
   auto find = [&](const std::string& name) -> const GgufTensor* {
@@ -733,7 +735,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   LOAD_CUDA(cudaMemsetAsync(m->d_pos, 0, (size_t)std::max(B, 8) * 4, m->stream));
   const int nrep = m->n_head / m->n_head_kv;
   m->attn_cap_tokens = (size_t)std::max(B, ATTN_TOK_PER_LAUNCH);
-  LOAD_CUDA(cudaMalloc(&m->attn_part, m->attn_cap_tokens * m->n_head_kv * ATTN_SPLITS * nrep * (m->head_dim + 2) * 4));
+  LOAD_CUDA(cudaMalloc(&m->attn_part, m->attn_cap_tokens * m->n_head_kv * ATT_SPLITS * nrep * (m->head_dim + 2) * 4));
   LOAD_CUDA(cudaMalloc(&m->attn_cnt, m->attn_cap_tokens * m->n_head_kv * 4));
   LOAD_CUDA(cudaMemsetAsync(m->attn_cnt, 0, m->attn_cap_tokens * m->n_head_kv * 4, m->stream));
   const int nsm = sm_count();
@@ -777,11 +779,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (!arc) arc = set_smem_attr<MODE_RESID, PREFILL_TILE>(std::max(m->pl_woT.smem, m->pl_downT.smem));
   if (!arc) arc = set_smem_attr<MODE_GATEUP, PREFILL_TILE>(m->pl_guT.smem);
   if (arc) { free_model(m); return arc; }
-  const int max_chunk = (m->max_seq + ATTN_SPLITS - 1) / ATTN_SPLITS;
-  m->attn_smem = (size_t)(nrep * m->head_dim + nrep * max_chunk + 2 * nrep) * 4;
-  if (m->attn_smem > 48 * 1024)
-    LOAD_CUDA(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->attn_smem));
-  if (m->attn_smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "max_seq_len too large for the attention kernel"); }
+  m->attn_smem = attn_smem_floats(m->head_dim) * 4;
   m->n_kernels_step = 2 + 5 * m->n_layer;
   LOAD_CUDA(cudaStreamSynchronize(m->stream));
 

@@ -27,7 +27,7 @@ namespace armai {
 
 constexpr int MV_THREADS = 384;  // 12 warps; two CTAs (of consecutive kernels) fit one SM
 constexpr int MV_WARPS = MV_THREADS / 32;
-constexpr uint32_t WAIT_LIMIT = 1u << 20;
+constexpr uint32_t WAIT_LIMIT = 1u << 18;  // with 256 ns sleeps: a stuck copy ends the CTA in well under a second or two
 
 enum { MODE_QKV = 0, MODE_RESID = 1, MODE_GATEUP = 2, MODE_HEAD = 3, MODE_STORE = 4 };
 
@@ -129,9 +129,11 @@ struct MvParams {
 
 // Shared-memory layout of k_matvec (bytes), host and device agree on it.
 struct MvSmem {
-  size_t stages, act_qs, act_d, act_bs, xbuf, bars, red, total;
+  size_t stages, act_qs, act_d, act_bs, gamma, bars, red, total;
 };
 __host__ __device__ inline size_t al16(size_t v) { return (v + 15) & ~size_t(15); }
+// red: 64 floats of scratch, NB*(K/256) per-block partial sums of squares,
+// NB rms values.
 __host__ __device__ inline MvSmem mv_smem_layout(int ns, uint32_t stage_bytes, int K, int NB,
                                                  bool norm) {
   MvSmem L;
@@ -140,9 +142,9 @@ __host__ __device__ inline MvSmem mv_smem_layout(int ns, uint32_t stage_bytes, i
   L.act_qs = o;  o += al16((size_t)NB * K);
   L.act_d = o;   o += al16((size_t)NB * (K / QK_K) * 4);
   L.act_bs = o;  o += al16((size_t)NB * (K / 16) * 4);
-  L.xbuf = o;    o += norm ? al16((size_t)NB * K * 4) : 0;
-  L.bars = o;    o += al16((size_t)ns * 8);
-  L.red = o;     o += al16(64 * 4 + NB * 8);
+  L.gamma = o;   o += norm ? al16((size_t)K * 4) : 0;
+  L.bars = o;    o += al16((size_t)(ns + 1) * 8);
+  L.red = o;     o += al16((64 + (size_t)NB * (K / QK_K) + NB) * 4);
   L.total = o;
   return L;
 }
@@ -195,77 +197,66 @@ __device__ __forceinline__ void issue_chunk(const MvParams& p, int c0, int c1, u
 }
 
 // ---------------------------------------------------------------------------
-// Prologues: build the Q8_K activation(s) in shared memory.
+// Prologue: build the Q8_K activation(s) in shared memory.
+// Warp w owns 256-value jobs (b, j) = w, w + nwarps, ...: it loads its x
+// values, (norm) contributes its per-block sum of squares, and after one
+// barrier quantises them (candle rms_norm: y = x / sqrt(sum(x^2)/K + eps) *
+// gamma; then BlockQ8K::from_float). The per-block partial sums are added in
+// block order by every thread, so the result does not depend on scheduling.
+// gamma was brought into shared memory by the bulk-copy engine before the
+// kernel waited on its producer.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float block_sum(float v, float* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float t = 0.f;
-  if (warp == 0) {
-    t = lane < nw ? red[lane] : 0.f;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-    if (lane == 0) red[32] = t;
-  }
-  __syncthreads();
-  return red[32];
-}
-
-// Q8_K of NB rows of `src` (global), optionally rmsnorm'ed first (candle
-// rms_norm: y = x / sqrt(sum(x^2)/K + eps) * gamma, then Q8_K).
 template <int NB>
-__device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, ActQ8 (&act)[NB]) {
+__device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, ActQ8 (&act)[NB],
+                          uint64_t* gamma_bar) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const int K = p.K, nb = p.nb;
   float* red = reinterpret_cast<float*>(smem + L.red);
-  float* rms = red + 64;
+  float* part = red + 64;              // [NB][nb]
+  float* rms = part + NB * nb;         // [NB]
   for (int b = 0; b < NB; b++) {
     act[b].qs = reinterpret_cast<int8_t*>(smem + L.act_qs) + (size_t)b * K;
     act[b].d = reinterpret_cast<float*>(smem + L.act_d) + (size_t)b * nb;
     act[b].bs = reinterpret_cast<int32_t*>(smem + L.act_bs) + (size_t)b * (K / 16);
   }
   const float* src = p.x;
-  if (p.gamma) {
-    float* xs = reinterpret_cast<float*>(smem + L.xbuf);
-    for (int b = 0; b < NB; b++) {
-      float ss = 0.f;
-      for (int i = tid * 4; i < K; i += blockDim.x * 4) {
-        const float4 v = *reinterpret_cast<const float4*>(src + (size_t)b * K + i);
-        *reinterpret_cast<float4*>(xs + (size_t)b * K + i) = v;
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      }
-      const float sum2 = block_sum(ss, red);
-      if (tid == 0) rms[b] = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)K), p.eps));
-    }
-    __syncthreads();
+  const bool norm = p.gamma != nullptr;
+  if (norm) {
     for (int job = warp; job < NB * nb; job += nw) {
       const int b = job / nb, j = job % nb;
+      const float4* xr = reinterpret_cast<const float4*>(src + (size_t)b * K + j * QK_K + 8 * lane);
+      const float4 x0 = xr[0], x1 = xr[1];
+      float ss = x0.x * x0.x + x0.y * x0.y + x0.z * x0.z + x0.w * x0.w +
+                 x1.x * x1.x + x1.y * x1.y + x1.z * x1.z + x1.w * x1.w;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) part[b * nb + j] = ss;
+    }
+    __syncthreads();
+    if (tid < NB) {
+      float sum2 = 0.f;
+      for (int j = 0; j < nb; j++) sum2 += part[tid * nb + j];
+      rms[tid] = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)K), p.eps));
+    }
+    // gamma must have landed before anyone reads it
+    if (!mbar_wait(gamma_bar, 0, p.err)) { /* error flagged; values unused */ }
+    __syncthreads();
+  }
+  const float* gs = reinterpret_cast<const float*>(smem + L.gamma);
+  for (int job = warp; job < NB * nb; job += nw) {
+    const int b = job / nb, j = job % nb;
+    const float4* xr = reinterpret_cast<const float4*>(src + (size_t)b * K + j * QK_K + 8 * lane);
+    const float4 x0 = xr[0], x1 = xr[1];
+    float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    if (norm) {
       const float m = rms[b];
-      const float* xr = xs + (size_t)b * K + j * QK_K + 8 * lane;
-      const float* gr = p.gamma + j * QK_K + 8 * lane;
-      const float4 x0 = *reinterpret_cast<const float4*>(xr);
-      const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
-      const float4 g0 = *reinterpret_cast<const float4*>(gr);
-      const float4 g1 = *reinterpret_cast<const float4*>(gr + 4);
-      float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+      const float4* gr = reinterpret_cast<const float4*>(gs + j * QK_K + 8 * lane);
+      const float4 g0 = gr[0], g1 = gr[1];
       const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), g[i]);
-      q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16);
     }
-  } else {
-    for (int job = warp; job < NB * nb; job += nw) {
-      const int b = job / nb, j = job % nb;
-      const float* xr = src + (size_t)b * K + j * QK_K + 8 * lane;
-      const float4 x0 = *reinterpret_cast<const float4*>(xr);
-      const float4 x1 = *reinterpret_cast<const float4*>(xr + 4);
-      float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16);
-    }
+    q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16);
   }
   __syncthreads();
 }
@@ -300,12 +291,16 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
   uint8_t* stages = smem + L.stages;
 
   if (tid == 0) {
-    for (int s = 0; s < p.ns; s++) mbar_init(&bars[s], 1);
+    for (int s = 0; s <= p.ns; s++) mbar_init(&bars[s], 1);  // ns stages + gamma
     fence_mbar_init();
   }
   __syncthreads();
   if (tid == 0) {
     const uint64_t pol = l2_evict_first_policy();
+    if (p.gamma) {
+      mbar_expect_tx(&bars[p.ns], (uint32_t)p.K * 4u);
+      bulk_g2s(smem + L.gamma, p.gamma, (uint32_t)p.K * 4u, &bars[p.ns], pol);
+    }
     for (int c = 0; c < min(p.ns, nchunks); c++) {
       const int c0 = r0 + c * p.chunk_rows, c1 = min(c0 + p.chunk_rows, r1);
       issue_chunk<MODE>(p, c0, c1, stages + (size_t)c * p.stage_bytes, &bars[c], pol);
@@ -317,13 +312,15 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
   pdl_wait();
 
   ActQ8 act[NB];
-  build_act<NB>(p, smem, L, act);
+  build_act<NB>(p, smem, L, act, &bars[p.ns]);
 
   float best_v[NB];
   int best_i[NB];
 #pragma unroll
   for (int b = 0; b < NB; b++) { best_v[b] = -INFINITY; best_i[b] = 0x7fffffff; }
 
+  const int t = lane & 3, bl = lane >> 2;
+  const int npass = (p.nb + 7) >> 3;
   for (int c = 0; c < nchunks; c++) {
     const int s = c % p.ns;
     const int c0 = r0 + c * p.chunk_rows, c1 = min(c0 + p.chunk_rows, r1);
@@ -332,37 +329,90 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
     Part parts[3];
     const int np = chunk_parts<MODE>(p, c0, c1, parts);
-    (void)np;
-    if (MODE == MODE_QKV) {
-      const int npairs = (c1 - c0) >> 1;
-      for (int pr = warp; pr < npairs; pr += MV_WARPS) {
-        const int r = c0 + 2 * pr;
-        // segment of virtual row r and its first virtual row
-        const int si = r < p.qn ? 0 : (r < p.qn + p.kn ? 1 : 2);
-        const int sb = si == 0 ? 0 : (si == 1 ? p.qn : p.qn + p.kn);
-        int pi = 0;
-        for (int i = 0; i < np; i++)
-          if (parts[i].seg == si) pi = i;
-        const Seg& sg = p.seg[parts[pi].seg];
-        const uint8_t* row = stage + parts[pi].off + (size_t)(r - sb - parts[pi].lo) * sg.row_bytes;
+    // A unit is what one warp reduces at a time: a row pair (QKV, RoPE
+    // needs both), a gate/up row pair (GATEUP) or a single row.
+    const int nunits = MODE == MODE_QKV ? (c1 - c0) >> 1 : (c1 - c0);
+    for (int b = 0; b < NB; b++) {
+      for (int u0 = warp; u0 < nunits; u0 += 2 * MV_WARPS) {
+        const uint8_t* rp[4];
+        int ty[4];
+        bool va[4];
+        int ur[2];    // first (virtual) row of each unit
+        int useg[2];  // segment of each QKV unit
 #pragma unroll
-        for (int b = 0; b < NB; b++) {
-          const float d0 = row_dot(sg.type, row, sg.nb, act[b], lane);
-          const float d1 = row_dot(sg.type, row + sg.row_bytes, sg.nb, act[b], lane);
-          if (lane == 0) {
+        for (int k = 0; k < 2; k++) {
+          const int u = u0 + k * MV_WARPS;
+          const bool uv = u < nunits;
+          va[2 * k] = uv;
+          va[2 * k + 1] = uv && (MODE == MODE_QKV || MODE == MODE_GATEUP);
+          rp[2 * k] = rp[2 * k + 1] = stage;
+          ty[2 * k] = ty[2 * k + 1] = GGML_Q4_K;
+          ur[k] = 0;
+          useg[k] = 0;
+          if (!uv) continue;
+          if (MODE == MODE_QKV) {
+            const int r = c0 + 2 * u;
+            const int si = r < p.qn ? 0 : (r < p.qn + p.kn ? 1 : 2);
+            const int sb = si == 0 ? 0 : (si == 1 ? p.qn : p.qn + p.kn);
+            int pi = 0;
+            for (int i = 0; i < np; i++)
+              if (parts[i].seg == si) pi = i;
+            const Seg& sg = p.seg[si];
+            rp[2 * k] = stage + parts[pi].off + (size_t)(r - sb - parts[pi].lo) * sg.row_bytes;
+            rp[2 * k + 1] = rp[2 * k] + sg.row_bytes;
+            ty[2 * k] = ty[2 * k + 1] = sg.type;
+            ur[k] = r;
+            useg[k] = si;
+          } else if (MODE == MODE_GATEUP) {
+            const int r = c0 + u;
+            rp[2 * k] = stage + (size_t)(r - c0) * p.seg[0].row_bytes;
+            rp[2 * k + 1] = stage + parts[1].off + (size_t)(r - c0) * p.seg[1].row_bytes;
+            ty[2 * k] = p.seg[0].type;
+            ty[2 * k + 1] = p.seg[1].type;
+            ur[k] = r;
+          } else {
+            const int r = c0 + u;
+            rp[2 * k] = stage + (size_t)(r - c0) * p.seg[0].row_bytes;
+            ty[2 * k] = p.seg[0].type;
+            ur[k] = r;
+          }
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int ps = 0; ps < npass; ps++) {
+          const int blk = ps * 8 + bl;
+          if (blk < p.nb) {
+            ActSlice A;
+            load_slice(act[b], blk, t, A);
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+              if (va[k]) acc[k] += quarter_dot(ty[k], rp[k], p.nb, blk, t, A);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          if (!va[k]) continue;  // warp-uniform
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+        }
+        if (lane != 0) continue;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+          if (!va[2 * k]) continue;
+          const float d0 = acc[2 * k], d1 = acc[2 * k + 1];
+          const int r = ur[k];
+          if (MODE == MODE_QKV) {
             const int pos = p.pos[b];
             const int half = p.hd >> 1;
-            if (r < p.qn + p.kn) {
-              const int rr = r < p.qn ? r : r - p.qn;
+            if (useg[k] < 2) {
+              const int rr = useg[k] == 0 ? r : r - p.qn;
               const int i2 = (rr % p.hd) >> 1;
               const float cs = p.cos_t[(size_t)pos * half + i2];
               const float sn = p.sin_t[(size_t)pos * half + i2];
               // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
               const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
               const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
-              if (r < p.qn) {
-                p.out[(size_t)b * p.out_stride + r] = o0;
-                p.out[(size_t)b * p.out_stride + r + 1] = o1;
+              if (useg[k] == 0) {
+                *reinterpret_cast<float2*>(p.out + (size_t)b * p.out_stride + r) = make_float2(o0, o1);
               } else {
                 const int kvh = rr / p.hd, dd = rr % p.hd;
                 const int64_t idx = (int64_t)b * p.kv_seq_stride + ((int64_t)kvh * p.max_seq + pos) * p.hd + dd;
@@ -374,39 +424,16 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
               const int64_t idx = (int64_t)b * p.kv_seq_stride + ((int64_t)kvh * p.max_seq + pos) * p.hd + dd;
               store_kv(p.vc, p.kv_f16, idx, d0, d1);
             }
-          }
-        }
-      }
-    } else if (MODE == MODE_GATEUP) {
-      const Seg& sg = p.seg[0];
-      const Seg& su = p.seg[1];
-      for (int r = c0 + warp; r < c1; r += MV_WARPS) {
-        const uint8_t* rg = stage + (size_t)(r - c0) * sg.row_bytes;
-        const uint8_t* ru = stage + parts[1].off + (size_t)(r - c0) * su.row_bytes;
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-          const float g = row_dot(sg.type, rg, sg.nb, act[b], lane);
-          const float u = row_dot(su.type, ru, su.nb, act[b], lane);
-          if (lane == 0) {
+          } else if (MODE == MODE_GATEUP) {
             // candle: silu(v) = v / (1 + exp(-v)); then * up
-            const float sl = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-            p.out[(size_t)b * p.out_stride + r] = __fmul_rn(sl, u);
-          }
-        }
-      }
-    } else {
-      const Seg& sg = p.seg[0];
-      for (int r = c0 + warp; r < c1; r += MV_WARPS) {
-        const uint8_t* row = stage + (size_t)(r - c0) * sg.row_bytes;
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-          const float v = row_dot(sg.type, row, sg.nb, act[b], lane);
-          if (lane == 0) {
+            const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
+            p.out[(size_t)b * p.out_stride + r] = __fmul_rn(sl, d1);
+          } else {
             float* o = p.out + (size_t)b * p.out_stride + r;
-            if (MODE == MODE_RESID) *o = __fadd_rn(v, *o);
-            else *o = v;
-            if (MODE == MODE_HEAD && am_better(v, r, best_v[b], best_i[b])) {
-              best_v[b] = v;
+            if (MODE == MODE_RESID) *o = __fadd_rn(d0, *o);
+            else *o = d0;
+            if (MODE == MODE_HEAD && am_better(d0, r, best_v[b], best_i[b])) {
+              best_v[b] = d0;
               best_i[b] = r;
             }
           }
@@ -487,7 +514,7 @@ struct AttnParams {
   int64_t kv_seq_stride;
   int kv_f16;
   const int* pos;      // [NB]
-  int max_seq, hd, n_head, n_kv, splits, max_chunk;
+  int max_seq, hd, n_head, n_kv;
   float scale;
   float* part;         // [NB][n_kv][splits][nrep][hd+2]
   unsigned* counters;  // [NB][n_kv]
@@ -495,107 +522,184 @@ struct AttnParams {
   uint32_t* err;
 };
 
-__device__ __forceinline__ float kv_load(const void* base, int kv_f16, int64_t idx) {
-  return kv_f16 ? __half2float(reinterpret_cast<const __half*>(base)[idx])
-                : reinterpret_cast<const float*>(base)[idx];
+constexpr int ATT_TILE = 32;     // positions per shared-memory tile
+constexpr int ATT_THREADS = 128;
+constexpr int ATT_MAX_REP = 8;   // query heads per KV head
+constexpr int ATT_SPLITS = 16;   // split-K factor (fixed: the combine is unrolled over it)
+
+// Shared memory of k_attn_decode<HD> (floats): q[rep][HD], K[TILE][HD+1],
+// V[TILE][HD], p[rep][TILE], corr/m/l[rep], combine weights[SPLITS][rep].
+__host__ __device__ inline size_t attn_smem_floats(int hd) {
+  return (size_t)ATT_MAX_REP * hd + (size_t)ATT_TILE * (hd + 1) + (size_t)ATT_TILE * hd +
+         (size_t)ATT_MAX_REP * ATT_TILE + 3 * ATT_MAX_REP + (size_t)ATT_SPLITS * ATT_MAX_REP + ATT_MAX_REP;
 }
 
-static __global__ void __launch_bounds__(128) k_attn_decode(const AttnParams p) {
+template <int HD, typename KV>
+__device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, float* Vs, const KV* vbase) {
+  // n rows of HD values; K rows padded to HD+1 floats (conflict-free column reads)
+  constexpr int V4 = HD / 4;
+  for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
+    const int t = i / V4, c = (i % V4) * 4;
+    float4 kv, vv;
+    if constexpr (sizeof(KV) == 4) {
+      kv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + (size_t)t * HD + c);
+      vv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vbase) + (size_t)t * HD + c);
+    } else {
+      const uint2 kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + (size_t)t * HD + c);
+      const uint2 vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(vbase) + (size_t)t * HD + c);
+      const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
+      const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
+      const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
+      const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
+      kv = make_float4(k0.x, k0.y, k1.x, k1.y);
+      vv = make_float4(v0.x, v0.y, v1.x, v1.y);
+    }
+    float* kd = Ks + t * (HD + 1) + c;
+    kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+    *reinterpret_cast<float4*>(Vs + t * HD + c) = vv;
+  }
+}
+
+// Split-K GQA flash-decode. grid (n_kv, ATT_SPLITS, NB), ATT_THREADS threads.
+// CTA (kvh, s, b) covers positions [t0, t1) of sequence b for the nrep query
+// heads sharing KV head kvh (repeat_kv: kvh = h / nrep), in tiles of 32:
+// scores s = (q . k) * scale with a lane per position, an online softmax per
+// head, o += p v with a thread per output dim. The last CTA of (b, kvh)
+// merges the splits in split order: y = sum_s o_s e^{m_s-M} / sum_s l_s e^{m_s-M}.
+// For prefill the batch index runs over the prompt's tokens with a shared
+// cache (kv_seq_stride 0): token b attends positions 0..pos[b] (causal).
+template <int HD, typename KV>
+__global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p) {
   extern __shared__ __align__(16) float sm[];
   const int kvh = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nrep = p.n_head / p.n_kv, hd = p.hd;
-  float* qs = sm;                        // [nrep][hd]
-  float* sc = qs + nrep * hd;            // [nrep][max_chunk]
-  float* ml = sc + nrep * p.max_chunk;   // [nrep][2]
+  const int nrep = p.n_head / p.n_kv;
+  float* qs = sm;                                   // [ATT_MAX_REP][HD]
+  float* Ks = qs + ATT_MAX_REP * HD;                // [TILE][HD+1]
+  float* Vs = Ks + ATT_TILE * (HD + 1);             // [TILE][HD]
+  float* ps = Vs + ATT_TILE * HD;                   // [ATT_MAX_REP][TILE]
+  float* corr = ps + ATT_MAX_REP * ATT_TILE;        // [rep]
+  float* mrow = corr + ATT_MAX_REP;                 // [rep]
+  float* lrow = mrow + ATT_MAX_REP;                 // [rep]
+  float* wts = lrow + ATT_MAX_REP;                  // [SPLITS][rep]
+  float* Ltot = wts + ATT_SPLITS * ATT_MAX_REP;     // [rep]
   __shared__ int s_last;
   pdl_launch();
   pdl_wait();
   const int T = p.pos[b] + 1;
-  const int chunk = (T + p.splits - 1) / p.splits;
-  const int t0 = min(T, s * chunk), t1 = min(T, t0 + chunk), n = t1 - t0;
-  const float* qb = p.q + (size_t)b * p.n_head * hd + (size_t)kvh * nrep * hd;
-  for (int i = tid; i < nrep * hd; i += blockDim.x) qs[i] = qb[i];
-  __syncthreads();
-  const int64_t kvbase = (int64_t)b * p.kv_seq_stride + (int64_t)kvh * p.max_seq * hd;
-  // scores: one position per thread
-  for (int t = tid; t < n; t += blockDim.x) {
-    float acc[8];
+  const int chunk = (T + ATT_SPLITS - 1) / ATT_SPLITS;
+  const int t0 = min(T, s * chunk), t1 = min(T, t0 + chunk);
+  const float* qb = p.q + (size_t)b * p.n_head * HD + (size_t)kvh * nrep * HD;
+  for (int i = tid; i < nrep * HD / 4; i += blockDim.x)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(qb)[i];
+  if (tid < ATT_MAX_REP) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
+  const int64_t kvbase = (int64_t)b * p.kv_seq_stride + (int64_t)kvh * p.max_seq * HD;
+  const KV* kc = reinterpret_cast<const KV*>(p.kc) + kvbase;
+  const KV* vc = reinterpret_cast<const KV*>(p.vc) + kvbase;
+  // PV ownership: thread -> (dim d, group of heads)
+  constexpr int DGROUPS = ATT_THREADS / HD;          // 2 for HD=64, 1 for HD=128
+  constexpr int RPG = ATT_MAX_REP / DGROUPS;         // heads per thread
+  const int d = tid % HD, rg = tid / HD;
+  float o[RPG];
 #pragma unroll
-    for (int r = 0; r < 8; r++) acc[r] = 0.f;
-    const int64_t kb = kvbase + (int64_t)(t0 + t) * hd;
-    for (int d = 0; d < hd; d++) {
-      const float kv = kv_load(p.kc, p.kv_f16, kb + d);
+  for (int i = 0; i < RPG; i++) o[i] = 0.f;
+  for (int tt0 = t0; tt0 < t1; tt0 += ATT_TILE) {
+    const int n = min(ATT_TILE, t1 - tt0);
+    __syncthreads();  // previous tile fully consumed (and q / m / l initialised)
+    load_kv_tile<HD, KV>(kc + (size_t)tt0 * HD, n, Ks, Vs, vc + (size_t)tt0 * HD);
+    __syncthreads();
+    for (int r = warp; r < nrep; r += ATT_THREADS / 32) {
+      float sc = -INFINITY;
+      if (lane < n) {
+        float acc = 0.f;
+#pragma unroll 16
+        for (int dd = 0; dd < HD; dd++) acc += qs[r * HD + dd] * Ks[lane * (HD + 1) + dd];
+        sc = acc * p.scale;
+      }
+      float mt = sc;
 #pragma unroll
-      for (int r = 0; r < 8; r++)
-        if (r < nrep) acc[r] += qs[r * hd + d] * kv;
+      for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mold = mrow[r];
+      const float mnew = fmaxf(mold, mt);
+      const float pe = lane < n ? expf(sc - mnew) : 0.f;
+      float ls = pe;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      ps[r * ATT_TILE + lane] = pe;
+      __syncwarp();
+      if (lane == 0) {
+        const float c = expf(mold - mnew);  // 0 on the first tile (mold = -inf)
+        corr[r] = c;
+        lrow[r] = lrow[r] * c + ls;
+        mrow[r] = mnew;
+      }
     }
-    for (int r = 0; r < nrep; r++) sc[r * p.max_chunk + t] = acc[r] * p.scale;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < RPG; i++) {
+      const int r = rg * RPG + i;
+      if (r < nrep) {
+        float acc = o[i] * corr[r];
+        for (int tt = 0; tt < n; tt++) acc += ps[r * ATT_TILE + tt] * Vs[tt * HD + d];
+        o[i] = acc;
+      }
+    }
   }
   __syncthreads();
-  // per-head max / exp / sum over this split
-  for (int r = warp; r < nrep; r += 4) {
-    float m = -INFINITY;
-    for (int t = lane; t < n; t += 32) m = fmaxf(m, sc[r * p.max_chunk + t]);
+  // partial of this split: o[rep][HD], m[rep], l[rep]
+  const size_t pbase = ((((size_t)b * p.n_kv + kvh) * ATT_SPLITS + s) * nrep) * (HD + 2);
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float l = 0.f;
-    for (int t = lane; t < n; t += 32) {
-      const float e = n > 0 ? expf(sc[r * p.max_chunk + t] - m) : 0.f;
-      sc[r * p.max_chunk + t] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    if (lane == 0) { ml[2 * r] = m; ml[2 * r + 1] = l; }
-  }
-  __syncthreads();
-  // o[r][d] = sum_t p[r][t] * v[t][d]
-  const size_t pbase = ((((size_t)b * p.n_kv + kvh) * p.splits + s) * nrep) * (hd + 2);
-  for (int d = tid; d < hd; d += blockDim.x) {
-    float o[8];
-#pragma unroll
-    for (int r = 0; r < 8; r++) o[r] = 0.f;
-    for (int t = 0; t < n; t++) {
-      const float v = kv_load(p.vc, p.kv_f16, kvbase + (int64_t)(t0 + t) * hd + d);
-#pragma unroll
-      for (int r = 0; r < 8; r++)
-        if (r < nrep) o[r] += sc[r * p.max_chunk + t] * v;
-    }
-    for (int r = 0; r < nrep; r++) p.part[pbase + (size_t)r * (hd + 2) + d] = o[r];
+  for (int i = 0; i < RPG; i++) {
+    const int r = rg * RPG + i;
+    if (r < nrep) p.part[pbase + (size_t)r * (HD + 2) + d] = o[i];
   }
   if (tid < nrep) {
-    p.part[pbase + (size_t)tid * (hd + 2) + hd] = ml[2 * tid];
-    p.part[pbase + (size_t)tid * (hd + 2) + hd + 1] = ml[2 * tid + 1];
+    p.part[pbase + (size_t)tid * (HD + 2) + HD] = mrow[tid];
+    p.part[pbase + (size_t)tid * (HD + 2) + HD + 1] = lrow[tid];
   }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const unsigned prev = atomicAdd(&p.counters[b * p.n_kv + kvh], 1u);
-    s_last = (prev == (unsigned)p.splits - 1);
+    s_last = (prev == (unsigned)ATT_SPLITS - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const size_t base0 = (((size_t)b * p.n_kv + kvh) * p.splits) * nrep * (hd + 2);
-  for (int i = tid; i < nrep * hd; i += blockDim.x) {
-    const int r = i / hd, d = i % hd;
+  const size_t base0 = (((size_t)b * p.n_kv + kvh) * ATT_SPLITS) * nrep * (HD + 2);
+  // 1) (m, l) of every (split, head) -> smem; per-head max and weights
+  if (tid < ATT_SPLITS * nrep) {
+    const int s2 = tid / nrep, r = tid % nrep;
+    const size_t o2 = base0 + ((size_t)s2 * nrep + r) * (HD + 2);
+    wts[s2 * ATT_MAX_REP + r] = __ldcg(p.part + o2 + HD);        // m
+    ps[s2 * ATT_MAX_REP + r] = __ldcg(p.part + o2 + HD + 1);     // l (ps reused)
+  }
+  __syncthreads();
+  if (tid < nrep) {
     float M = -INFINITY;
-    for (int s2 = 0; s2 < p.splits; s2++) {
-      const size_t o = base0 + ((size_t)s2 * nrep + r) * (hd + 2);
-      if (__ldcg(p.part + o + hd + 1) > 0.f) M = fmaxf(M, __ldcg(p.part + o + hd));
+    for (int s2 = 0; s2 < ATT_SPLITS; s2++)
+      if (ps[s2 * ATT_MAX_REP + tid] > 0.f) M = fmaxf(M, wts[s2 * ATT_MAX_REP + tid]);
+    float Ls = 0.f;
+    for (int s2 = 0; s2 < ATT_SPLITS; s2++) {
+      const float l = ps[s2 * ATT_MAX_REP + tid];
+      const float w = l > 0.f ? expf(wts[s2 * ATT_MAX_REP + tid] - M) : 0.f;
+      wts[s2 * ATT_MAX_REP + tid] = w;
+      Ls += l * w;
     }
-    float Lsum = 0.f, O = 0.f;
-    for (int s2 = 0; s2 < p.splits; s2++) {
-      const size_t o = base0 + ((size_t)s2 * nrep + r) * (hd + 2);
-      const float l = __ldcg(p.part + o + hd + 1);
-      if (l > 0.f) {
-        const float w = expf(__ldcg(p.part + o + hd) - M);
-        Lsum += l * w;
-        O += __ldcg(p.part + o + d) * w;
-      }
-    }
-    p.y[(size_t)b * p.n_head * hd + ((size_t)kvh * nrep + r) * hd + d] = O / Lsum;
+    Ltot[tid] = Ls;
+  }
+  __syncthreads();
+  // 2) y[r][d] = sum_s w_s o_s[r][d] / L
+  for (int i = tid; i < nrep * HD; i += blockDim.x) {
+    const int r = i / HD, dd = i % HD;
+    float ov[ATT_SPLITS];
+#pragma unroll
+    for (int s2 = 0; s2 < ATT_SPLITS; s2++)
+      ov[s2] = __ldcg(p.part + base0 + ((size_t)s2 * nrep + r) * (HD + 2) + dd);
+    float O = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < ATT_SPLITS; s2++) O += wts[s2 * ATT_MAX_REP + r] * ov[s2];
+    p.y[(size_t)b * p.n_head * HD + ((size_t)kvh * nrep + r) * HD + dd] = O / Ltot[r];
   }
   if (tid == 0) p.counters[b * p.n_kv + kvh] = 0u;
 }

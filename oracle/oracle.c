@@ -388,7 +388,31 @@ struct orc_llama {
   float *cos_t, *sin_t; /* [max_seq][rope_dim/2] */
   float *kc, *vc;       /* [L][n_head_kv][max_seq][head_dim] */
   int kv_len;
+  int kv_f16;
 };
+
+/* f32 -> binary16 (round to nearest even) -> f32. */
+static float round_f16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7fffffffu;
+  uint16_t h;
+  if (ax >= 0x7f800000u) h = (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0));
+  else if (ax >= 0x477ff000u) h = (uint16_t)(sign | 0x7c00u);
+  else if (ax < 0x38800000u) {
+    float a;
+    memcpy(&a, &ax, 4);
+    h = (uint16_t)(sign | (uint32_t)nearbyintf(a * 16777216.0f));
+  } else {
+    uint32_t hh = (((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13);
+    uint32_t rem = ax & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (hh & 1u))) hh++;
+    h = (uint16_t)(sign | hh);
+  }
+  return orc_f16_to_f32(h);
+}
+
+void orc_llama_set_kv_f16(orc_llama* m, int on) { m->kv_f16 = on ? 1 : 0; }
 
 orc_llama* orc_llama_new(int n_layer, int n_embd, int n_head, int n_head_kv, int rope_dim,
                          int n_vocab, int n_ff, float eps, float rope_base, int max_seq) {
@@ -547,6 +571,11 @@ int orc_llama_forward(orc_llama* m, const uint32_t* tokens, int S, int index_pos
         size_t o = lbase + ((size_t)h * m->max_seq + (m->kv_len + s)) * D;
         memcpy(m->kc + o, kk + (size_t)s * KN + h * D, sizeof(float) * D);
         memcpy(m->vc + o, vv + (size_t)s * KN + h * D, sizeof(float) * D);
+        if (m->kv_f16)
+          for (int d = 0; d < D; d++) {
+            m->kc[o + d] = round_f16(m->kc[o + d]);
+            m->vc[o + d] = round_f16(m->vc[o + d]);
+          }
       }
     const int nrep = H / HKV;
 #pragma omp parallel for collapse(2) schedule(static)

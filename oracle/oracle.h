@@ -86,6 +86,10 @@ orc_llama* orc_llama_new(int n_layer, int n_embd, int n_head, int n_head_kv, int
 int orc_llama_set_tensor(orc_llama* m, const char* role, int layer, const void* data,
                          int ggml_type, int64_t rows, int64_t cols);
 int orc_llama_finalize(orc_llama* m);
+/* Store K/V cache entries rounded to IEEE binary16 (round to nearest even)
+ * and read them back as f32: the f16 KV cache of BASELINE config 3. candle's
+ * quantized_llama keeps an f32 cache; this mode is off by default. */
+void orc_llama_set_kv_f16(orc_llama* m, int on);
 void orc_llama_free(orc_llama* m);
 /* ModelWeights::forward(tokens[1,n], index_pos) -> logits of last position. */
 int orc_llama_forward(orc_llama* m, const uint32_t* tokens, int n, int index_pos,

@@ -43,6 +43,7 @@ def lib() -> ctypes.CDLL:
             "orc_llama_new": (V, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_int]),
             "orc_llama_set_tensor": (c_int, [V, c_char_p, c_int, V, c_int, I64, I64]),
             "orc_llama_finalize": (c_int, [V]),
+            "orc_llama_set_kv_f16": (None, [V, c_int]),
             "orc_llama_free": (None, [V]),
             "orc_llama_forward": (c_int, [V, V, c_int, c_int, V]),
             "orc_llama_generate": (c_int, [V, V, c_int, c_int, V, c_int, V, POINTER(c_int),
@@ -136,7 +137,7 @@ def qmatmul(wtype: int, w_rows: np.ndarray, k: int, x: np.ndarray) -> np.ndarray
 class OracleLlama:
     """candle quantized_llama ModelWeights restated in C, weights from gguf-py."""
 
-    def __init__(self, path: str, max_seq: int = 4096):
+    def __init__(self, path: str, max_seq: int = 4096, kv_f16: bool = False):
         import gguf
         self.reader = gguf.GGUFReader(path)
         f = self.reader.fields
@@ -182,6 +183,7 @@ class OracleLlama:
                          "ffn_gate", "ffn_up", "ffn_down"):
                 put(role, l, f"blk.{l}.{role}.weight")
         check(L.orc_llama_finalize(self.h))
+        L.orc_llama_set_kv_f16(self.h, int(kv_f16))
 
     def forward(self, tokens, index_pos: int) -> np.ndarray:
         t = np.asarray(tokens, dtype=np.uint32)

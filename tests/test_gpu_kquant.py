@@ -31,8 +31,8 @@ def _activations(m, k, seed):
     x = rng.standard_normal((m, k)).astype(np.float32)
     x[0, :256] = 0.0                                   # all-zero block
     if m > 1:
-        x[1, 256:512] = np.float32(0.75)               # every value ties on |x|
-        x[1, 300] = np.float32(-0.75)
+        x[1, :256] = np.float32(0.75)                  # every value ties on |x|
+        x[1, 44] = np.float32(-0.75)
     if m > 2:
         # max |x| = 2 -> iscale = 64; 64 * (i + 0.5)/64 = i + 0.5 exactly, so
         # every value sits on a rounding tie (half away from zero).
