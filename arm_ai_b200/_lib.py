@@ -24,7 +24,7 @@ class LlamaOpts(Structure):
     _fields_ = [("device", c_int32), ("max_seq_len", c_int32), ("kv_f16", c_int32),
                 ("max_batch", c_int32), ("use_graph", c_int32), ("use_pdl", c_int32),
                 ("tp_size", c_int32), ("tp_rank", c_int32), ("tp_unique_id", c_void_p),
-                ("reserved", c_int32 * 8)]
+                ("decode_kernel", c_int32), ("reserved", c_int32 * 7)]
 
 
 class LlamaInfo(Structure):
@@ -52,6 +52,7 @@ _SIGS = {
                                     POINTER(c_uint32)]),
     "armai_llama_bench_decode": (c_int, [c_void_p, c_int32, POINTER(c_float)]),
     "armai_llama_bench_kernel": (c_int, [c_void_p, c_int32, c_int32, POINTER(c_float), POINTER(c_int64)]),
+    "armai_llama_trace_decode": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_int32), POINTER(c_int32)]),
     "armai_int8_matmul_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p, c_size_t,
                                       c_double, c_size_t, c_size_t, c_size_t, c_void_p]),
     "armai_int8_matmul_f32_per_token": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p,

@@ -1,0 +1,743 @@
+// decode_mega.cuh — persistent single-launch decode step (sm_100a).
+//
+// One CTA per SM runs the whole decode step of one sequence:
+//   for each layer: QKV (+RoPE, KV append) | attention | attn_output (+residual)
+//                   | gate/up (+SiLU*up) | ffn_down (+residual)
+//   then output_norm + output head + greedy argmax.
+// Phases are separated by grid barriers (a monotonic counter in global
+// memory, release/acquire). Warp 0 is a producer: one lane walks the same
+// phase/chunk sequence as the consumers and streams every weight row this CTA
+// owns HBM -> shared memory with cp.async.bulk into a ring of stages
+// (full/empty mbarriers). It runs ahead across phase boundaries, so weight
+// traffic continues while the consumers wait at a barrier or run attention.
+// The other 15 warps are consumers: they build the Q8_K activation of the
+// phase (rmsnorm + quantisation), run the register-slice dot products on
+// the staged rows, and apply the epilogue.
+//
+// Every wait is bounded and checks the device error word, so a stuck copy or
+// a CTA that left early ends the launch with an error instead of a hang.
+// Data written by other CTAs within the launch is read with L1-bypassing
+// loads (ld.global.cg).
+#pragma once
+
+#include "llama_kernels.cuh"
+
+namespace armai {
+
+#ifndef ARMAI_MK_CW
+#define ARMAI_MK_CW 15
+#endif
+constexpr int MK_CW = ARMAI_MK_CW;             // consumer warps
+constexpr int MK_THREADS = 32 * (1 + MK_CW);
+constexpr int MK_CT = 32 * MK_CW;             // consumer threads
+constexpr uint32_t MK_STAGE = 32 * 1024;
+constexpr int MK_MAX_NS = 6;
+constexpr uint32_t MK_BAR_LIMIT = 1u << 24;   // grid-barrier polls before giving up
+constexpr int MK_MAX_RES = 64;                // residual rows per CTA kept in shared memory
+constexpr int MK_REGJ = 2;                    // prologue blocks per warp kept in registers
+
+enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_GATEUP = 3, PH_DOWN = 4, PH_HEAD = 5 };
+
+struct MkPhase {
+  int kind, layer;
+  Seg seg[3];
+  int nseg;
+  int total_rows;     // QKV: q+k+v rows; GATEUP: rows of each matrix; else rows
+  int rows_per_cta;   // multiple of 2 for QKV
+  int chunk_rows;     // multiple of 2 for QKV
+  int K, nb;
+  const float* gamma; // rmsnorm weight, or nullptr
+  const float* in;    // activation input; nullptr on layer 0's QKV (token embedding)
+  float* out;         // q (QKV), x (WO, DOWN), h (GATEUP), logits (HEAD)
+  void* kc;           // layer KV cache
+  void* vc;
+};
+
+struct MkParams {
+  const MkPhase* ph;
+  int n_ph;
+  int ns;
+  const uint8_t* embd;
+  int embd_type, embd_row_bytes, n_embd;
+  float* x;
+  const float* cos_t;
+  const float* sin_t;
+  int hd, n_head, n_kv, max_seq, kv_f16;
+  float eps;
+  float att_scale;
+  float* att_part;
+  unsigned* att_cnt;
+  float* q;
+  float* y;
+  float* am_val;
+  int* am_idx;
+  unsigned* am_cnt;
+  uint32_t* token;
+  int* pos;
+  unsigned* gbar;
+  uint32_t* err;
+  unsigned long long* trace;  // nullptr, or [n_ph][grid][MK_TRACE_SLOTS] globaltimer stamps
+  size_t off_bars, off_act_qs, off_act_d, off_act_bs, off_red, off_att;  // smem layout
+  int kmax;
+  int res_per_cta;  // rows per CTA of attn_output / ffn_down (same split)
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Phase timeline (profiling), stamped by the first consumer thread: slot 0
+// phase start (grid barrier passed), 1 activation built, 2 phase done,
+// 3 producer issued the phase's first chunk, 4 first chunk's data ready,
+// 5 first chunk computed, 6 prologue's first pass done, 7 rms scale known,
+// 8 / 9 first unit's dot products / epilogue done.
+constexpr int MK_TRACE_SLOTS = 10;
+__device__ __forceinline__ void mk_stamp(const MkParams& p, int phase, int slot) {
+  if (p.trace) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * MK_TRACE_SLOTS + slot] = global_ns();
+}
+
+__device__ __forceinline__ void prefetch_l1(const void* ptr) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(ptr));
+}
+
+__device__ __forceinline__ void named_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ bool dev_failed(const uint32_t* err) {
+  return *reinterpret_cast<const volatile uint32_t*>(err) != 0u;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded mbarrier wait that also gives up when another CTA flagged an error.
+__device__ __forceinline__ bool mk_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (i > 8) {
+      if ((i & 63) == 0 && dev_failed(err)) return false;
+      __nanosleep(128);
+    }
+  }
+  atomicOr(err, DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+
+template <int MODE>
+__device__ __forceinline__ int mk_parts(const MkPhase& ph, int c0, int c1, Part (&parts)[3]) {
+  int n = 0;
+  uint32_t off = 0;
+  if (MODE == MODE_QKV) {
+    int sb = 0;
+    for (int s = 0; s < ph.nseg; s++) {
+      const int se = sb + ph.seg[s].rows;
+      const int lo = max(c0, sb), hi = min(c1, se);
+      if (lo < hi) {
+        parts[n++] = Part{s, lo - sb, hi - sb, off};
+        off += (uint32_t)(hi - lo) * ph.seg[s].row_bytes;
+      }
+      sb = se;
+    }
+  } else if (MODE == MODE_GATEUP) {
+    parts[n++] = Part{0, c0, c1, 0};
+    parts[n++] = Part{1, c0, c1, (uint32_t)(c1 - c0) * ph.seg[0].row_bytes};
+  } else {
+    parts[n++] = Part{0, c0, c1, 0};
+  }
+  return n;
+}
+
+__device__ __forceinline__ int mode_of(int kind) {
+  return kind == PH_QKV ? MODE_QKV : kind == PH_GATEUP ? MODE_GATEUP : kind == PH_HEAD ? MODE_HEAD
+                                                                                     : MODE_RESID;
+}
+
+__device__ __forceinline__ void phase_rows(const MkPhase& ph, int& r0, int& r1) {
+  r0 = min((int)blockIdx.x * ph.rows_per_cta, ph.total_rows);
+  r1 = min(r0 + ph.rows_per_cta, ph.total_rows);
+}
+
+// ---------------------------------------------------------------------------
+// Producer: one lane streams this CTA's rows of every weight phase.
+// ---------------------------------------------------------------------------
+__device__ void mk_producer(const MkParams& p, uint8_t* smem) {
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+  uint64_t* empty = full + MK_MAX_NS;
+  const uint64_t pol = l2_evict_first_policy();
+  int sidx = 0;
+  for (int i = 0; i < p.n_ph; i++) {
+    const MkPhase& ph = p.ph[i];
+    if (ph.kind == PH_ATTN) continue;
+    int r0, r1;
+    phase_rows(ph, r0, r1);
+    const int mode = mode_of(ph.kind);
+    for (int c0 = r0; c0 < r1; c0 += ph.chunk_rows) {
+      const int c1 = min(c0 + ph.chunk_rows, r1);
+      const int s = sidx % p.ns;
+      if (sidx >= p.ns && !mk_wait(&empty[s], (uint32_t)(((sidx / p.ns) - 1) & 1), p.err)) return;
+      if (c0 == r0) mk_stamp(p, i, 3);
+      Part parts[3];
+      const int n = mode == MODE_QKV ? mk_parts<MODE_QKV>(ph, c0, c1, parts)
+                    : mode == MODE_GATEUP ? mk_parts<MODE_GATEUP>(ph, c0, c1, parts)
+                                          : mk_parts<MODE_RESID>(ph, c0, c1, parts);
+      uint32_t total = 0;
+      for (int k = 0; k < n; k++) total += (uint32_t)(parts[k].hi - parts[k].lo) * ph.seg[parts[k].seg].row_bytes;
+      uint8_t* stage = smem + (size_t)s * MK_STAGE;
+      fence_proxy_async();
+      mbar_expect_tx(&full[s], total);
+      for (int k = 0; k < n; k++) {
+        const Seg& sg = ph.seg[parts[k].seg];
+        bulk_g2s(stage + parts[k].off, sg.w + (int64_t)parts[k].lo * sg.row_bytes,
+                 (uint32_t)(parts[k].hi - parts[k].lo) * sg.row_bytes, &full[s], pol);
+      }
+      sidx++;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Grid barrier among consumers of all CTAs: phase `idx` may start once every
+// CTA has finished phase idx-1.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ bool mk_arrive(const MkParams& p, int ctid) {
+  named_sync(1, MK_CT);
+  // bar.sync orders the CTA's phase writes before this release (cumulative).
+  if (ctid == 0) red_release_add(p.gbar, 1u);
+  return true;
+}
+__device__ __forceinline__ bool mk_wait_grid(const MkParams& p, int ctid, unsigned target,
+                                             int* s_flag) {
+  if (ctid == 0) {
+    int ok = 1;
+    uint32_t it = 0;
+    while (ld_acquire_u32(p.gbar) < target) {
+      if (++it > 32) __nanosleep(32);
+      if ((it & 255) == 0 && dev_failed(p.err)) { ok = 0; break; }
+      if (it > MK_BAR_LIMIT) { atomicOr(p.err, DEVERR_COUNTER_TIMEOUT); ok = 0; break; }
+    }
+    *s_flag = ok;
+  }
+  named_sync(1, MK_CT);
+  return *s_flag != 0;
+}
+
+// Values [8 lane, 8 lane + 8) of super-block j of the current token's
+// embedding row (BlockQ4K / BlockQ6K::to_float). Kept out of line: it runs
+// once per token and would otherwise crowd the prologue's registers.
+struct F8 {
+  float v[8];
+};
+__device__ __noinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, int nb) {
+  F8 out;
+  const uint32_t tok = min(__ldcg(p.token), (uint32_t)(0x7fffffff));
+  const uint8_t* row = p.embd + (int64_t)tok * p.embd_row_bytes;
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int i = 8 * lane + k;
+    if (p.embd_type == GGML_Q4_K) {
+      const uint8_t* blk = row + (int64_t)j * Q4K_BLOCK_BYTES;
+      const int c = i / 64, l = i % 64, sj = 2 * c + (l >= 32);
+      const uint8_t byte = blk[16 + 32 * c + (l & 31)];
+      const int q = l >= 32 ? (byte >> 4) : (byte & 0xF);
+      int sc, m;
+      q4k_scale_min(blk + 4, sj, sc, m);
+      const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+      const float dmin = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
+      out.v[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+    } else {
+      const uint8_t* body = row + (int64_t)j * Q6K_BODY_BYTES;
+      const uint16_t* dv = reinterpret_cast<const uint16_t*>(row + (int64_t)nb * Q6K_BODY_BYTES);
+      const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
+      const uint8_t qlb = body[64 * n + l + (g & 1) * 32];
+      const int lo = (g < 2) ? (qlb & 0xF) : (qlb >> 4);
+      const int hi = (body[128 + 32 * n + l] >> (2 * g)) & 3;
+      const int8_t sc = reinterpret_cast<const int8_t*>(body + 192)[8 * n + l / 16 + 2 * g];
+      out.v[k] = __fmul_rn(__fmul_rn(h2f(dv[j]), (float)sc), (float)((lo | (hi << 4)) - 32));
+    }
+  }
+  return out;
+}
+
+// ---------------------------------------------------------------------------
+// Consumer prologue: Q8_K activation of the phase input (optionally rmsnorm).
+// Layer 0's QKV reads the token's embedding row (dequantised here; CTA 0 also
+// stores it as the residual stream x).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8]) {
+  if (ph.in) {
+    const float4* xr = reinterpret_cast<const float4*>(ph.in + j * QK_K + 8 * lane);
+    const float4 x0 = __ldcg(xr), x1 = __ldcg(xr + 1);
+    vv[0] = x0.x; vv[1] = x0.y; vv[2] = x0.z; vv[3] = x0.w;
+    vv[4] = x1.x; vv[5] = x1.y; vv[6] = x1.z; vv[7] = x1.w;
+  } else {
+    const F8 e = mk_embed_vals(p, j, lane, ph.nb);
+#pragma unroll
+    for (int k = 0; k < 8; k++) vv[k] = e.v[k];
+  }
+}
+
+// The first MK_REGJ blocks of a warp stay in registers between the two
+// passes; any further ones (K > MK_REGJ * 256 * consumer warps) are loaded
+// again in the second pass.
+__device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, uint8_t* smem,
+                             ActQ8& act, int cw, int lane, float* xres, int res0, int res_n) {
+  const int K = ph.K, nb = ph.nb;
+  float* part = reinterpret_cast<float*>(smem + p.off_red) + 64;
+  act.qs = reinterpret_cast<int8_t*>(smem + p.off_act_qs);
+  act.d = reinterpret_cast<float*>(smem + p.off_act_d);
+  act.bs = reinterpret_cast<int32_t*>(smem + p.off_act_bs);
+  const bool norm = ph.gamma != nullptr;
+  float v[MK_REGJ][8];
+  for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
+    float vv[8];
+    mk_load_vals(p, ph, j, lane, vv);
+    if (!ph.in) {
+      // token embedding = initial residual stream: keep this CTA's rows
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int e = j * QK_K + 8 * lane + k - res0;
+        if (e >= 0 && e < res_n) xres[e] = vv[k];
+      }
+    }
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; k++) ss += vv[k] * vv[k];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (lane == 0) part[j] = ss;
+    }
+#pragma unroll
+    for (int r = 0; r < MK_REGJ; r++)
+      if (jj == r) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) v[r][k] = vv[k];
+      }
+  }
+  float m = 1.f;
+  if (cw == 0 && lane == 0) mk_stamp(p, phase, 6);
+  if (norm) {
+    named_sync(1, MK_CT);
+    // candle rms_norm: m = sqrt(sum2 / K + eps); block partials added in
+    // block order by every thread (same value everywhere, no second barrier).
+    float sum2 = 0.f;
+    for (int j = 0; j < nb; j++) sum2 += part[j];
+    m = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)K), p.eps));
+  }
+  if (cw == 0 && lane == 0) mk_stamp(p, phase, 7);
+  for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
+    float vv[8];
+    if (jj < MK_REGJ) {
+#pragma unroll
+      for (int r = 0; r < MK_REGJ; r++)
+        if (jj == r) {
+#pragma unroll
+          for (int k = 0; k < 8; k++) vv[k] = v[r][k];
+        }
+    } else {
+      mk_load_vals(p, ph, j, lane, vv);
+    }
+    if (norm) {
+      const float4* gr = reinterpret_cast<const float4*>(ph.gamma + j * QK_K + 8 * lane);
+      const float4 g0 = __ldg(gr), g1 = __ldg(gr + 1);
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+      for (int k = 0; k < 8; k++) vv[k] = __fmul_rn(__fdiv_rn(vv[k], m), g[k]);
+    }
+    q8k_quant_block_warp(vv, lane, act.qs + j * QK_K, act.d + j, act.bs + j * 16, j & 7);
+  }
+  named_sync(1, MK_CT);
+}
+
+// ---------------------------------------------------------------------------
+// Consumer: dot products + epilogue of the staged chunks (chunk_units).
+// ---------------------------------------------------------------------------
+// Context of the persistent kernel's matvec phases.
+struct MkCtx {
+  const MkParams& p;
+  const MkPhase& ph;
+  int pos_v;
+  __device__ const Seg& seg(int i) const { return ph.seg[i]; }
+  __device__ int nb() const { return ph.nb; }
+  __device__ float* out() const { return ph.out; }
+  __device__ int qn() const { return ph.seg[0].rows; }
+  __device__ int kn() const { return ph.seg[1].rows; }
+  __device__ int hd() const { return p.hd; }
+  __device__ int max_seq() const { return p.max_seq; }
+  __device__ int kv_f16() const { return p.kv_f16; }
+  __device__ void* kc() const { return ph.kc; }
+  __device__ void* vc() const { return ph.vc; }
+  __device__ int64_t kv_off() const { return 0; }
+  __device__ int pos() const { return pos_v; }
+  int phase;
+  float* xres;  // this CTA's rows of the residual stream (shared memory)
+  int res0;     // first of those rows
+  __device__ void stamp(int slot) const { mk_stamp(p, phase, slot); }
+  // x[r] += v on the CTA's own copy of its rows; the global x is only
+  // written (for the other CTAs' next prologue), never read back here.
+  __device__ void resid_add(float* o, int r, float v) const {
+    const float nv = __fadd_rn(v, xres[r - res0]);
+    xres[r - res0] = nv;
+    *o = nv;
+  }
+  __device__ const float* cos_t() const { return p.cos_t; }
+  __device__ const float* sin_t() const { return p.sin_t; }
+};
+
+// All chunks of this CTA's rows in one matvec phase: wait for each stage,
+// compute, hand the stage back to the producer.
+template <int MODE>
+__device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, float* xres, int res0,
+                          uint8_t* smem, uint64_t* full,
+                          uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
+                          float& best_v, int& best_i) {
+  int r0, r1;
+  phase_rows(ph, r0, r1);
+  for (int c0 = r0; c0 < r1; c0 += ph.chunk_rows) {
+    const int c1 = min(c0 + ph.chunk_rows, r1);
+    const int s = cidx % p.ns;
+    if (!mk_wait(&full[s], (uint32_t)((cidx / p.ns) & 1), p.err)) return false;
+    if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
+    Part parts[3];
+    const int np = mk_parts<MODE>(ph, c0, c1, parts);
+    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0}, smem + (size_t)s * MK_STAGE, c0, c1, parts, np, act, cw, MK_CW,
+                      lane, best_v, best_i);
+    __syncwarp();
+    if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
+    if (lane == 0) mbar_arrive(&empty[s]);
+    cidx++;
+  }
+  return true;
+}
+
+template <typename KV>
+__device__ __forceinline__ float4 kv_load4(const KV* base, size_t idx) {
+  if constexpr (sizeof(KV) == 4) {
+    return __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx));
+  } else {
+    const uint2 r = __ldcg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + idx));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumer: attention unit (g, s) = kv head g, context split s of `splits`,
+// on all consumer warps. Tiles of MK_ATT_TILE(HD) positions: K and V of the
+// tile are staged in shared memory with one wave of loads, then scores
+// (thread per (head, position)), online softmax (warp per head) and P.V
+// (thread per (head, dimension)). With splits > 1 the split partials go
+// through global memory and the last split's CTA merges them.
+// ---------------------------------------------------------------------------
+template <int HD>
+constexpr int mk_att_tile() { return 4096 / HD; }
+
+// Shared-memory floats of the attention unit.
+__host__ __device__ inline size_t mk_att_floats(int hd, int nrep) {
+  const int tile = 4096 / hd;
+  return (size_t)nrep * hd + (size_t)tile * (hd + 1) + (size_t)tile * hd + (size_t)nrep * tile +
+         3 * (size_t)nrep + 2 * (size_t)ATT_SPLITS * nrep + nrep + 1;
+}
+
+template <int HD, typename KV>
+__device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s, int splits, int T,
+                             float* sm, int cw, int lane) {
+  constexpr int TILE = mk_att_tile<HD>();
+  constexpr int MAXE = (ATT_MAX_REP * HD + MK_CT - 1) / MK_CT;  // (head, dim) elements per thread
+  const int nrep = p.n_head / p.n_kv;
+  const int tid = cw * 32 + lane;
+  float* qs = sm;                              // [nrep][HD]
+  float* Ks = qs + nrep * HD;                  // [TILE][HD + 1]
+  float* Vs = Ks + TILE * (HD + 1);            // [TILE][HD]
+  float* ps = Vs + TILE * HD;                  // [nrep][TILE]
+  float* mrow = ps + nrep * TILE;              // [nrep]
+  float* lrow = mrow + nrep;
+  float* corr = lrow + nrep;
+  float* cw_m = corr + nrep;                   // [ATT_SPLITS][nrep]
+  float* cw_l = cw_m + ATT_SPLITS * nrep;
+  float* ltot = cw_l + ATT_SPLITS * nrep;      // [nrep]
+  int* s_last = reinterpret_cast<int*>(ltot + nrep);
+
+  const int chunk = (T + splits - 1) / splits;
+  const int t0 = min(T, s * chunk), t1 = min(T, t0 + chunk);
+  const int64_t kvbase = (int64_t)g * p.max_seq * HD;
+  const KV* kc = reinterpret_cast<const KV*>(ph.kc) + kvbase;
+  const KV* vc = reinterpret_cast<const KV*>(ph.vc) + kvbase;
+  const float4* qb = reinterpret_cast<const float4*>(p.q + (size_t)g * nrep * HD);
+  for (int i = tid; i < nrep * HD / 4; i += MK_CT) reinterpret_cast<float4*>(qs)[i] = __ldcg(qb + i);
+  if (tid < nrep) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
+  float o[MAXE];
+#pragma unroll
+  for (int k = 0; k < MAXE; k++) o[k] = 0.f;
+  constexpr int V4 = HD / 4;
+  for (int tb = t0; tb < t1; tb += TILE) {
+    const int n = min(TILE, t1 - tb);
+    for (int i = tid; i < n * V4; i += MK_CT) {
+      const int tt = i / V4, c = (i % V4) * 4;
+      const float4 kv = kv_load4(kc, (size_t)(tb + tt) * HD + c);
+      const float4 vv = kv_load4(vc, (size_t)(tb + tt) * HD + c);
+      float* kd = Ks + tt * (HD + 1) + c;
+      kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+      *reinterpret_cast<float4*>(Vs + tt * HD + c) = vv;
+    }
+    named_sync(1, MK_CT);
+    // scores: thread per (head, position)
+    for (int e = tid; e < nrep * TILE; e += MK_CT) {
+      const int h = e / TILE, t = e % TILE;
+      float sc = -INFINITY;
+      if (t < n) {
+        const float* q = qs + h * HD;
+        const float* k = Ks + t * (HD + 1);
+        float acc = 0.f;
+#pragma unroll 16
+        for (int d = 0; d < HD; d++) acc += q[d] * k[d];
+        sc = acc * p.att_scale;
+      }
+      ps[h * TILE + t] = sc;
+    }
+    named_sync(1, MK_CT);
+    // online softmax: warp per head
+    for (int h = cw; h < nrep; h += MK_CW) {
+      float mt = -INFINITY;
+      for (int t = lane; t < n; t += 32) mt = fmaxf(mt, ps[h * TILE + t]);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mold = mrow[h];
+      const float mnew = fmaxf(mold, mt);
+      float ls = 0.f;
+      for (int t = lane; t < TILE; t += 32) {
+        const float pe = t < n ? expf(ps[h * TILE + t] - mnew) : 0.f;
+        ps[h * TILE + t] = pe;
+        ls += pe;
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      if (lane == 0) {
+        const float c = expf(mold - mnew);  // 0 on the first tile (mold = -inf)
+        corr[h] = c;
+        lrow[h] = lrow[h] * c + ls;
+        mrow[h] = mnew;
+      }
+    }
+    named_sync(1, MK_CT);
+    // P.V: thread per (head, dimension)
+#pragma unroll
+    for (int k = 0; k < MAXE; k++) {
+      const int e = tid + k * MK_CT;
+      if (e < nrep * HD) {
+        const int h = e / HD, d = e % HD;
+        float acc = o[k] * corr[h];
+        const float* pr = ps + h * TILE;
+        for (int t = 0; t < n; t++) acc += pr[t] * Vs[t * HD + d];
+        o[k] = acc;
+      }
+    }
+    named_sync(1, MK_CT);
+  }
+  if (splits == 1) {
+#pragma unroll
+    for (int k = 0; k < MAXE; k++) {
+      const int e = tid + k * MK_CT;
+      if (e < nrep * HD) p.y[(size_t)g * nrep * HD + e] = o[k] / lrow[e / HD];
+    }
+    return;
+  }
+  const size_t pbase = (((size_t)g * ATT_SPLITS + s) * nrep) * (HD + 2);
+#pragma unroll
+  for (int k = 0; k < MAXE; k++) {
+    const int e = tid + k * MK_CT;
+    if (e < nrep * HD) p.att_part[pbase + (size_t)(e / HD) * (HD + 2) + e % HD] = o[k];
+  }
+  if (tid < nrep) {
+    p.att_part[pbase + (size_t)tid * (HD + 2) + HD] = mrow[tid];
+    p.att_part[pbase + (size_t)tid * (HD + 2) + HD + 1] = lrow[tid];
+  }
+  __threadfence();
+  named_sync(1, MK_CT);
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&p.att_cnt[g], 1u);
+    *s_last = (prev == (unsigned)splits - 1);
+  }
+  named_sync(1, MK_CT);
+  if (!*s_last) return;
+  __threadfence();
+  // the last split of head g merges all splits
+  const size_t base0 = ((size_t)g * ATT_SPLITS) * nrep * (HD + 2);
+  for (int i = tid; i < splits * nrep; i += MK_CT) {
+    const int s2 = i / nrep, h = i % nrep;
+    const size_t o2 = base0 + ((size_t)s2 * nrep + h) * (HD + 2);
+    cw_m[s2 * nrep + h] = __ldcg(p.att_part + o2 + HD);
+    cw_l[s2 * nrep + h] = __ldcg(p.att_part + o2 + HD + 1);
+  }
+  named_sync(1, MK_CT);
+  if (tid < nrep) {
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < splits; s2++)
+      if (cw_l[s2 * nrep + tid] > 0.f) M = fmaxf(M, cw_m[s2 * nrep + tid]);
+    float Ls = 0.f;
+    for (int s2 = 0; s2 < splits; s2++) {
+      const float lv = cw_l[s2 * nrep + tid];
+      const float w = lv > 0.f ? expf(cw_m[s2 * nrep + tid] - M) : 0.f;
+      cw_m[s2 * nrep + tid] = w;
+      Ls += lv * w;
+    }
+    ltot[tid] = Ls;
+  }
+  named_sync(1, MK_CT);
+  for (int e = tid; e < nrep * HD; e += MK_CT) {
+    const int h = e / HD, d = e % HD;
+    float O = 0.f;
+    for (int s2 = 0; s2 < splits; s2++) {
+      const float w = cw_m[s2 * nrep + h];
+      if (w != 0.f) O += w * __ldcg(p.att_part + base0 + ((size_t)s2 * nrep + h) * (HD + 2) + d);
+    }
+    p.y[((size_t)g * nrep + h) * HD + d] = O / ltot[h];
+  }
+  if (tid == 0) p.att_cnt[g] = 0u;
+}
+
+// ---------------------------------------------------------------------------
+// The kernel.
+// ---------------------------------------------------------------------------
+template <int HD, typename KV>
+__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int s_flag;
+  __shared__ __align__(16) MkPhase s_ph[2];
+  __shared__ int s_pos;  // position of this step's token (constant during the step)
+  __shared__ float s_xres[MK_MAX_RES];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
+  uint64_t* empty = full + MK_MAX_NS;
+  if (tid == 0) {
+    mk_stamp(p, p.n_ph, 0);  // kernel entry
+    for (int s = 0; s < p.ns; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], MK_CW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) mk_producer(p, smem);
+    return;
+  }
+  const int ctid = tid - 32, cw = warp - 1;
+  if (ctid == 0) s_pos = (int)__ldcg(p.pos);
+  // rows of the residual stream this CTA updates (attn_output / ffn_down)
+  const int res0 = min((int)blockIdx.x * p.res_per_cta, p.n_embd);
+  const int res_n = min(res0 + p.res_per_cta, p.n_embd) - res0;
+  ActQ8 act;
+  int cidx = 0;
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+  for (int i = 0; i < p.n_ph; i++) {
+    // Before waiting on the grid: copy the phase descriptor into shared
+    // memory (double-buffered by parity: warps may still be reading phase
+    // i-1's copy) and pull this phase's rmsnorm weights into L1, so that
+    // neither sits on the critical path after the barrier.
+    MkPhase& ph = s_ph[i & 1];
+    {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph + i);
+      uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
+      for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
+      const float* g = reinterpret_cast<const float*>(
+          __ldg(reinterpret_cast<const unsigned long long*>(&p.ph[i].gamma)));
+      if (g) {
+        const int nb = __ldg(&p.ph[i].nb);
+        for (int j = cw; j < nb; j += MK_CW) prefetch_l1(g + j * QK_K + 8 * lane);
+      }
+    }
+    if (i > 0) {
+      if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
+    } else {
+      named_sync(1, MK_CT);
+    }
+    if (ctid == 0) mk_stamp(p, i, 0);
+    if (ph.kind == PH_ATTN) {
+      // Split the context across CTAs only when it spans several tiles.
+      const int T = s_pos + 1;
+      constexpr int per = 2 * mk_att_tile<HD>();
+      const int splits = min(ATT_SPLITS, (T + per - 1) / per);
+      const int nunits = p.n_kv * splits;
+      float* asm_ = reinterpret_cast<float*>(smem + p.off_att);
+      for (int u = blockIdx.x; u < nunits; u += gridDim.x)
+        mk_attn_unit<HD, KV>(p, ph, u / splits, u % splits, splits, T, asm_, cw, lane);
+    } else {
+      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n);
+      if (ctid == 0) mk_stamp(p, i, 1);
+      const int mode = mode_of(ph.kind);
+      bool ok;
+      if (mode == MODE_QKV) ok = mk_chunks<MODE_QKV>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_GATEUP) ok = mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_HEAD) ok = mk_chunks<MODE_HEAD>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else ok = mk_chunks<MODE_RESID>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      if (!ok) return;
+    }
+    if (ctid == 0) mk_stamp(p, i, 2);
+    if (i + 1 < p.n_ph) mk_arrive(p, ctid);
+  }
+  // HEAD: CTA argmax partial, the last CTA reduces all partials.
+  float* rv = reinterpret_cast<float*>(smem + p.off_red);
+  int* ri = reinterpret_cast<int*>(rv + 32);
+  if (lane == 0) { rv[cw] = best_v; ri[cw] = best_i; }
+  named_sync(1, MK_CT);
+  if (ctid == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < MK_CW; w++)
+      if (am_better(rv[w], ri[w], bv, bi)) { bv = rv[w]; bi = ri[w]; }
+    p.am_val[blockIdx.x] = bv;
+    p.am_idx[blockIdx.x] = bi;
+    __threadfence();
+    const unsigned prev = atomicAdd(p.am_cnt, 1u);
+    s_flag = (prev == gridDim.x - 1);
+  }
+  named_sync(1, MK_CT);
+  if (!s_flag) return;
+  __threadfence();
+  if (cw == 0) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = lane; i < (int)gridDim.x; i += 32) {
+      const float v = __ldcg(p.am_val + i);
+      const int ix = __ldcg(p.am_idx + i);
+      if (am_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) {
+      *p.token = (bi == 0x7fffffff) ? 0u : (uint32_t)bi;
+      *p.pos = __ldcg(p.pos) + 1;
+      *p.am_cnt = 0u;
+      // every CTA has passed its last grid barrier (it reached am_cnt after
+      // the head phase), so the counter can be rearmed for the next step
+      *p.gbar = 0u;
+      mk_stamp(p, p.n_ph, 1);  // step result written
+    }
+  }
+}
+
+}  // namespace armai

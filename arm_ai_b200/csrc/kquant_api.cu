@@ -39,11 +39,14 @@ __global__ void k_quant_q8k(const float* x, int64_t m, int K, BlockQ8K* out, int
   if (lane < 16) b->bsums[lane] = (int16_t)bs[lane];
 }
 
-// BlockQ8K structs -> the split ActQ8 layout the kernels read.
-__global__ void k_q8k_split(const BlockQ8K* in, int64_t nblocks, int8_t* qs, float* d, int32_t* bs) {
+// BlockQ8K structs -> the split ActQ8 layout the kernels read (qs chunks
+// swizzled by block index, as load_slice expects). `nb` = blocks per row.
+__global__ void k_q8k_split(const BlockQ8K* in, int64_t nblocks, int nb, int8_t* qs, float* d, int32_t* bs) {
   const int64_t b = blockIdx.x;
   if (b >= nblocks) return;
-  for (int i = threadIdx.x; i < QK_K; i += blockDim.x) qs[b * QK_K + i] = in[b].qs[i];
+  const int swz = (int)(b % nb) & 7;
+  for (int i = threadIdx.x; i < QK_K; i += blockDim.x)
+    qs[b * QK_K + (((i >> 4) ^ swz) << 4) + (i & 15)] = in[b].qs[i];
   if (threadIdx.x < 16) bs[b * 16 + threadIdx.x] = in[b].bsums[threadIdx.x];
   if (threadIdx.x == 0) d[b] = in[b].d;
 }
@@ -144,7 +147,7 @@ extern "C" int armai_kquant_block_dots(const void* w, int type, size_t n, size_t
   ARMAI_CUDA(cudaMalloc(&dqs.p, nblk * QK_K));
   ARMAI_CUDA(cudaMalloc(&dd.p, nblk * 4));
   ARMAI_CUDA(cudaMalloc(&dbs.p, nblk * 16 * 4));
-  k_q8k_split<<<(unsigned)nblk, 256>>>((const BlockQ8K*)dq.p, nblk, (int8_t*)dqs.p, (float*)dd.p,
+  k_q8k_split<<<(unsigned)nblk, 256>>>((const BlockQ8K*)dq.p, nblk, nb, (int8_t*)dqs.p, (float*)dd.p,
                                        (int32_t*)dbs.p);
   const size_t outn = (size_t)m * n * nb;
   ARMAI_CUDA(cudaMalloc(&di.p, outn * 4));

@@ -11,6 +11,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode_mega.cuh"
 #include "gguf.h"
 #include "llama_kernels.cuh"
 
@@ -99,6 +100,13 @@ struct armai_llama {
   cudaGraphExec_t graph = nullptr;
   int kv_len = 0;  // positions currently in the cache (host mirror)
   size_t device_bytes = 0;
+  // persistent decode kernel
+  bool use_mega = true;
+  MkPhase* d_phases = nullptr;
+  unsigned* gbar = nullptr;
+  MkParams mk;
+  size_t mk_smem = 0;
+  int mk_grid = 0;
 };
 
 namespace {
@@ -295,8 +303,170 @@ cudaError_t launch_embed(armai_llama* m, const uint32_t* tokens, float* x, int n
                   (int64_t)m->tok_embd.row_bytes, tokens, x, m->n_embd, m->n_vocab, m->d_err);
 }
 
+cudaError_t launch_mega(armai_llama* m) {
+  // the grid-barrier counter starts at 0: set at setup, reset by the kernel's
+  // last CTA at the end of every step
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->mk_grid);
+  cfg.blockDim = dim3(MK_THREADS);
+  cfg.dynamicSmemBytes = m->mk_smem;
+  cfg.stream = m->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (m->head_dim == 64)
+    return m->kv_f16 ? cudaLaunchKernelEx(&cfg, k_decode_mega<64, __half>, m->mk)
+                     : cudaLaunchKernelEx(&cfg, k_decode_mega<64, float>, m->mk);
+  return m->kv_f16 ? cudaLaunchKernelEx(&cfg, k_decode_mega<128, __half>, m->mk)
+                   : cudaLaunchKernelEx(&cfg, k_decode_mega<128, float>, m->mk);
+}
+
+// Phase list and shared-memory layout of the persistent decode kernel.
+int setup_mega(armai_llama* m, int nsm) {
+  const int E = m->n_embd, F = m->n_ff, QN = m->n_head * m->head_dim;
+  auto per_cta = [&](int total, int unit) {
+    int per = (total + nsm - 1) / nsm;
+    return ((per + unit - 1) / unit) * unit;
+  };
+  auto chunk_for = [&](int unit_bytes, int unit, int per) {
+    int c = (int)(MK_STAGE / (uint32_t)unit_bytes);
+    c = (c / unit) * unit;
+    if (c < unit) c = unit;
+    return std::min(c, per);
+  };
+  std::vector<MkPhase> ph;
+  auto mat_phase = [&](int kind, int layer, std::initializer_list<const DevMat*> mats, int total, int unit,
+                       int unit_bytes, int K, const float* gamma, const float* in, float* out) {
+    MkPhase p;
+    std::memset(&p, 0, sizeof p);
+    p.kind = kind;
+    p.layer = layer;
+    int i = 0;
+    for (const DevMat* d : mats) p.seg[i++] = d->seg();
+    p.nseg = i;
+    p.total_rows = total;
+    p.rows_per_cta = per_cta(total, unit);
+    p.chunk_rows = chunk_for(unit_bytes, unit, p.rows_per_cta);
+    p.K = K;
+    p.nb = K / QK_K;
+    p.gamma = gamma;
+    p.in = in;
+    p.out = out;
+    if (layer >= 0) {
+      p.kc = kv_layer_ptr(m, m->kc, layer);
+      p.vc = kv_layer_ptr(m, m->vc, layer);
+    }
+    ph.push_back(p);
+  };
+  for (int l = 0; l < m->n_layer; l++) {
+    const Layer& L = m->layers[l];
+    const int qkv_rb = std::max(L.wq.row_bytes, std::max(L.wk.row_bytes, L.wv.row_bytes));
+    mat_phase(PH_QKV, l, {&L.wq, &L.wk, &L.wv}, L.wq.rows + L.wk.rows + L.wv.rows, 2, qkv_rb, E, L.attn_norm,
+              l == 0 ? nullptr : m->x, m->q);
+    MkPhase a;
+    std::memset(&a, 0, sizeof a);
+    a.kind = PH_ATTN;
+    a.layer = l;
+    a.kc = kv_layer_ptr(m, m->kc, l);
+    a.vc = kv_layer_ptr(m, m->vc, l);
+    ph.push_back(a);
+    mat_phase(PH_WO, l, {&L.wo}, L.wo.rows, 1, L.wo.row_bytes, QN, nullptr, m->y, m->x);
+    mat_phase(PH_GATEUP, l, {&L.wg, &L.wu}, L.wg.rows, 1, L.wg.row_bytes + L.wu.row_bytes, E, L.ffn_norm, m->x,
+              m->h);
+    mat_phase(PH_DOWN, l, {&L.wd}, L.wd.rows, 1, L.wd.row_bytes, F, nullptr, m->h, m->x);
+  }
+  mat_phase(PH_HEAD, -1, {&m->output}, m->output.rows, 1, m->output.row_bytes, E, m->out_norm, m->x, m->logits);
+  ARMAI_CUDA(cudaMalloc(&m->d_phases, ph.size() * sizeof(MkPhase)));
+  ARMAI_CUDA(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
+  ARMAI_CUDA(cudaMalloc(&m->gbar, 64));
+  ARMAI_CUDA(cudaMemset(m->gbar, 0, 64));
+  const int kmax = std::max(E, std::max(F, QN));
+  MkParams& k = m->mk;
+  std::memset(&k, 0, sizeof k);
+  size_t o = 0;
+  const int nrep = m->n_head / m->n_head_kv;
+  const size_t att_bytes = mk_att_floats(m->head_dim, nrep) * 4 + 64;
+  size_t fixed = al16((size_t)2 * MK_MAX_NS * 8) + al16((size_t)kmax) + al16((size_t)kmax / QK_K * 4) +
+                 al16((size_t)kmax / 16 * 4) + al16((64 + (size_t)kmax / QK_K + 8) * 4) + al16(att_bytes);
+  // 2 KB of headroom for the kernel's static shared memory (phase copies etc.)
+  int ns = (int)std::min<size_t>(MK_MAX_NS, (SMEM_LIMIT - fixed - 2048) / MK_STAGE);
+  if (ns < 2) return fail(ARMAI_E_INVALID, "persistent decode kernel: not enough shared memory");
+  k.ns = ns;
+  o = (size_t)ns * MK_STAGE;
+  k.off_bars = o;   o += al16((size_t)2 * MK_MAX_NS * 8);
+  k.off_act_qs = o; o += al16((size_t)kmax);
+  k.off_act_d = o;  o += al16((size_t)kmax / QK_K * 4);
+  k.off_act_bs = o; o += al16((size_t)kmax / 16 * 4);
+  k.off_red = o;    o += al16((64 + (size_t)kmax / QK_K + 8) * 4);
+  k.off_att = o;    o += al16(att_bytes);
+  m->mk_smem = o;
+  k.kmax = kmax;
+  // attn_output and ffn_down split the residual stream's rows identically;
+  // each CTA keeps its rows in shared memory across the step.
+  int res_per = -1;
+  for (const MkPhase& q : ph)
+    if (q.kind == PH_WO || q.kind == PH_DOWN) {
+      if (res_per >= 0 && q.rows_per_cta != res_per)
+        return fail(ARMAI_E_INVALID, "persistent decode kernel: residual row split differs between phases");
+      res_per = q.rows_per_cta;
+    }
+  if (res_per > MK_MAX_RES)
+    return fail(ARMAI_E_INVALID, "persistent decode kernel: " + std::to_string(res_per) +
+                                     " residual rows per CTA exceed " + std::to_string(MK_MAX_RES));
+  k.res_per_cta = res_per;
+  k.ph = m->d_phases;
+  k.n_ph = (int)ph.size();
+  k.embd = m->tok_embd.w;
+  k.embd_type = m->tok_embd.type;
+  k.embd_row_bytes = m->tok_embd.row_bytes;
+  k.n_embd = E;
+  k.x = m->x;
+  k.cos_t = m->cos_t;
+  k.sin_t = m->sin_t;
+  k.hd = m->head_dim;
+  k.n_head = m->n_head;
+  k.n_kv = m->n_head_kv;
+  k.max_seq = m->max_seq;
+  k.kv_f16 = m->kv_f16;
+  k.eps = m->eps;
+  k.att_scale = (float)(1.0 / sqrt((double)m->head_dim));
+  k.att_part = m->attn_part;
+  k.att_cnt = m->attn_cnt;
+  k.q = m->q;
+  k.y = m->y;
+  k.am_val = m->am_val;
+  k.am_idx = m->am_idx;
+  k.am_cnt = m->am_cnt;
+  k.token = m->d_token;
+  k.pos = m->d_pos;
+  k.gbar = m->gbar;
+  k.err = m->d_err;
+  m->mk_grid = nsm;
+  if (m->head_dim == 64) {
+    ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
+    ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
+  } else {
+    ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
+    ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
+  }
+  // every CTA must be resident at once (grid barriers)
+  int per_sm = 0;
+  if (m->head_dim == 64)
+    ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mega<64, float>, MK_THREADS, o));
+  else
+    ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mega<128, float>, MK_THREADS, o));
+  if (per_sm < 1) return fail(ARMAI_E_INVALID, "persistent decode kernel does not fit one SM");
+  return ARMAI_OK;
+}
+
 // The single-sequence decode step: token d_token at position d_pos.
 int enqueue_decode_step(armai_llama* m) {
+  if (m->use_mega) {
+    ARMAI_CUDA(launch_mega(m));
+    return ARMAI_OK;
+  }
   ARMAI_CUDA(launch_embed(m, m->d_token, m->x, 1));
   for (int l = 0; l < m->n_layer; l++) {
     ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->x, m->q, m->d_pos, 0));
@@ -537,7 +707,7 @@ void free_model(armai_llama* m) {
   if (m->graph) cudaGraphExecDestroy(m->graph);
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
-                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok};
+                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }
@@ -579,6 +749,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   m->max_batch = std::max(1, o.max_batch);
   m->use_graph = o.use_graph != 0;
   m->use_pdl = o.use_pdl != 0;
+  m->use_mega = o.decode_kernel == 0;
   if (o.tp_size > 1) {
     delete m;
     return fail(ARMAI_E_INVALID, "tensor parallelism is not available in this build");
@@ -599,6 +770,12 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (m->n_head / m->n_head_kv > ATT_MAX_REP || (m->head_dim != 64 && m->head_dim != 128)) {
     delete m;
     return fail(ARMAI_E_FORMAT, "unsupported attention geometry (query heads per KV head > 8, or head_dim not 64 or 128)");
+  }
+  {
+    // the persistent kernel's attention is specialised for 1, 2, 4 or 8
+    // query heads per KV head; other groupings take the per-kernel chain
+    const int nrep = m->n_head / m->n_head_kv;
+    if (nrep & (nrep - 1)) m->use_mega = false;
   }
 
   auto find = [&](const std::string& name) -> const GgufTensor* {
@@ -781,10 +958,16 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (arc) { free_model(m); return arc; }
   m->attn_smem = attn_smem_floats(m->head_dim) * 4;
   m->n_kernels_step = 2 + 5 * m->n_layer;
+  if (m->use_mega) {
+    int src = setup_mega(m, nsm);
+    if (src != ARMAI_OK) { free_model(m); return src; }
+    m->n_kernels_step = 1;
+  }
   LOAD_CUDA(cudaStreamSynchronize(m->stream));
 
-  // capture the decode step
-  if (m->use_graph) {
+  // capture the decode step (the per-kernel chain only: the persistent
+  // kernel is a single launch, and as a graph node it ran slower)
+  if (m->use_graph && !m->use_mega) {
     cudaGraph_t gr = nullptr;
     LOAD_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int erc = enqueue_decode_step(m);
@@ -1013,5 +1196,34 @@ extern "C" int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t ro
   cudaEventDestroy(b);
   *ms_per_launch = ms / (float)launches;
   *bytes_per_launch = bytes / launches;
+  return check_device_error(m);
+}
+
+extern "C" int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t cap, int32_t* n_phases,
+                                        int32_t* n_ctas) {
+  if (!m || !out || !n_phases || !n_ctas) return fail(ARMAI_E_INVALID, "trace_decode: bad argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
+  if (!m->use_mega) return fail(ARMAI_E_INVALID, "trace_decode: needs the persistent decode kernel");
+  const size_t n = (size_t)(m->mk.n_ph + 1) * m->mk_grid * MK_TRACE_SLOTS;
+  if (cap < n) return fail(ARMAI_E_RANGE, "trace_decode: buffer holds " + std::to_string(cap) +
+                                              " stamps, needs " + std::to_string(n));
+  if (m->kv_len + 1 > m->max_seq) return fail(ARMAI_E_RANGE, "trace_decode: KV cache is full");
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  unsigned long long* d = nullptr;
+  ARMAI_CUDA(cudaMalloc(&d, n * 8));
+  cudaError_t e = cudaMemsetAsync(d, 0, n * 8, m->stream);
+  if (e == cudaSuccess) {
+    m->mk.trace = d;
+    e = launch_mega(m);
+    m->mk.trace = nullptr;
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * 8, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  cudaFree(d);
+  if (e != cudaSuccess) return cuda_fail(e, "trace_decode", __FILE__, __LINE__);
+  m->kv_len += 1;
+  *n_phases = m->mk.n_ph + 1;
+  *n_ctas = m->mk_grid;
   return check_device_error(m);
 }

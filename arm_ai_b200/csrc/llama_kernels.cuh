@@ -256,7 +256,7 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), g[i]);
     }
-    q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16);
+    q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16, j & 7);
   }
   __syncthreads();
 }
@@ -275,6 +275,182 @@ __device__ __forceinline__ void store_kv(void* base, int kv_f16, int64_t idx, fl
     *reinterpret_cast<float2*>(reinterpret_cast<float*>(base) + idx) = make_float2(a, b);
   }
 }
+
+// ---------------------------------------------------------------------------
+// The chunk routine shared by k_matvec and the persistent decode kernel.
+// A warp takes one "unit" at a time: two dot products that share an epilogue
+// — rows r, r+1 of one segment (QKV: the RoPE pair), gate row r and up row r
+// (GATEUP), or rows r, r+1 (RESID / HEAD / STORE; the second may be absent).
+// The weight types of the two rows are dispatched once per unit into
+// compile-time-typed inner loops.
+// ---------------------------------------------------------------------------
+// Ctx supplies the segment table and the epilogue's parameters through
+// accessors, so that what a kernel keeps in its constant bank (its own launch
+// parameters) is read from there instead of occupying registers.
+template <int T0, int T1, bool ONEPASS>
+__device__ __forceinline__ void unit_dots(const uint8_t* p0, const uint8_t* p1, bool has1, int nb,
+                                          const ActQ8& act, const ActSlice& A0, int lane,
+                                          float& d0, float& d1) {
+  const int t = lane & 3, bl = lane >> 2;
+  float a0 = 0.f, a1 = 0.f;
+  if (ONEPASS) {
+    if (bl < nb) {
+      a0 = quarter_dot_t<T0>(p0, nb, bl, t, A0);
+      if (has1) a1 = quarter_dot_t<T1>(p1, nb, bl, t, A0);
+    }
+  } else {
+    const int npass = (nb + 7) >> 3;
+    for (int ps = 0; ps < npass; ps++) {
+      const int blk = ps * 8 + bl;
+      if (blk < nb) {
+        ActSlice A;
+        load_slice(act, blk, t, A);
+        a0 += quarter_dot_t<T0>(p0, nb, blk, t, A);
+        if (has1) a1 += quarter_dot_t<T1>(p1, nb, blk, t, A);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+  }
+  d0 = a0;
+  d1 = a1;
+}
+
+// ONEPASS: K <= 2048, so each lane's activation slice is loaded once per
+// chunk and kept in registers for every row.
+template <int MODE, bool ONEPASS, class Ctx>
+__device__ __forceinline__ void chunk_units_p(const Ctx& cx, const uint8_t* stage, int c0, int c1,
+                                              const Part (&parts)[3], int np, const ActQ8& act,
+                                              int warp, int nwarps, int lane, float& best_v,
+                                              int& best_i) {
+  const int t = lane & 3, bl = lane >> 2;
+  const int nb = cx.nb();
+  ActSlice A0;
+  if (ONEPASS && bl < nb) load_slice(act, bl, t, A0);
+  const int n = c1 - c0;
+  const int nunits = MODE == MODE_GATEUP ? n : (n + 1) >> 1;
+  for (int u = warp; u < nunits; u += nwarps) {
+    const uint8_t *p0, *p1;
+    int ty0, ty1, r, si = 0;
+    bool has1 = true;
+    if (MODE == MODE_QKV) {
+      r = c0 + 2 * u;
+      const int qn = cx.qn(), kn = cx.kn();
+      si = r < qn ? 0 : (r < qn + kn ? 1 : 2);
+      const int sb = si == 0 ? 0 : (si == 1 ? qn : qn + kn);
+      uint32_t off = parts[0].off;
+      int lo = parts[0].lo;
+#pragma unroll
+      for (int i = 1; i < 3; i++)
+        if (i < np && parts[i].seg == si) { off = parts[i].off; lo = parts[i].lo; }
+      const Seg& sg = cx.seg(si);
+      p0 = stage + off + (size_t)(r - sb - lo) * sg.row_bytes;
+      p1 = p0 + sg.row_bytes;
+      ty0 = ty1 = sg.type;
+    } else if (MODE == MODE_GATEUP) {
+      r = c0 + u;
+      p0 = stage + (size_t)u * cx.seg(0).row_bytes;
+      p1 = stage + parts[1].off + (size_t)u * cx.seg(1).row_bytes;
+      ty0 = cx.seg(0).type;
+      ty1 = cx.seg(1).type;
+    } else {
+      r = c0 + 2 * u;
+      p0 = stage + (size_t)(2 * u) * cx.seg(0).row_bytes;
+      p1 = p0 + cx.seg(0).row_bytes;
+      has1 = r + 1 < c1;
+      ty0 = ty1 = cx.seg(0).type;
+    }
+    float d0, d1;
+    if (MODE != MODE_GATEUP || ty0 == ty1) {  // both rows of one matrix
+      if (ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+      else unit_dots<GGML_Q6_K, GGML_Q6_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+    } else if (ty0 == GGML_Q4_K) {
+      unit_dots<GGML_Q4_K, GGML_Q6_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+    } else {
+      unit_dots<GGML_Q6_K, GGML_Q4_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+    }
+    if (lane != 0) continue;
+    if (u == 0) cx.stamp(8);
+    float* out = cx.out();
+    if (MODE == MODE_QKV) {
+      const int hd = cx.hd(), half = hd >> 1, pos = cx.pos();
+      const int qn = cx.qn(), kn = cx.kn();
+      if (si < 2) {
+        const int rr = si == 0 ? r : r - qn;
+        const int i2 = (rr % hd) >> 1;
+        const float cs = __ldg(cx.cos_t() + (size_t)pos * half + i2);
+        const float sn = __ldg(cx.sin_t() + (size_t)pos * half + i2);
+        // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
+        const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
+        const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
+        if (si == 0) {
+          *reinterpret_cast<float2*>(out + r) = make_float2(o0, o1);
+        } else {
+          const int kvh = rr / hd, dd = rr % hd;
+          store_kv(cx.kc(), cx.kv_f16(), cx.kv_off() + ((int64_t)kvh * cx.max_seq() + pos) * hd + dd, o0, o1);
+        }
+      } else {
+        const int rv = r - qn - kn;
+        const int kvh = rv / hd, dd = rv % hd;
+        store_kv(cx.vc(), cx.kv_f16(), cx.kv_off() + ((int64_t)kvh * cx.max_seq() + pos) * hd + dd, d0, d1);
+      }
+    } else if (MODE == MODE_GATEUP) {
+      // candle: silu(v) = v / (1 + exp(-v)); then * up
+      const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
+      out[r] = __fmul_rn(sl, d1);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 2; k++) {
+        if (k == 1 && !has1) break;
+        const float v = k == 0 ? d0 : d1;
+        float* o = out + r + k;
+        if (MODE == MODE_RESID) cx.resid_add(o, r + k, v);
+        else *o = v;
+        if (MODE == MODE_HEAD && am_better(v, r + k, best_v, best_i)) {
+          best_v = v;
+          best_i = r + k;
+        }
+      }
+    }
+    if (u == 0) cx.stamp(9);
+  }
+}
+
+template <int MODE, class Ctx>
+__device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage, int c0, int c1,
+                                            const Part (&parts)[3], int np, const ActQ8& act, int warp,
+                                            int nwarps, int lane, float& best_v, int& best_i) {
+  if (cx.nb() <= 8)
+    chunk_units_p<MODE, true>(cx, stage, c0, c1, parts, np, act, warp, nwarps, lane, best_v, best_i);
+  else
+    chunk_units_p<MODE, false>(cx, stage, c0, c1, parts, np, act, warp, nwarps, lane, best_v, best_i);
+}
+
+// Context of k_matvec: its launch parameters and the sequence index.
+struct MvCtx {
+  const MvParams& p;
+  int b;
+  __device__ const Seg& seg(int i) const { return p.seg[i]; }
+  __device__ int nb() const { return p.nb; }
+  __device__ float* out() const { return p.out + (size_t)b * p.out_stride; }
+  __device__ int qn() const { return p.qn; }
+  __device__ int kn() const { return p.kn; }
+  __device__ int hd() const { return p.hd; }
+  __device__ int max_seq() const { return p.max_seq; }
+  __device__ int kv_f16() const { return p.kv_f16; }
+  __device__ void* kc() const { return p.kc; }
+  __device__ void* vc() const { return p.vc; }
+  __device__ int64_t kv_off() const { return (int64_t)b * p.kv_seq_stride; }
+  __device__ int pos() const { return p.pos[b]; }
+  __device__ const float* cos_t() const { return p.cos_t; }
+  __device__ const float* sin_t() const { return p.sin_t; }
+  __device__ void stamp(int) const {}
+  // x[r] += v (the residual stream lives in global memory between kernels)
+  __device__ void resid_add(float* o, int, float v) const { *o = __fadd_rn(v, __ldcg(o)); }
+};
 
 // ---------------------------------------------------------------------------
 // The streaming matvec kernel.
@@ -319,8 +495,6 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
 #pragma unroll
   for (int b = 0; b < NB; b++) { best_v[b] = -INFINITY; best_i[b] = 0x7fffffff; }
 
-  const int t = lane & 3, bl = lane >> 2;
-  const int npass = (p.nb + 7) >> 3;
   for (int c = 0; c < nchunks; c++) {
     const int s = c % p.ns;
     const int c0 = r0 + c * p.chunk_rows, c1 = min(c0 + p.chunk_rows, r1);
@@ -329,117 +503,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
     Part parts[3];
     const int np = chunk_parts<MODE>(p, c0, c1, parts);
-    // A unit is what one warp reduces at a time: a row pair (QKV, RoPE
-    // needs both), a gate/up row pair (GATEUP) or a single row.
-    const int nunits = MODE == MODE_QKV ? (c1 - c0) >> 1 : (c1 - c0);
-    for (int b = 0; b < NB; b++) {
-      for (int u0 = warp; u0 < nunits; u0 += 2 * MV_WARPS) {
-        const uint8_t* rp[4];
-        int ty[4];
-        bool va[4];
-        int ur[2];    // first (virtual) row of each unit
-        int useg[2];  // segment of each QKV unit
-#pragma unroll
-        for (int k = 0; k < 2; k++) {
-          const int u = u0 + k * MV_WARPS;
-          const bool uv = u < nunits;
-          va[2 * k] = uv;
-          va[2 * k + 1] = uv && (MODE == MODE_QKV || MODE == MODE_GATEUP);
-          rp[2 * k] = rp[2 * k + 1] = stage;
-          ty[2 * k] = ty[2 * k + 1] = GGML_Q4_K;
-          ur[k] = 0;
-          useg[k] = 0;
-          if (!uv) continue;
-          if (MODE == MODE_QKV) {
-            const int r = c0 + 2 * u;
-            const int si = r < p.qn ? 0 : (r < p.qn + p.kn ? 1 : 2);
-            const int sb = si == 0 ? 0 : (si == 1 ? p.qn : p.qn + p.kn);
-            int pi = 0;
-            for (int i = 0; i < np; i++)
-              if (parts[i].seg == si) pi = i;
-            const Seg& sg = p.seg[si];
-            rp[2 * k] = stage + parts[pi].off + (size_t)(r - sb - parts[pi].lo) * sg.row_bytes;
-            rp[2 * k + 1] = rp[2 * k] + sg.row_bytes;
-            ty[2 * k] = ty[2 * k + 1] = sg.type;
-            ur[k] = r;
-            useg[k] = si;
-          } else if (MODE == MODE_GATEUP) {
-            const int r = c0 + u;
-            rp[2 * k] = stage + (size_t)(r - c0) * p.seg[0].row_bytes;
-            rp[2 * k + 1] = stage + parts[1].off + (size_t)(r - c0) * p.seg[1].row_bytes;
-            ty[2 * k] = p.seg[0].type;
-            ty[2 * k + 1] = p.seg[1].type;
-            ur[k] = r;
-          } else {
-            const int r = c0 + u;
-            rp[2 * k] = stage + (size_t)(r - c0) * p.seg[0].row_bytes;
-            ty[2 * k] = p.seg[0].type;
-            ur[k] = r;
-          }
-        }
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int ps = 0; ps < npass; ps++) {
-          const int blk = ps * 8 + bl;
-          if (blk < p.nb) {
-            ActSlice A;
-            load_slice(act[b], blk, t, A);
-#pragma unroll
-            for (int k = 0; k < 4; k++)
-              if (va[k]) acc[k] += quarter_dot(ty[k], rp[k], p.nb, blk, t, A);
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-          if (!va[k]) continue;  // warp-uniform
-#pragma unroll
-          for (int off = 16; off >= 1; off >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
-        }
-        if (lane != 0) continue;
-#pragma unroll
-        for (int k = 0; k < 2; k++) {
-          if (!va[2 * k]) continue;
-          const float d0 = acc[2 * k], d1 = acc[2 * k + 1];
-          const int r = ur[k];
-          if (MODE == MODE_QKV) {
-            const int pos = p.pos[b];
-            const int half = p.hd >> 1;
-            if (useg[k] < 2) {
-              const int rr = useg[k] == 0 ? r : r - p.qn;
-              const int i2 = (rr % p.hd) >> 1;
-              const float cs = p.cos_t[(size_t)pos * half + i2];
-              const float sn = p.sin_t[(size_t)pos * half + i2];
-              // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
-              const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
-              const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
-              if (useg[k] == 0) {
-                *reinterpret_cast<float2*>(p.out + (size_t)b * p.out_stride + r) = make_float2(o0, o1);
-              } else {
-                const int kvh = rr / p.hd, dd = rr % p.hd;
-                const int64_t idx = (int64_t)b * p.kv_seq_stride + ((int64_t)kvh * p.max_seq + pos) * p.hd + dd;
-                store_kv(p.kc, p.kv_f16, idx, o0, o1);
-              }
-            } else {
-              const int rv = r - p.qn - p.kn;
-              const int kvh = rv / p.hd, dd = rv % p.hd;
-              const int64_t idx = (int64_t)b * p.kv_seq_stride + ((int64_t)kvh * p.max_seq + pos) * p.hd + dd;
-              store_kv(p.vc, p.kv_f16, idx, d0, d1);
-            }
-          } else if (MODE == MODE_GATEUP) {
-            // candle: silu(v) = v / (1 + exp(-v)); then * up
-            const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
-            p.out[(size_t)b * p.out_stride + r] = __fmul_rn(sl, d1);
-          } else {
-            float* o = p.out + (size_t)b * p.out_stride + r;
-            if (MODE == MODE_RESID) *o = __fadd_rn(d0, *o);
-            else *o = d0;
-            if (MODE == MODE_HEAD && am_better(d0, r, best_v[b], best_i[b])) {
-              best_v[b] = d0;
-              best_i[b] = r;
-            }
-          }
-        }
-      }
-    }
+#pragma unroll 1
+    for (int b = 0; b < NB; b++)
+      chunk_units<MODE>(MvCtx{p, b}, stage, c0, c1, parts, np, act[b], warp, MV_WARPS, lane, best_v[b],
+                        best_i[b]);
     __syncthreads();
     if (tid == 0 && c + p.ns < nchunks) {
       fence_proxy_async();

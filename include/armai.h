@@ -58,7 +58,9 @@ typedef struct armai_llama_opts {
   int32_t tp_size;      /* tensor-parallel degree; default 1 */
   int32_t tp_rank;      /* this process's rank in the TP group */
   const void* tp_unique_id; /* ncclUniqueId bytes (128), same on every rank */
-  int32_t reserved[8];
+  int32_t decode_kernel;/* 0: one persistent kernel per decode step (default);
+                           1: one kernel per operation (PDL chain) */
+  int32_t reserved[7];
 } armai_llama_opts;
 
 /* Fill `o` with the defaults above. */
@@ -135,6 +137,22 @@ ARMAI_API int armai_llama_bench_decode(armai_llama* m, int32_t n_steps, float* m
  * launches read whatever activations are resident; results are discarded. */
 ARMAI_API int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t rounds, float* ms_per_launch,
                                        int64_t* bytes_per_launch);
+
+/* Phase timeline of one decode step of the persistent decode kernel (no
+ * reference counterpart; the reference only times prefill and decode as a
+ * whole, native/arm_ai_nif/src/llama_candle.rs:83-130). Runs one step from
+ * the current state and writes, for phase p (in kernel order: per layer
+ * q/k/v, attention, attn_output, gate/up, ffn_down; then the head) and CTA c,
+ * ten globaltimer stamps in ns at out[(p * n_ctas + c) * 10 + s]:
+ * s = 0 phase start, 1 activation built, 2 phase done, 3 weight producer
+ * issued the phase's first copy, 4 first copy landed, 5 first chunk
+ * computed, 6 activation loaded, 7 rms scale known, 8 / 9 first row unit's
+ * dot products / epilogue done (0 where a phase has no such step). A last
+ * row (p = number of phases) holds each CTA's kernel entry in s = 0 and, for
+ * the CTA that wrote the step's token, that moment in s = 1. `cap` is the
+ * capacity of `out` in stamps. */
+ARMAI_API int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t cap, int32_t* n_phases,
+                                       int32_t* n_ctas);
 
 /* ------------------------------------------------------------------ */
 /* Primitive NIFs (nx_arm building blocks). Host buffers in, caller-owned  */

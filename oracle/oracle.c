@@ -493,10 +493,29 @@ void orc_llama_free(orc_llama* m) {
 
 /* candle-nn 0.8.4 ops.rs RmsNorm::cpu_fwd: sum2 = sum(v*v) (sequential f32),
  * m = sqrt(sum2/dim + eps), y = x / m * alpha. */
+/* Sensitivity probe (tests only, not candle's arithmetic): 1 = accumulate
+ * the rmsnorm sum of squares in f64; 2 / 3 = move the rms scale m one ulp
+ * up / down; 4 = sum the squares in reverse order.
+ * Either moves the normalised values by about one ulp, which is what the
+ * CUDA path's different f32 summation orders do; how far the logits then
+ * move is the model's own sensitivity. */
+static int g_norm_variant = 0;
+void orc_set_norm_variant(int v) { g_norm_variant = v; }
+
 static void rms_norm_row(const float* x, const float* alpha, int dim, float eps, float* y) {
   float sum2 = -0.0f;
-  for (int i = 0; i < dim; i++) sum2 += x[i] * x[i];
+  if (g_norm_variant == 1) {
+    double s = 0.0;
+    for (int i = 0; i < dim; i++) s += (double)x[i] * (double)x[i];
+    sum2 = (float)s;
+  } else if (g_norm_variant == 4) {
+    for (int i = dim - 1; i >= 0; i--) sum2 += x[i] * x[i];
+  } else {
+    for (int i = 0; i < dim; i++) sum2 += x[i] * x[i];
+  }
   float mm = sqrtf(sum2 / (float)dim + eps);
+  if (g_norm_variant == 2) mm = nextafterf(mm, INFINITY);
+  if (g_norm_variant == 3) mm = nextafterf(mm, 0.0f);
   for (int i = 0; i < dim; i++) y[i] = x[i] / mm * alpha[i];
 }
 

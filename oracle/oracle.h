@@ -101,6 +101,14 @@ int orc_llama_generate(orc_llama* m, const uint32_t* prompt, int n_prompt, int m
 uint32_t orc_argmax(const float* v, int64_t n);
 const char* orc_last_error(void);
 void orc_set_threads(int n);
+/* Test perturbation, not the reference's arithmetic: v = 1 accumulates
+ * rms_norm's sum of squares in f64, v = 2 / 3 moves its rms scale one ulp
+ * up / down, v = 4 sums the squares in reverse order.
+ * The change either causes in a model's logits is the model's sensitivity to
+ * last-bit f32 differences (activation quantisation rounds a value the other
+ * way once in a while and the model carries that forward); parity tests size
+ * their bound by it. v = 0 is the restatement of candle. Process-wide. */
+void orc_set_norm_variant(int v);
 int orc_get_threads(void);
 
 /* ---- reference primitive kernels (shape_ops.rs, x86 scalar paths) ---- */

@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
             "orc_argmax": (c_uint32, [V, I64]),
             "orc_last_error": (c_char_p, []),
             "orc_set_threads": (None, [c_int]),
+            "orc_set_norm_variant": (None, [c_int]),
             "orc_get_threads": (c_int, []),
             "orc_int8_matmul_f32": (c_int, [V, V, c_float, V, I64, I64, I64, V]),
             "orc_int8_matmul_f32_per_token": (c_int, [V, V, V, V, I64, I64, I64, V]),
@@ -82,6 +83,24 @@ def check(rc):
 
 def set_threads(n: int) -> None:
     lib().orc_set_threads(int(n))
+
+
+class norm_perturbed:
+    """Context manager: a last-bit perturbation of rms_norm inside the block
+    (orc_set_norm_variant; variant 1 = f64 sum of squares, 2 = rms scale one
+    ulp up). For measuring a model's own sensitivity, not the reference's
+    arithmetic."""
+
+    def __init__(self, variant: int = 2):
+        self.variant = variant
+
+    def __enter__(self):
+        lib().orc_set_norm_variant(self.variant)
+        return self
+
+    def __exit__(self, *exc):
+        lib().orc_set_norm_variant(0)
+        return False
 
 
 # ---------------------------------------------------------------- k-quants
