@@ -140,30 +140,6 @@ __device__ __forceinline__ bool mk_wait(uint64_t* bar, uint32_t parity, uint32_t
   return false;
 }
 
-template <int MODE>
-__device__ __forceinline__ int mk_parts(const MkPhase& ph, int c0, int c1, Part (&parts)[3]) {
-  int n = 0;
-  uint32_t off = 0;
-  if (MODE == MODE_QKV) {
-    int sb = 0;
-    for (int s = 0; s < ph.nseg; s++) {
-      const int se = sb + ph.seg[s].rows;
-      const int lo = max(c0, sb), hi = min(c1, se);
-      if (lo < hi) {
-        parts[n++] = Part{s, lo - sb, hi - sb, off};
-        off += (uint32_t)(hi - lo) * ph.seg[s].row_bytes;
-      }
-      sb = se;
-    }
-  } else if (MODE == MODE_GATEUP) {
-    parts[n++] = Part{0, c0, c1, 0};
-    parts[n++] = Part{1, c0, c1, (uint32_t)(c1 - c0) * ph.seg[0].row_bytes};
-  } else {
-    parts[n++] = Part{0, c0, c1, 0};
-  }
-  return n;
-}
-
 __device__ __forceinline__ int mode_of(int kind) {
   return kind == PH_QKV ? MODE_QKV : kind == PH_GATEUP ? MODE_GATEUP : kind == PH_HEAD ? MODE_HEAD
                                                                                      : MODE_RESID;
@@ -194,19 +170,11 @@ __device__ void mk_producer(const MkParams& p, uint8_t* smem) {
       if (sidx >= p.ns && !mk_wait(&empty[s], (uint32_t)(((sidx / p.ns) - 1) & 1), p.err)) return;
       if (c0 == r0) mk_stamp(p, i, 3);
       Part parts[3];
-      const int n = mode == MODE_QKV ? mk_parts<MODE_QKV>(ph, c0, c1, parts)
-                    : mode == MODE_GATEUP ? mk_parts<MODE_GATEUP>(ph, c0, c1, parts)
-                                          : mk_parts<MODE_RESID>(ph, c0, c1, parts);
-      uint32_t total = 0;
-      for (int k = 0; k < n; k++) total += (uint32_t)(parts[k].hi - parts[k].lo) * ph.seg[parts[k].seg].row_bytes;
-      uint8_t* stage = smem + (size_t)s * MK_STAGE;
+      if (mode == MODE_QKV) make_parts<MODE_QKV>(ph.seg, ph.nseg, c0, c1, parts);
+      else if (mode == MODE_GATEUP) make_parts<MODE_GATEUP>(ph.seg, ph.nseg, c0, c1, parts);
+      else make_parts<MODE_RESID>(ph.seg, ph.nseg, c0, c1, parts);
       fence_proxy_async();
-      mbar_expect_tx(&full[s], total);
-      for (int k = 0; k < n; k++) {
-        const Seg& sg = ph.seg[parts[k].seg];
-        bulk_g2s(stage + parts[k].off, sg.w + (int64_t)parts[k].lo * sg.row_bytes,
-                 (uint32_t)(parts[k].hi - parts[k].lo) * sg.row_bytes, &full[s], pol);
-      }
+      issue_parts(ph.seg, parts, smem + (size_t)s * MK_STAGE, &full[s], pol);
       sidx++;
     }
   }
@@ -416,9 +384,9 @@ __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int p
     if (!mk_wait(&full[s], (uint32_t)((cidx / p.ns) & 1), p.err)) return false;
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
     Part parts[3];
-    const int np = mk_parts<MODE>(ph, c0, c1, parts);
-    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0}, smem + (size_t)s * MK_STAGE, c0, c1, parts, np, act, cw, MK_CW,
-                      lane, best_v, best_i);
+    make_parts<MODE>(ph.seg, ph.nseg, c0, c1, parts);
+    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw,
+                      MK_CW, lane, best_v, best_i);
     __syncwarp();
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
     if (lane == 0) mbar_arrive(&empty[s]);

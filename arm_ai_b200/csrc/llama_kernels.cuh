@@ -152,48 +152,59 @@ __host__ __device__ inline MvSmem mv_smem_layout(int ns, uint32_t stage_bytes, i
 // ---------------------------------------------------------------------------
 // Chunk geometry: which bytes of which segment land where in a stage.
 // ---------------------------------------------------------------------------
+// parts[s] covers segment s (rows [lo, hi), segment-local, possibly empty)
+// at byte `off` of the stage. Fixed slots, so every index is a compile-time
+// constant and the array stays in registers.
 struct Part {
-  int seg, lo, hi;   // rows [lo, hi) of segment `seg` (segment-local)
-  uint32_t off;      // byte offset in the stage
+  int lo, hi;
+  uint32_t off;
 };
 
 template <int MODE>
-__device__ __forceinline__ int chunk_parts(const MvParams& p, int c0, int c1, Part (&parts)[3]) {
-  int n = 0;
-  uint32_t off = 0;
+__device__ __forceinline__ void make_parts(const Seg* seg, int nseg, int c0, int c1, Part (&parts)[3]) {
   if (MODE == MODE_QKV) {
     int sb = 0;
-    for (int s = 0; s < p.nseg; s++) {
-      const int se = sb + p.seg[s].rows;
-      const int lo = max(c0, sb), hi = min(c1, se);
-      if (lo < hi) {
-        parts[n++] = Part{s, lo - sb, hi - sb, off};
-        off += (uint32_t)(hi - lo) * p.seg[s].row_bytes;
-      }
+    uint32_t off = 0;
+#pragma unroll
+    for (int s = 0; s < 3; s++) {
+      const int rows = s < nseg ? seg[s].rows : 0;
+      const int se = sb + rows;
+      const int lo = min(max(c0, sb), se), hi = max(lo, min(c1, se));
+      parts[s] = Part{lo - sb, hi - sb, off};
+      off += (uint32_t)(hi - lo) * (s < nseg ? (uint32_t)seg[s].row_bytes : 0u);
       sb = se;
     }
   } else if (MODE == MODE_GATEUP) {
-    parts[n++] = Part{0, c0, c1, 0};
-    parts[n++] = Part{1, c0, c1, (uint32_t)(c1 - c0) * p.seg[0].row_bytes};
+    parts[0] = Part{c0, c1, 0};
+    parts[1] = Part{c0, c1, (uint32_t)(c1 - c0) * seg[0].row_bytes};
+    parts[2] = Part{0, 0, 0};
   } else {
-    parts[n++] = Part{0, c0, c1, 0};
+    parts[0] = Part{c0, c1, 0};
+    parts[1] = Part{0, 0, 0};
+    parts[2] = Part{0, 0, 0};
   }
-  return n;
+}
+
+// One bulk copy per non-empty part, all completing on `bar`.
+__device__ __forceinline__ void issue_parts(const Seg* seg, const Part (&parts)[3], uint8_t* stage,
+                                            uint64_t* bar, uint64_t pol) {
+  uint32_t total = 0;
+#pragma unroll
+  for (int k = 0; k < 3; k++) total += (uint32_t)(parts[k].hi - parts[k].lo) * seg[k].row_bytes;
+  mbar_expect_tx(bar, total);
+#pragma unroll
+  for (int k = 0; k < 3; k++)
+    if (parts[k].hi > parts[k].lo)
+      bulk_g2s(stage + parts[k].off, seg[k].w + (int64_t)parts[k].lo * seg[k].row_bytes,
+               (uint32_t)(parts[k].hi - parts[k].lo) * seg[k].row_bytes, bar, pol);
 }
 
 template <int MODE>
 __device__ __forceinline__ void issue_chunk(const MvParams& p, int c0, int c1, uint8_t* stage,
                                             uint64_t* bar, uint64_t pol) {
   Part parts[3];
-  const int n = chunk_parts<MODE>(p, c0, c1, parts);
-  uint32_t total = 0;
-  for (int i = 0; i < n; i++) total += (uint32_t)(parts[i].hi - parts[i].lo) * p.seg[parts[i].seg].row_bytes;
-  mbar_expect_tx(bar, total);
-  for (int i = 0; i < n; i++) {
-    const Seg& s = p.seg[parts[i].seg];
-    bulk_g2s(stage + parts[i].off, s.w + (int64_t)parts[i].lo * s.row_bytes,
-             (uint32_t)(parts[i].hi - parts[i].lo) * s.row_bytes, bar, pol);
-  }
+  make_parts<MODE>(p.seg, p.nseg, c0, c1, parts);
+  issue_parts(p.seg, parts, stage, bar, pol);
 }
 
 // ---------------------------------------------------------------------------
@@ -287,27 +298,21 @@ __device__ __forceinline__ void store_kv(void* base, int kv_f16, int64_t idx, fl
 // Ctx supplies the segment table and the epilogue's parameters through
 // accessors, so that what a kernel keeps in its constant bank (its own launch
 // parameters) is read from there instead of occupying registers.
-template <int T0, int T1, bool ONEPASS>
+template <int T0, int T1>
 __device__ __forceinline__ void unit_dots(const uint8_t* p0, const uint8_t* p1, bool has1, int nb,
-                                          const ActQ8& act, const ActSlice& A0, int lane,
-                                          float& d0, float& d1) {
+                                          const ActQ8& act, int lane, float& d0, float& d1) {
   const int t = lane & 3, bl = lane >> 2;
   float a0 = 0.f, a1 = 0.f;
-  if (ONEPASS) {
-    if (bl < nb) {
-      a0 = quarter_dot_t<T0>(p0, nb, bl, t, A0);
-      if (has1) a1 = quarter_dot_t<T1>(p1, nb, bl, t, A0);
-    }
-  } else {
-    const int npass = (nb + 7) >> 3;
-    for (int ps = 0; ps < npass; ps++) {
-      const int blk = ps * 8 + bl;
-      if (blk < nb) {
-        ActSlice A;
-        load_slice(act, blk, t, A);
-        a0 += quarter_dot_t<T0>(p0, nb, blk, t, A);
-        if (has1) a1 += quarter_dot_t<T1>(p1, nb, blk, t, A);
-      }
+  const int npass = (nb + 7) >> 3;
+  for (int ps = 0; ps < npass; ps++) {
+    const int blk = ps * 8 + bl;
+    if (blk < nb) {
+      // the activation slice is re-read from shared memory per row pair:
+      // keeping it in registers across rows spilled elsewhere
+      ActSlice A;
+      load_slice(act, blk, t, A);
+      a0 += quarter_dot_t<T0>(p0, nb, blk, t, A);
+      if (has1) a1 += quarter_dot_t<T1>(p1, nb, blk, t, A);
     }
   }
 #pragma unroll
@@ -319,17 +324,11 @@ __device__ __forceinline__ void unit_dots(const uint8_t* p0, const uint8_t* p1, 
   d1 = a1;
 }
 
-// ONEPASS: K <= 2048, so each lane's activation slice is loaded once per
-// chunk and kept in registers for every row.
-template <int MODE, bool ONEPASS, class Ctx>
-__device__ __forceinline__ void chunk_units_p(const Ctx& cx, const uint8_t* stage, int c0, int c1,
-                                              const Part (&parts)[3], int np, const ActQ8& act,
-                                              int warp, int nwarps, int lane, float& best_v,
-                                              int& best_i) {
-  const int t = lane & 3, bl = lane >> 2;
+template <int MODE, class Ctx>
+__device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage, int c0, int c1,
+                                            const Part (&parts)[3], const ActQ8& act, int warp,
+                                            int nwarps, int lane, float& best_v, int& best_i) {
   const int nb = cx.nb();
-  ActSlice A0;
-  if (ONEPASS && bl < nb) load_slice(act, bl, t, A0);
   const int n = c1 - c0;
   const int nunits = MODE == MODE_GATEUP ? n : (n + 1) >> 1;
   for (int u = warp; u < nunits; u += nwarps) {
@@ -341,11 +340,8 @@ __device__ __forceinline__ void chunk_units_p(const Ctx& cx, const uint8_t* stag
       const int qn = cx.qn(), kn = cx.kn();
       si = r < qn ? 0 : (r < qn + kn ? 1 : 2);
       const int sb = si == 0 ? 0 : (si == 1 ? qn : qn + kn);
-      uint32_t off = parts[0].off;
-      int lo = parts[0].lo;
-#pragma unroll
-      for (int i = 1; i < 3; i++)
-        if (i < np && parts[i].seg == si) { off = parts[i].off; lo = parts[i].lo; }
+      const uint32_t off = si == 0 ? parts[0].off : (si == 1 ? parts[1].off : parts[2].off);
+      const int lo = si == 0 ? parts[0].lo : (si == 1 ? parts[1].lo : parts[2].lo);
       const Seg& sg = cx.seg(si);
       p0 = stage + off + (size_t)(r - sb - lo) * sg.row_bytes;
       p1 = p0 + sg.row_bytes;
@@ -365,12 +361,12 @@ __device__ __forceinline__ void chunk_units_p(const Ctx& cx, const uint8_t* stag
     }
     float d0, d1;
     if (MODE != MODE_GATEUP || ty0 == ty1) {  // both rows of one matrix
-      if (ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
-      else unit_dots<GGML_Q6_K, GGML_Q6_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+      if (ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K>(p0, p1, has1, nb, act, lane, d0, d1);
+      else unit_dots<GGML_Q6_K, GGML_Q6_K>(p0, p1, has1, nb, act, lane, d0, d1);
     } else if (ty0 == GGML_Q4_K) {
-      unit_dots<GGML_Q4_K, GGML_Q6_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+      unit_dots<GGML_Q4_K, GGML_Q6_K>(p0, p1, has1, nb, act, lane, d0, d1);
     } else {
-      unit_dots<GGML_Q6_K, GGML_Q4_K, ONEPASS>(p0, p1, has1, nb, act, A0, lane, d0, d1);
+      unit_dots<GGML_Q6_K, GGML_Q4_K>(p0, p1, has1, nb, act, lane, d0, d1);
     }
     if (lane != 0) continue;
     if (u == 0) cx.stamp(8);
@@ -417,16 +413,6 @@ __device__ __forceinline__ void chunk_units_p(const Ctx& cx, const uint8_t* stag
     }
     if (u == 0) cx.stamp(9);
   }
-}
-
-template <int MODE, class Ctx>
-__device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage, int c0, int c1,
-                                            const Part (&parts)[3], int np, const ActQ8& act, int warp,
-                                            int nwarps, int lane, float& best_v, int& best_i) {
-  if (cx.nb() <= 8)
-    chunk_units_p<MODE, true>(cx, stage, c0, c1, parts, np, act, warp, nwarps, lane, best_v, best_i);
-  else
-    chunk_units_p<MODE, false>(cx, stage, c0, c1, parts, np, act, warp, nwarps, lane, best_v, best_i);
 }
 
 // Context of k_matvec: its launch parameters and the sequence index.
@@ -502,10 +488,10 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     if (__syncthreads_or(!ok)) return;
     const uint8_t* stage = stages + (size_t)s * p.stage_bytes;
     Part parts[3];
-    const int np = chunk_parts<MODE>(p, c0, c1, parts);
+    make_parts<MODE>(p.seg, p.nseg, c0, c1, parts);
 #pragma unroll 1
     for (int b = 0; b < NB; b++)
-      chunk_units<MODE>(MvCtx{p, b}, stage, c0, c1, parts, np, act[b], warp, MV_WARPS, lane, best_v[b],
+      chunk_units<MODE>(MvCtx{p, b}, stage, c0, c1, parts, act[b], warp, MV_WARPS, lane, best_v[b],
                         best_i[b]);
     __syncthreads();
     if (tid == 0 && c + p.ns < nchunks) {

@@ -6,9 +6,10 @@ on): TinyLlama-1.1B-architecture, Q4_K_M, batch 1, greedy; 32-token seeded
 prompt, 128 new tokens. A "step" is one generation's decode phase: 127
 single-token decode steps after the prompt's prefill.
 
-  value  decode tokens/s, device-timed (CUDA events around back-to-back CUDA
-         graph replays; the prompt's prefill between steps is not timed),
-         summed over ranks / max rank time.
+  value  decode tokens/s, device-timed (CUDA events around back-to-back
+         launches of the persistent decode kernel, one per token; the
+         prompt's prefill between steps is not timed), summed over ranks /
+         max rank time.
   e2e    the same metric through the C ABI call (armai_llama_generate) with
          host buffers: prompt H2D, every token D2H to the host for the stop
          check, measured the way the reference measures it
@@ -145,6 +146,18 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def profiled_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/<kernel>_tinyllama_b1.md, line "dram_bytes_per_launch = N")."""
+    import re
+    try:
+        with open(os.path.join(ROOT, "profiles", f"{kernel}_tinyllama_b1.md")) as f:
+            m = re.search(r"dram_bytes_per_launch = (\d+)", f.read())
+        return int(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
 def measured_peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -247,17 +260,29 @@ def run_armai(args, d):
     e2e_rank = e2e_tok * 1e6 / max(e2e_dec, 1)
     e2e_total = d.sum(e2e_rank)
 
-    # roofline of the dominant kernel (gate/up matvec, cycled over the layers)
-    kern = {}
-    for kind in ("gateup", "ffn_down", "qkv", "attn_output", "head"):
-        kern[kind] = native.llama_bench_kernel(gpu, kind, rounds=5)
-    ms_k, bytes_k = kern["gateup"]
+    # Roofline of the dominant kernel. With the persistent decode kernel the
+    # whole decode step is one launch: its algorithmic bytes are the step's
+    # weight bytes plus the KV cache it reads (average context of the timed
+    # generation), its duration the device time per step measured above.
     peak, peak_kind = measured_peaks()
-    achieved = bytes_k / (ms_k * 1e-3) / 1e9
     bytes_tok = info.weight_bytes
-    kv_bytes = 2 * info.n_layer * info.n_head_kv * info.head_dim * (2 if info.kv_f16 else 4) * \
-        (PROMPT + (PROMPT + n_dec)) / 2
-    ws_gbs = (bytes_tok + kv_bytes) * (value / d.world) / 1e9
+    kv_row = 2 * info.n_layer * info.n_head_kv * info.head_dim * (2 if info.kv_f16 else 4)
+    kv_bytes = kv_row * (PROMPT + 1 + PROMPT + n_dec) / 2
+    step_s = max_s / (args.steps * n_dec)
+    ws_gbs = (bytes_tok + kv_bytes) / step_s / 1e9
+    per_op = {}
+    for kind in ("gateup", "ffn_down", "qkv", "attn_output", "head"):
+        m_, b_ = native.llama_bench_kernel(gpu, kind, rounds=5)
+        per_op[kind] = {"us": m_ * 1e3, "gb_s": b_ / (m_ * 1e-3) / 1e9}
+    if info.n_kernels_per_step == 1:
+        kname = "k_decode_mega"
+        achieved = ws_gbs
+        traffic = profiled_traffic(kname)
+    else:
+        kname = "k_matvec_gateup"
+        ms_k, bytes_k = native.llama_bench_kernel(gpu, "gateup", rounds=5)
+        achieved = bytes_k / (ms_k * 1e-3) / 1e9
+        traffic = None
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(path, prompt)
@@ -272,19 +297,22 @@ def run_armai(args, d):
                                    f"tokens ({n_dec} timed decode steps per step)",
                        "arch": "22 layers, hidden 2048, FFN 5632, 32/4 heads, head_dim 64, vocab 32000",
                        "l2": f"inputs larger than L2: {bytes_tok / 1e6:.0f} MB of weights streamed per token",
-                       "timed": "decode graph replays on device (CUDA events); prefill between steps untimed",
+                       "timed": "decode steps back to back on device (CUDA events); prefill between steps untimed",
                        "parallelism": f"replicas x{d.world}" if d.world > 1 else "1 GPU"},
             "weight_stream": {"gb_s_per_gpu": ws_gbs, "frac_of_hbm": ws_gbs / peak,
                               "bytes_per_token": bytes_tok + kv_bytes, "peak_gbs": peak, "peak_source": peak_kind},
+            "decode_kernel": kname,
             "e2e": {"value": e2e_total, "unit": "tokens/s",
                     "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": MAX_NEW * 4,
                     "wall_tokens_per_s_incl_prefill": e2e_tok / max(e2e_wall, 1e-9) * d.world,
                     "prefill_tokens_per_s": PROMPT * 1e6 / max(pre_us_all / max(1, args.steps), 1)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "kernel": "k_matvec<MODE_GATEUP,1>",
-                         "peak_source": peak_kind,
-                         "per_kernel_gbs": {k: b / (m_ * 1e-3) / 1e9 for k, (m_, b) in kern.items()},
-                         "per_kernel_us": {k: m_ * 1e3 for k, (m_, b) in kern.items()}},
+                         "frac": achieved / peak, "traffic": traffic, "kernel": kname,
+                         "algorithmic_bytes_per_launch": bytes_tok + kv_bytes,
+                         "launch_us": step_s * 1e6, "peak_source": peak_kind,
+                         "traffic_source": "profiles/k_decode_mega_tinyllama_b1.md (ncu dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum, one launch)" if traffic else None,
+                         "per_op_kernels": per_op},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "gpu_launches": int(args.steps * n_dec * info.n_kernels_per_step * d.world),
