@@ -207,12 +207,13 @@ __device__ __forceinline__ bool mk_wait_grid(const MkParams& p, int ctid, unsign
 }
 
 // Values [8 lane, 8 lane + 8) of super-block j of the current token's
-// embedding row (BlockQ4K / BlockQ6K::to_float). Kept out of line: it runs
-// once per token and would otherwise crowd the prologue's registers.
+// embedding row (BlockQ4K / BlockQ6K::to_float). Inlined: out of line, the
+// returned struct went through local memory and dragged the prologue's
+// value array there with it.
 struct F8 {
   float v[8];
 };
-__device__ __noinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, int nb) {
+__device__ __forceinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, int nb) {
   F8 out;
   const uint32_t tok = min(__ldcg(p.token), (uint32_t)(0x7fffffff));
   const uint8_t* row = p.embd + (int64_t)tok * p.embd_row_bytes;
