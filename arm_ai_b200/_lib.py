@@ -85,6 +85,8 @@ _SIGS = {
                                           c_int64, c_void_p]),
     "armai_dev_int4_gemv_q4_x_q8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                             c_int64, c_void_p]),
+    "armai_dev_int4_gemv_q4_x_q8_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                            c_int64, c_void_p]),
     "armai_dev_int4_gemv_f16s": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                                          c_void_p]),
     "armai_dev_rmsnorm_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float,

@@ -10,6 +10,7 @@
 // tolerance.
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cstring>
 #include <string>
 
@@ -685,6 +686,59 @@ int q4q8_dev_alloc(const float* a, const uint8_t* w_packed, const SCALE_T* w_sca
 extern "C" int armai_dev_int4_gemv_q4_x_q8(const float* a, const uint8_t* w_packed, const float* w_scales,
                                            float* out, int64_t n, int64_t k, void* stream) {
   return q4q8_dev_alloc<float>(a, w_packed, w_scales, out, n, k, (cudaStream_t)stream);
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of armai_dev_int4_gemv_q4_x_q8: the stage-1 scratch
+// (K int8 activations, then K/32 f32 group scales) is a file-scope device
+// array sized for the kernel's largest K, so a call makes no allocation.
+// Nothing in it needs to start at zero: stage 1 writes every byte stage 2
+// reads. Calls on one device share it, so they must not overlap in time.
+// ---------------------------------------------------------------------------
+constexpr int64_t Q4Q8_NOALLOC_MAX_K = 32LL * 32 * MAX_GROUPS_PER_LANE;  // 16384
+static __device__ __align__(256) uint8_t g_q4q8_scratch[Q4Q8_NOALLOC_MAX_K + Q4Q8_NOALLOC_MAX_K / 32 * 4];
+
+namespace {
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::atomic<void*> g_q4q8_scratch_ptr[NOALLOC_MAX_DEVICES];
+
+// Device address of this device's copy of the scratch; looked up once per
+// device (the first call, which may also load the module).
+int q4q8_scratch(uint8_t** out) {
+  int dev = 0;
+  ARMAI_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
+    return fail(ARMAI_E_INVALID, "int4_gemv_q4_x_q8_noalloc: device ordinal " + std::to_string(dev) +
+                                     " beyond " + std::to_string(NOALLOC_MAX_DEVICES));
+  void* p = g_q4q8_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_q4q8_scratch);
+    if (e != cudaSuccess)
+      return cuda_fail(e, "cudaGetSymbolAddress(g_q4q8_scratch)", __FILE__, __LINE__);
+    g_q4q8_scratch_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = static_cast<uint8_t*>(p);
+  return ARMAI_OK;
+}
+}  // namespace
+
+extern "C" int armai_dev_int4_gemv_q4_x_q8_noalloc(const float* a, const uint8_t* w_packed,
+                                                   const float* w_scales, float* out, int64_t n, int64_t k,
+                                                   void* stream) {
+  if (k <= 0 || k % 32)
+    return fail(ARMAI_E_INVALID, "int4_gemv_q4_x_q8_noalloc: K=" + std::to_string(k) +
+                                     " must be a positive multiple of 32");
+  if (k > Q4Q8_NOALLOC_MAX_K)
+    return fail(ARMAI_E_RANGE, "int4_gemv_q4_x_q8_noalloc: K=" + std::to_string(k) +
+                                   " exceeds the static scratch (K <= " + std::to_string(Q4Q8_NOALLOC_MAX_K) +
+                                   "); use armai_dev_int4_gemv_q4_x_q8");
+  if (n < 0) return fail(ARMAI_E_INVALID, "int4_gemv_q4_x_q8_noalloc: negative N");
+  if (!n) return ARMAI_OK;
+  uint8_t* scratch = nullptr;
+  ARMAI_TRY(q4q8_scratch(&scratch));
+  int8_t* aq = reinterpret_cast<int8_t*>(scratch);
+  float* as = reinterpret_cast<float*>(scratch + k);  // k % 32 == 0 keeps this 4-byte aligned
+  return q4q8_dev<float>(a, w_packed, w_scales, out, n, k, aq, as, (cudaStream_t)stream);
 }
 
 extern "C" int armai_dev_int4_gemv_f16s(const float* a, const uint8_t* w_packed, const uint16_t* w_scales,

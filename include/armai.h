@@ -231,6 +231,20 @@ ARMAI_API int armai_dev_int4_matmul_f32(const float* a, const uint8_t* w_packed,
                               float* out, int64_t m, int64_t n, int64_t k, void* stream);
 ARMAI_API int armai_dev_int4_gemv_q4_x_q8(const float* a, const uint8_t* w_packed, const float* w_scales,
                                 float* out, int64_t n, int64_t k, void* stream);
+/* No-allocation variant of armai_dev_int4_gemv_q4_x_q8 (no reference
+ * counterpart: the reference's NIF allocates its Vec scratch on the CPU
+ * heap, native/arm_ai_nif/src/shape_ops.rs:2923-3028). For callers that must
+ * not allocate device memory on the call path, e.g. a serving loop that has
+ * reserved the device's memory up front and cannot afford an allocation's
+ * latency or its failure in mid-step. Same arguments and results as
+ * armai_dev_int4_gemv_q4_x_q8; the stage-1 scratch is a static device array
+ * sized for K <= 16384 (ARMAI_E_RANGE above that). Calls on one device share
+ * that scratch: they must not overlap (use one stream, or order them). The
+ * first call on each device looks the scratch up (and may load the module);
+ * make it before any stream capture. */
+ARMAI_API int armai_dev_int4_gemv_q4_x_q8_noalloc(const float* a, const uint8_t* w_packed,
+                                                  const float* w_scales, float* out, int64_t n, int64_t k,
+                                                  void* stream);
 /* BASELINE config 5's int4 variant: per-32-group f16 scales [N,K/32]. */
 ARMAI_API int armai_dev_int4_gemv_f16s(const float* a, const uint8_t* w_packed, const uint16_t* w_scales,
                              float* out, int64_t n, int64_t k, void* stream);
