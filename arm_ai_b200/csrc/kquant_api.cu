@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm_tc.cuh"
 #include "llama_kernels.cuh"
 
 using namespace armai;
@@ -185,6 +186,7 @@ int qmm_launch(const uint8_t* w, int type, int n, int k, int rb, const float* x,
   p.seg[0] = Seg{w, type, n, k / QK_K, rb};
   p.nseg = 1;
   p.total_rows = n;
+  p.nrows = NB;
   p.rows_per_cta = per;
   p.chunk_rows = chunk;
   p.ns = ns;
@@ -220,6 +222,44 @@ extern "C" int armai_qmatmul(const void* w, int type, size_t n, size_t k, const 
   uint32_t herr = 0;
   ARMAI_CUDA(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
   if (herr) return fail(ARMAI_E_DEVICE, "qmatmul: device error flag set");
+  ARMAI_CUDA(cudaMemcpy(out, dout.p, m * n * 4, cudaMemcpyDeviceToHost));
+  return ARMAI_OK;
+}
+
+extern "C" int armai_qgemm(const void* w, int type, size_t n, size_t k, const float* x, size_t m,
+                           const float* gamma, float eps, float* out) {
+  if (!w || !x || !out) return fail(ARMAI_E_INVALID, "qgemm: null argument");
+  if (k % QK_K || k > 16384) return fail(ARMAI_E_INVALID, "qgemm: K must be a multiple of 256, at most 16384");
+  if (!m || !n) return ARMAI_OK;
+  DevBuf dw, dx, dg, da, dout, derr;
+  int rb = 0;
+  ARMAI_TRY(upload_weights(w, type, n, k, dw, rb));
+  ARMAI_CUDA(cudaMalloc(&dx.p, m * k * 4));
+  ARMAI_CUDA(cudaMemcpy(dx.p, x, m * k * 4, cudaMemcpyHostToDevice));
+  if (gamma) {
+    ARMAI_CUDA(cudaMalloc(&dg.p, k * 4));
+    ARMAI_CUDA(cudaMemcpy(dg.p, gamma, k * 4, cudaMemcpyHostToDevice));
+  }
+  ARMAI_CUDA(cudaMalloc(&da.p, qgemm_a_bytes((int)m, (int)k)));
+  ARMAI_CUDA(cudaMalloc(&dout.p, m * n * 4));
+  ARMAI_CUDA(cudaMalloc(&derr.p, 4));
+  ARMAI_CUDA(cudaMemset(derr.p, 0, 4));
+  ARMAI_TRY(qgemm_act_launch((const float*)dx.p, (const float*)dg.p, eps, (int)m, (int)k, (uint8_t*)da.p, 0));
+  QgParams p;
+  std::memset(&p, 0, sizeof p);
+  p.a_tiles = (const uint8_t*)da.p;
+  p.m = (int)m;
+  p.n = (int)n;
+  p.k = (int)k;
+  p.seg[0] = QgSeg{(const uint8_t*)dw.p, type, (int)n, rb};
+  p.nseg = 1;
+  p.out = (float*)dout.p;
+  p.ldo = (int)n;
+  p.err = (uint32_t*)derr.p;
+  ARMAI_TRY(qgemm_launch(p, 0));
+  uint32_t herr = 0;
+  ARMAI_CUDA(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
+  if (herr) return fail(ARMAI_E_DEVICE, "qgemm: device error flag set");
   ARMAI_CUDA(cudaMemcpy(out, dout.p, m * n * 4, cudaMemcpyDeviceToHost));
   return ARMAI_OK;
 }

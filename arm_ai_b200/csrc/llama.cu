@@ -20,6 +20,7 @@ using namespace armai;
 namespace {
 
 constexpr int PREFILL_TILE = 8;       // tokens per prefill matvec launch
+constexpr int BATCH_NB = 16;          // sequences per batched-decode matvec launch
 
 constexpr int ATTN_TOK_PER_LAUNCH = 64;
 constexpr uint32_t STAGE_MAX = 44 * 1024;
@@ -95,6 +96,8 @@ struct armai_llama {
   // plans
   Plan pl_qkv1, pl_wo1, pl_gu1, pl_down1, pl_head1;
   Plan pl_qkvT, pl_woT, pl_guT, pl_downT;
+  Plan pl_qkvB, pl_woB, pl_guB, pl_downB, pl_headB;  // batched decode (max_batch > 1)
+  uint32_t* h_btok = nullptr;  // pinned [max_batch] tokens of a batched step
   size_t attn_smem = 0;
   int n_kernels_step = 0;
   cudaGraphExec_t graph = nullptr;
@@ -163,7 +166,8 @@ int set_smem_attr(size_t smem) {
 }
 
 template <int MODE, int NB>
-cudaError_t launch_mv(armai_llama* m, const Plan& pl, const MvParams& p) {
+cudaError_t launch_mv(armai_llama* m, const Plan& pl, MvParams p, int nrows = NB) {
+  p.nrows = nrows;
   return launch_k(k_matvec<MODE, NB>, dim3(pl.grid), dim3(MV_THREADS), pl.smem, m->stream,
                   m->use_pdl, p);
 }
@@ -190,11 +194,16 @@ void* kv_layer_ptr(armai_llama* m, void* base, int l) {
   return (uint8_t*)base + (size_t)l * m->kv_layer_stride * es;
 }
 
+// KV cache of sequence slot `seq` in layer l.
+void* kv_seq_ptr(armai_llama* m, void* base, int l, int seq) {
+  const size_t es = m->kv_f16 ? 2 : 4;
+  return (uint8_t*)kv_layer_ptr(m, base, l) + (size_t)seq * m->kv_seq_stride * es;
+}
+
 // ---- one layer's launches for NB tokens whose activations live at x/q/y/h ----
 template <int NB>
 cudaError_t launch_qkv(armai_llama* m, const Plan& pl, int l, const float* x, float* q,
-                       const int* pos, int64_t kv_seq_stride, void* kc_override = nullptr,
-                       void* vc_override = nullptr) {
+                       const int* pos, int64_t kv_seq_stride, int seq = 0, int nrows = NB) {
   const Layer& L = m->layers[l];
   MvParams p = base_params(m, pl);
   p.x = x;
@@ -210,16 +219,16 @@ cudaError_t launch_qkv(armai_llama* m, const Plan& pl, int l, const float* x, fl
   p.total_rows = L.wq.rows + L.wk.rows + L.wv.rows;
   p.out = q;
   p.out_stride = m->n_head * m->head_dim;
-  p.kc = kc_override ? kc_override : kv_layer_ptr(m, m->kc, l);
-  p.vc = vc_override ? vc_override : kv_layer_ptr(m, m->vc, l);
+  p.kc = kv_seq_ptr(m, m->kc, l, seq);
+  p.vc = kv_seq_ptr(m, m->vc, l, seq);
   p.kv_seq_stride = kv_seq_stride;
   p.pos = pos;
-  return launch_mv<MODE_QKV, NB>(m, pl, p);
+  return launch_mv<MODE_QKV, NB>(m, pl, p, nrows);
 }
 
 template <int NB>
 cudaError_t launch_resid(armai_llama* m, const Plan& pl, const DevMat& w, const float* in,
-                         float* x) {
+                         float* x, int nrows = NB) {
   MvParams p = base_params(m, pl);
   p.x = in;
   p.gamma = nullptr;
@@ -230,11 +239,12 @@ cudaError_t launch_resid(armai_llama* m, const Plan& pl, const DevMat& w, const 
   p.total_rows = w.rows;
   p.out = x;
   p.out_stride = m->n_embd;
-  return launch_mv<MODE_RESID, NB>(m, pl, p);
+  return launch_mv<MODE_RESID, NB>(m, pl, p, nrows);
 }
 
 template <int NB>
-cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x, float* h) {
+cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x, float* h,
+                          int nrows = NB) {
   const Layer& L = m->layers[l];
   MvParams p = base_params(m, pl);
   p.x = x;
@@ -247,11 +257,14 @@ cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x,
   p.total_rows = L.wg.rows;
   p.out = h;
   p.out_stride = m->n_ff;
-  return launch_mv<MODE_GATEUP, NB>(m, pl, p);
+  return launch_mv<MODE_GATEUP, NB>(m, pl, p, nrows);
 }
 
-cudaError_t launch_head(armai_llama* m, const float* x, const int* pos, int* pos_out) {
-  const Plan& pl = m->pl_head1;
+// Output norm + logits + argmax for `nrows` rows of x (plan pl_head1 for one
+// row, pl_headB for a batch): token[b] = argmax, pos_out[b] = pos[b] + 1.
+template <int NB>
+cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const int* pos, int* pos_out,
+                        uint32_t* token, int nrows = NB) {
   MvParams p = base_params(m, pl);
   p.x = x;
   p.gamma = m->out_norm;
@@ -265,18 +278,18 @@ cudaError_t launch_head(armai_llama* m, const float* x, const int* pos, int* pos
   p.am_val = m->am_val;
   p.am_idx = m->am_idx;
   p.counter = m->am_cnt;
-  p.token = m->d_token;
+  p.token = token;
   p.pos = pos;
   p.pos_out = pos_out;
-  return launch_mv<MODE_HEAD, 1>(m, pl, p);
+  return launch_mv<MODE_HEAD, NB>(m, pl, p, nrows);
 }
 
 cudaError_t launch_attn(armai_llama* m, int l, const float* q, float* y, const int* pos, int nb_tok,
-                        int64_t kv_seq_stride) {
+                        int64_t kv_seq_stride, int seq = 0) {
   AttnParams a;
   a.q = q;
-  a.kc = kv_layer_ptr(m, m->kc, l);
-  a.vc = kv_layer_ptr(m, m->vc, l);
+  a.kc = kv_seq_ptr(m, m->kc, l, seq);
+  a.vc = kv_seq_ptr(m, m->vc, l, seq);
   a.kv_seq_stride = kv_seq_stride;
   a.kv_f16 = m->kv_f16;
   a.pos = pos;
@@ -475,7 +488,7 @@ int enqueue_decode_step(armai_llama* m) {
     ARMAI_CUDA(launch_gateup<1>(m, m->pl_gu1, l, m->x, m->h));
     ARMAI_CUDA(launch_resid<1>(m, m->pl_down1, m->layers[l].wd, m->h, m->x));
   }
-  ARMAI_CUDA(launch_head(m, m->x, m->d_pos, m->d_pos));
+  ARMAI_CUDA(launch_head<1>(m, m->pl_head1, m->x, m->d_pos, m->d_pos, m->d_token));
   return ARMAI_OK;
 }
 
@@ -527,7 +540,10 @@ int ensure_prefill(armai_llama* m, int S) {
 // Integer path: the same Q8_K x Q4_K/Q6_K kernels as decode, over tiles of
 // PREFILL_TILE tokens (weights streamed once per tile), and the split-K
 // attention with per-token causal limits.
-int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S) {
+// Prompt of S tokens at positions 0..S-1 into sequence slot `seq` (its KV
+// cache); the head writes the first generated token to d_token[seq] and S to
+// d_pos[seq].
+int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) {
   ARMAI_TRY(ensure_prefill(m, S));
   uint32_t* ht = m->h_prompt;
   int* hp = reinterpret_cast<int*>(m->h_prompt + m->h_prompt_cap);
@@ -541,12 +557,12 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S) {
   for (int l = 0; l < m->n_layer; l++) {
     int t = 0;
     for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
-      ARMAI_CUDA(launch_qkv<PREFILL_TILE>(m, m->pl_qkvT, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0));
+      ARMAI_CUDA(launch_qkv<PREFILL_TILE>(m, m->pl_qkvT, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0, seq));
     for (; t < S; t++)
-      ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0));
+      ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0, seq));
     for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
       const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
-      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0));
+      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0, seq));
     }
     t = 0;
     for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
@@ -564,7 +580,33 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S) {
     for (; t < S; t++)
       ARMAI_CUDA(launch_resid<1>(m, m->pl_down1, m->layers[l].wd, m->pH + t * F, m->pX + t * E));
   }
-  ARMAI_CUDA(launch_head(m, m->pX + (size_t)(S - 1) * E, m->p_pos + (S - 1), m->d_pos));
+  ARMAI_CUDA(launch_head<1>(m, m->pl_head1, m->pX + (size_t)(S - 1) * E, m->p_pos + (S - 1), m->d_pos + seq,
+                            m->d_token + seq));
+  return ARMAI_OK;
+}
+
+// One greedy decode step for sequence slots 0..n-1: token d_token[b] at
+// position d_pos[b] of slot b's KV cache; writes the next token and position
+// back. Matvecs run BATCH_NB sequences per weight pass.
+int enqueue_batch_step(armai_llama* m, int n) {
+  const size_t E = m->n_embd, QN = (size_t)m->n_head * m->head_dim, F = m->n_ff;
+  ARMAI_CUDA(launch_embed(m, m->d_token, m->x, n));
+  for (int l = 0; l < m->n_layer; l++) {
+    const Layer& L = m->layers[l];
+    for (int g = 0; g < n; g += BATCH_NB)
+      ARMAI_CUDA(launch_qkv<BATCH_NB>(m, m->pl_qkvB, l, m->x + g * E, m->q + g * QN, m->d_pos + g,
+                                      m->kv_seq_stride, g, std::min(BATCH_NB, n - g)));
+    ARMAI_CUDA(launch_attn(m, l, m->q, m->y, m->d_pos, n, m->kv_seq_stride, 0));
+    for (int g = 0; g < n; g += BATCH_NB)
+      ARMAI_CUDA(launch_resid<BATCH_NB>(m, m->pl_woB, L.wo, m->y + g * QN, m->x + g * E, std::min(BATCH_NB, n - g)));
+    for (int g = 0; g < n; g += BATCH_NB)
+      ARMAI_CUDA(launch_gateup<BATCH_NB>(m, m->pl_guB, l, m->x + g * E, m->h + g * F, std::min(BATCH_NB, n - g)));
+    for (int g = 0; g < n; g += BATCH_NB)
+      ARMAI_CUDA(launch_resid<BATCH_NB>(m, m->pl_downB, L.wd, m->h + g * F, m->x + g * E, std::min(BATCH_NB, n - g)));
+  }
+  for (int g = 0; g < n; g += BATCH_NB)
+    ARMAI_CUDA(launch_head<BATCH_NB>(m, m->pl_headB, m->x + g * E, m->d_pos + g, m->d_pos + g, m->d_token + g,
+                                     std::min(BATCH_NB, n - g)));
   return ARMAI_OK;
 }
 
@@ -712,6 +754,7 @@ void free_model(armai_llama* m) {
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }
   if (m->h_tok) cudaFreeHost(m->h_tok);
+  if (m->h_btok) cudaFreeHost(m->h_btok);
   if (m->h_misc) cudaFreeHost(m->h_misc);
   if (m->h_prompt) cudaFreeHost(m->h_prompt);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -955,6 +998,23 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (!arc) arc = set_smem_attr<MODE_QKV, PREFILL_TILE>(m->pl_qkvT.smem);
   if (!arc) arc = set_smem_attr<MODE_RESID, PREFILL_TILE>(std::max(m->pl_woT.smem, m->pl_downT.smem));
   if (!arc) arc = set_smem_attr<MODE_GATEUP, PREFILL_TILE>(m->pl_guT.smem);
+  if (!arc && m->max_batch > 1) {
+    m->pl_qkvB = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
+    m->pl_woB = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, BATCH_NB, false, nsm, SMEM_LIMIT);
+    m->pl_guB = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
+    m->pl_downB = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, BATCH_NB, false, nsm, SMEM_LIMIT);
+    m->pl_headB = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
+    for (const Plan* pl : {&m->pl_qkvB, &m->pl_woB, &m->pl_guB, &m->pl_downB, &m->pl_headB})
+      if (pl->smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "model rows too wide for batched decode"); }
+    arc = set_smem_attr<MODE_QKV, BATCH_NB>(m->pl_qkvB.smem);
+    if (!arc) arc = set_smem_attr<MODE_RESID, BATCH_NB>(std::max(m->pl_woB.smem, m->pl_downB.smem));
+    if (!arc) arc = set_smem_attr<MODE_GATEUP, BATCH_NB>(m->pl_guB.smem);
+    if (!arc) arc = set_smem_attr<MODE_HEAD, BATCH_NB>(m->pl_headB.smem);
+    if (!arc) {
+      const cudaError_t he = cudaMallocHost(&m->h_btok, (size_t)m->max_batch * 4);
+      if (he != cudaSuccess) arc = cuda_fail(he, "cudaMallocHost", __FILE__, __LINE__);
+    }
+  }
   if (arc) { free_model(m); return arc; }
   m->attn_smem = attn_smem_floats(m->head_dim) * 4;
   m->n_kernels_step = 2 + 5 * m->n_layer;
@@ -1122,9 +1182,72 @@ extern "C" int armai_llama_generate_batch(armai_llama* m, const uint32_t* prompt
                                           size_t n_seq, size_t max_new, const uint32_t* stop, size_t n_stop,
                                           uint32_t* out, size_t* n_out, uint64_t* prefill_us,
                                           uint64_t* decode_us) {
-  (void)m; (void)prompts; (void)n_prompt; (void)n_seq; (void)max_new; (void)stop; (void)n_stop;
-  (void)out; (void)n_out; (void)prefill_us; (void)decode_us;
-  return fail(ARMAI_E_INVALID, "generate_batch: not implemented yet");
+  if (!m || (n_seq && (!n_prompt || !n_out)) || !prefill_us || !decode_us || (n_stop && !stop))
+    return fail(ARMAI_E_INVALID, "generate_batch: bad argument");
+  *prefill_us = *decode_us = 0;
+  for (size_t s = 0; s < n_seq; s++) n_out[s] = 0;
+  if (!n_seq || !max_new) return ARMAI_OK;
+  if (!out || !prompts) return fail(ARMAI_E_INVALID, "generate_batch: bad argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
+  if ((int64_t)n_seq > m->max_batch)
+    return fail(ARMAI_E_INVALID, "generate_batch: " + std::to_string(n_seq) +
+                                     " sequences but the model was loaded with max_batch " +
+                                     std::to_string(m->max_batch));
+  size_t off = 0;
+  for (size_t s = 0; s < n_seq; s++) {
+    for (size_t i = 0; i < n_prompt[s]; i++)
+      if (prompts[off + i] >= (uint32_t)m->n_vocab)
+        return fail(ARMAI_E_INVALID, "generate_batch: sequence " + std::to_string(s) + ": token id " +
+                                         std::to_string(prompts[off + i]) + " out of range for vocab " +
+                                         std::to_string(m->n_vocab));
+    if (n_prompt[s] && n_prompt[s] + max_new - 1 > (size_t)m->max_seq)
+      return fail(ARMAI_E_RANGE, "generate_batch: sequence " + std::to_string(s) + ": " +
+                                     std::to_string(n_prompt[s]) + " prompt + " + std::to_string(max_new) +
+                                     " new tokens exceed max_seq_len " + std::to_string(m->max_seq));
+    off += n_prompt[s];
+  }
+  ARMAI_CUDA(cudaSetDevice(m->device));
+  m->kv_len = -1;  // the single-sequence cache (slot 0) no longer continues
+  const int n = (int)n_seq;
+  // Prefill every sequence into its slot; empty prompts decode from token 0
+  // at position 0 and their outputs are discarded.
+  auto t0 = std::chrono::steady_clock::now();
+  ARMAI_CUDA(cudaMemsetAsync(m->d_token, 0, (size_t)n * 4, m->stream));
+  ARMAI_CUDA(cudaMemsetAsync(m->d_pos, 0, (size_t)n * 4, m->stream));
+  off = 0;
+  for (int s = 0; s < n; s++) {
+    if (n_prompt[s]) ARMAI_TRY(enqueue_prefill(m, prompts + off, (int)n_prompt[s], s));
+    off += n_prompt[s];
+  }
+  ARMAI_TRY(check_device_error(m));
+  auto t1 = std::chrono::steady_clock::now();
+  std::vector<char> done(n, 0);
+  int live = 0;
+  for (int s = 0; s < n; s++) live += (done[s] = n_prompt[s] == 0) ? 0 : 1;
+  auto record = [&]() {
+    for (int s = 0; s < n; s++) {
+      if (done[s]) continue;
+      const uint32_t t = m->h_btok[s];
+      out[(size_t)s * max_new + n_out[s]++] = t;
+      bool hit = n_out[s] >= max_new;
+      for (size_t k = 0; k < n_stop && !hit; k++) hit = stop[k] == t;
+      if (hit) { done[s] = 1; live--; }
+    }
+  };
+  ARMAI_CUDA(cudaMemcpyAsync(m->h_btok, m->d_token, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
+  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  record();
+  while (live > 0) {
+    ARMAI_TRY(enqueue_batch_step(m, n));
+    ARMAI_CUDA(cudaMemcpyAsync(m->h_btok, m->d_token, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
+    ARMAI_TRY(check_device_error(m));
+    record();
+  }
+  auto t2 = std::chrono::steady_clock::now();
+  *prefill_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(t1 - t0).count();
+  *decode_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(t2 - t1).count();
+  return ARMAI_OK;
 }
 
 extern "C" int armai_llama_bench_decode(armai_llama* m, int32_t n_steps, float* ms) {
@@ -1169,7 +1292,7 @@ extern "C" int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t ro
       case 3: bytes += (int64_t)L.wd.rows * L.wd.row_bytes;
               return launch_resid<1>(m, m->pl_down1, L.wd, m->h, m->x);
       case 4: bytes += (int64_t)m->output.rows * m->output.row_bytes;
-              return launch_head(m, m->x, m->d_pos, nullptr);
+              return launch_head<1>(m, m->pl_head1, m->x, m->d_pos, nullptr, m->d_token);
       default: return launch_attn(m, l, m->q, m->y, m->d_pos, 1, 0);
     }
   };

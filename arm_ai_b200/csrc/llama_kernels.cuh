@@ -105,6 +105,7 @@ struct MvParams {
   int K, nb;
   Seg seg[3];
   int nseg;
+  int nrows;           // activation rows (tokens / sequences) of this launch, <= NB
   int total_rows;      // QKV: q+k+v rows; GATEUP: rows of one of the pair; else rows
   int rows_per_cta, chunk_rows, ns;
   uint32_t stage_bytes;
@@ -233,7 +234,7 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
   const float* src = p.x;
   const bool norm = p.gamma != nullptr;
   if (norm) {
-    for (int job = warp; job < NB * nb; job += nw) {
+    for (int job = warp; job < p.nrows * nb; job += nw) {
       const int b = job / nb, j = job % nb;
       const float4* xr = reinterpret_cast<const float4*>(src + (size_t)b * K + j * QK_K + 8 * lane);
       const float4 x0 = xr[0], x1 = xr[1];
@@ -244,7 +245,7 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
       if (lane == 0) part[b * nb + j] = ss;
     }
     __syncthreads();
-    if (tid < NB) {
+    if (tid < p.nrows) {
       float sum2 = 0.f;
       for (int j = 0; j < nb; j++) sum2 += part[tid * nb + j];
       rms[tid] = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)K), p.eps));
@@ -254,7 +255,7 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
     __syncthreads();
   }
   const float* gs = reinterpret_cast<const float*>(smem + L.gamma);
-  for (int job = warp; job < NB * nb; job += nw) {
+  for (int job = warp; job < p.nrows * nb; job += nw) {
     const int b = job / nb, j = job % nb;
     const float4* xr = reinterpret_cast<const float4*>(src + (size_t)b * K + j * QK_K + 8 * lane);
     const float4 x0 = xr[0], x1 = xr[1];
@@ -490,7 +491,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     Part parts[3];
     make_parts<MODE>(p.seg, p.nseg, c0, c1, parts);
 #pragma unroll 1
-    for (int b = 0; b < NB; b++)
+    for (int b = 0; b < p.nrows; b++)
       chunk_units<MODE>(MvCtx{p, b}, stage, c0, c1, parts, act[b], warp, MV_WARPS, lane, best_v[b],
                         best_i[b]);
     __syncthreads();
@@ -507,7 +508,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     float* rv = reinterpret_cast<float*>(smem + L.red);
     int* ri = reinterpret_cast<int*>(rv + 32);
     __shared__ int s_last;
-    for (int b = 0; b < NB; b++) {
+    for (int b = 0; b < p.nrows; b++) {
       if (lane == 0) { rv[warp] = best_v[b]; ri[warp] = best_i[b]; }
       __syncthreads();
       if (tid == 0) {
@@ -528,7 +529,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
     __syncthreads();
     if (s_last) {
       __threadfence();
-      for (int b = warp; b < NB; b += MV_WARPS) {
+      for (int b = warp; b < p.nrows; b += MV_WARPS) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
         for (int i = lane; i < (int)gridDim.x; i += 32) {

@@ -6,6 +6,8 @@ checked bit for bit against the CPU oracle.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 
 from ._lib import check, load_cuda, ptr
@@ -38,4 +40,17 @@ def qmatmul(wtype: int, w_rows: np.ndarray, k: int, x: np.ndarray) -> np.ndarray
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
     out = np.empty((x.shape[0], w_rows.shape[0]), dtype=np.float32)
     check(load_cuda().armai_qmatmul(ptr(w_rows), wtype, w_rows.shape[0], k, ptr(x), x.shape[0], ptr(out)))
+    return out
+
+
+def qgemm(wtype: int, w_rows: np.ndarray, k: int, x: np.ndarray, gamma=None, eps: float = 1e-5) -> np.ndarray:
+    """Prefill tensor-core GEMM (armai_qgemm): x [m, k] f32 (rms-normalised
+    with gamma when given) quantised per token to Q8_K and expanded to f16,
+    times the f16-dequantised weight rows: [m, n] f32."""
+    w_rows = np.ascontiguousarray(w_rows, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    g = None if gamma is None else np.ascontiguousarray(gamma, dtype=np.float32)
+    out = np.empty((x.shape[0], w_rows.shape[0]), dtype=np.float32)
+    check(load_cuda().armai_qgemm(ptr(w_rows), wtype, w_rows.shape[0], k, ptr(x), x.shape[0], ptr(g),
+                                  ctypes.c_float(eps), ptr(out)))
     return out

@@ -116,6 +116,30 @@ def llama_candle_stream_op(model: LlamaResource, prompt, max_new: int, stop_toke
     return _generate(model, prompt, max_new, stop_tokens, on_token=lambda t: send(("llama_token", t)))
 
 
+def llama_generate_batch(model: LlamaResource, prompts, max_new: int, stop_tokens=()):
+    """Batched greedy decode of independent sequences (no
+    reference counterpart, the reference holds one cache per handle):
+    ([tokens per sequence], prefill_us, decode_us). Each sequence behaves as
+    one llama_candle_generate_op call; the model must be loaded with
+    max_batch >= len(prompts)."""
+    lib = load_cuda()
+    n = len(prompts)
+    lens = np.array([len(p) for p in prompts], dtype=np.uint64)
+    flat = _u32([t for p in prompts for t in p]) if lens.sum() else np.zeros(1, np.uint32)
+    stop = _u32(list(stop_tokens))
+    out = np.zeros(max(n * max_new, 1), dtype=np.uint32)
+    n_out = np.zeros(max(n, 1), dtype=np.uint64)
+    pre, dec = c_uint64(0), c_uint64(0)
+    try:
+        check(lib.armai_llama_generate_batch(model.handle, ptr(flat), ptr(lens), n, int(max_new), ptr(stop),
+                                             stop.size, ptr(out), ptr(n_out), ctypes.byref(pre),
+                                             ctypes.byref(dec)))
+    except ArmaiError as e:
+        raise NifError("candle generate: " + str(e)) from None
+    toks = [out[i * max_new: i * max_new + int(n_out[i])].tolist() for i in range(n)]
+    return toks, int(pre.value), int(dec.value)
+
+
 def llama_forward(model: LlamaResource, tokens, index_pos: int, want_logits: bool = True):
     """ModelWeights::forward(tokens, index_pos): (logits f32[n_vocab] | None, argmax)."""
     lib = load_cuda()
@@ -157,6 +181,6 @@ def llama_trace_decode(model: LlamaResource):
     return buf[: nph.value * nct.value * 10].reshape(nph.value, nct.value, 10)
 
 
-__all__ = ["llama_bench_kernel", "llama_trace_decode", "NifError", "LlamaResource", "llama_candle_load_op", "llama_candle_generate_op",
+__all__ = ["llama_bench_kernel", "llama_trace_decode", "llama_generate_batch", "NifError", "LlamaResource", "llama_candle_load_op", "llama_candle_generate_op",
            "llama_candle_stream_op", "llama_forward", "llama_bench_decode", "default_opts",
            "ArmaiError"]

@@ -275,6 +275,15 @@ ARMAI_API int armai_kquant_block_dots(const void* w, int type, size_t n, size_t 
 ARMAI_API int armai_qmatmul(const void* w, int type, size_t n, size_t k, const float* x, size_t m,
                   float* out);
 
+/* Test entry (no reference counterpart): the prefill tensor-core GEMM on
+ * host buffers. x [m][k] f32 (rms-normalised with gamma when not null),
+ * quantised per token to Q8_K and expanded to f16; w [n] rows of GGML
+ * Q4_K/Q6_K blocks dequantised to f16; out [m][n] = A W^T with f32
+ * accumulation (tcgen05). The reference computes the same product through
+ * QMatMul (llama_candle.rs:92-94) with integer Q8_K dots. */
+ARMAI_API int armai_qgemm(const void* w, int type, size_t n, size_t k, const float* x, size_t m,
+                          const float* gamma, float eps, float* out);
+
 /* Thread-local message of the last failing call on this thread. */
 ARMAI_API const char* armai_last_error(void);
 /* Library version string. */

@@ -75,3 +75,44 @@ def test_qmatmul_matches_oracle(built, qtype, k, n, m):
     xq = (q8["qs"].astype(np.float64) * q8["d"][..., None]).reshape(m, k)
     mag = np.abs(xq) @ np.abs(deq).T
     assert np.all(np.abs(ours - theirs) <= 2e-6 * mag + 1e-12)
+
+
+def _f16_operands(qtype, w, k, x):
+    """The prefill GEMM's operands in f64: Q8_K q * d rounded to f16, and the
+    dequantised weights rounded to f16."""
+    q8 = ref.quantize_q8k(x)
+    a = (q8["qs"].astype(np.float32) * q8["d"][..., None].astype(np.float32)).astype(np.float16)
+    a = a.reshape(x.shape[0], k).astype(np.float64)
+    wd = ref.dequant_rows(qtype, w, k).astype(np.float16).astype(np.float64)
+    return a, wd
+
+
+@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K])
+@pytest.mark.parametrize("k,n,m", [(256, 128, 128), (2048, 384, 200), (5632, 256, 77), (2048, 1000, 5)])
+def test_qgemm_tensor_cores(built, qtype, k, n, m):
+    """tcgen05 prefill GEMM: exactly the f16 operands' product up to the f32
+    summation order (2e-6 of the magnitude sum), ragged m and n included."""
+    w = _rows(qtype, n, k, seed=7 * n + k)
+    x = _activations(m, k, 5)
+    ours = kquant.qgemm(qtype, w, k, x)
+    a, wd = _f16_operands(qtype, w, k, x)
+    exact = a @ wd.T
+    mag = np.abs(a) @ np.abs(wd).T
+    assert np.all(np.abs(ours - exact) <= 2e-6 * mag + 1e-12)
+    # and against candle's integer path (QMatMul) at f16 precision
+    theirs = ref.qmatmul(qtype, w, k, x)
+    assert np.all(np.abs(ours - theirs) <= 2e-3 * mag + 1e-9)
+
+
+def test_qgemm_with_rms_norm(built):
+    k, n, m = 2048, 256, 130
+    w = _rows(kquant.Q4_K, n, k, seed=99)
+    rng = np.random.default_rng(8)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    g = (1.0 + 0.05 * rng.standard_normal(k)).astype(np.float32)
+    ours = kquant.qgemm(kquant.Q4_K, w, k, x, gamma=g, eps=1e-5)
+    xn = (x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=1, keepdims=True) + 1e-5) * g).astype(np.float32)
+    a, wd = _f16_operands(kquant.Q4_K, w, k, xn)
+    mag = np.abs(a) @ np.abs(wd).T
+    # one activation may round the other way (norm summation order): 2e-3
+    assert np.all(np.abs(ours - a @ wd.T) <= 2e-3 * mag + 1e-9)
