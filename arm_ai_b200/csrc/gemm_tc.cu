@@ -368,6 +368,71 @@ __global__ void __launch_bounds__(256) k_qgemm_act(const float* __restrict__ x, 
   }
 }
 
+// ---- prefill epilogues --------------------------------------------------
+__global__ void k_qkv_post(const float* __restrict__ g, int ldg, int S, const int* __restrict__ pos, int qn,
+                           int kn, int hd, int max_seq, const float* __restrict__ cos_t,
+                           const float* __restrict__ sin_t, float* __restrict__ q_out, void* kc, void* vc,
+                           int kv_f16) {
+  const int t = blockIdx.y;
+  const int pr = blockIdx.x * blockDim.x + threadIdx.x;  // row pair
+  const int rows = ldg;
+  if (t >= S || 2 * pr >= rows) return;
+  const int r = 2 * pr;
+  const float d0 = g[(size_t)t * ldg + r], d1 = g[(size_t)t * ldg + r + 1];
+  const int p = pos[t], half = hd >> 1;
+  if (r < qn + kn) {
+    const int rr = r < qn ? r : r - qn;
+    const int i2 = (rr % hd) >> 1;
+    const float cs = cos_t[(size_t)p * half + i2], sn = sin_t[(size_t)p * half + i2];
+    // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
+    const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
+    const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
+    if (r < qn) {
+      *reinterpret_cast<float2*>(q_out + (size_t)t * qn + r) = make_float2(o0, o1);
+    } else {
+      const int kvh = rr / hd, dd = rr % hd;
+      store_kv(kc, kv_f16, ((int64_t)kvh * max_seq + p) * hd + dd, o0, o1);
+    }
+  } else {
+    const int rv = r - qn - kn;
+    const int kvh = rv / hd, dd = rv % hd;
+    store_kv(vc, kv_f16, ((int64_t)kvh * max_seq + p) * hd + dd, d0, d1);
+  }
+}
+
+__global__ void k_resid_add(float* __restrict__ x, const float* __restrict__ g, int S, int n, int ldg) {
+  const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < S && i < n) x[(size_t)t * n + i] = __fadd_rn(g[(size_t)t * ldg + i], x[(size_t)t * n + i]);
+}
+
+__global__ void k_silu_mul(const float* __restrict__ g, int S, int n, float* __restrict__ h) {
+  const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= S || i >= n) return;
+  const float v = g[(size_t)t * 2 * n + i], u = g[(size_t)t * 2 * n + n + i];
+  h[(size_t)t * n + i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+}
+
+int qkv_post_launch(const float* g, int ldg, int S, const int* pos, int qn, int kn, int hd, int max_seq,
+                    const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
+                    cudaStream_t s) {
+  const dim3 grid((unsigned)((ldg / 2 + 127) / 128), (unsigned)S);
+  k_qkv_post<<<grid, 128, 0, s>>>(g, ldg, S, pos, qn, kn, hd, max_seq, cos_t, sin_t, q_out, kc, vc, kv_f16);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream_t s) {
+  k_resid_add<<<dim3((unsigned)((n + 255) / 256), (unsigned)S), 256, 0, s>>>(x, g, S, n, ldg);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+int silu_mul_launch(const float* g, int S, int n, float* h, cudaStream_t s) {
+  k_silu_mul<<<dim3((unsigned)((n + 255) / 256), (unsigned)S), 256, 0, s>>>(g, S, n, h);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
 int qgemm_act_launch(const float* x, const float* gamma, float eps, int m, int k, uint8_t* a_tiles,
                      cudaStream_t s) {
   if (k % QK_K || k / QK_K > 64) return fail(ARMAI_E_INVALID, "qgemm: K must be a multiple of 256, at most 16384");

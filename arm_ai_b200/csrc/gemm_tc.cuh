@@ -68,4 +68,15 @@ int qgemm_act_launch(const float* x, const float* gamma, float eps, int m, int k
 // qgemm_act_launch. Sets the kernel's shared-memory limit on first use.
 int qgemm_launch(const QgParams& p, cudaStream_t s);
 
+// Prefill epilogues on the GEMM output g (row stride ldg), t = 0..S-1:
+// q|k|v rows -> RoPE'd q into q_out[t][QN], RoPE'd k and v into the KV cache
+// of the sequence (positions pos[t]), as the matvec QKV epilogue does.
+int qkv_post_launch(const float* g, int ldg, int S, const int* pos, int qn, int kn, int hd, int max_seq,
+                    const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
+                    cudaStream_t s);
+// x[t][i] += g[t][i] (residual), i < n.
+int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream_t s);
+// h[t][i] = silu(g[t][i]) * g[t][n + i] (candle: v / (1 + exp(-v)), then * up).
+int silu_mul_launch(const float* g, int S, int n, float* h, cudaStream_t s);
+
 }  // namespace armai

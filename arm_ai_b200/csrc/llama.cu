@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "decode_mega.cuh"
 #include "gguf.h"
+#include "gemm_tc.cuh"
 #include "llama_kernels.cuh"
 
 using namespace armai;
@@ -21,6 +22,7 @@ namespace {
 
 constexpr int PREFILL_TILE = 8;       // tokens per prefill matvec launch
 constexpr int BATCH_NB = 16;          // sequences per batched-decode matvec launch
+constexpr int TC_PREFILL_MIN = 64;    // prompts this long use the tensor-core GEMM (prefill_gemm 0)
 
 constexpr int ATTN_TOK_PER_LAUNCH = 64;
 constexpr uint32_t STAGE_MAX = 44 * 1024;
@@ -88,6 +90,10 @@ struct armai_llama {
   float *pX = nullptr, *pQ = nullptr, *pY = nullptr, *pH = nullptr;
   int* p_pos = nullptr;
   uint32_t* p_tok = nullptr;
+  uint8_t* pA = nullptr;       // tensor-core GEMM A tiles
+  float* pG = nullptr;         // GEMM output [cap][g_cols]
+  int g_cols = 0;
+  int prefill_gemm = 0;        // armai_llama_opts.prefill_gemm
   // pinned host staging
   uint32_t* h_tok = nullptr;   // ring of 8 token slots
   int* h_misc = nullptr;       // small pinned scratch
@@ -516,10 +522,18 @@ int ensure_prefill(armai_llama* m, int S) {
   int cap = std::max(S, 64);
   cap = ((cap + PREFILL_TILE - 1) / PREFILL_TILE) * PREFILL_TILE;
   cudaFree(m->pX); cudaFree(m->pQ); cudaFree(m->pY); cudaFree(m->pH);
-  cudaFree(m->p_pos); cudaFree(m->p_tok);
-  m->pX = m->pQ = m->pY = m->pH = nullptr;
+  cudaFree(m->p_pos); cudaFree(m->p_tok); cudaFree(m->pA); cudaFree(m->pG);
+  m->pX = m->pQ = m->pY = m->pH = m->pG = nullptr;
+  m->pA = nullptr;
   m->pf_cap = 0;
   const size_t qn = (size_t)m->n_head * m->head_dim;
+  if (m->prefill_gemm != 1) {
+    const Layer& L0 = m->layers[0];
+    const int kmax = std::max(m->n_embd, std::max(m->n_ff, (int)qn));
+    m->g_cols = std::max(L0.wq.rows + L0.wk.rows + L0.wv.rows, std::max(2 * m->n_ff, m->n_embd));
+    ARMAI_CUDA(cudaMalloc(&m->pA, qgemm_a_bytes(cap, kmax)));
+    ARMAI_CUDA(cudaMalloc(&m->pG, (size_t)cap * m->g_cols * 4));
+  }
   ARMAI_CUDA(cudaMalloc(&m->pX, (size_t)cap * m->n_embd * 4));
   ARMAI_CUDA(cudaMalloc(&m->pQ, (size_t)cap * qn * 4));
   ARMAI_CUDA(cudaMalloc(&m->pY, (size_t)cap * qn * 4));
@@ -554,7 +568,47 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
   ARMAI_CUDA(cudaMemcpyAsync(m->p_pos, hp, (size_t)S * 4, cudaMemcpyHostToDevice, m->stream));
   const size_t E = m->n_embd, QN = (size_t)m->n_head * m->head_dim, F = m->n_ff;
   ARMAI_CUDA(launch_embed(m, m->p_tok, m->pX, S));
-  for (int l = 0; l < m->n_layer; l++) {
+  const bool gemm = m->prefill_gemm == 2 || (m->prefill_gemm == 0 && S >= TC_PREFILL_MIN);
+  for (int l = 0; l < m->n_layer && gemm; l++) {
+    const Layer& L = m->layers[l];
+    auto gemm_into = [&](std::initializer_list<const DevMat*> mats, int K, int ldo) -> int {
+      QgParams p;
+      std::memset(&p, 0, sizeof p);
+      p.a_tiles = m->pA;
+      p.m = S;
+      p.k = K;
+      int i = 0;
+      for (const DevMat* d : mats) {
+        p.seg[i++] = QgSeg{d->w, d->type, d->rows, d->row_bytes};
+        p.n += d->rows;
+      }
+      p.nseg = i;
+      p.out = m->pG;
+      p.ldo = ldo;
+      p.err = m->d_err;
+      return qgemm_launch(p, m->stream);
+    };
+    const int qkv_rows = L.wq.rows + L.wk.rows + L.wv.rows;
+    ARMAI_TRY(qgemm_act_launch(m->pX, L.attn_norm, m->eps, S, (int)E, m->pA, m->stream));
+    ARMAI_TRY(gemm_into({&L.wq, &L.wk, &L.wv}, (int)E, qkv_rows));
+    ARMAI_TRY(qkv_post_launch(m->pG, qkv_rows, S, m->p_pos, L.wq.rows, L.wk.rows, m->head_dim, m->max_seq,
+                              m->cos_t, m->sin_t, m->pQ, kv_seq_ptr(m, m->kc, l, seq), kv_seq_ptr(m, m->vc, l, seq),
+                              m->kv_f16, m->stream));
+    for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
+      const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
+      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0, seq));
+    }
+    ARMAI_TRY(qgemm_act_launch(m->pY, nullptr, m->eps, S, (int)QN, m->pA, m->stream));
+    ARMAI_TRY(gemm_into({&L.wo}, (int)QN, (int)E));
+    ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
+    ARMAI_TRY(qgemm_act_launch(m->pX, L.ffn_norm, m->eps, S, (int)E, m->pA, m->stream));
+    ARMAI_TRY(gemm_into({&L.wg, &L.wu}, (int)E, (int)(2 * F)));
+    ARMAI_TRY(silu_mul_launch(m->pG, S, (int)F, m->pH, m->stream));
+    ARMAI_TRY(qgemm_act_launch(m->pH, nullptr, m->eps, S, (int)F, m->pA, m->stream));
+    ARMAI_TRY(gemm_into({&L.wd}, (int)F, (int)E));
+    ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
+  }
+  for (int l = 0; l < m->n_layer && !gemm; l++) {
     int t = 0;
     for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)
       ARMAI_CUDA(launch_qkv<PREFILL_TILE>(m, m->pl_qkvT, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0, seq));
@@ -749,7 +803,8 @@ void free_model(armai_llama* m) {
   if (m->graph) cudaGraphExecDestroy(m->graph);
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
-                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar};
+                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar,
+                   m->pA, m->pG};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }
@@ -793,6 +848,11 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   m->use_graph = o.use_graph != 0;
   m->use_pdl = o.use_pdl != 0;
   m->use_mega = o.decode_kernel == 0;
+  m->prefill_gemm = o.prefill_gemm;
+  if (o.prefill_gemm < 0 || o.prefill_gemm > 2) {
+    delete m;
+    return fail(ARMAI_E_INVALID, "prefill_gemm must be 0, 1 or 2");
+  }
   if (o.tp_size > 1) {
     delete m;
     return fail(ARMAI_E_INVALID, "tensor parallelism is not available in this build");

@@ -246,7 +246,7 @@ def run_config2(d):
             "prefill_tokens_per_s": n_seq * plen * 1e6 / max(pre_us, 1),
             "decode_s": dec_us / 1e6, "prefill_s": pre_us / 1e6,
             "timing": "host wall clock around the batched call (max over ranks), as the reference times generate",
-            "prefill_path": "dp4a matvec over 8-token tiles (not tensor cores)"}
+            "prefill_path": "tcgen05 GEMM (f16 operands, TMEM f32 accumulator), k_qgemm"}
 
 
 def run_armai(args, d):

@@ -60,7 +60,10 @@ typedef struct armai_llama_opts {
   const void* tp_unique_id; /* ncclUniqueId bytes (128), same on every rank */
   int32_t decode_kernel;/* 0: one persistent kernel per decode step (default);
                            1: one kernel per operation (PDL chain) */
-  int32_t reserved[7];
+  int32_t prefill_gemm; /* prompt matmuls: 0 = tensor-core GEMM for prompts of
+                           at least 64 tokens, dp4a matvec below (default);
+                           1 = always the dp4a matvec; 2 = always the GEMM */
+  int32_t reserved[6];
 } armai_llama_opts;
 
 /* Fill `o` with the defaults above. */

@@ -63,7 +63,9 @@ def test_teacher_forced_decode_matches_oracle(tiny):
     (2040, 16, set(range(16))),
 ])
 def test_long_context_decode_matches_oracle(tiny, n_prompt, steps, check):
-    path, gpu, orc = tiny
+    # the integer (dp4a) prefill, so that only the decode attention is on trial
+    path, _, orc = tiny
+    gpu = native.llama_candle_load_op(path, prefill_gemm=1)
     prompt = synth.prompt_tokens(n_prompt, orc.n_vocab, 77)
     native.llama_forward(gpu, prompt, 0, want_logits=False)
     orc.forward(prompt, 0)
@@ -76,6 +78,7 @@ def test_long_context_decode_matches_oracle(tiny, n_prompt, steps, check):
         if i in check:
             errs.append(rel_maxabs(lg, lo))
     check_errors(errs, flip_bound(path))
+    gpu.close()
 
 
 @pytest.mark.parametrize("seed", [11, 12, 13])
@@ -182,3 +185,33 @@ def test_f16_kv_cache(small_model):
     check_errors(errs, bound)
     ours = native.llama_candle_generate_op(gpu, prompt, 33, [])[0]
     assert greedy_consistent(small_model, prompt, ours[:32], tol=2 * bound, kv_f16=True) is None
+
+
+@pytest.mark.parametrize("n", [8, 64, 130, 300, 2040])
+def test_prefill_tensor_core_gemm(tiny_model, n):
+    """Prompt through the tcgen05 GEMM path (prefill_gemm = 2: f16 operands,
+    f32 accumulation): final logits and the KV cache it leaves behind (decode
+    steps after it). The f16 rounding of both operands is an approximation of
+    candle's int8 dots on top of the flip noise, so the bound is 1.5 x the
+    flip bound."""
+    gpu = native.llama_candle_load_op(tiny_model, prefill_gemm=2)
+    orc = ref.OracleLlama(tiny_model)
+    prompt = synth.prompt_tokens(n, orc.n_vocab, 4000 + n)
+    lg, tok = native.llama_forward(gpu, prompt, 0)
+    bound = 1.5 * flip_bound(tiny_model)
+    errs = [rel_maxabs(lg, orc.forward(prompt, 0))]
+    assert tok == int(np.argmax(lg))
+    for i in range(4):
+        lg, _ = native.llama_forward(gpu, [50 + i], n + i)
+        errs.append(rel_maxabs(lg, orc.forward([50 + i], n + i)))
+    check_errors(errs, bound)
+    gpu.close()
+
+
+def test_prefill_gemm_small_model(small_model):
+    gpu = native.llama_candle_load_op(small_model, prefill_gemm=2)
+    orc = ref.OracleLlama(small_model)
+    prompt = synth.prompt_tokens(200, orc.n_vocab, 77)
+    lg, _ = native.llama_forward(gpu, prompt, 0)
+    assert rel_maxabs(lg, orc.forward(prompt, 0)) < 1.5 * flip_bound(small_model, lengths=SMALL_LENGTHS)
+    gpu.close()
