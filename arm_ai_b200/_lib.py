@@ -100,6 +100,7 @@ _SIGS = {
     "armai_quantize_q8k": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p]),
     "armai_kquant_block_dots": (c_int, [c_void_p, c_int, c_size_t, c_size_t, c_void_p, c_size_t,
                                         c_void_p, c_void_p]),
+    "armai_nccl_unique_id": (c_int, [c_void_p]),
     "armai_qgemm": (c_int, [c_void_p, c_int, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p, c_float,
                             c_void_p]),
     "armai_qmatmul": (c_int, [c_void_p, c_int, c_size_t, c_size_t, c_void_p, c_size_t, c_void_p]),

@@ -14,6 +14,7 @@
 #include "decode_mega.cuh"
 #include "gguf.h"
 #include "gemm_tc.cuh"
+#include "nccl_dyn.h"
 #include "llama_kernels.cuh"
 
 using namespace armai;
@@ -94,6 +95,17 @@ struct armai_llama {
   float* pG = nullptr;         // GEMM output [cap][g_cols]
   int g_cols = 0;
   int prefill_gemm = 0;        // armai_llama_opts.prefill_gemm
+  // tensor parallelism (tp > 1): this rank holds a slice of every matrix, the
+  // residual stream x is replicated, row-split products are summed by NCCL
+  int tp = 1, tp_rank = 0;
+  void* comm = nullptr;
+  int v0 = 0, v_stride = 0;      // first vocab row of this rank; vocab rows per rank
+  float* tp_part = nullptr;      // [E] partial sum of a row-split matvec
+  float* best_val = nullptr;     // head winner: value and local row
+  int* best_idx = nullptr;
+  uint32_t* tp_send = nullptr;   // 2 words: winner bits, global row
+  uint32_t* tp_recv = nullptr;   // 2 * tp words
+  float* logits_all = nullptr;   // [tp * v_stride] gathered logits
   // pinned host staging
   uint32_t* h_tok = nullptr;   // ring of 8 token slots
   int* h_misc = nullptr;       // small pinned scratch
@@ -287,6 +299,10 @@ cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const in
   p.token = token;
   p.pos = pos;
   p.pos_out = pos_out;
+  if (m->tp > 1) {
+    p.best_val = m->best_val;
+    p.best_idx = m->best_idx;
+  }
   return launch_mv<MODE_HEAD, NB>(m, pl, p, nrows);
 }
 
@@ -481,6 +497,60 @@ int setup_mega(armai_llama* m, int nsm) {
 }
 
 // The single-sequence decode step: token d_token at position d_pos.
+// Tensor parallelism, winner of the head across ranks: (value, global row)
+// of every rank, then the reference's argmax order (larger value, then the
+// smaller row; NaN never wins).
+__global__ void k_tp_pack(const float* best_val, const int* best_idx, int v0, uint32_t* send) {
+  const int bi = best_idx[0];
+  send[0] = __float_as_uint(best_val[0]);
+  send[1] = bi == 0x7fffffff ? 0xffffffffu : (uint32_t)(bi + v0);
+}
+__global__ void k_tp_pick(const uint32_t* recv, int tp, uint32_t* token) {
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (int r = 0; r < tp; r++) {
+    const float v = __uint_as_float(recv[2 * r]);
+    const uint32_t i = recv[2 * r + 1];
+    if (i != 0xffffffffu && (bi == 0xffffffffu || v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
+  }
+  token[0] = bi == 0xffffffffu ? 0u : bi;
+}
+
+int tp_head_merge(armai_llama* m, uint32_t* token) {
+  k_tp_pack<<<1, 1, 0, m->stream>>>(m->best_val, m->best_idx, m->v0, m->tp_send);
+  ARMAI_CUDA(cudaGetLastError());
+  ARMAI_TRY(nccl_allgather_b32(m->tp_send, m->tp_recv, 2, m->comm, m->stream));
+  k_tp_pick<<<1, 1, 0, m->stream>>>(m->tp_recv, m->tp, token);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+// x += W y for a matrix split along K over the ranks: rank 0 adds its part
+// into x, the others write theirs to tp_part, and an all-reduce sums them
+// into x everywhere.
+int rowsplit_resid(armai_llama* m, const Plan& pl, const DevMat& w, const float* y) {
+  if (m->tp == 1) {
+    ARMAI_CUDA(launch_resid<1>(m, pl, w, y, m->x));
+    return ARMAI_OK;
+  }
+  if (m->tp_rank == 0) {
+    ARMAI_CUDA(launch_resid<1>(m, pl, w, y, m->x));
+  } else {
+    MvParams p = base_params(m, pl);
+    p.x = y;
+    p.K = w.cols;
+    p.nb = w.cols / QK_K;
+    p.seg[0] = w.seg();
+    p.nseg = 1;
+    p.total_rows = w.rows;
+    p.out = m->tp_part;
+    p.out_stride = m->n_embd;
+    const cudaError_t e = launch_mv<MODE_STORE, 1>(m, pl, p);
+    ARMAI_CUDA(e);
+  }
+  return nccl_allreduce_sum_f32(m->tp_rank == 0 ? m->x : m->tp_part, m->x, (size_t)m->n_embd, m->comm, m->stream);
+}
+
 int enqueue_decode_step(armai_llama* m) {
   if (m->use_mega) {
     ARMAI_CUDA(launch_mega(m));
@@ -490,11 +560,12 @@ int enqueue_decode_step(armai_llama* m) {
   for (int l = 0; l < m->n_layer; l++) {
     ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->x, m->q, m->d_pos, 0));
     ARMAI_CUDA(launch_attn(m, l, m->q, m->y, m->d_pos, 1, 0));
-    ARMAI_CUDA(launch_resid<1>(m, m->pl_wo1, m->layers[l].wo, m->y, m->x));
+    ARMAI_TRY(rowsplit_resid(m, m->pl_wo1, m->layers[l].wo, m->y));
     ARMAI_CUDA(launch_gateup<1>(m, m->pl_gu1, l, m->x, m->h));
-    ARMAI_CUDA(launch_resid<1>(m, m->pl_down1, m->layers[l].wd, m->h, m->x));
+    ARMAI_TRY(rowsplit_resid(m, m->pl_down1, m->layers[l].wd, m->h));
   }
   ARMAI_CUDA(launch_head<1>(m, m->pl_head1, m->x, m->d_pos, m->d_pos, m->d_token));
+  if (m->tp > 1) ARMAI_TRY(tp_head_merge(m, m->d_token));
   return ARMAI_OK;
 }
 
@@ -600,12 +671,14 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
     }
     ARMAI_TRY(qgemm_act_launch(m->pY, nullptr, m->eps, S, (int)QN, m->pA, m->stream));
     ARMAI_TRY(gemm_into({&L.wo}, (int)QN, (int)E));
+    if (m->tp > 1) ARMAI_TRY(nccl_allreduce_sum_f32(m->pG, m->pG, (size_t)S * E, m->comm, m->stream));
     ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
     ARMAI_TRY(qgemm_act_launch(m->pX, L.ffn_norm, m->eps, S, (int)E, m->pA, m->stream));
     ARMAI_TRY(gemm_into({&L.wg, &L.wu}, (int)E, (int)(2 * F)));
     ARMAI_TRY(silu_mul_launch(m->pG, S, (int)F, m->pH, m->stream));
     ARMAI_TRY(qgemm_act_launch(m->pH, nullptr, m->eps, S, (int)F, m->pA, m->stream));
     ARMAI_TRY(gemm_into({&L.wd}, (int)F, (int)E));
+    if (m->tp > 1) ARMAI_TRY(nccl_allreduce_sum_f32(m->pG, m->pG, (size_t)S * E, m->comm, m->stream));
     ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
   }
   for (int l = 0; l < m->n_layer && !gemm; l++) {
@@ -636,6 +709,7 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
   }
   ARMAI_CUDA(launch_head<1>(m, m->pl_head1, m->pX + (size_t)(S - 1) * E, m->p_pos + (S - 1), m->d_pos + seq,
                             m->d_token + seq));
+  if (m->tp > 1) ARMAI_TRY(tp_head_merge(m, m->d_token + seq));
   return ARMAI_OK;
 }
 
@@ -723,6 +797,8 @@ struct TensorJob {
   const GgufTensor* t;
   DevMat* mat;      // for matrices
   float** vec;      // for f32 vectors (norms)
+  int64_t r0 = 0, nr = -1;   // row slice (tensor parallelism)
+  int64_t b0 = 0, nbk = -1;  // super-block slice along K (tensor parallelism)
 };
 
 int upload_tensors(armai_llama* m, const char* path, const GgufFile& g, std::vector<TensorJob>& jobs) {
@@ -746,25 +822,36 @@ int upload_tensors(armai_llama* m, const char* path, const GgufFile& g, std::vec
   int slot = 0;
   for (TensorJob& j : jobs) {
     const GgufTensor& t = *j.t;
-    const int64_t rows = t.rows(), cols = t.cols();
+    const int64_t rows = j.nr >= 0 ? j.nr : t.rows(), full_cols = t.cols();
+    const int64_t full_rb = ggml_row_bytes(t.type, full_cols);
+    const bool kslice = j.mat && j.nbk >= 0;
+    const int64_t cols = kslice ? j.nbk * QK_K : full_cols;
     const int64_t raw_rb = ggml_row_bytes(t.type, cols);
-    int64_t rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)std::max<int64_t>(raw_rb, 1)));
-    if (j.mat && t.type == GGML_Q6_K) rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)dev_row_bytes(GGML_Q6_K, cols)));
-    if (fseeko(f, (off_t)(g.data_offset + t.offset), SEEK_SET) != 0) { rc = fail(ARMAI_E_IO, "seek failed"); break; }
+    const int64_t boff = kslice ? ggml_row_bytes(t.type, j.b0 * QK_K) : 0;
+    int64_t rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)std::max<int64_t>(full_rb, 1)));
+    if (j.mat && t.type == GGML_Q6_K) rows_per = std::max<int64_t>(1, (int64_t)(STG / (size_t)dev_row_bytes(GGML_Q6_K, full_cols)));
+    if (fseeko(f, (off_t)(g.data_offset + t.offset + (uint64_t)j.r0 * full_rb), SEEK_SET) != 0) {
+      rc = fail(ARMAI_E_IO, "seek failed");
+      break;
+    }
     uint8_t* dst = j.mat ? j.mat->w : (uint8_t*)*j.vec;
     for (int64_t r0 = 0; r0 < rows && rc == ARMAI_OK; r0 += rows_per) {
       const int64_t nr = std::min(rows_per, rows - r0);
       cudaEventSynchronize(ev[slot]);
       uint8_t* buf = stg[slot];
-      size_t bytes = (size_t)(nr * raw_rb);
-      if (fread(j.mat && t.type == GGML_Q6_K ? rep : buf, 1, bytes, f) != bytes) {
+      const bool via_rep = (j.mat && t.type == GGML_Q6_K) || kslice;
+      if (fread(via_rep ? rep : buf, 1, (size_t)(nr * full_rb), f) != (size_t)(nr * full_rb)) {
         rc = fail(ARMAI_E_IO, "short read of tensor '" + t.name + "'");
         break;
       }
-      size_t out_bytes = bytes;
+      if (kslice)  // keep each row's super-blocks [b0, b0 + nbk)
+        for (int64_t r = 0; r < nr; r++) memmove(rep + r * raw_rb, rep + r * full_rb + boff, (size_t)raw_rb);
+      size_t out_bytes = (size_t)(nr * raw_rb);
       if (j.mat && t.type == GGML_Q6_K) {
         repack_q6k_rows(rep, nr, cols, buf);
         out_bytes = (size_t)(nr * dev_row_bytes(GGML_Q6_K, cols));
+      } else if (kslice) {
+        memcpy(buf, rep, out_bytes);
       } else if (!j.mat && t.type == GGML_F16) {
         // f16 vector -> f32 (candle dequantises norm weights at load)
         float* tmp = (float*)rep;
@@ -800,11 +887,13 @@ void free_model(armai_llama* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
-  if (m->graph) cudaGraphExecDestroy(m->graph);
+  if (m->graph) cudaGraphExecDestroy(m->graph);  // before the NCCL communicator it may hold
+  if (m->comm) nccl_comm_destroy(m->comm);
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
                    m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar,
-                   m->pA, m->pG};
+                   m->pA, m->pG, m->tp_part, m->best_val, m->best_idx, m->tp_send, m->tp_recv,
+                   m->logits_all};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }
@@ -853,9 +942,21 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     delete m;
     return fail(ARMAI_E_INVALID, "prefill_gemm must be 0, 1 or 2");
   }
-  if (o.tp_size > 1) {
-    delete m;
-    return fail(ARMAI_E_INVALID, "tensor parallelism is not available in this build");
+  m->tp = std::max(1, o.tp_size);
+  m->tp_rank = o.tp_rank;
+  if (m->tp > 1) {
+    if (o.tp_rank < 0 || o.tp_rank >= m->tp || !o.tp_unique_id) {
+      delete m;
+      return fail(ARMAI_E_INVALID, "tensor parallel: tp_rank must be in [0, tp_size) and tp_unique_id set");
+    }
+    if (o.prefill_gemm == 1 || m->max_batch > 1) {
+      delete m;
+      return fail(ARMAI_E_INVALID, "tensor parallel: prompts run the GEMM path and batches are not sharded "
+                                   "(prefill_gemm 1 and max_batch > 1 are not available with tp_size > 1)");
+    }
+    m->use_mega = false;  // per-kernel chain with NCCL between the row-split matvecs
+    m->use_pdl = false;
+    m->prefill_gemm = 2;
   }
   m->n_layer = (int)block_count;
   m->n_embd = (int)embd;
@@ -888,7 +989,8 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   std::vector<TensorJob> jobs;
   size_t arena = 0;
   int rc = ARMAI_OK;
-  auto add_mat = [&](const std::string& name, DevMat& dm, int64_t want_cols, int64_t want_rows) -> int {
+  auto add_mat = [&](const std::string& name, DevMat& dm, int64_t want_cols, int64_t want_rows, int64_t r0 = 0,
+                     int64_t nr = -1, int64_t b0 = 0, int64_t nbk = -1) -> int {
     const GgufTensor* t = find(name);
     if (!t) return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find tensor info for " + name);
     if (t->dims.size() != 2) return fail(ARMAI_E_FORMAT, "tensor " + name + " is not 2-D");
@@ -898,13 +1000,18 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     if ((want_cols > 0 && t->cols() != want_cols) || (want_rows > 0 && t->rows() != want_rows))
       return fail(ARMAI_E_FORMAT, "tensor " + name + " has an unexpected shape");
     dm.type = (int)t->type;
-    dm.rows = (int)t->rows();
-    dm.cols = (int)t->cols();
+    dm.rows = (int)(nr >= 0 ? nr : t->rows());
+    dm.cols = (int)(nbk >= 0 ? nbk * QK_K : t->cols());
     dm.row_bytes = (int)dev_row_bytes(dm.type, dm.cols);
     dm.w = reinterpret_cast<uint8_t*>(arena);  // offset for now
     arena += al16((size_t)dm.row_bytes * dm.rows + 255) & ~size_t(255);
     m->weight_bytes_per_token += (int64_t)dm.row_bytes * dm.rows;
-    jobs.push_back(TensorJob{t, &dm, nullptr});
+    TensorJob job{t, &dm, nullptr};
+    job.r0 = r0;
+    job.nr = nr;
+    job.b0 = b0;
+    job.nbk = nbk;
+    jobs.push_back(job);
     return ARMAI_OK;
   };
   std::vector<float*> vec_offsets;
@@ -928,29 +1035,60 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   // token_embd streams one row per token, not the whole table
   if (rc == ARMAI_OK) m->weight_bytes_per_token -= (int64_t)m->tok_embd.row_bytes * (m->tok_embd.rows - 1);
   if (rc == ARMAI_OK) rc = add_vec("output_norm.weight", m->out_norm, m->n_embd);
+  const int T = m->tp, TR = m->tp_rank;
+  // tensor parallelism: vocab rows of the head split in contiguous blocks
+  m->v_stride = (m->n_vocab + T - 1) / T;
+  m->v0 = std::min(TR * m->v_stride, m->n_vocab);
+  const int64_t v_rows = std::min(m->v_stride, m->n_vocab - m->v0);
+  if (T > 1 && v_rows <= 0) rc = fail(ARMAI_E_INVALID, "tensor parallel: more ranks than vocab rows");
   if (rc == ARMAI_OK) {
-    if (find("output.weight")) rc = add_mat("output.weight", m->output, m->n_embd, m->n_vocab);
-    else {
+    if (find("output.weight")) rc = add_mat("output.weight", m->output, m->n_embd, m->n_vocab, m->v0, T > 1 ? v_rows : -1);
+    else if (T > 1) {
+      rc = add_mat("token_embd.weight", m->output, m->n_embd, -1, m->v0, v_rows);  // tied, this rank's rows
+    } else {
       m->output = m->tok_embd;  // tied: candle falls back to token_embd
       m->weight_bytes_per_token += (int64_t)m->output.row_bytes * (m->output.rows - 1);
     }
   }
   const int64_t QN = (int64_t)m->n_head * m->head_dim, KN = (int64_t)m->n_head_kv * m->head_dim;
+  if (rc == ARMAI_OK && T > 1 &&
+      (m->n_head % T || m->n_head_kv % T || (QN / T) % QK_K))
+    rc = fail(ARMAI_E_INVALID, "tensor parallel: " + std::to_string(T) + " ranks must divide the query heads (" +
+                                   std::to_string(m->n_head) + ") and KV heads (" + std::to_string(m->n_head_kv) +
+                                   ") with whole 256-value blocks of attn_output per rank");
+  const int64_t QNl = QN / T, KNl = KN / T;
   for (int l = 0; l < m->n_layer && rc == ARMAI_OK; l++) {
     Layer& L = m->layers[l];
     const std::string p = "blk." + std::to_string(l) + ".";
-    rc = add_mat(p + "attn_q.weight", L.wq, m->n_embd, QN);
-    if (!rc) rc = add_mat(p + "attn_k.weight", L.wk, m->n_embd, KN);
-    if (!rc) rc = add_mat(p + "attn_v.weight", L.wv, m->n_embd, KN);
-    if (!rc) rc = add_mat(p + "attn_output.weight", L.wo, QN, m->n_embd);
-    if (!rc) rc = add_mat(p + "ffn_gate.weight", L.wg, m->n_embd, -1);
-    if (!rc) { m->n_ff = L.wg.rows; rc = add_mat(p + "ffn_up.weight", L.wu, m->n_embd, m->n_ff); }
-    if (!rc) rc = add_mat(p + "ffn_down.weight", L.wd, m->n_ff, m->n_embd);
+    const int64_t sl = T > 1 ? 1 : 0;  // slice only when sharded
+    rc = add_mat(p + "attn_q.weight", L.wq, m->n_embd, QN, TR * QNl * sl, sl ? QNl : -1);
+    if (!rc) rc = add_mat(p + "attn_k.weight", L.wk, m->n_embd, KN, TR * KNl * sl, sl ? KNl : -1);
+    if (!rc) rc = add_mat(p + "attn_v.weight", L.wv, m->n_embd, KN, TR * KNl * sl, sl ? KNl : -1);
+    if (!rc) rc = add_mat(p + "attn_output.weight", L.wo, QN, m->n_embd, 0, -1, TR * (QNl / QK_K) * sl,
+                          sl ? QNl / QK_K : -1);
+    int64_t F = 0;
+    if (!rc) {
+      const GgufTensor* tg = find(p + "ffn_gate.weight");
+      F = tg && tg->dims.size() == 2 ? tg->rows() : 0;
+      if (T > 1 && (F % ((int64_t)T * QK_K)))
+        rc = fail(ARMAI_E_INVALID, "tensor parallel: feed-forward length " + std::to_string(F) +
+                                       " does not split into whole 256-value blocks over " + std::to_string(T) + " ranks");
+    }
+    const int64_t Fl = T > 1 ? F / T : -1;
+    if (!rc) rc = add_mat(p + "ffn_gate.weight", L.wg, m->n_embd, -1, T > 1 ? TR * Fl : 0, Fl);
+    if (!rc) { m->n_ff = (int)F; rc = add_mat(p + "ffn_up.weight", L.wu, m->n_embd, m->n_ff, T > 1 ? TR * Fl : 0, Fl); }
+    if (!rc) rc = add_mat(p + "ffn_down.weight", L.wd, m->n_ff, m->n_embd, 0, -1, T > 1 ? TR * (Fl / QK_K) : 0,
+                          T > 1 ? Fl / QK_K : -1);
     if (!rc) rc = add_vec(p + "attn_norm.weight", L.attn_norm, m->n_embd);
     if (!rc) rc = add_vec(p + "ffn_norm.weight", L.ffn_norm, m->n_embd);
     if (!rc && (m->n_ff % QK_K)) rc = fail(ARMAI_E_FORMAT, "feed-forward length must be a multiple of 256");
   }
   if (rc != ARMAI_OK) { delete m; return rc; }
+  if (T > 1) {  // from here on the model is this rank's shard
+    m->n_head /= T;
+    m->n_head_kv /= T;
+    m->n_ff /= T;
+  }
 
   cudaError_t ce = cudaSetDevice(m->device);
   if (ce != cudaSuccess) { delete m; return cuda_fail(ce, "cudaSetDevice", __FILE__, __LINE__); }
@@ -1023,6 +1161,16 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   LOAD_CUDA(cudaMalloc(&m->am_idx, (size_t)B * nsm * 4));
   LOAD_CUDA(cudaMalloc(&m->am_cnt, 64));
   LOAD_CUDA(cudaMemsetAsync(m->am_cnt, 0, 64, m->stream));
+  if (m->tp > 1) {
+    LOAD_CUDA(cudaMalloc(&m->tp_part, (size_t)m->n_embd * 4));
+    LOAD_CUDA(cudaMalloc(&m->best_val, 64));
+    LOAD_CUDA(cudaMalloc(&m->best_idx, 64));
+    LOAD_CUDA(cudaMalloc(&m->tp_send, 64));
+    LOAD_CUDA(cudaMalloc(&m->tp_recv, (size_t)m->tp * 8));
+    LOAD_CUDA(cudaMalloc(&m->logits_all, (size_t)m->tp * m->v_stride * 4));
+    const int nrc = nccl_comm_init(&m->comm, m->tp, opts->tp_unique_id, m->tp_rank);
+    if (nrc != ARMAI_OK) { free_model(m); return nrc; }
+  }
   LOAD_CUDA(cudaMallocHost(&m->h_tok, 64));
   LOAD_CUDA(cudaMallocHost(&m->h_misc, 64));
 
@@ -1055,6 +1203,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (!arc) arc = set_smem_attr<MODE_RESID, 1>(std::max(m->pl_wo1.smem, m->pl_down1.smem));
   if (!arc) arc = set_smem_attr<MODE_GATEUP, 1>(m->pl_gu1.smem);
   if (!arc) arc = set_smem_attr<MODE_HEAD, 1>(m->pl_head1.smem);
+  if (!arc) arc = set_smem_attr<MODE_STORE, 1>(std::max(m->pl_wo1.smem, m->pl_down1.smem));
   if (!arc) arc = set_smem_attr<MODE_QKV, PREFILL_TILE>(m->pl_qkvT.smem);
   if (!arc) arc = set_smem_attr<MODE_RESID, PREFILL_TILE>(std::max(m->pl_woT.smem, m->pl_downT.smem));
   if (!arc) arc = set_smem_attr<MODE_GATEUP, PREFILL_TILE>(m->pl_guT.smem);
@@ -1162,8 +1311,12 @@ extern "C" int armai_llama_forward(armai_llama* m, const uint32_t* tokens, size_
   if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
   ARMAI_CUDA(cudaSetDevice(m->device));
   ARMAI_TRY(forward_locked(m, tokens, (int)n, (int)index_pos));
-  if (logits)
+  if (logits && m->tp > 1) {  // every rank's vocab rows, in rank order
+    ARMAI_TRY(nccl_allgather_b32(m->logits, m->logits_all, (size_t)m->v_stride, m->comm, m->stream));
+    ARMAI_CUDA(cudaMemcpyAsync(logits, m->logits_all, (size_t)m->n_vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+  } else if (logits) {
     ARMAI_CUDA(cudaMemcpyAsync(logits, m->logits, (size_t)m->n_vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+  }
   ARMAI_CUDA(cudaMemcpyAsync(m->h_tok, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
   ARMAI_TRY(check_device_error(m));
   if (token) *token = m->h_tok[0];
@@ -1248,6 +1401,9 @@ extern "C" int armai_llama_generate_batch(armai_llama* m, const uint32_t* prompt
   for (size_t s = 0; s < n_seq; s++) n_out[s] = 0;
   if (!n_seq || !max_new) return ARMAI_OK;
   if (!out || !prompts) return fail(ARMAI_E_INVALID, "generate_batch: bad argument");
+  if (m->max_batch == 1 && n_seq == 1)  // no batch slots: the single-sequence path
+    return armai_llama_generate(m, prompts, n_prompt[0], max_new, stop, n_stop, nullptr, nullptr, out, n_out,
+                                prefill_us, decode_us);
   std::lock_guard<std::mutex> lk(m->mu);
   if (m->broken) return fail(ARMAI_E_DEVICE, "model is in an error state; reload it");
   if ((int64_t)n_seq > m->max_batch)
@@ -1409,4 +1565,9 @@ extern "C" int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t ca
   *n_phases = m->mk.n_ph + 1;
   *n_ctas = m->mk_grid;
   return check_device_error(m);
+}
+
+extern "C" int armai_nccl_unique_id(void* out128) {
+  if (!out128) return fail(ARMAI_E_INVALID, "nccl_unique_id: null argument");
+  return nccl_unique_id(out128);
 }

@@ -125,6 +125,8 @@ struct MvParams {
   unsigned* counter;
   uint32_t* token;        // [NB]
   int* pos_out;           // [NB] or nullptr: pos_out[b] = pos[b] + 1
+  float* best_val;        // [NB] or nullptr: the winning logit (tensor-parallel merge)
+  int* best_idx;          // [NB] or nullptr: its row, 0x7fffffff when nothing won
   uint32_t* err;
 };
 
@@ -547,6 +549,7 @@ __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
           // No finite winner (all NaN / -inf): the reference's fold keeps index 0.
           p.token[b] = (bi == 0x7fffffff) ? 0u : (uint32_t)bi;
           if (p.pos_out) p.pos_out[b] = p.pos[b] + 1;
+          if (p.best_val) { p.best_val[b] = bv; p.best_idx[b] = bi; }
         }
       }
       if (tid == 0) *p.counter = 0u;

@@ -66,6 +66,15 @@ typedef struct armai_llama_opts {
   int32_t reserved[6];
 } armai_llama_opts;
 
+/* Tensor parallelism (tp_size > 1): every rank calls
+ * armai_llama_load with the same path, its tp_rank and the same 128-byte
+ * NCCL unique id, which rank 0 creates with armai_nccl_unique_id and shares
+ * out of band (no reference counterpart: the reference runs on one CPU).
+ * Query/KV heads, gate/up rows and vocab rows are split over the ranks;
+ * attn_output and ffn_down are split along K and summed by an NCCL
+ * all-reduce; prompts run the tensor-core GEMM path. */
+ARMAI_API int armai_nccl_unique_id(void* out128);
+
 /* Fill `o` with the defaults above. */
 ARMAI_API void armai_llama_default_opts(armai_llama_opts* o);
 

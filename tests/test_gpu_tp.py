@@ -1,0 +1,81 @@
+"""Tensor parallelism on two GPUs (BASELINE config 4's structure on the small
+test model: 8 query / 2 KV heads, FFN 1536, vocab 4096 split over 2 ranks).
+
+Each rank holds half the heads, gate/up rows and vocab rows and a K-half of
+attn_output / ffn_down; the halves are summed by NCCL. Against the oracle:
+prompt logits (gathered from both ranks) within the model's flip bound and
+greedy tokens consistent with the oracle, identical on both ranks. Skipped
+with fewer than two GPUs.
+"""
+import os
+import socket
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, path, prompt, q):
+    import datetime
+
+    import numpy as np
+    import torch.distributed as dist
+
+    from arm_ai_b200 import native, tp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")  # plain NVLink transfers, no multicast objects
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        uid = tp.share_unique_id(rank)
+        gpu = tp.load_tp(path, rank, world, rank, uid)
+        lg, tok = native.llama_forward(gpu, prompt, 0)
+        toks = native.llama_candle_generate_op(gpu, prompt, 24, [])[0]
+        long_prompt = list(prompt) * 8  # 104 tokens: the GEMM prefill path
+        lg2, _ = native.llama_forward(gpu, long_prompt, 0)
+        gpu.close()
+        q.put((rank, np.asarray(lg), tok, toks, np.asarray(lg2)))
+    except Exception as e:  # report instead of hanging the other rank
+        q.put((rank, repr(e), None, None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_oracle(small_model):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    import ref
+    from arm_ai_b200 import synth
+    from parity import flip_bound, greedy_consistent, rel_maxabs
+
+    prompt = synth.prompt_tokens(13, 4096, 21)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, small_model, prompt, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for r in res:
+        assert not isinstance(r[1], str), r[1]
+    bound = flip_bound(small_model, lengths=(16, 24, 64, 100, 128))
+    orc = ref.OracleLlama(small_model)
+    lo = orc.forward(prompt, 0)
+    for _, lg, tok, toks, lg2 in res:
+        assert rel_maxabs(lg, lo) < bound
+        assert greedy_consistent(small_model, prompt, toks, tol=2 * bound) is None
+    lo2 = ref.OracleLlama(small_model).forward(list(prompt) * 8, 0)
+    assert rel_maxabs(res[0][4], lo2) < 1.5 * bound  # GEMM prefill: f16 operands
+    assert res[0][3] == res[1][3]
+    assert res[0][2] == res[1][2]
