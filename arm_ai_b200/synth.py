@@ -144,7 +144,9 @@ def model_path(arch_name: str, seed: int = 0, cache_dir: str | None = None, tie_
     key = hashlib.sha256(repr((asdict(arch), seed, tie_output, 1)).encode()).hexdigest()[:12]
     p = os.path.join(cache_dir, f"{arch_name}-s{seed}{'-tied' if tie_output else ''}-{key}.gguf")
     if not os.path.exists(p):
-        write_model(p, arch, seed, tie_output)
+        tmp = f"{p}.{os.getpid()}.tmp"  # complete files only, even if interrupted or raced
+        write_model(tmp, arch, seed, tie_output)
+        os.replace(tmp, p)
     return p
 
 

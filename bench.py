@@ -47,6 +47,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--no-config2", action="store_true", help="skip the batched-decode (config 2) figures")
+    p.add_argument("--no-config4", action="store_true", help="skip the Llama-3-8B tensor-parallel (config 4) figures")
     return p.parse_args()
 
 
@@ -249,6 +250,48 @@ def run_config2(d):
             "prefill_path": "tcgen05 GEMM (f16 operands, TMEM f32 accumulator), k_qgemm"}
 
 
+def run_config4(d, peak):
+    """Llama-3-8B-architecture Q4_K_M, b = 1, 1024-token
+    seeded prompt, 128 new tokens, tensor-parallel over the N ranks (NCCL
+    all-reduce after attn_output and ffn_down; N = 1 runs the persistent
+    kernel). Decode device-timed (CUDA events, max over ranks)."""
+    from arm_ai_b200 import native, synth, tp
+    arch = "llama-3-8b"
+    if d.rank == 0:
+        synth.model_path(arch, seed=0)
+    d.barrier()
+    path = synth.model_path(arch, seed=0)
+    if d.world > 1:
+        uid = tp.share_unique_id(d.rank)
+        gpu = tp.load_tp(path, d.local, d.world, d.rank, uid, max_seq_len=2048)
+    else:
+        gpu = native.llama_candle_load_op(path, device=d.local, max_seq_len=2048)
+    info = gpu.info()
+    prompt = synth.prompt_tokens(1024, info.n_vocab, 3000)
+    native.llama_forward(gpu, prompt[:64], 0, want_logits=False)  # warm-up
+    d.barrier()
+    t0 = time.time()
+    native.llama_forward(gpu, prompt, 0, want_logits=False)
+    pre_s = d.max(time.time() - t0)
+    n_dec = 127
+    native.llama_bench_decode(gpu, 8)  # warm-up steps
+    native.llama_forward(gpu, prompt, 0, want_logits=False)
+    d.barrier()
+    ms = d.max(native.llama_bench_decode(gpu, n_dec))
+    step_s = ms / 1e3 / n_dec
+    kv_row = 2 * info.n_layer * info.n_head_kv * info.head_dim * (2 if info.kv_f16 else 4)
+    bytes_gpu = info.weight_bytes + kv_row * (1024 + 1024 + n_dec) / 2
+    gpu.close()
+    return {"workload": f"{arch} Q4_K_M b=1: 1024-token prompt + {n_dec + 1} new tokens, "
+                        f"{'tensor-parallel over ' + str(d.world) + ' GPUs (NCCL all-reduce)' if d.world > 1 else '1 GPU'}",
+            "decode_tokens_per_s": 1.0 / step_s, "ms_per_token": step_s * 1e3,
+            "prefill_tokens_per_s": 1024 / pre_s,
+            "weight_stream_gb_s_per_gpu": bytes_gpu / step_s / 1e9,
+            "frac_of_hbm_per_gpu": bytes_gpu / step_s / 1e9 / peak,
+            "bytes_per_token_per_gpu": bytes_gpu,
+            "timing": "decode: CUDA events over 127 back-to-back steps, max over ranks; prefill: host wall clock"}
+
+
 def run_armai(args, d):
     from arm_ai_b200 import native, synth
     if d.rank == 0:
@@ -315,6 +358,7 @@ def run_armai(args, d):
     gpu_launches = int(args.steps * n_dec * info.n_kernels_per_step * d.world)
     gpu.close()
     cfg2 = None if args.no_config2 else run_config2(d)
+    cfg4 = None if args.no_config4 else run_config4(d, peak)
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(path, prompt)
@@ -350,6 +394,7 @@ def run_armai(args, d):
             "gpu_launches": gpu_launches,
             "wall_s_timed_region": t_wall,
             "config2_batched": cfg2,
+            "config4_llama3_8b": cfg4,
         }
         print(json.dumps(out), flush=True)
 
