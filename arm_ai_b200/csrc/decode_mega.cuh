@@ -33,6 +33,7 @@ constexpr int MK_CT = 32 * MK_CW;             // consumer threads
 constexpr uint32_t MK_STAGE = 32 * 1024;
 constexpr int MK_MAX_NS = 6;
 constexpr uint32_t MK_BAR_LIMIT = 1u << 24;   // grid-barrier polls before giving up
+constexpr int MK_ATT_PER_HEAD_MAX_T = 512;    // attention unit per query head up to this context
 constexpr int MK_MAX_RES = 64;                // residual rows per CTA kept in shared memory
 constexpr int MK_REGJ = 2;                    // prologue blocks per warp kept in registers
 
@@ -274,9 +275,22 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
   act.bs = reinterpret_cast<int32_t*>(smem + p.off_act_bs);
   const bool norm = ph.gamma != nullptr;
   float v[MK_REGJ][8];
+  // the register-held blocks' loads are all issued before any is used
+#pragma unroll
+  for (int r = 0; r < MK_REGJ; r++)
+    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r]);
   for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
     float vv[8];
-    mk_load_vals(p, ph, j, lane, vv);
+    if (jj < MK_REGJ) {
+#pragma unroll
+      for (int r = 0; r < MK_REGJ; r++)
+        if (jj == r) {
+#pragma unroll
+          for (int k = 0; k < 8; k++) vv[k] = v[r][k];
+        }
+    } else {
+      mk_load_vals(p, ph, j, lane, vv);
+    }
     if (!ph.in) {
       // token embedding = initial residual stream: keep this CTA's rows
 #pragma unroll
@@ -293,12 +307,6 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
       for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (lane == 0) part[j] = ss;
     }
-#pragma unroll
-    for (int r = 0; r < MK_REGJ; r++)
-      if (jj == r) {
-#pragma unroll
-        for (int k = 0; k < 8; k++) v[r][k] = vv[k];
-      }
   }
   float m = 1.f;
   if (cw == 0 && lane == 0) mk_stamp(p, phase, 6);
@@ -427,11 +435,11 @@ __host__ __device__ inline size_t mk_att_floats(int hd, int nrep) {
 }
 
 template <int HD, typename KV>
-__device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s, int splits, int T,
-                             float* sm, int cw, int lane) {
+__device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0, int nh, int s, int splits,
+                             int T, float* sm, int cw, int lane) {
   constexpr int TILE = mk_att_tile<HD>();
   constexpr int MAXE = (ATT_MAX_REP * HD + MK_CT - 1) / MK_CT;  // (head, dim) elements per thread
-  const int nrep = p.n_head / p.n_kv;
+  const int nrep = p.n_head / p.n_kv;   // heads of group g; this unit takes [r0, r0 + nh)
   const int tid = cw * 32 + lane;
   float* qs = sm;                              // [nrep][HD]
   float* Ks = qs + nrep * HD;                  // [TILE][HD + 1]
@@ -450,9 +458,9 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
   const int64_t kvbase = (int64_t)g * p.max_seq * HD;
   const KV* kc = reinterpret_cast<const KV*>(ph.kc) + kvbase;
   const KV* vc = reinterpret_cast<const KV*>(ph.vc) + kvbase;
-  const float4* qb = reinterpret_cast<const float4*>(p.q + (size_t)g * nrep * HD);
-  for (int i = tid; i < nrep * HD / 4; i += MK_CT) reinterpret_cast<float4*>(qs)[i] = __ldcg(qb + i);
-  if (tid < nrep) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
+  const float4* qb = reinterpret_cast<const float4*>(p.q + (size_t)(g * nrep + r0) * HD);
+  for (int i = tid; i < nh * HD / 4; i += MK_CT) reinterpret_cast<float4*>(qs)[i] = __ldcg(qb + i);
+  if (tid < nh) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
   float o[MAXE];
 #pragma unroll
   for (int k = 0; k < MAXE; k++) o[k] = 0.f;
@@ -469,7 +477,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
     }
     named_sync(1, MK_CT);
     // scores: thread per (head, position)
-    for (int e = tid; e < nrep * TILE; e += MK_CT) {
+    for (int e = tid; e < nh * TILE; e += MK_CT) {
       const int h = e / TILE, t = e % TILE;
       float sc = -INFINITY;
       if (t < n) {
@@ -484,7 +492,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
     }
     named_sync(1, MK_CT);
     // online softmax: warp per head
-    for (int h = cw; h < nrep; h += MK_CW) {
+    for (int h = cw; h < nh; h += MK_CW) {
       float mt = -INFINITY;
       for (int t = lane; t < n; t += 32) mt = fmaxf(mt, ps[h * TILE + t]);
 #pragma unroll
@@ -511,7 +519,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
 #pragma unroll
     for (int k = 0; k < MAXE; k++) {
       const int e = tid + k * MK_CT;
-      if (e < nrep * HD) {
+      if (e < nh * HD) {
         const int h = e / HD, d = e % HD;
         float acc = o[k] * corr[h];
         const float* pr = ps + h * TILE;
@@ -525,24 +533,24 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
 #pragma unroll
     for (int k = 0; k < MAXE; k++) {
       const int e = tid + k * MK_CT;
-      if (e < nrep * HD) p.y[(size_t)g * nrep * HD + e] = o[k] / lrow[e / HD];
+      if (e < nh * HD) p.y[(size_t)(g * nrep + r0) * HD + e] = o[k] / lrow[e / HD];
     }
     return;
   }
-  const size_t pbase = (((size_t)g * ATT_SPLITS + s) * nrep) * (HD + 2);
+  const size_t pbase = (((size_t)g * ATT_SPLITS + s) * nrep + r0) * (HD + 2);
 #pragma unroll
   for (int k = 0; k < MAXE; k++) {
     const int e = tid + k * MK_CT;
-    if (e < nrep * HD) p.att_part[pbase + (size_t)(e / HD) * (HD + 2) + e % HD] = o[k];
+    if (e < nh * HD) p.att_part[pbase + (size_t)(e / HD) * (HD + 2) + e % HD] = o[k];
   }
-  if (tid < nrep) {
+  if (tid < nh) {
     p.att_part[pbase + (size_t)tid * (HD + 2) + HD] = mrow[tid];
     p.att_part[pbase + (size_t)tid * (HD + 2) + HD + 1] = lrow[tid];
   }
   __threadfence();
   named_sync(1, MK_CT);
   if (tid == 0) {
-    const unsigned prev = atomicAdd(&p.att_cnt[g], 1u);
+    const unsigned prev = atomicAdd(&p.att_cnt[g * nrep + r0], 1u);
     *s_last = (prev == (unsigned)splits - 1);
   }
   named_sync(1, MK_CT);
@@ -550,37 +558,37 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int s,
   __threadfence();
   // the last split of head g merges all splits
   const size_t base0 = ((size_t)g * ATT_SPLITS) * nrep * (HD + 2);
-  for (int i = tid; i < splits * nrep; i += MK_CT) {
-    const int s2 = i / nrep, h = i % nrep;
-    const size_t o2 = base0 + ((size_t)s2 * nrep + h) * (HD + 2);
-    cw_m[s2 * nrep + h] = __ldcg(p.att_part + o2 + HD);
-    cw_l[s2 * nrep + h] = __ldcg(p.att_part + o2 + HD + 1);
+  for (int i = tid; i < splits * nh; i += MK_CT) {
+    const int s2 = i / nh, h = i % nh;
+    const size_t o2 = base0 + ((size_t)s2 * nrep + r0 + h) * (HD + 2);
+    cw_m[s2 * nh + h] = __ldcg(p.att_part + o2 + HD);
+    cw_l[s2 * nh + h] = __ldcg(p.att_part + o2 + HD + 1);
   }
   named_sync(1, MK_CT);
-  if (tid < nrep) {
+  if (tid < nh) {
     float M = -INFINITY;
     for (int s2 = 0; s2 < splits; s2++)
-      if (cw_l[s2 * nrep + tid] > 0.f) M = fmaxf(M, cw_m[s2 * nrep + tid]);
+      if (cw_l[s2 * nh + tid] > 0.f) M = fmaxf(M, cw_m[s2 * nh + tid]);
     float Ls = 0.f;
     for (int s2 = 0; s2 < splits; s2++) {
-      const float lv = cw_l[s2 * nrep + tid];
-      const float w = lv > 0.f ? expf(cw_m[s2 * nrep + tid] - M) : 0.f;
-      cw_m[s2 * nrep + tid] = w;
+      const float lv = cw_l[s2 * nh + tid];
+      const float w = lv > 0.f ? expf(cw_m[s2 * nh + tid] - M) : 0.f;
+      cw_m[s2 * nh + tid] = w;
       Ls += lv * w;
     }
     ltot[tid] = Ls;
   }
   named_sync(1, MK_CT);
-  for (int e = tid; e < nrep * HD; e += MK_CT) {
+  for (int e = tid; e < nh * HD; e += MK_CT) {
     const int h = e / HD, d = e % HD;
     float O = 0.f;
     for (int s2 = 0; s2 < splits; s2++) {
-      const float w = cw_m[s2 * nrep + h];
-      if (w != 0.f) O += w * __ldcg(p.att_part + base0 + ((size_t)s2 * nrep + h) * (HD + 2) + d);
+      const float w = cw_m[s2 * nh + h];
+      if (w != 0.f) O += w * __ldcg(p.att_part + base0 + ((size_t)s2 * nrep + r0 + h) * (HD + 2) + d);
     }
-    p.y[((size_t)g * nrep + h) * HD + d] = O / ltot[h];
+    p.y[((size_t)g * nrep + r0 + h) * HD + d] = O / ltot[h];
   }
-  if (tid == 0) p.att_cnt[g] = 0u;
+  if (tid == 0) p.att_cnt[g * nrep + r0] = 0u;
 }
 
 // ---------------------------------------------------------------------------
@@ -646,10 +654,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       const int T = s_pos + 1;
       constexpr int per = 2 * mk_att_tile<HD>();
       const int splits = min(ATT_SPLITS, (T + per - 1) / per);
-      const int nunits = p.n_kv * splits;
+      // Short contexts: one unit per query head (more CTAs, the K/V tile is
+      // re-read from L2 by each head of a group); long contexts: one unit per
+      // KV head (every K/V byte read once).
+      const int nrep = p.n_head / p.n_kv;
+      const int hpu = T <= MK_ATT_PER_HEAD_MAX_T ? 1 : nrep, hsplit = nrep / hpu;
+      const int nunits = p.n_kv * hsplit * splits;
       float* asm_ = reinterpret_cast<float*>(smem + p.off_att);
-      for (int u = blockIdx.x; u < nunits; u += gridDim.x)
-        mk_attn_unit<HD, KV>(p, ph, u / splits, u % splits, splits, T, asm_, cw, lane);
+      for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+        const int hu = u / splits;  // head unit: (KV head, first query head of the unit)
+        mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane);
+      }
     } else {
       mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n);
       if (ctid == 0) mk_stamp(p, i, 1);

@@ -22,6 +22,13 @@ __device__ __forceinline__ float h2f(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }
 
+// dp4a with unsigned bytes in a and signed bytes in b.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -157,12 +164,15 @@ __device__ __forceinline__ void q4k_quarter(const uint8_t* blk, int t, const Act
   const int4 qb = *reinterpret_cast<const int4*>(blk + 32 + 32 * t);
   const uint32_t w[8] = {(uint32_t)qa.x, (uint32_t)qa.y, (uint32_t)qa.z, (uint32_t)qa.w,
                          (uint32_t)qb.x, (uint32_t)qb.y, (uint32_t)qb.z, (uint32_t)qb.w};
-  int dlo = 0, dhi = 0;
+  // High nibbles stay in place (q << 4, u8) against signed activations:
+  // the sum is exactly 16x the sub-block dot, one shift-free mask per word.
+  int dlo = 0, dhi16 = 0;
 #pragma unroll
   for (int i = 0; i < 8; i++) {
     dlo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), (int)A.q[i], dlo);
-    dhi = __dp4a((int)((w[i] >> 4) & 0x0F0F0F0Fu), (int)A.q[8 + i], dhi);
+    dhi16 = dp4a_us(w[i] & 0xF0F0F0F0u, A.q[8 + i], dhi16);
   }
+  const int dhi = dhi16 >> 4;
   // 12 scale bytes s[0..11] live in words hd.y (s0..3), hd.z (s4..7), hd.w (s8..11).
   // All eight 6-bit scales / mins, one per byte (get_scale_min_k4 in word form):
   //   sc0..3 = s0..3 & 63            sc4..7 = (s8..11 & 15) | (s0..3 >> 6) << 4
