@@ -267,7 +267,8 @@ __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& p
 // passes; any further ones (K > MK_REGJ * 256 * consumer warps) are loaded
 // again in the second pass.
 __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, uint8_t* smem,
-                             ActQ8& act, int cw, int lane, float* xres, int res0, int res_n) {
+                             ActQ8& act, int cw, int lane, float* xres, int res0, int res_n,
+                             uint64_t* gbar, uint32_t gpar) {
   const int K = ph.K, nb = ph.nb;
   float* part = reinterpret_cast<float*>(smem + p.off_red) + 64;
   act.qs = reinterpret_cast<int8_t*>(smem + p.off_act_qs);
@@ -317,7 +318,9 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
     float sum2 = 0.f;
     for (int j = 0; j < nb; j++) sum2 += part[j];
     m = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)K), p.eps));
+    mk_wait(gbar, gpar, p.err);  // rmsnorm weights staged in shared memory
   }
+  const float* gs = reinterpret_cast<const float*>(smem + p.off_att);
   if (cw == 0 && lane == 0) mk_stamp(p, phase, 7);
   for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
     float vv[8];
@@ -332,8 +335,8 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
       mk_load_vals(p, ph, j, lane, vv);
     }
     if (norm) {
-      const float4* gr = reinterpret_cast<const float4*>(ph.gamma + j * QK_K + 8 * lane);
-      const float4 g0 = __ldg(gr), g1 = __ldg(gr + 1);
+      const float4* gr = reinterpret_cast<const float4*>(gs + j * QK_K + 8 * lane);
+      const float4 g0 = gr[0], g1 = gr[1];
       const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
       for (int k = 0; k < 8; k++) vv[k] = __fmul_rn(__fdiv_rn(vv[k], m), g[k]);
@@ -610,6 +613,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], MK_CW);
     }
+    mbar_init(empty + MK_MAX_NS, 1);  // rmsnorm weights staged in the attention region
     fence_mbar_init();
   }
   __syncthreads();
@@ -624,6 +628,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   const int res_n = min(res0 + p.res_per_cta, p.n_embd) - res0;
   ActQ8 act;
   int cidx = 0;
+  uint64_t* gbar = empty + MK_MAX_NS;
+  uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
   for (int i = 0; i < p.n_ph; i++) {
@@ -636,17 +642,25 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph + i);
       uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
       for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
-      const float* g = reinterpret_cast<const float*>(
-          __ldg(reinterpret_cast<const unsigned long long*>(&p.ph[i].gamma)));
-      if (g) {
-        const int nb = __ldg(&p.ph[i].nb);
-        for (int j = cw; j < nb; j += MK_CW) prefetch_l1(g + j * QK_K + 8 * lane);
-      }
     }
     if (i > 0) {
       if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
     } else {
       named_sync(1, MK_CT);
+    }
+    // Stage the rmsnorm weights of the next phase (gate/up after attn_output,
+    // q/k/v or the head after ffn_down; phase 0 its own) in the attention
+    // region, idle until then, so the prologue reads them from shared memory.
+    if (ctid == 0) {
+      const int gi = i == 0 ? 0 : ((ph.kind == PH_WO || ph.kind == PH_DOWN) && i + 1 < p.n_ph ? i + 1 : -1);
+      const float* g = gi < 0 ? nullptr : reinterpret_cast<const float*>(
+                                              __ldg(reinterpret_cast<const unsigned long long*>(&p.ph[gi].gamma)));
+      if (g) {
+        const uint32_t bytes = (uint32_t)__ldg(&p.ph[gi].K) * 4u;
+        fence_proxy_async();
+        mbar_expect_tx(gbar, bytes);
+        bulk_g2s(smem + p.off_att, g, bytes, gbar, l2_evict_first_policy());
+      }
     }
     if (ctid == 0) mk_stamp(p, i, 0);
     if (ph.kind == PH_ATTN) {
@@ -666,7 +680,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
         mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane);
       }
     } else {
-      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n);
+      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n, gbar, gcount & 1u);
+      if (ph.gamma) gcount++;
       if (ctid == 0) mk_stamp(p, i, 1);
       const int mode = mode_of(ph.kind);
       bool ok;

@@ -422,15 +422,16 @@ int setup_mega(armai_llama* m, int nsm) {
   std::memset(&k, 0, sizeof k);
   size_t o = 0;
   const int nrep = m->n_head / m->n_head_kv;
-  const size_t att_bytes = mk_att_floats(m->head_dim, nrep) * 4 + 64;
-  size_t fixed = al16((size_t)2 * MK_MAX_NS * 8) + al16((size_t)kmax) + al16((size_t)kmax / QK_K * 4) +
+  // the attention region also holds the staged rmsnorm weights (n_embd f32)
+  const size_t att_bytes = std::max(mk_att_floats(m->head_dim, nrep) * 4, (size_t)m->n_embd * 4) + 64;
+  size_t fixed = al16((size_t)(2 * MK_MAX_NS + 1) * 8) + al16((size_t)kmax) + al16((size_t)kmax / QK_K * 4) +
                  al16((size_t)kmax / 16 * 4) + al16((64 + (size_t)kmax / QK_K + 8) * 4) + al16(att_bytes);
   // 2 KB of headroom for the kernel's static shared memory (phase copies etc.)
   int ns = (int)std::min<size_t>(MK_MAX_NS, (SMEM_LIMIT - fixed - 2048) / MK_STAGE);
   if (ns < 2) return fail(ARMAI_E_INVALID, "persistent decode kernel: not enough shared memory");
   k.ns = ns;
   o = (size_t)ns * MK_STAGE;
-  k.off_bars = o;   o += al16((size_t)2 * MK_MAX_NS * 8);
+  k.off_bars = o;   o += al16((size_t)(2 * MK_MAX_NS + 1) * 8);
   k.off_act_qs = o; o += al16((size_t)kmax);
   k.off_act_d = o;  o += al16((size_t)kmax / QK_K * 4);
   k.off_act_bs = o; o += al16((size_t)kmax / 16 * 4);
