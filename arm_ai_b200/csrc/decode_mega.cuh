@@ -52,7 +52,13 @@ struct MkPhase {
   float* out;         // q (QKV), x (WO, DOWN), h (GATEUP), logits (HEAD)
   void* kc;           // layer KV cache
   void* vc;
+  // tensor parallelism: attn_output / ffn_down write residual version
+  // tp_res >= 1 into the ranks' slots; a phase with tp_in >= 1 reads x as
+  // x(tp_in - 1) + the ranks' slots of version tp_in (0: not involved)
+  int tp_res, tp_in;
 };
+
+constexpr int MK_TP_MAX = 8;
 
 struct MkParams {
   const MkPhase* ph;
@@ -81,6 +87,16 @@ struct MkParams {
   size_t off_bars, off_act_qs, off_act_d, off_act_bs, off_red, off_att;  // smem layout
   int kmax;
   int res_per_cta;  // rows per CTA of attn_output / ffn_down (same split)
+  // ---- tensor parallelism (tp > 1) over peer memory (CUDA IPC mappings) ----
+  int tp, tp_rank, v0;                  // v0: first vocab row of this rank
+  float* xslot[MK_TP_MAX];              // rank k's slots [2][tp][E] (own rank included)
+  float* xbuf;                          // [2][E] residual stream, by version parity
+  unsigned long long* xbar[MK_TP_MAX];  // rank k's cross-rank barrier counter
+  uint32_t* hslot[MK_TP_MAX];           // rank k's head winners [2][tp][2]
+  unsigned long long* hctr[MK_TP_MAX];  // rank k's head counter
+  int me_slot;                          // index of this rank in the arrays above (= tp_rank)
+  unsigned long long* epoch;            // decode steps this rank completed
+  int xbars_per_step;
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -113,6 +129,28 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
 __device__ __forceinline__ void red_release_add(unsigned* p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void red_release_sys_add64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *ctr >= target (system scope); false (and the error flag)
+// when it gives up.
+__device__ __forceinline__ bool wait_ge_sys(const unsigned long long* ctr, unsigned long long target, uint32_t* err) {
+  for (uint32_t it = 0;; ++it) {
+    if (ld_acquire_sys_u64(ctr) >= target) return true;
+    if (it > 32) __nanosleep(64);
+    if ((it & 255) == 0 && *reinterpret_cast<const volatile uint32_t*>(err) != 0u) return false;
+    if (it > MK_BAR_LIMIT) { atomicOr(err, DEVERR_COUNTER_TIMEOUT); return false; }
+  }
+}
+
 __device__ __forceinline__ bool dev_failed(const uint32_t* err) {
   return *reinterpret_cast<const volatile uint32_t*>(err) != 0u;
 }
@@ -251,7 +289,21 @@ __device__ __forceinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, 
 // stores it as the residual stream x).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8]) {
-  if (ph.in) {
+  if (ph.tp_in > 0) {
+    // x(v) = x(v - 1) + sum over ranks of their version-v slots, in rank order
+    const int v = ph.tp_in, E = p.n_embd;
+    const float4* xo = reinterpret_cast<const float4*>(p.xbuf + (size_t)((v - 1) & 1) * E + j * QK_K + 8 * lane);
+    float4 a = __ldcg(xo), b = __ldcg(xo + 1);
+    const float* sl = p.xslot[p.me_slot] + (size_t)(v & 1) * p.tp * E + j * QK_K + 8 * lane;
+    for (int k = 0; k < p.tp; k++) {
+      const float4 c = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)k * E));
+      const float4 d = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)k * E) + 1);
+      a.x = __fadd_rn(a.x, c.x); a.y = __fadd_rn(a.y, c.y); a.z = __fadd_rn(a.z, c.z); a.w = __fadd_rn(a.w, c.w);
+      b.x = __fadd_rn(b.x, d.x); b.y = __fadd_rn(b.y, d.y); b.z = __fadd_rn(b.z, d.z); b.w = __fadd_rn(b.w, d.w);
+    }
+    vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
+    vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
+  } else if (ph.in) {
     const float4* xr = reinterpret_cast<const float4*>(ph.in + j * QK_K + 8 * lane);
     const float4 x0 = __ldcg(xr), x1 = __ldcg(xr + 1);
     vv[0] = x0.x; vv[1] = x0.y; vv[2] = x0.z; vv[3] = x0.w;
@@ -292,7 +344,19 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
     } else {
       mk_load_vals(p, ph, j, lane, vv);
     }
-    if (!ph.in) {
+    if (ph.tp_in > 0 || (p.tp > 1 && !ph.in)) {
+      // tensor parallel: x(v) of this CTA's rows into its shared copy and the
+      // version's buffer (read back, whole, by the next residual fold)
+      const int v = ph.tp_in;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int e = j * QK_K + 8 * lane + k - res0;
+        if (e >= 0 && e < res_n) {
+          xres[e] = vv[k];
+          p.xbuf[(size_t)(v & 1) * p.n_embd + res0 + e] = vv[k];
+        }
+      }
+    } else if (!ph.in) {
       // token embedding = initial residual stream: keep this CTA's rows
 #pragma unroll
       for (int k = 0; k < 8; k++) {
@@ -373,6 +437,11 @@ struct MkCtx {
   // x[r] += v on the CTA's own copy of its rows; the global x is only
   // written (for the other CTAs' next prologue), never read back here.
   __device__ void resid_add(float* o, int r, float v) const {
+    if (ph.tp_res > 0) {  // this rank's part of the sum, to every rank's slot
+      const size_t off = ((size_t)((ph.tp_res & 1) * p.tp + p.tp_rank)) * p.n_embd + r;
+      for (int k = 0; k < p.tp; k++) p.xslot[k][off] = v;
+      return;
+    }
     const float nv = __fadd_rn(v, xres[r - res0]);
     xres[r - res0] = nv;
     *o = nv;
@@ -630,6 +699,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   int cidx = 0;
   uint64_t* gbar = empty + MK_MAX_NS;
   uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
+  // tensor parallelism: cross-rank barriers after each row-split phase; the
+  // counters only grow, this step's targets start after the previous steps'
+  const unsigned long long xb_base =
+      p.tp > 1 ? __ldcg(p.epoch) * (unsigned long long)p.xbars_per_step * p.tp * gridDim.x : 0ull;
+  int xb_idx = 0;
+  bool prev_tp_res = false;
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
   for (int i = 0; i < p.n_ph; i++) {
@@ -643,7 +718,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
       for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
     }
-    if (i > 0) {
+    if (i > 0 && prev_tp_res) {
+      // every CTA of every rank has written its slots of the residual version
+      const unsigned long long target = xb_base + (unsigned long long)(++xb_idx) * p.tp * gridDim.x;
+      if (ctid == 0) s_flag = wait_ge_sys(p.xbar[p.me_slot], target, p.err) ? 1 : 0;
+      named_sync(1, MK_CT);
+      if (!s_flag) return;
+    } else if (i > 0) {
       if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
     } else {
       named_sync(1, MK_CT);
@@ -692,7 +773,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       if (!ok) return;
     }
     if (ctid == 0) mk_stamp(p, i, 2);
-    if (i + 1 < p.n_ph) mk_arrive(p, ctid);
+    prev_tp_res = ph.tp_res > 0;
+    if (i + 1 < p.n_ph) {
+      mk_arrive(p, ctid);  // bar.sync inside: the CTA's slot stores precede the release below
+      if (prev_tp_res && ctid == 0)
+        for (int k = 0; k < p.tp; k++) red_release_sys_add64(p.xbar[k], 1ull);
+    }
   }
   // HEAD: CTA argmax partial, the last CTA reduces all partials.
   float* rv = reinterpret_cast<float*>(smem + p.off_red);
@@ -726,6 +812,30 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
       if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0 && p.tp > 1) {
+      // every rank's winner (value, global row) to every rank, then the
+      // reference's order: larger value, then smaller row; NaN never wins
+      const unsigned long long ep = __ldcg(p.epoch);
+      const size_t base = (size_t)(ep & 1) * p.tp * 2;
+      for (int k = 0; k < p.tp; k++) {
+        uint32_t* hs = p.hslot[k] + base + (size_t)p.tp_rank * 2;
+        hs[0] = __float_as_uint(bv);
+        hs[1] = bi == 0x7fffffff ? 0xffffffffu : (uint32_t)(bi + p.v0);
+      }
+      for (int k = 0; k < p.tp; k++) red_release_sys_add64(p.hctr[k], 1ull);
+      float gv = -INFINITY;
+      uint32_t gi = 0xffffffffu;
+      if (wait_ge_sys(p.hctr[p.me_slot], (ep + 1) * (unsigned long long)p.tp, p.err)) {
+        const uint32_t* hs = p.hslot[p.me_slot] + base;
+        for (int r = 0; r < p.tp; r++) {
+          const float v = __uint_as_float(hs[2 * r]);
+          const uint32_t ix = hs[2 * r + 1];
+          if (ix != 0xffffffffu && (gi == 0xffffffffu || v > gv || (v == gv && ix < gi))) { gv = v; gi = ix; }
+        }
+      }
+      bi = gi == 0xffffffffu ? 0x7fffffff : (int)gi;
+      *p.epoch = ep + 1;
     }
     if (lane == 0) {
       *p.token = (bi == 0x7fffffff) ? 0u : (uint32_t)bi;

@@ -106,6 +106,10 @@ struct armai_llama {
   uint32_t* tp_send = nullptr;   // 2 words: winner bits, global row
   uint32_t* tp_recv = nullptr;   // 2 * tp words
   float* logits_all = nullptr;   // [tp * v_stride] gathered logits
+  void* xchg = nullptr;          // persistent kernel: this rank's exchange area (IPC-shared)
+  void* peer_xchg[8] = {};       // the other ranks' exchange areas, mapped here
+  float* xbuf = nullptr;         // [2][E] residual stream of the persistent kernel
+  void* epoch = nullptr;         // decode steps completed (persistent kernel)
   // pinned host staging
   uint32_t* h_tok = nullptr;   // ring of 8 token slots
   int* h_misc = nullptr;       // small pinned scratch
@@ -358,6 +362,58 @@ cudaError_t launch_mega(armai_llama* m) {
                    : cudaLaunchKernelEx(&cfg, k_decode_mega<128, float>, m->mk);
 }
 
+// Tensor parallelism in the persistent kernel: each rank's exchange area
+// (cross-rank barrier counter, head counter, head winners, residual slots) is
+// shared with the other ranks through CUDA IPC; the handles travel by one
+// NCCL all-gather.
+constexpr size_t XCHG_SLOTS_OFF = 512;
+int setup_peer_exchange(armai_llama* m, MkParams& k) {
+  if (m->tp > MK_TP_MAX) return fail(ARMAI_E_INVALID, "tensor parallel: at most 8 ranks");
+  const size_t E = m->n_embd;
+  const size_t bytes = XCHG_SLOTS_OFF + 2 * (size_t)m->tp * E * 4;
+  ARMAI_CUDA(cudaMalloc(&m->xchg, bytes));
+  ARMAI_CUDA(cudaMemset(m->xchg, 0, bytes));
+  ARMAI_CUDA(cudaMalloc(&m->xbuf, 2 * E * 4));
+  ARMAI_CUDA(cudaMalloc(&m->epoch, 64));
+  ARMAI_CUDA(cudaMemset(m->epoch, 0, 64));
+  cudaIpcMemHandle_t mine;
+  ARMAI_CUDA(cudaIpcGetMemHandle(&mine, m->xchg));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  void* dh = nullptr;
+  ARMAI_CUDA(cudaMalloc(&dh, (size_t)m->tp * 64));
+  std::vector<cudaIpcMemHandle_t> all(m->tp);
+  int rc = ARMAI_OK;
+  cudaError_t e = cudaMemcpyAsync((uint8_t*)dh + (size_t)m->tp_rank * 64, &mine, 64, cudaMemcpyHostToDevice, m->stream);
+  if (e == cudaSuccess)
+    rc = nccl_allgather_b32((uint8_t*)dh + (size_t)m->tp_rank * 64, dh, 16, m->comm, m->stream);
+  if (e == cudaSuccess && rc == ARMAI_OK)
+    e = cudaMemcpyAsync(all.data(), dh, (size_t)m->tp * 64, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess && rc == ARMAI_OK) e = cudaStreamSynchronize(m->stream);
+  cudaFree(dh);
+  if (rc != ARMAI_OK) return rc;
+  if (e != cudaSuccess) return cuda_fail(e, "exchange of IPC handles", __FILE__, __LINE__);
+  for (int r = 0; r < m->tp; r++) {
+    uint8_t* base = nullptr;
+    if (r == m->tp_rank) {
+      base = (uint8_t*)m->xchg;
+    } else {
+      void* pr = nullptr;
+      ARMAI_CUDA(cudaIpcOpenMemHandle(&pr, all[r], cudaIpcMemLazyEnablePeerAccess));
+      m->peer_xchg[r] = pr;
+      base = (uint8_t*)pr;
+    }
+    k.xbar[r] = reinterpret_cast<unsigned long long*>(base);
+    k.hctr[r] = reinterpret_cast<unsigned long long*>(base + 128);
+    k.hslot[r] = reinterpret_cast<uint32_t*>(base + 256);
+    k.xslot[r] = reinterpret_cast<float*>(base + XCHG_SLOTS_OFF);
+  }
+  k.me_slot = m->tp_rank;
+  k.xbuf = m->xbuf;
+  k.epoch = reinterpret_cast<unsigned long long*>(m->epoch);
+  k.xbars_per_step = 2 * m->n_layer;
+  return ARMAI_OK;
+}
+
 // Phase list and shared-memory layout of the persistent decode kernel.
 int setup_mega(armai_llama* m, int nsm) {
   const int E = m->n_embd, F = m->n_ff, QN = m->n_head * m->head_dim;
@@ -395,6 +451,7 @@ int setup_mega(armai_llama* m, int nsm) {
     }
     ph.push_back(p);
   };
+  const bool tpx = m->tp > 1;
   for (int l = 0; l < m->n_layer; l++) {
     const Layer& L = m->layers[l];
     const int qkv_rb = std::max(L.wq.row_bytes, std::max(L.wk.row_bytes, L.wv.row_bytes));
@@ -407,12 +464,17 @@ int setup_mega(armai_llama* m, int nsm) {
     a.kc = kv_layer_ptr(m, m->kc, l);
     a.vc = kv_layer_ptr(m, m->vc, l);
     ph.push_back(a);
+    if (tpx && l > 0) ph[ph.size() - 2].tp_in = 2 * l;  // this layer's q/k/v folds in ffn_down of the last
     mat_phase(PH_WO, l, {&L.wo}, L.wo.rows, 1, L.wo.row_bytes, QN, nullptr, m->y, m->x);
+    if (tpx) ph.back().tp_res = 2 * l + 1;
     mat_phase(PH_GATEUP, l, {&L.wg, &L.wu}, L.wg.rows, 1, L.wg.row_bytes + L.wu.row_bytes, E, L.ffn_norm, m->x,
               m->h);
+    if (tpx) ph.back().tp_in = 2 * l + 1;
     mat_phase(PH_DOWN, l, {&L.wd}, L.wd.rows, 1, L.wd.row_bytes, F, nullptr, m->h, m->x);
+    if (tpx) ph.back().tp_res = 2 * l + 2;
   }
   mat_phase(PH_HEAD, -1, {&m->output}, m->output.rows, 1, m->output.row_bytes, E, m->out_norm, m->x, m->logits);
+  if (tpx) ph.back().tp_in = 2 * m->n_layer;
   ARMAI_CUDA(cudaMalloc(&m->d_phases, ph.size() * sizeof(MkPhase)));
   ARMAI_CUDA(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
   ARMAI_CUDA(cudaMalloc(&m->gbar, 64));
@@ -452,6 +514,10 @@ int setup_mega(armai_llama* m, int nsm) {
     return fail(ARMAI_E_INVALID, "persistent decode kernel: " + std::to_string(res_per) +
                                      " residual rows per CTA exceed " + std::to_string(MK_MAX_RES));
   k.res_per_cta = res_per;
+  k.tp = m->tp;
+  k.tp_rank = m->tp_rank;
+  k.v0 = m->v0;
+  if (m->tp > 1) ARMAI_TRY(setup_peer_exchange(m, k));
   k.ph = m->d_phases;
   k.n_ph = (int)ph.size();
   k.embd = m->tok_embd.w;
@@ -889,12 +955,23 @@ void free_model(armai_llama* m) {
   cudaSetDevice(m->device);
   if (m->stream) cudaStreamSynchronize(m->stream);
   if (m->graph) cudaGraphExecDestroy(m->graph);  // before the NCCL communicator it may hold
+  if (m->comm && m->xchg) {
+    // no rank may still write into this rank's exchange area: meet first
+    float* one = nullptr;
+    if (cudaMalloc(&one, 4) == cudaSuccess) {
+      nccl_allreduce_sum_f32(one, one, 1, m->comm, m->stream);
+      cudaStreamSynchronize(m->stream);
+      cudaFree(one);
+    }
+  }
+  for (void* pp : m->peer_xchg)
+    if (pp) cudaIpcCloseMemHandle(pp);
   if (m->comm) nccl_comm_destroy(m->comm);
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
                    m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar,
                    m->pA, m->pG, m->tp_part, m->best_val, m->best_idx, m->tp_send, m->tp_recv,
-                   m->logits_all};
+                   m->logits_all, m->xchg, m->xbuf, m->epoch};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }
@@ -955,7 +1032,8 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
       return fail(ARMAI_E_INVALID, "tensor parallel: prompts run the GEMM path and batches are not sharded "
                                    "(prefill_gemm 1 and max_batch > 1 are not available with tp_size > 1)");
     }
-    m->use_mega = false;  // per-kernel chain with NCCL between the row-split matvecs
+    // decode: the persistent kernel sums the row-split products through peer
+    // memory (decode_kernel 0), or the per-kernel chain through NCCL (1)
     m->use_pdl = false;
     m->prefill_gemm = 2;
   }

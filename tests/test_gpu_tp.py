@@ -33,16 +33,20 @@ def _rank(rank, world, port, path, prompt, q):
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")  # plain NVLink transfers, no multicast objects
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
-        uid = tp.share_unique_id(rank)
-        gpu = tp.load_tp(path, rank, world, rank, uid)
-        lg, tok = native.llama_forward(gpu, prompt, 0)
-        toks = native.llama_candle_generate_op(gpu, prompt, 24, [])[0]
-        long_prompt = list(prompt) * 8  # 104 tokens: the GEMM prefill path
-        lg2, _ = native.llama_forward(gpu, long_prompt, 0)
-        gpu.close()
-        q.put((rank, np.asarray(lg), tok, toks, np.asarray(lg2)))
+        out = []
+        for kernel in (0, 1):  # persistent kernel (peer memory), per-kernel chain (NCCL)
+            uid = tp.share_unique_id(rank)
+            gpu = tp.load_tp(path, rank, world, rank, uid, decode_kernel=kernel)
+            lg, tok = native.llama_forward(gpu, prompt, 0)
+            lg1, _ = native.llama_forward(gpu, [77], len(prompt))  # one decode step's logits
+            toks = native.llama_candle_generate_op(gpu, prompt, 24, [])[0]
+            long_prompt = list(prompt) * 8  # 104 tokens: the GEMM prefill path
+            lg2, _ = native.llama_forward(gpu, long_prompt, 0)
+            gpu.close()
+            out.append((np.asarray(lg), tok, toks, np.asarray(lg1), np.asarray(lg2)))
+        q.put((rank, out))
     except Exception as e:  # report instead of hanging the other rank
-        q.put((rank, repr(e), None, None, None))
+        q.put((rank, repr(e)))
     finally:
         dist.destroy_process_group()
 
@@ -72,10 +76,14 @@ def test_tp2_matches_oracle(small_model):
     bound = flip_bound(small_model, lengths=(16, 24, 64, 100, 128))
     orc = ref.OracleLlama(small_model)
     lo = orc.forward(prompt, 0)
-    for _, lg, tok, toks, lg2 in res:
-        assert rel_maxabs(lg, lo) < bound
-        assert greedy_consistent(small_model, prompt, toks, tol=2 * bound) is None
+    lo1 = orc.forward([77], len(prompt))
     lo2 = ref.OracleLlama(small_model).forward(list(prompt) * 8, 0)
-    assert rel_maxabs(res[0][4], lo2) < 1.5 * bound  # GEMM prefill: f16 operands
-    assert res[0][3] == res[1][3]
-    assert res[0][2] == res[1][2]
+    for kernel in (0, 1):
+        for _, out in res:
+            lg, tok, toks, lg1, lg2 = out[kernel]
+            assert rel_maxabs(lg, lo) < bound, kernel
+            assert rel_maxabs(lg1, lo1) < bound, kernel
+            assert greedy_consistent(small_model, prompt, toks, tol=2 * bound) is None, kernel
+            assert rel_maxabs(lg2, lo2) < 1.5 * bound, kernel  # GEMM prefill: f16 operands
+        assert res[0][1][kernel][2] == res[1][1][kernel][2]  # both ranks decode the same tokens
+        assert res[0][1][kernel][1] == res[1][1][kernel][1]
