@@ -702,7 +702,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   // tensor parallelism: cross-rank barriers after each row-split phase; the
   // counters only grow, this step's targets start after the previous steps'
   const unsigned long long xb_base =
-      p.tp > 1 ? __ldcg(p.epoch) * (unsigned long long)p.xbars_per_step * p.tp * gridDim.x : 0ull;
+      p.tp > 1 ? __ldcg(p.epoch) * (unsigned long long)p.xbars_per_step * p.tp : 0ull;
   int xb_idx = 0;
   bool prev_tp_res = false;
   float best_v = -INFINITY;
@@ -719,9 +719,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
     }
     if (i > 0 && prev_tp_res) {
-      // every CTA of every rank has written its slots of the residual version
-      const unsigned long long target = xb_base + (unsigned long long)(++xb_idx) * p.tp * gridDim.x;
-      if (ctid == 0) s_flag = wait_ge_sys(p.xbar[p.me_slot], target, p.err) ? 1 : 0;
+      // Cross-rank barrier: once every CTA of this rank has written its slots
+      // (local grid barrier), CTA 0 tells every rank with one system-scope
+      // fence and one increment each; all CTAs wait for all ranks.
+      if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
+      const unsigned long long target = xb_base + (unsigned long long)(++xb_idx) * p.tp;
+      if (ctid == 0) {
+        if (blockIdx.x == 0) {
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          for (int k = 0; k < p.tp; k++)
+            asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p.xbar[k]) : "memory");
+        }
+        s_flag = wait_ge_sys(p.xbar[p.me_slot], target, p.err) ? 1 : 0;
+      }
       named_sync(1, MK_CT);
       if (!s_flag) return;
     } else if (i > 0) {
@@ -774,11 +784,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
     }
     if (ctid == 0) mk_stamp(p, i, 2);
     prev_tp_res = ph.tp_res > 0;
-    if (i + 1 < p.n_ph) {
-      mk_arrive(p, ctid);  // bar.sync inside: the CTA's slot stores precede the release below
-      if (prev_tp_res && ctid == 0)
-        for (int k = 0; k < p.tp; k++) red_release_sys_add64(p.xbar[k], 1ull);
-    }
+    if (i + 1 < p.n_ph) mk_arrive(p, ctid);
   }
   // HEAD: CTA argmax partial, the last CTA reduces all partials.
   float* rv = reinterpret_cast<float*>(smem + p.off_red);
