@@ -89,14 +89,14 @@ struct MkParams {
   int res_per_cta;  // rows per CTA of attn_output / ffn_down (same split)
   // ---- tensor parallelism (tp > 1) over peer memory (CUDA IPC mappings) ----
   int tp, tp_rank, v0;                  // v0: first vocab row of this rank
-  float* xslot[MK_TP_MAX];              // rank k's slots [2][tp][E] (own rank included)
+  unsigned long long* xslot[MK_TP_MAX]; // rank k's slots [2][tp][E]: generation | value bits << 32
   float* xbuf;                          // [2][E] residual stream, by version parity
   unsigned long long* xbar[MK_TP_MAX];  // rank k's cross-rank barrier counter
   uint32_t* hslot[MK_TP_MAX];           // rank k's head winners [2][tp][2]
   unsigned long long* hctr[MK_TP_MAX];  // rank k's head counter
   int me_slot;                          // index of this rank in the arrays above (= tp_rank)
   unsigned long long* epoch;            // decode steps this rank completed
-  int xbars_per_step;
+  int xbars_per_step;                   // residual versions per step (generation stride)
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -288,19 +288,61 @@ __device__ __forceinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, 
 // Layer 0's QKV reads the token's embedding row (dequantised here; CTA 0 also
 // stores it as the residual stream x).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8]) {
+// A residual slot element is one 64-bit word: generation tag (low half),
+// value bits (high half), stored by one single-copy-atomic 64-bit store, so
+// a reader that sees the tag sees the value stored with it.
+__device__ __forceinline__ unsigned long long slot_word(uint32_t tag, float v) {
+  return (unsigned long long)tag | ((unsigned long long)__float_as_uint(v) << 32);
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Two slot words; each is read atomically (a vector access is a pair of
+// 64-bit accesses, each of which is atomic).
+__device__ __forceinline__ void ld_relaxed_sys_2u64(const unsigned long long* p, unsigned long long& a,
+                                                    unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Eight consecutive slot words of one rank (this lane's 8 elements).
+__device__ __forceinline__ void ld_slot8(const unsigned long long* p, unsigned long long (&w)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) ld_relaxed_sys_2u64(p + e, w[e], w[e + 1]);
+}
+__device__ __forceinline__ bool slot8_ready(const unsigned long long (&w)[8], uint32_t want) {
+  bool ok = true;
+#pragma unroll
+  for (int e = 0; e < 8; e++) ok &= (uint32_t)w[e] == want;
+  return ok;
+}
+
+__device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8],
+                                             uint32_t gen_base) {
   if (ph.tp_in > 0) {
     // x(v) = x(v - 1) + sum over ranks of their version-v slots, in rank order
     const int v = ph.tp_in, E = p.n_embd;
     const float4* xo = reinterpret_cast<const float4*>(p.xbuf + (size_t)((v - 1) & 1) * E + j * QK_K + 8 * lane);
     float4 a = __ldcg(xo), b = __ldcg(xo + 1);
-    const float* sl = p.xslot[p.me_slot] + (size_t)(v & 1) * p.tp * E + j * QK_K + 8 * lane;
+    // Wait until this step's generation of version v is in every rank's
+    // slots of these 8 elements (one rank's 8 words in flight at a time).
+    const unsigned long long* sl = p.xslot[p.me_slot] + (size_t)(v & 1) * p.tp * E + j * QK_K + 8 * lane;
+    const uint32_t want = gen_base + (uint32_t)v;
+    float acc[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     for (int k = 0; k < p.tp; k++) {
-      const float4 c = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)k * E));
-      const float4 d = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)k * E) + 1);
-      a.x = __fadd_rn(a.x, c.x); a.y = __fadd_rn(a.y, c.y); a.z = __fadd_rn(a.z, c.z); a.w = __fadd_rn(a.w, c.w);
-      b.x = __fadd_rn(b.x, d.x); b.y = __fadd_rn(b.y, d.y); b.z = __fadd_rn(b.z, d.z); b.w = __fadd_rn(b.w, d.w);
+      unsigned long long w[8];
+      ld_slot8(sl + (size_t)k * E, w);
+      for (uint32_t it = 0; !slot8_ready(w, want); ++it) {
+        if (it > MK_BAR_LIMIT || (((it & 255) == 255) && dev_failed(p.err))) {
+          atomicOr(p.err, DEVERR_COUNTER_TIMEOUT);
+          break;
+        }
+        __nanosleep(20);
+        ld_slot8(sl + (size_t)k * E, w);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], __uint_as_float((uint32_t)(w[e] >> 32)));
     }
+    a = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    b = make_float4(acc[4], acc[5], acc[6], acc[7]);
     vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
     vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
   } else if (ph.in) {
@@ -320,7 +362,7 @@ __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& p
 // again in the second pass.
 __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, uint8_t* smem,
                              ActQ8& act, int cw, int lane, float* xres, int res0, int res_n,
-                             uint64_t* gbar, uint32_t gpar) {
+                             uint64_t* gbar, uint32_t gpar, uint32_t gen_base) {
   const int K = ph.K, nb = ph.nb;
   float* part = reinterpret_cast<float*>(smem + p.off_red) + 64;
   act.qs = reinterpret_cast<int8_t*>(smem + p.off_act_qs);
@@ -331,7 +373,7 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
   // the register-held blocks' loads are all issued before any is used
 #pragma unroll
   for (int r = 0; r < MK_REGJ; r++)
-    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r]);
+    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r], gen_base);
   for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
     float vv[8];
     if (jj < MK_REGJ) {
@@ -342,7 +384,7 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
           for (int k = 0; k < 8; k++) vv[k] = v[r][k];
         }
     } else {
-      mk_load_vals(p, ph, j, lane, vv);
+      mk_load_vals(p, ph, j, lane, vv, gen_base);
     }
     if (ph.tp_in > 0 || (p.tp > 1 && !ph.in)) {
       // tensor parallel: x(v) of this CTA's rows into its shared copy and the
@@ -396,7 +438,7 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
           for (int k = 0; k < 8; k++) vv[k] = v[r][k];
         }
     } else {
-      mk_load_vals(p, ph, j, lane, vv);
+      mk_load_vals(p, ph, j, lane, vv, gen_base);
     }
     if (norm) {
       const float4* gr = reinterpret_cast<const float4*>(gs + j * QK_K + 8 * lane);
@@ -433,13 +475,15 @@ struct MkCtx {
   int phase;
   float* xres;  // this CTA's rows of the residual stream (shared memory)
   int res0;     // first of those rows
+  uint32_t gen_base;  // tensor parallel: slot generation of this step's version 0
   __device__ void stamp(int slot) const { mk_stamp(p, phase, slot); }
   // x[r] += v on the CTA's own copy of its rows; the global x is only
   // written (for the other CTAs' next prologue), never read back here.
   __device__ void resid_add(float* o, int r, float v) const {
-    if (ph.tp_res > 0) {  // this rank's part of the sum, to every rank's slot
+    if (ph.tp_res > 0) {  // this rank's part of the sum, to every rank's slot, tagged
       const size_t off = ((size_t)((ph.tp_res & 1) * p.tp + p.tp_rank)) * p.n_embd + r;
-      for (int k = 0; k < p.tp; k++) p.xslot[k][off] = v;
+      const unsigned long long tv = slot_word(gen_base + (uint32_t)ph.tp_res, v);
+      for (int k = 0; k < p.tp; k++) st_relaxed_sys_u64(p.xslot[k] + off, tv);
       return;
     }
     const float nv = __fadd_rn(v, xres[r - res0]);
@@ -454,6 +498,7 @@ struct MkCtx {
 // compute, hand the stage back to the producer.
 template <int MODE>
 __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, float* xres, int res0,
+                          uint32_t gen_base,
                           uint8_t* smem, uint64_t* full,
                           uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
                           float& best_v, int& best_i) {
@@ -466,7 +511,7 @@ __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int p
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
     Part parts[3];
     make_parts<MODE>(ph.seg, ph.nseg, c0, c1, parts);
-    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw,
+    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0, gen_base}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw,
                       MK_CW, lane, best_v, best_i);
     __syncwarp();
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
@@ -699,12 +744,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   int cidx = 0;
   uint64_t* gbar = empty + MK_MAX_NS;
   uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
-  // tensor parallelism: cross-rank barriers after each row-split phase; the
-  // counters only grow, this step's targets start after the previous steps'
-  const unsigned long long xb_base =
-      p.tp > 1 ? __ldcg(p.epoch) * (unsigned long long)p.xbars_per_step * p.tp : 0ull;
-  int xb_idx = 0;
-  bool prev_tp_res = false;
+  // tensor parallelism: residual slots carry a generation tag that grows by
+  // one per residual version; readers wait for the tag, no cross-rank barrier
+  const uint32_t gen_base = p.tp > 1 ? (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.xbars_per_step + 1)) : 0u;
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
   for (int i = 0; i < p.n_ph; i++) {
@@ -718,23 +760,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
       for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
     }
-    if (i > 0 && prev_tp_res) {
-      // Cross-rank barrier: once every CTA of this rank has written its slots
-      // (local grid barrier), CTA 0 tells every rank with one system-scope
-      // fence and one increment each; all CTAs wait for all ranks.
-      if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
-      const unsigned long long target = xb_base + (unsigned long long)(++xb_idx) * p.tp;
-      if (ctid == 0) {
-        if (blockIdx.x == 0) {
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          for (int k = 0; k < p.tp; k++)
-            asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(p.xbar[k]) : "memory");
-        }
-        s_flag = wait_ge_sys(p.xbar[p.me_slot], target, p.err) ? 1 : 0;
-      }
-      named_sync(1, MK_CT);
-      if (!s_flag) return;
-    } else if (i > 0) {
+    if (i > 0) {
       if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
     } else {
       named_sync(1, MK_CT);
@@ -771,19 +797,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
         mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane);
       }
     } else {
-      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n, gbar, gcount & 1u);
+      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n, gbar, gcount & 1u, gen_base);
       if (ph.gamma) gcount++;
       if (ctid == 0) mk_stamp(p, i, 1);
       const int mode = mode_of(ph.kind);
       bool ok;
-      if (mode == MODE_QKV) ok = mk_chunks<MODE_QKV>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_GATEUP) ok = mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_HEAD) ok = mk_chunks<MODE_HEAD>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else ok = mk_chunks<MODE_RESID>(p, ph, i, s_pos, s_xres, res0, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      if (mode == MODE_QKV) ok = mk_chunks<MODE_QKV>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_GATEUP) ok = mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_HEAD) ok = mk_chunks<MODE_HEAD>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else ok = mk_chunks<MODE_RESID>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
       if (!ok) return;
     }
     if (ctid == 0) mk_stamp(p, i, 2);
-    prev_tp_res = ph.tp_res > 0;
     if (i + 1 < p.n_ph) mk_arrive(p, ctid);
   }
   // HEAD: CTA argmax partial, the last CTA reduces all partials.

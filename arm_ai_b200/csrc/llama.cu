@@ -370,7 +370,7 @@ constexpr size_t XCHG_SLOTS_OFF = 512;
 int setup_peer_exchange(armai_llama* m, MkParams& k) {
   if (m->tp > MK_TP_MAX) return fail(ARMAI_E_INVALID, "tensor parallel: at most 8 ranks");
   const size_t E = m->n_embd;
-  const size_t bytes = XCHG_SLOTS_OFF + 2 * (size_t)m->tp * E * 4;
+  const size_t bytes = XCHG_SLOTS_OFF + 2 * (size_t)m->tp * E * 8;  // (generation, value) pairs
   ARMAI_CUDA(cudaMalloc(&m->xchg, bytes));
   ARMAI_CUDA(cudaMemset(m->xchg, 0, bytes));
   ARMAI_CUDA(cudaMalloc(&m->xbuf, 2 * E * 4));
@@ -405,7 +405,7 @@ int setup_peer_exchange(armai_llama* m, MkParams& k) {
     k.xbar[r] = reinterpret_cast<unsigned long long*>(base);
     k.hctr[r] = reinterpret_cast<unsigned long long*>(base + 128);
     k.hslot[r] = reinterpret_cast<uint32_t*>(base + 256);
-    k.xslot[r] = reinterpret_cast<float*>(base + XCHG_SLOTS_OFF);
+    k.xslot[r] = reinterpret_cast<unsigned long long*>(base + XCHG_SLOTS_OFF);
   }
   k.me_slot = m->tp_rank;
   k.xbuf = m->xbuf;
