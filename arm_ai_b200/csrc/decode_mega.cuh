@@ -91,12 +91,11 @@ struct MkParams {
   int tp, tp_rank, v0;                  // v0: first vocab row of this rank
   unsigned long long* xslot[MK_TP_MAX]; // rank k's slots [2][tp][E]: generation | value bits << 32
   float* xbuf;                          // [2][E] residual stream, by version parity
-  unsigned long long* xbar[MK_TP_MAX];  // rank k's cross-rank barrier counter
   uint32_t* hslot[MK_TP_MAX];           // rank k's head winners [2][tp][2]
   unsigned long long* hctr[MK_TP_MAX];  // rank k's head counter
   int me_slot;                          // index of this rank in the arrays above (= tp_rank)
   unsigned long long* epoch;            // decode steps this rank completed
-  int xbars_per_step;                   // residual versions per step (generation stride)
+  int xbars_per_step;                   // residual versions per step (generation stride - 1)
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {

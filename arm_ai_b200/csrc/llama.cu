@@ -363,9 +363,9 @@ cudaError_t launch_mega(armai_llama* m) {
 }
 
 // Tensor parallelism in the persistent kernel: each rank's exchange area
-// (cross-rank barrier counter, head counter, head winners, residual slots) is
-// shared with the other ranks through CUDA IPC; the handles travel by one
-// NCCL all-gather.
+// (head counter at 128, head winners at 256, generation-tagged residual slots
+// at XCHG_SLOTS_OFF) is shared with the other ranks through CUDA IPC; the
+// handles travel by one NCCL all-gather.
 constexpr size_t XCHG_SLOTS_OFF = 512;
 int setup_peer_exchange(armai_llama* m, MkParams& k) {
   if (m->tp > MK_TP_MAX) return fail(ARMAI_E_INVALID, "tensor parallel: at most 8 ranks");
@@ -376,33 +376,49 @@ int setup_peer_exchange(armai_llama* m, MkParams& k) {
   ARMAI_CUDA(cudaMalloc(&m->xbuf, 2 * E * 4));
   ARMAI_CUDA(cudaMalloc(&m->epoch, 64));
   ARMAI_CUDA(cudaMemset(m->epoch, 0, 64));
-  cudaIpcMemHandle_t mine;
-  ARMAI_CUDA(cudaIpcGetMemHandle(&mine, m->xchg));
-  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  // Per rank: its IPC handle (64 B) and its GPU's UUID (16 B), all-gathered.
+  struct Rec {
+    cudaIpcMemHandle_t h;
+    cudaUUID_t uuid;
+  };
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64 && sizeof(Rec) == 80, "exchange record");
+  Rec mine;
+  ARMAI_CUDA(cudaIpcGetMemHandle(&mine.h, m->xchg));
+  cudaDeviceProp prop;
+  ARMAI_CUDA(cudaGetDeviceProperties(&prop, m->device));
+  mine.uuid = prop.uuid;
   void* dh = nullptr;
-  ARMAI_CUDA(cudaMalloc(&dh, (size_t)m->tp * 64));
-  std::vector<cudaIpcMemHandle_t> all(m->tp);
+  ARMAI_CUDA(cudaMalloc(&dh, (size_t)m->tp * sizeof(Rec)));
+  std::vector<Rec> all(m->tp);
   int rc = ARMAI_OK;
-  cudaError_t e = cudaMemcpyAsync((uint8_t*)dh + (size_t)m->tp_rank * 64, &mine, 64, cudaMemcpyHostToDevice, m->stream);
+  cudaError_t e = cudaMemcpyAsync((uint8_t*)dh + (size_t)m->tp_rank * sizeof(Rec), &mine, sizeof(Rec),
+                                  cudaMemcpyHostToDevice, m->stream);
   if (e == cudaSuccess)
-    rc = nccl_allgather_b32((uint8_t*)dh + (size_t)m->tp_rank * 64, dh, 16, m->comm, m->stream);
+    rc = nccl_allgather_b32((uint8_t*)dh + (size_t)m->tp_rank * sizeof(Rec), dh, sizeof(Rec) / 4, m->comm,
+                            m->stream);
   if (e == cudaSuccess && rc == ARMAI_OK)
-    e = cudaMemcpyAsync(all.data(), dh, (size_t)m->tp * 64, cudaMemcpyDeviceToHost, m->stream);
+    e = cudaMemcpyAsync(all.data(), dh, (size_t)m->tp * sizeof(Rec), cudaMemcpyDeviceToHost, m->stream);
   if (e == cudaSuccess && rc == ARMAI_OK) e = cudaStreamSynchronize(m->stream);
   cudaFree(dh);
   if (rc != ARMAI_OK) return rc;
   if (e != cudaSuccess) return cuda_fail(e, "exchange of IPC handles", __FILE__, __LINE__);
+  // The ranks' persistent kernels wait on one another: they must run on
+  // distinct GPUs (on one GPU nothing makes them resident at the same time).
+  for (int a = 0; a < m->tp; a++)
+    for (int b = a + 1; b < m->tp; b++)
+      if (std::memcmp(&all[a].uuid, &all[b].uuid, sizeof(cudaUUID_t)) == 0)
+        return fail(ARMAI_E_INVALID, "tensor parallel: ranks " + std::to_string(a) + " and " + std::to_string(b) +
+                                         " are on the same GPU");
   for (int r = 0; r < m->tp; r++) {
     uint8_t* base = nullptr;
     if (r == m->tp_rank) {
       base = (uint8_t*)m->xchg;
     } else {
       void* pr = nullptr;
-      ARMAI_CUDA(cudaIpcOpenMemHandle(&pr, all[r], cudaIpcMemLazyEnablePeerAccess));
+      ARMAI_CUDA(cudaIpcOpenMemHandle(&pr, all[r].h, cudaIpcMemLazyEnablePeerAccess));
       m->peer_xchg[r] = pr;
       base = (uint8_t*)pr;
     }
-    k.xbar[r] = reinterpret_cast<unsigned long long*>(base);
     k.hctr[r] = reinterpret_cast<unsigned long long*>(base + 128);
     k.hslot[r] = reinterpret_cast<uint32_t*>(base + 256);
     k.xslot[r] = reinterpret_cast<unsigned long long*>(base + XCHG_SLOTS_OFF);

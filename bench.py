@@ -252,9 +252,11 @@ def run_config2(d):
 
 def run_config4(d, peak):
     """Llama-3-8B-architecture Q4_K_M, b = 1, 1024-token
-    seeded prompt, 128 new tokens, tensor-parallel over the N ranks (NCCL
-    all-reduce after attn_output and ffn_down; N = 1 runs the persistent
-    kernel). Decode device-timed (CUDA events, max over ranks)."""
+    seeded prompt, 128 new tokens, tensor-parallel over the N ranks: decode
+    by the persistent kernel, whose attn_output / ffn_down partial sums cross
+    NVLink as generation-tagged peer-memory stores; prefill by the tensor-core
+    GEMMs with NCCL all-reduces. Decode device-timed (CUDA events, max over
+    ranks)."""
     from arm_ai_b200 import native, synth, tp
     arch = "llama-3-8b"
     if d.rank == 0:
@@ -283,7 +285,7 @@ def run_config4(d, peak):
     bytes_gpu = info.weight_bytes + kv_row * (1024 + 1024 + n_dec) / 2
     gpu.close()
     return {"workload": f"{arch} Q4_K_M b=1: 1024-token prompt + {n_dec + 1} new tokens, "
-                        f"{'tensor-parallel over ' + str(d.world) + ' GPUs (NCCL all-reduce)' if d.world > 1 else '1 GPU'}",
+                        f"{'tensor-parallel over ' + str(d.world) + ' GPUs (peer-memory partial sums)' if d.world > 1 else '1 GPU'}",
             "decode_tokens_per_s": 1.0 / step_s, "ms_per_token": step_s * 1e3,
             "prefill_tokens_per_s": 1024 / pre_s,
             "weight_stream_gb_s_per_gpu": bytes_gpu / step_s / 1e9,
