@@ -4,20 +4,34 @@
 //   for each layer: QKV (+RoPE, KV append) | attention | attn_output (+residual)
 //                   | gate/up (+SiLU*up) | ffn_down (+residual)
 //   then output_norm + output head + greedy argmax.
-// Phases are separated by grid barriers (a monotonic counter in global
-// memory, release/acquire). Warp 0 is a producer: one lane walks the same
-// phase/chunk sequence as the consumers and streams every weight row this CTA
-// owns HBM -> shared memory with cp.async.bulk into a ring of stages
-// (full/empty mbarriers). It runs ahead across phase boundaries, so weight
-// traffic continues while the consumers wait at a barrier or run attention.
-// The other 15 warps are consumers: they build the Q8_K activation of the
-// phase (rmsnorm + quantisation), run the register-slice dot products on
-// the staged rows, and apply the epilogue.
+// There is no grid barrier. Every value a phase hands to the next one (q, the
+// new K/V row, the attention output y, h = silu(gate) * up, the attn_output /
+// ffn_down row sums) is a 64-bit word: a generation tag in the low half, the
+// f32 bits in the high half, written by one single-copy-atomic store. A
+// reader polls the words it needs until they carry the tag of this step's
+// producing phase (generation = step * (phases + 1) + phase + 1), so each
+// phase starts as soon as its own inputs exist. Every CTA keeps the whole
+// residual stream x in shared memory and folds the row sums of attn_output /
+// ffn_down into it itself (tensor parallelism: the sums of every rank, in
+// rank order, from slots that each rank writes into every rank's memory).
+//
+// Buffers are reused from layer to layer (q, K/V row, y, h) or by parity (row
+// sums of attn_output vs ffn_down). That is safe because every CTA owns rows
+// in every matvec phase and reads its whole input vector: a phase's output
+// can only be overwritten after every CTA has read it, since the overwriting
+// phase depends on outputs of all CTAs of a later phase.
+//
+// Warp 0 is a producer: one lane walks the same phase/chunk sequence as the
+// consumers and streams every weight row this CTA owns HBM -> shared memory
+// with cp.async.bulk into a ring of stages (full/empty mbarriers). It runs
+// ahead across phase boundaries, so weight traffic continues while the
+// consumers wait for their inputs or run attention. The other 15 warps are
+// consumers: they build the Q8_K activation of the phase (rmsnorm +
+// quantisation), run the register-slice dot products on the staged rows, and
+// apply the epilogue.
 //
 // Every wait is bounded and checks the device error word, so a stuck copy or
 // a CTA that left early ends the launch with an error instead of a hang.
-// Data written by other CTAs within the launch is read with L1-bypassing
-// loads (ld.global.cg).
 #pragma once
 
 #include "llama_kernels.cuh"
@@ -34,7 +48,6 @@ constexpr uint32_t MK_STAGE = 32 * 1024;
 constexpr int MK_MAX_NS = 6;
 constexpr uint32_t MK_BAR_LIMIT = 1u << 24;   // grid-barrier polls before giving up
 constexpr int MK_ATT_PER_HEAD_MAX_T = 512;    // attention unit per query head up to this context
-constexpr int MK_MAX_RES = 64;                // residual rows per CTA kept in shared memory
 constexpr int MK_REGJ = 2;                    // prologue blocks per warp kept in registers
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_GATEUP = 3, PH_DOWN = 4, PH_HEAD = 5 };
@@ -48,14 +61,9 @@ struct MkPhase {
   int chunk_rows;     // multiple of 2 for QKV
   int K, nb;
   const float* gamma; // rmsnorm weight, or nullptr
-  const float* in;    // activation input; nullptr on layer 0's QKV (token embedding)
-  float* out;         // q (QKV), x (WO, DOWN), h (GATEUP), logits (HEAD)
+  float* out;         // HEAD: logits (nullptr: not kept)
   void* kc;           // layer KV cache
   void* vc;
-  // tensor parallelism: attn_output / ffn_down write residual version
-  // tp_res >= 1 into the ranks' slots; a phase with tp_in >= 1 reads x as
-  // x(tp_in - 1) + the ranks' slots of version tp_in (0: not involved)
-  int tp_res, tp_in;
 };
 
 constexpr int MK_TP_MAX = 8;
@@ -66,7 +74,6 @@ struct MkParams {
   int ns;
   const uint8_t* embd;
   int embd_type, embd_row_bytes, n_embd;
-  float* x;
   const float* cos_t;
   const float* sin_t;
   int hd, n_head, n_kv, max_seq, kv_f16;
@@ -74,28 +81,29 @@ struct MkParams {
   float att_scale;
   float* att_part;
   unsigned* att_cnt;
-  float* q;
-  float* y;
+  // tagged words (see the top of this file)
+  unsigned long long* fq;   // [n_head * hd] RoPE'd q
+  unsigned long long* fkv;  // [2][n_kv][hd] this step's K and V rows (as the cache holds them)
+  unsigned long long* fy;   // [n_head * hd] attention output
+  unsigned long long* fh;   // [n_ff] silu(gate) * up
   float* am_val;
   int* am_idx;
   unsigned* am_cnt;
   uint32_t* token;
   int* pos;
-  unsigned* gbar;
   uint32_t* err;
   unsigned long long* trace;  // nullptr, or [n_ph][grid][MK_TRACE_SLOTS] globaltimer stamps
   size_t off_bars, off_act_qs, off_act_d, off_act_bs, off_red, off_att;  // smem layout
   int kmax;
-  int res_per_cta;  // rows per CTA of attn_output / ffn_down (same split)
-  // ---- tensor parallelism (tp > 1) over peer memory (CUDA IPC mappings) ----
+  size_t off_xrep;  // smem: this CTA's copy of the residual stream x [n_embd]
+  unsigned long long* epoch;            // decode steps completed (generation base)
+  // Row sums of attn_output (parity 1) / ffn_down (parity 0): rank k's slots
+  // [2][tp][n_embd]; tp = 1 is one local array. Tensor parallelism maps the
+  // other ranks' arrays through CUDA IPC.
   int tp, tp_rank, v0;                  // v0: first vocab row of this rank
-  unsigned long long* xslot[MK_TP_MAX]; // rank k's slots [2][tp][E]: generation | value bits << 32
-  float* xbuf;                          // [2][E] residual stream, by version parity
-  uint32_t* hslot[MK_TP_MAX];           // rank k's head winners [2][tp][2]
-  unsigned long long* hctr[MK_TP_MAX];  // rank k's head counter
-  int me_slot;                          // index of this rank in the arrays above (= tp_rank)
-  unsigned long long* epoch;            // decode steps this rank completed
-  int xbars_per_step;                   // residual versions per step (generation stride - 1)
+  unsigned long long* xslot[MK_TP_MAX];
+  uint32_t* hslot[MK_TP_MAX];           // rank k's head winners [2][tp][2] (tp > 1)
+  unsigned long long* hctr[MK_TP_MAX];  // rank k's head counter (tp > 1)
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -183,9 +191,15 @@ __device__ __forceinline__ int mode_of(int kind) {
                                                                                      : MODE_RESID;
 }
 
+// Rows [r0, r1) of this CTA: the phase's units (QKV: RoPE pairs of rows,
+// else single rows) split as evenly as possible over the grid. The grid is
+// no larger than the smallest phase's unit count, so every CTA owns rows in
+// every matvec phase (which the buffer reuse relies on).
 __device__ __forceinline__ void phase_rows(const MkPhase& ph, int& r0, int& r1) {
-  r0 = min((int)blockIdx.x * ph.rows_per_cta, ph.total_rows);
-  r1 = min(r0 + ph.rows_per_cta, ph.total_rows);
+  const int unit = ph.kind == PH_QKV ? 2 : 1;
+  const long long U = (ph.total_rows + unit - 1) / unit, G = gridDim.x, b = blockIdx.x;
+  r0 = min((int)(b * U / G) * unit, ph.total_rows);
+  r1 = min((int)((b + 1) * U / G) * unit, ph.total_rows);
 }
 
 // ---------------------------------------------------------------------------
@@ -216,32 +230,6 @@ __device__ void mk_producer(const MkParams& p, uint8_t* smem) {
       sidx++;
     }
   }
-}
-
-// ---------------------------------------------------------------------------
-// Grid barrier among consumers of all CTAs: phase `idx` may start once every
-// CTA has finished phase idx-1.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ bool mk_arrive(const MkParams& p, int ctid) {
-  named_sync(1, MK_CT);
-  // bar.sync orders the CTA's phase writes before this release (cumulative).
-  if (ctid == 0) red_release_add(p.gbar, 1u);
-  return true;
-}
-__device__ __forceinline__ bool mk_wait_grid(const MkParams& p, int ctid, unsigned target,
-                                             int* s_flag) {
-  if (ctid == 0) {
-    int ok = 1;
-    uint32_t it = 0;
-    while (ld_acquire_u32(p.gbar) < target) {
-      if (++it > 32) __nanosleep(32);
-      if ((it & 255) == 0 && dev_failed(p.err)) { ok = 0; break; }
-      if (it > MK_BAR_LIMIT) { atomicOr(p.err, DEVERR_COUNTER_TIMEOUT); ok = 0; break; }
-    }
-    *s_flag = ok;
-  }
-  named_sync(1, MK_CT);
-  return *s_flag != 0;
 }
 
 // Values [8 lane, 8 lane + 8) of super-block j of the current token's
@@ -284,95 +272,126 @@ __device__ __forceinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, 
 
 // ---------------------------------------------------------------------------
 // Consumer prologue: Q8_K activation of the phase input (optionally rmsnorm).
-// Layer 0's QKV reads the token's embedding row (dequantised here; CTA 0 also
-// stores it as the residual stream x).
+// Layer 0's QKV reads the token's embedding row (dequantised here by every
+// CTA into its copy of x).
 // ---------------------------------------------------------------------------
-// A residual slot element is one 64-bit word: generation tag (low half),
-// value bits (high half), stored by one single-copy-atomic 64-bit store, so
-// a reader that sees the tag sees the value stored with it.
-__device__ __forceinline__ unsigned long long slot_word(uint32_t tag, float v) {
+// Tagged words: generation tag (low half) | f32 bits (high half), each
+// stored by one single-copy-atomic 64-bit store, so a reader that sees the
+// tag sees the value stored with it. Local words use gpu scope; the row-sum
+// slots, which other ranks write over NVLink, system scope.
+__device__ __forceinline__ unsigned long long tag_word(uint32_t tag, float v) {
   return (unsigned long long)tag | ((unsigned long long)__float_as_uint(v) << 32);
 }
-__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+__device__ __forceinline__ float word_val(unsigned long long w) { return __uint_as_float((uint32_t)(w >> 32)); }
+__device__ __forceinline__ void st_word_gpu(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_word_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-// Two slot words; each is read atomically (a vector access is a pair of
-// 64-bit accesses, each of which is atomic).
-__device__ __forceinline__ void ld_relaxed_sys_2u64(const unsigned long long* p, unsigned long long& a,
-                                                    unsigned long long& b) {
-  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+// Two words per load; each of the pair is read atomically.
+template <bool SYS>
+__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  if constexpr (SYS)
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
-// Eight consecutive slot words of one rank (this lane's 8 elements).
-__device__ __forceinline__ void ld_slot8(const unsigned long long* p, unsigned long long (&w)[8]) {
-#pragma unroll
-  for (int e = 0; e < 8; e += 2) ld_relaxed_sys_2u64(p + e, w[e], w[e + 1]);
+template <bool SYS>
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+  unsigned long long v;
+  if constexpr (SYS)
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
-__device__ __forceinline__ bool slot8_ready(const unsigned long long (&w)[8], uint32_t want) {
-  bool ok = true;
+// Bounded poll: false (and the error flag) when it gives up or another CTA
+// failed.
+__device__ __forceinline__ bool poll_continue(uint32_t it, uint32_t* err) {
+  if (it > MK_BAR_LIMIT || (((it & 255) == 255) && dev_failed(err))) {
+    atomicOr(err, DEVERR_COUNTER_TIMEOUT);
+    return false;
+  }
+  if (it > 4) __nanosleep(20);
+  return true;
+}
+// N (even) consecutive words (16-byte aligned) carrying tag `want`.
+template <bool SYS, int N>
+__device__ __forceinline__ void wait_words(const unsigned long long* p, uint32_t want, unsigned long long (&w)[N],
+                                           uint32_t* err) {
 #pragma unroll
-  for (int e = 0; e < 8; e++) ok &= (uint32_t)w[e] == want;
-  return ok;
+  for (int e = 0; e < N; e += 2) ld_words2<SYS>(p + e, w[e], w[e + 1]);
+  for (uint32_t it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < N; e++) ok &= (uint32_t)w[e] == want;
+    if (ok || !poll_continue(it, err)) return;
+#pragma unroll
+    for (int e = 0; e < N; e += 2)
+      if ((uint32_t)w[e] != want || (uint32_t)w[e + 1] != want) ld_words2<SYS>(p + e, w[e], w[e + 1]);
+  }
+}
+// One word carrying tag `want`; its value.
+template <bool SYS>
+__device__ __forceinline__ float wait_word(const unsigned long long* p, uint32_t want, uint32_t* err) {
+  unsigned long long w = ld_word<SYS>(p);
+  for (uint32_t it = 0; (uint32_t)w != want && poll_continue(it, err); ++it) w = ld_word<SYS>(p);
+  return word_val(w);
 }
 
+// Values [8 lane, 8 lane + 8) of block j of phase i's input: the token
+// embedding (layer 0's QKV), y (attn_output), h (ffn_down), or the residual
+// stream x = this CTA's copy + the previous phase's row sums of every rank,
+// added in rank order (QKV of later layers, gate/up, the head).
 __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8],
-                                             uint32_t gen_base) {
-  if (ph.tp_in > 0) {
-    // x(v) = x(v - 1) + sum over ranks of their version-v slots, in rank order
-    const int v = ph.tp_in, E = p.n_embd;
-    const float4* xo = reinterpret_cast<const float4*>(p.xbuf + (size_t)((v - 1) & 1) * E + j * QK_K + 8 * lane);
-    float4 a = __ldcg(xo), b = __ldcg(xo + 1);
-    // Wait until this step's generation of version v is in every rank's
-    // slots of these 8 elements (one rank's 8 words in flight at a time).
-    const unsigned long long* sl = p.xslot[p.me_slot] + (size_t)(v & 1) * p.tp * E + j * QK_K + 8 * lane;
-    const uint32_t want = gen_base + (uint32_t)v;
-    float acc[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    for (int k = 0; k < p.tp; k++) {
-      unsigned long long w[8];
-      ld_slot8(sl + (size_t)k * E, w);
-      for (uint32_t it = 0; !slot8_ready(w, want); ++it) {
-        if (it > MK_BAR_LIMIT || (((it & 255) == 255) && dev_failed(p.err))) {
-          atomicOr(p.err, DEVERR_COUNTER_TIMEOUT);
-          break;
-        }
-        __nanosleep(20);
-        ld_slot8(sl + (size_t)k * E, w);
-      }
+                                             uint32_t want, const float* xrep) {
+  if (ph.kind == PH_WO || ph.kind == PH_DOWN) {
+    unsigned long long w[8];
+    wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err);
 #pragma unroll
-      for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], __uint_as_float((uint32_t)(w[e] >> 32)));
-    }
-    a = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    b = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
-    vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
-  } else if (ph.in) {
-    const float4* xr = reinterpret_cast<const float4*>(ph.in + j * QK_K + 8 * lane);
-    const float4 x0 = __ldcg(xr), x1 = __ldcg(xr + 1);
-    vv[0] = x0.x; vv[1] = x0.y; vv[2] = x0.z; vv[3] = x0.w;
-    vv[4] = x1.x; vv[5] = x1.y; vv[6] = x1.z; vv[7] = x1.w;
-  } else {
+    for (int e = 0; e < 8; e++) vv[e] = word_val(w[e]);
+  } else if (ph.kind == PH_QKV && ph.layer == 0) {
     const F8 e = mk_embed_vals(p, j, lane, ph.nb);
 #pragma unroll
     for (int k = 0; k < 8; k++) vv[k] = e.v[k];
+  } else {
+    const int E = p.n_embd, par = ph.kind == PH_GATEUP ? 1 : 0;  // after attn_output : after ffn_down
+    const float4* xr = reinterpret_cast<const float4*>(xrep + j * QK_K + 8 * lane);
+    const float4 a = xr[0], b = xr[1];
+    float acc[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    const unsigned long long* sl = p.xslot[p.tp_rank] + (size_t)par * p.tp * E + j * QK_K + 8 * lane;
+    for (int k = 0; k < p.tp; k++) {
+      unsigned long long w[8];
+      wait_words<true, 8>(sl + (size_t)k * E, want, w, p.err);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], word_val(w[e]));
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) vv[e] = acc[e];
   }
 }
 
-// The first MK_REGJ blocks of a warp stay in registers between the two
-// passes; any further ones (K > MK_REGJ * 256 * consumer warps) are loaded
-// again in the second pass.
+// Q8_K activation of phase i's input in shared memory (rmsnorm first when
+// the phase has one). Phases that read x also store the new x into the CTA's
+// copy. The first MK_REGJ blocks of a warp stay in registers between the two
+// passes; any further ones (K > MK_REGJ * 256 * consumer warps) are read
+// again in the second pass (from the copy of x, or the same tagged words).
 __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, uint8_t* smem,
-                             ActQ8& act, int cw, int lane, float* xres, int res0, int res_n,
-                             uint64_t* gbar, uint32_t gpar, uint32_t gen_base) {
+                             ActQ8& act, int cw, int lane, float* xrep, uint64_t* gbar, uint32_t gpar,
+                             uint32_t want) {
   const int K = ph.K, nb = ph.nb;
   float* part = reinterpret_cast<float*>(smem + p.off_red) + 64;
   act.qs = reinterpret_cast<int8_t*>(smem + p.off_act_qs);
   act.d = reinterpret_cast<float*>(smem + p.off_act_d);
   act.bs = reinterpret_cast<int32_t*>(smem + p.off_act_bs);
   const bool norm = ph.gamma != nullptr;
+  const bool is_x = ph.kind != PH_WO && ph.kind != PH_DOWN;
   float v[MK_REGJ][8];
   // the register-held blocks' loads are all issued before any is used
 #pragma unroll
   for (int r = 0; r < MK_REGJ; r++)
-    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r], gen_base);
+    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r], want, xrep);
   for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
     float vv[8];
     if (jj < MK_REGJ) {
@@ -383,27 +402,12 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
           for (int k = 0; k < 8; k++) vv[k] = v[r][k];
         }
     } else {
-      mk_load_vals(p, ph, j, lane, vv, gen_base);
+      mk_load_vals(p, ph, j, lane, vv, want, xrep);
     }
-    if (ph.tp_in > 0 || (p.tp > 1 && !ph.in)) {
-      // tensor parallel: x(v) of this CTA's rows into its shared copy and the
-      // version's buffer (read back, whole, by the next residual fold)
-      const int v = ph.tp_in;
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const int e = j * QK_K + 8 * lane + k - res0;
-        if (e >= 0 && e < res_n) {
-          xres[e] = vv[k];
-          p.xbuf[(size_t)(v & 1) * p.n_embd + res0 + e] = vv[k];
-        }
-      }
-    } else if (!ph.in) {
-      // token embedding = initial residual stream: keep this CTA's rows
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        const int e = j * QK_K + 8 * lane + k - res0;
-        if (e >= 0 && e < res_n) xres[e] = vv[k];
-      }
+    if (is_x) {
+      float4* xw = reinterpret_cast<float4*>(xrep + j * QK_K + 8 * lane);
+      xw[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      xw[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
     }
     if (norm) {
       float ss = 0.f;
@@ -436,8 +440,13 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
 #pragma unroll
           for (int k = 0; k < 8; k++) vv[k] = v[r][k];
         }
+    } else if (is_x) {
+      const float4* xr = reinterpret_cast<const float4*>(xrep + j * QK_K + 8 * lane);
+      const float4 a = xr[0], b = xr[1];
+      vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
+      vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
     } else {
-      mk_load_vals(p, ph, j, lane, vv, gen_base);
+      mk_load_vals(p, ph, j, lane, vv, want, xrep);
     }
     if (norm) {
       const float4* gr = reinterpret_cast<const float4*>(gs + j * QK_K + 8 * lane);
@@ -459,47 +468,48 @@ struct MkCtx {
   const MkParams& p;
   const MkPhase& ph;
   int pos_v;
+  int phase;
+  uint32_t tag;  // generation of this phase's outputs
   __device__ const Seg& seg(int i) const { return ph.seg[i]; }
   __device__ int nb() const { return ph.nb; }
   __device__ float* out() const { return ph.out; }
   __device__ int qn() const { return ph.seg[0].rows; }
   __device__ int kn() const { return ph.seg[1].rows; }
   __device__ int hd() const { return p.hd; }
-  __device__ int max_seq() const { return p.max_seq; }
-  __device__ int kv_f16() const { return p.kv_f16; }
-  __device__ void* kc() const { return ph.kc; }
-  __device__ void* vc() const { return ph.vc; }
-  __device__ int64_t kv_off() const { return 0; }
   __device__ int pos() const { return pos_v; }
-  int phase;
-  float* xres;  // this CTA's rows of the residual stream (shared memory)
-  int res0;     // first of those rows
-  uint32_t gen_base;  // tensor parallel: slot generation of this step's version 0
-  __device__ void stamp(int slot) const { mk_stamp(p, phase, slot); }
-  // x[r] += v on the CTA's own copy of its rows; the global x is only
-  // written (for the other CTAs' next prologue), never read back here.
-  __device__ void resid_add(float* o, int r, float v) const {
-    if (ph.tp_res > 0) {  // this rank's part of the sum, to every rank's slot, tagged
-      const size_t off = ((size_t)((ph.tp_res & 1) * p.tp + p.tp_rank)) * p.n_embd + r;
-      const unsigned long long tv = slot_word(gen_base + (uint32_t)ph.tp_res, v);
-      for (int k = 0; k < p.tp; k++) st_relaxed_sys_u64(p.xslot[k] + off, tv);
-      return;
-    }
-    const float nv = __fadd_rn(v, xres[r - res0]);
-    xres[r - res0] = nv;
-    *o = nv;
-  }
   __device__ const float* cos_t() const { return p.cos_t; }
   __device__ const float* sin_t() const { return p.sin_t; }
+  __device__ void stamp(int slot) const { mk_stamp(p, phase, slot); }
+  __device__ void put_q(int r, float a, float b) const {
+    st_word_gpu(p.fq + r, tag_word(tag, a));
+    st_word_gpu(p.fq + r + 1, tag_word(tag, b));
+  }
+  // The cache row (read by later steps) and the tagged copy this step's
+  // attention reads, with the cache's rounding.
+  __device__ void put_kv(int which, int kvh, int dd, float a, float b) const {
+    store_kv(which ? ph.vc : ph.kc, p.kv_f16, ((int64_t)kvh * p.max_seq + pos_v) * p.hd + dd, a, b);
+    if (p.kv_f16) {
+      a = __half2float(__float2half_rn(a));
+      b = __half2float(__float2half_rn(b));
+    }
+    unsigned long long* w = p.fkv + ((size_t)which * p.n_kv + kvh) * p.hd + dd;
+    st_word_gpu(w, tag_word(tag, a));
+    st_word_gpu(w + 1, tag_word(tag, b));
+  }
+  __device__ void put_h(int r, float v) const { st_word_gpu(p.fh + r, tag_word(tag, v)); }
+  // attn_output / ffn_down row r: this rank's sum into every rank's slot
+  __device__ void resid_add(float*, int r, float v) const {
+    const size_t off = ((size_t)(ph.kind == PH_WO ? 1 : 0) * p.tp + p.tp_rank) * p.n_embd + r;
+    const unsigned long long w = tag_word(tag, v);
+    for (int k = 0; k < p.tp; k++) st_word_sys(p.xslot[k] + off, w);
+  }
 };
 
 // All chunks of this CTA's rows in one matvec phase: wait for each stage,
 // compute, hand the stage back to the producer.
 template <int MODE>
-__device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, float* xres, int res0,
-                          uint32_t gen_base,
-                          uint8_t* smem, uint64_t* full,
-                          uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
+__device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, uint32_t tag, uint8_t* smem,
+                          uint64_t* full, uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
                           float& best_v, int& best_i) {
   int r0, r1;
   phase_rows(ph, r0, r1);
@@ -510,8 +520,8 @@ __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int p
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
     Part parts[3];
     make_parts<MODE>(ph.seg, ph.nseg, c0, c1, parts);
-    chunk_units<MODE>(MkCtx{p, ph, pos, phase, xres, res0, gen_base}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw,
-                      MK_CW, lane, best_v, best_i);
+    chunk_units<MODE>(MkCtx{p, ph, pos, phase, tag}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw, MK_CW,
+                      lane, best_v, best_i);
     __syncwarp();
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -538,7 +548,10 @@ __device__ __forceinline__ float4 kv_load4(const KV* base, size_t idx) {
 // tile are staged in shared memory with one wave of loads, then scores
 // (thread per (head, position)), online softmax (warp per head) and P.V
 // (thread per (head, dimension)). With splits > 1 the split partials go
-// through global memory and the last split's CTA merges them.
+// through global memory and the last split's CTA merges them. q and this
+// step's K/V row are the QKV phase's tagged words (tag `want`; earlier
+// positions come from the cache, written by earlier steps); y is written as
+// tagged words (tag `tag`).
 // ---------------------------------------------------------------------------
 template <int HD>
 constexpr int mk_att_tile() { return 4096 / HD; }
@@ -552,7 +565,7 @@ __host__ __device__ inline size_t mk_att_floats(int hd, int nrep) {
 
 template <int HD, typename KV>
 __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0, int nh, int s, int splits,
-                             int T, float* sm, int cw, int lane) {
+                             int T, float* sm, int cw, int lane, uint32_t want, uint32_t tag) {
   constexpr int TILE = mk_att_tile<HD>();
   constexpr int MAXE = (ATT_MAX_REP * HD + MK_CT - 1) / MK_CT;  // (head, dim) elements per thread
   const int nrep = p.n_head / p.n_kv;   // heads of group g; this unit takes [r0, r0 + nh)
@@ -574,8 +587,8 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
   const int64_t kvbase = (int64_t)g * p.max_seq * HD;
   const KV* kc = reinterpret_cast<const KV*>(ph.kc) + kvbase;
   const KV* vc = reinterpret_cast<const KV*>(ph.vc) + kvbase;
-  const float4* qb = reinterpret_cast<const float4*>(p.q + (size_t)(g * nrep + r0) * HD);
-  for (int i = tid; i < nh * HD / 4; i += MK_CT) reinterpret_cast<float4*>(qs)[i] = __ldcg(qb + i);
+  const unsigned long long* qw = p.fq + (size_t)(g * nrep + r0) * HD;
+  for (int i = tid; i < nh * HD; i += MK_CT) qs[i] = wait_word<false>(qw + i, want, p.err);
   if (tid < nh) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
   float o[MAXE];
 #pragma unroll
@@ -585,8 +598,17 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
     const int n = min(TILE, t1 - tb);
     for (int i = tid; i < n * V4; i += MK_CT) {
       const int tt = i / V4, c = (i % V4) * 4;
-      const float4 kv = kv_load4(kc, (size_t)(tb + tt) * HD + c);
-      const float4 vv = kv_load4(vc, (size_t)(tb + tt) * HD + c);
+      float4 kv, vv;
+      if (tb + tt == T - 1) {  // this step's row
+        unsigned long long kw[4], vw[4];
+        wait_words<false, 4>(p.fkv + (size_t)g * HD + c, want, kw, p.err);
+        wait_words<false, 4>(p.fkv + ((size_t)p.n_kv + g) * HD + c, want, vw, p.err);
+        kv = make_float4(word_val(kw[0]), word_val(kw[1]), word_val(kw[2]), word_val(kw[3]));
+        vv = make_float4(word_val(vw[0]), word_val(vw[1]), word_val(vw[2]), word_val(vw[3]));
+      } else {
+        kv = kv_load4(kc, (size_t)(tb + tt) * HD + c);
+        vv = kv_load4(vc, (size_t)(tb + tt) * HD + c);
+      }
       float* kd = Ks + tt * (HD + 1) + c;
       kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
       *reinterpret_cast<float4*>(Vs + tt * HD + c) = vv;
@@ -649,7 +671,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
 #pragma unroll
     for (int k = 0; k < MAXE; k++) {
       const int e = tid + k * MK_CT;
-      if (e < nh * HD) p.y[(size_t)(g * nrep + r0) * HD + e] = o[k] / lrow[e / HD];
+      if (e < nh * HD) st_word_gpu(p.fy + (size_t)(g * nrep + r0) * HD + e, tag_word(tag, o[k] / lrow[e / HD]));
     }
     return;
   }
@@ -702,7 +724,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
       const float w = cw_m[s2 * nh + h];
       if (w != 0.f) O += w * __ldcg(p.att_part + base0 + ((size_t)s2 * nrep + r0 + h) * (HD + 2) + d);
     }
-    p.y[((size_t)g * nrep + r0 + h) * HD + d] = O / ltot[h];
+    st_word_gpu(p.fy + ((size_t)g * nrep + r0 + h) * HD + d, tag_word(tag, O / ltot[h]));
   }
   if (tid == 0) p.att_cnt[g * nrep + r0] = 0u;
 }
@@ -716,7 +738,6 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   __shared__ int s_flag;
   __shared__ __align__(16) MkPhase s_ph[2];
   __shared__ int s_pos;  // position of this step's token (constant during the step)
-  __shared__ float s_xres[MK_MAX_RES];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
   uint64_t* empty = full + MK_MAX_NS;
@@ -736,34 +757,29 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   }
   const int ctid = tid - 32, cw = warp - 1;
   if (ctid == 0) s_pos = (int)__ldcg(p.pos);
-  // rows of the residual stream this CTA updates (attn_output / ffn_down)
-  const int res0 = min((int)blockIdx.x * p.res_per_cta, p.n_embd);
-  const int res_n = min(res0 + p.res_per_cta, p.n_embd) - res0;
+  float* xrep = reinterpret_cast<float*>(smem + p.off_xrep);
   ActQ8 act;
   int cidx = 0;
   uint64_t* gbar = empty + MK_MAX_NS;
   uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
-  // tensor parallelism: residual slots carry a generation tag that grows by
-  // one per residual version; readers wait for the tag, no cross-rank barrier
-  const uint32_t gen_base = p.tp > 1 ? (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.xbars_per_step + 1)) : 0u;
+  // phase i's outputs carry tag gen + i + 1; its inputs gen + i
+  const uint32_t gen = (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.n_ph + 1));
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
   for (int i = 0; i < p.n_ph; i++) {
-    // Before waiting on the grid: copy the phase descriptor into shared
-    // memory (double-buffered by parity: warps may still be reading phase
-    // i-1's copy) and pull this phase's rmsnorm weights into L1, so that
-    // neither sits on the critical path after the barrier.
+    // Copy the phase descriptor into shared memory (double-buffered by
+    // parity: no warp can still read phase i-1's copy once all passed the
+    // sync below); the sync also ends the CTA's previous phase, so the
+    // attention region is free for the rmsnorm weights staged next.
     MkPhase& ph = s_ph[i & 1];
     {
       const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph + i);
       uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
       for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
     }
-    if (i > 0) {
-      if (!mk_wait_grid(p, ctid, (unsigned)i * gridDim.x, &s_flag)) return;
-    } else {
-      named_sync(1, MK_CT);
-    }
+    if (ctid == 0) s_flag = dev_failed(p.err);
+    named_sync(1, MK_CT);
+    if (s_flag) return;  // a wait gave up somewhere: all consumer warps leave together
     // Stage the rmsnorm weights of the next phase (gate/up after attn_output,
     // q/k/v or the head after ffn_down; phase 0 its own) in the attention
     // region, idle until then, so the prologue reads them from shared memory.
@@ -779,6 +795,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       }
     }
     if (ctid == 0) mk_stamp(p, i, 0);
+    const uint32_t want = gen + (uint32_t)i, tag = want + 1u;
     if (ph.kind == PH_ATTN) {
       // Split the context across CTAs only when it spans several tiles.
       const int T = s_pos + 1;
@@ -793,22 +810,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       float* asm_ = reinterpret_cast<float*>(smem + p.off_att);
       for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
         const int hu = u / splits;  // head unit: (KV head, first query head of the unit)
-        mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane);
+        mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane,
+                             want, tag);
       }
     } else {
-      mk_build_act(p, ph, i, smem, act, cw, lane, s_xres, res0, res_n, gbar, gcount & 1u, gen_base);
+      mk_build_act(p, ph, i, smem, act, cw, lane, xrep, gbar, gcount & 1u, want);
       if (ph.gamma) gcount++;
       if (ctid == 0) mk_stamp(p, i, 1);
+      // a wait that gives up flags the error and goes on (in bounds); all
+      // warps leave at the next phase start
       const int mode = mode_of(ph.kind);
-      bool ok;
-      if (mode == MODE_QKV) ok = mk_chunks<MODE_QKV>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_GATEUP) ok = mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_HEAD) ok = mk_chunks<MODE_HEAD>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else ok = mk_chunks<MODE_RESID>(p, ph, i, s_pos, s_xres, res0, gen_base, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      if (!ok) return;
+      if (mode == MODE_QKV)
+        mk_chunks<MODE_QKV>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_GATEUP)
+        mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else if (mode == MODE_HEAD)
+        mk_chunks<MODE_HEAD>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      else
+        mk_chunks<MODE_RESID>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
     }
     if (ctid == 0) mk_stamp(p, i, 2);
-    if (i + 1 < p.n_ph) mk_arrive(p, ctid);
   }
   // HEAD: CTA argmax partial, the last CTA reduces all partials.
   float* rv = reinterpret_cast<float*>(smem + p.off_red);
@@ -843,10 +864,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
       if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
     }
+    const unsigned long long ep = __ldcg(p.epoch);
     if (lane == 0 && p.tp > 1) {
       // every rank's winner (value, global row) to every rank, then the
       // reference's order: larger value, then smaller row; NaN never wins
-      const unsigned long long ep = __ldcg(p.epoch);
       const size_t base = (size_t)(ep & 1) * p.tp * 2;
       for (int k = 0; k < p.tp; k++) {
         uint32_t* hs = p.hslot[k] + base + (size_t)p.tp_rank * 2;
@@ -856,8 +877,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       for (int k = 0; k < p.tp; k++) red_release_sys_add64(p.hctr[k], 1ull);
       float gv = -INFINITY;
       uint32_t gi = 0xffffffffu;
-      if (wait_ge_sys(p.hctr[p.me_slot], (ep + 1) * (unsigned long long)p.tp, p.err)) {
-        const uint32_t* hs = p.hslot[p.me_slot] + base;
+      if (wait_ge_sys(p.hctr[p.tp_rank], (ep + 1) * (unsigned long long)p.tp, p.err)) {
+        const uint32_t* hs = p.hslot[p.tp_rank] + base;
         for (int r = 0; r < p.tp; r++) {
           const float v = __uint_as_float(hs[2 * r]);
           const uint32_t ix = hs[2 * r + 1];
@@ -865,15 +886,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
         }
       }
       bi = gi == 0xffffffffu ? 0x7fffffff : (int)gi;
-      *p.epoch = ep + 1;
     }
     if (lane == 0) {
       *p.token = (bi == 0x7fffffff) ? 0u : (uint32_t)bi;
       *p.pos = __ldcg(p.pos) + 1;
       *p.am_cnt = 0u;
-      // every CTA has passed its last grid barrier (it reached am_cnt after
-      // the head phase), so the counter can be rearmed for the next step
-      *p.gbar = 0u;
+      // every CTA has read the epoch (it reached am_cnt after the head
+      // phase): the next step's tags start after this step's
+      *p.epoch = ep + 1;
       mk_stamp(p, p.n_ph, 1);  // step result written
     }
   }

@@ -108,8 +108,7 @@ struct armai_llama {
   float* logits_all = nullptr;   // [tp * v_stride] gathered logits
   void* xchg = nullptr;          // persistent kernel: this rank's exchange area (IPC-shared)
   void* peer_xchg[8] = {};       // the other ranks' exchange areas, mapped here
-  float* xbuf = nullptr;         // [2][E] residual stream of the persistent kernel
-  void* epoch = nullptr;         // decode steps completed (persistent kernel)
+  void* flow = nullptr;          // persistent kernel: tagged words (q, K/V row, y, h, row sums) + epoch
   // pinned host staging
   uint32_t* h_tok = nullptr;   // ring of 8 token slots
   int* h_misc = nullptr;       // small pinned scratch
@@ -128,7 +127,6 @@ struct armai_llama {
   // persistent decode kernel
   bool use_mega = true;
   MkPhase* d_phases = nullptr;
-  unsigned* gbar = nullptr;
   MkParams mk;
   size_t mk_smem = 0;
   int mk_grid = 0;
@@ -373,9 +371,6 @@ int setup_peer_exchange(armai_llama* m, MkParams& k) {
   const size_t bytes = XCHG_SLOTS_OFF + 2 * (size_t)m->tp * E * 8;  // (generation, value) pairs
   ARMAI_CUDA(cudaMalloc(&m->xchg, bytes));
   ARMAI_CUDA(cudaMemset(m->xchg, 0, bytes));
-  ARMAI_CUDA(cudaMalloc(&m->xbuf, 2 * E * 4));
-  ARMAI_CUDA(cudaMalloc(&m->epoch, 64));
-  ARMAI_CUDA(cudaMemset(m->epoch, 0, 64));
   // Per rank: its IPC handle (64 B) and its GPU's UUID (16 B), all-gathered.
   struct Rec {
     cudaIpcMemHandle_t h;
@@ -423,19 +418,24 @@ int setup_peer_exchange(armai_llama* m, MkParams& k) {
     k.hslot[r] = reinterpret_cast<uint32_t*>(base + 256);
     k.xslot[r] = reinterpret_cast<unsigned long long*>(base + XCHG_SLOTS_OFF);
   }
-  k.me_slot = m->tp_rank;
-  k.xbuf = m->xbuf;
-  k.epoch = reinterpret_cast<unsigned long long*>(m->epoch);
-  k.xbars_per_step = 2 * m->n_layer;
   return ARMAI_OK;
 }
 
 // Phase list and shared-memory layout of the persistent decode kernel.
 int setup_mega(armai_llama* m, int nsm) {
   const int E = m->n_embd, F = m->n_ff, QN = m->n_head * m->head_dim;
+  // Grid: one CTA per SM, but no more CTAs than the smallest matvec phase
+  // has units (QKV: row pairs), so every CTA owns rows in every phase.
+  int grid = nsm;
+  for (const Layer& L : m->layers)
+    grid = std::min({grid, (L.wq.rows + L.wk.rows + L.wv.rows) / 2, L.wo.rows, L.wg.rows, L.wd.rows});
+  grid = std::min(grid, m->output.rows);
+  if (grid < 1) return fail(ARMAI_E_INVALID, "persistent decode kernel: empty phase");
+  // largest row count of a CTA (the balanced split gives each CTA the floor
+  // or the ceiling of units / grid)
   auto per_cta = [&](int total, int unit) {
-    int per = (total + nsm - 1) / nsm;
-    return ((per + unit - 1) / unit) * unit;
+    const int units = (total + unit - 1) / unit;
+    return ((units + grid - 1) / grid) * unit;
   };
   auto chunk_for = [&](int unit_bytes, int unit, int per) {
     int c = (int)(MK_STAGE / (uint32_t)unit_bytes);
@@ -445,7 +445,7 @@ int setup_mega(armai_llama* m, int nsm) {
   };
   std::vector<MkPhase> ph;
   auto mat_phase = [&](int kind, int layer, std::initializer_list<const DevMat*> mats, int total, int unit,
-                       int unit_bytes, int K, const float* gamma, const float* in, float* out) {
+                       int unit_bytes, int K, const float* gamma, float* out) {
     MkPhase p;
     std::memset(&p, 0, sizeof p);
     p.kind = kind;
@@ -459,7 +459,6 @@ int setup_mega(armai_llama* m, int nsm) {
     p.K = K;
     p.nb = K / QK_K;
     p.gamma = gamma;
-    p.in = in;
     p.out = out;
     if (layer >= 0) {
       p.kc = kv_layer_ptr(m, m->kc, layer);
@@ -467,12 +466,11 @@ int setup_mega(armai_llama* m, int nsm) {
     }
     ph.push_back(p);
   };
-  const bool tpx = m->tp > 1;
   for (int l = 0; l < m->n_layer; l++) {
     const Layer& L = m->layers[l];
     const int qkv_rb = std::max(L.wq.row_bytes, std::max(L.wk.row_bytes, L.wv.row_bytes));
     mat_phase(PH_QKV, l, {&L.wq, &L.wk, &L.wv}, L.wq.rows + L.wk.rows + L.wv.rows, 2, qkv_rb, E, L.attn_norm,
-              l == 0 ? nullptr : m->x, m->q);
+              nullptr);
     MkPhase a;
     std::memset(&a, 0, sizeof a);
     a.kind = PH_ATTN;
@@ -480,21 +478,13 @@ int setup_mega(armai_llama* m, int nsm) {
     a.kc = kv_layer_ptr(m, m->kc, l);
     a.vc = kv_layer_ptr(m, m->vc, l);
     ph.push_back(a);
-    if (tpx && l > 0) ph[ph.size() - 2].tp_in = 2 * l;  // this layer's q/k/v folds in ffn_down of the last
-    mat_phase(PH_WO, l, {&L.wo}, L.wo.rows, 1, L.wo.row_bytes, QN, nullptr, m->y, m->x);
-    if (tpx) ph.back().tp_res = 2 * l + 1;
-    mat_phase(PH_GATEUP, l, {&L.wg, &L.wu}, L.wg.rows, 1, L.wg.row_bytes + L.wu.row_bytes, E, L.ffn_norm, m->x,
-              m->h);
-    if (tpx) ph.back().tp_in = 2 * l + 1;
-    mat_phase(PH_DOWN, l, {&L.wd}, L.wd.rows, 1, L.wd.row_bytes, F, nullptr, m->h, m->x);
-    if (tpx) ph.back().tp_res = 2 * l + 2;
+    mat_phase(PH_WO, l, {&L.wo}, L.wo.rows, 1, L.wo.row_bytes, QN, nullptr, nullptr);
+    mat_phase(PH_GATEUP, l, {&L.wg, &L.wu}, L.wg.rows, 1, L.wg.row_bytes + L.wu.row_bytes, E, L.ffn_norm, nullptr);
+    mat_phase(PH_DOWN, l, {&L.wd}, L.wd.rows, 1, L.wd.row_bytes, F, nullptr, nullptr);
   }
-  mat_phase(PH_HEAD, -1, {&m->output}, m->output.rows, 1, m->output.row_bytes, E, m->out_norm, m->x, m->logits);
-  if (tpx) ph.back().tp_in = 2 * m->n_layer;
+  mat_phase(PH_HEAD, -1, {&m->output}, m->output.rows, 1, m->output.row_bytes, E, m->out_norm, m->logits);
   ARMAI_CUDA(cudaMalloc(&m->d_phases, ph.size() * sizeof(MkPhase)));
   ARMAI_CUDA(cudaMemcpy(m->d_phases, ph.data(), ph.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
-  ARMAI_CUDA(cudaMalloc(&m->gbar, 64));
-  ARMAI_CUDA(cudaMemset(m->gbar, 0, 64));
   const int kmax = std::max(E, std::max(F, QN));
   MkParams& k = m->mk;
   std::memset(&k, 0, sizeof k);
@@ -503,7 +493,8 @@ int setup_mega(armai_llama* m, int nsm) {
   // the attention region also holds the staged rmsnorm weights (n_embd f32)
   const size_t att_bytes = std::max(mk_att_floats(m->head_dim, nrep) * 4, (size_t)m->n_embd * 4) + 64;
   size_t fixed = al16((size_t)(2 * MK_MAX_NS + 1) * 8) + al16((size_t)kmax) + al16((size_t)kmax / QK_K * 4) +
-                 al16((size_t)kmax / 16 * 4) + al16((64 + (size_t)kmax / QK_K + 8) * 4) + al16(att_bytes);
+                 al16((size_t)kmax / 16 * 4) + al16((64 + (size_t)kmax / QK_K + 8) * 4) + al16(att_bytes) +
+                 al16((size_t)E * 4);
   // 2 KB of headroom for the kernel's static shared memory (phase copies etc.)
   int ns = (int)std::min<size_t>(MK_MAX_NS, (SMEM_LIMIT - fixed - 2048) / MK_STAGE);
   if (ns < 2) return fail(ARMAI_E_INVALID, "persistent decode kernel: not enough shared memory");
@@ -515,32 +506,32 @@ int setup_mega(armai_llama* m, int nsm) {
   k.off_act_bs = o; o += al16((size_t)kmax / 16 * 4);
   k.off_red = o;    o += al16((64 + (size_t)kmax / QK_K + 8) * 4);
   k.off_att = o;    o += al16(att_bytes);
+  k.off_xrep = o;   o += al16((size_t)E * 4);
   m->mk_smem = o;
   k.kmax = kmax;
-  // attn_output and ffn_down split the residual stream's rows identically;
-  // each CTA keeps its rows in shared memory across the step.
-  int res_per = -1;
-  for (const MkPhase& q : ph)
-    if (q.kind == PH_WO || q.kind == PH_DOWN) {
-      if (res_per >= 0 && q.rows_per_cta != res_per)
-        return fail(ARMAI_E_INVALID, "persistent decode kernel: residual row split differs between phases");
-      res_per = q.rows_per_cta;
-    }
-  if (res_per > MK_MAX_RES)
-    return fail(ARMAI_E_INVALID, "persistent decode kernel: " + std::to_string(res_per) +
-                                     " residual rows per CTA exceed " + std::to_string(MK_MAX_RES));
-  k.res_per_cta = res_per;
+  // Tagged words, zeroed (tag 0 is never awaited): q, the K/V row, y, h,
+  // then (one rank) the row-sum slots, and the epoch.
+  const size_t KVW = 2 * (size_t)m->n_head_kv * m->head_dim;
+  const size_t nwords = 2 * (size_t)QN + KVW + F + (m->tp > 1 ? 0 : 2 * (size_t)E);
+  ARMAI_CUDA(cudaMalloc(&m->flow, nwords * 8 + 64));
+  ARMAI_CUDA(cudaMemset(m->flow, 0, nwords * 8 + 64));
+  unsigned long long* fw = reinterpret_cast<unsigned long long*>(m->flow);
+  k.fq = fw;
+  k.fkv = fw + QN;
+  k.fy = fw + QN + KVW;
+  k.fh = fw + 2 * (size_t)QN + KVW;
+  k.epoch = fw + nwords;
   k.tp = m->tp;
   k.tp_rank = m->tp_rank;
   k.v0 = m->v0;
   if (m->tp > 1) ARMAI_TRY(setup_peer_exchange(m, k));
+  else k.xslot[0] = fw + 2 * (size_t)QN + KVW + F;
   k.ph = m->d_phases;
   k.n_ph = (int)ph.size();
   k.embd = m->tok_embd.w;
   k.embd_type = m->tok_embd.type;
   k.embd_row_bytes = m->tok_embd.row_bytes;
   k.n_embd = E;
-  k.x = m->x;
   k.cos_t = m->cos_t;
   k.sin_t = m->sin_t;
   k.hd = m->head_dim;
@@ -552,16 +543,13 @@ int setup_mega(armai_llama* m, int nsm) {
   k.att_scale = (float)(1.0 / sqrt((double)m->head_dim));
   k.att_part = m->attn_part;
   k.att_cnt = m->attn_cnt;
-  k.q = m->q;
-  k.y = m->y;
   k.am_val = m->am_val;
   k.am_idx = m->am_idx;
   k.am_cnt = m->am_cnt;
   k.token = m->d_token;
   k.pos = m->d_pos;
-  k.gbar = m->gbar;
   k.err = m->d_err;
-  m->mk_grid = nsm;
+  m->mk_grid = grid;
   if (m->head_dim == 64) {
     ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
     ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<64, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
@@ -569,7 +557,7 @@ int setup_mega(armai_llama* m, int nsm) {
     ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<128, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
     ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<128, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
   }
-  // every CTA must be resident at once (grid barriers)
+  // every CTA must be resident at once (CTAs wait for one another's outputs)
   int per_sm = 0;
   if (m->head_dim == 64)
     ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mega<64, float>, MK_THREADS, o));
@@ -985,9 +973,9 @@ void free_model(armai_llama* m) {
   if (m->comm) nccl_comm_destroy(m->comm);
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
-                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->gbar,
+                   m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->flow,
                    m->pA, m->pG, m->tp_part, m->best_val, m->best_idx, m->tp_send, m->tp_recv,
-                   m->logits_all, m->xchg, m->xbuf, m->epoch};
+                   m->logits_all, m->xchg};
   for (void* p : dptrs)
     if (p) cudaFree(p);
   for (Layer& L : m->layers) { (void)L; }

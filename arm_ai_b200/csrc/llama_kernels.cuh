@@ -385,21 +385,16 @@ __device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage,
         // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
         const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
         const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
-        if (si == 0) {
-          *reinterpret_cast<float2*>(out + r) = make_float2(o0, o1);
-        } else {
-          const int kvh = rr / hd, dd = rr % hd;
-          store_kv(cx.kc(), cx.kv_f16(), cx.kv_off() + ((int64_t)kvh * cx.max_seq() + pos) * hd + dd, o0, o1);
-        }
+        if (si == 0) cx.put_q(r, o0, o1);
+        else cx.put_kv(0, rr / hd, rr % hd, o0, o1);
       } else {
         const int rv = r - qn - kn;
-        const int kvh = rv / hd, dd = rv % hd;
-        store_kv(cx.vc(), cx.kv_f16(), cx.kv_off() + ((int64_t)kvh * cx.max_seq() + pos) * hd + dd, d0, d1);
+        cx.put_kv(1, rv / hd, rv % hd, d0, d1);
       }
     } else if (MODE == MODE_GATEUP) {
       // candle: silu(v) = v / (1 + exp(-v)); then * up
       const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
-      out[r] = __fmul_rn(sl, d1);
+      cx.put_h(r, __fmul_rn(sl, d1));
     } else {
 #pragma unroll
       for (int k = 0; k < 2; k++) {
@@ -437,6 +432,14 @@ struct MvCtx {
   __device__ const float* cos_t() const { return p.cos_t; }
   __device__ const float* sin_t() const { return p.sin_t; }
   __device__ void stamp(int) const {}
+  // epilogue outputs: q rows, the K (which = 0) / V (1) cache row at pos, h
+  __device__ void put_q(int r, float a, float b) const {
+    *reinterpret_cast<float2*>(out() + r) = make_float2(a, b);
+  }
+  __device__ void put_kv(int which, int kvh, int dd, float a, float b) const {
+    store_kv(which ? vc() : kc(), kv_f16(), kv_off() + ((int64_t)kvh * max_seq() + pos()) * hd() + dd, a, b);
+  }
+  __device__ void put_h(int r, float v) const { out()[r] = v; }
   // x[r] += v (the residual stream lives in global memory between kernels)
   __device__ void resid_add(float* o, int, float v) const { *o = __fadd_rn(v, __ldcg(o)); }
 };
