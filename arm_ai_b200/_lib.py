@@ -77,6 +77,20 @@ _SIGS = {
     "armai_dequant_matmul_int8_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p,
                                               c_size_t, c_size_t, c_size_t, c_size_t, c_size_t,
                                               c_void_p]),
+    "armai_rope_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p, c_size_t, c_size_t,
+                               c_size_t, c_size_t, c_void_p]),
+    "armai_dequant_matmul_f16_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_size_t, c_size_t,
+                                             c_size_t, c_size_t, c_void_p]),
+    "armai_softmax_last_axis_f32": (c_int, [c_void_p, c_size_t, c_size_t, c_size_t, c_void_p]),
+    "armai_silu_gate_mul_up_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p]),
+    "armai_dequantize_q6_k": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p]),
+    "armai_dev_rope_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                   c_void_p]),
+    "armai_dev_softmax_last_axis_f32": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "armai_dev_silu_gate_mul_up_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "armai_dev_dequantize_q6_k": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "armai_dev_dequant_matmul_f16_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                                 c_void_p]),
     "armai_dev_int8_matmul_s32": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                           c_void_p]),
     "armai_dev_int8_matmul_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p,

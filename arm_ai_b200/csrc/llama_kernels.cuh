@@ -362,6 +362,15 @@ __device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage,
       has1 = r + 1 < c1;
       ty0 = ty1 = cx.seg(0).type;
     }
+    // RoPE factors of a q / k pair: loaded before the dots so that their
+    // latency overlaps them (same address for the whole warp)
+    float cs = 0.f, sn = 0.f;
+    if (MODE == MODE_QKV && si < 2) {
+      const int hd = cx.hd(), rr = si == 0 ? r : r - cx.qn();
+      const size_t ti = (size_t)cx.pos() * (hd >> 1) + ((rr % hd) >> 1);
+      cs = __ldg(cx.cos_t() + ti);
+      sn = __ldg(cx.sin_t() + ti);
+    }
     float d0, d1;
     if (MODE != MODE_GATEUP || ty0 == ty1) {  // both rows of one matrix
       if (ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K>(p0, p1, has1, nb, act, lane, d0, d1);
@@ -375,13 +384,10 @@ __device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage,
     if (u == 0) cx.stamp(8);
     float* out = cx.out();
     if (MODE == MODE_QKV) {
-      const int hd = cx.hd(), half = hd >> 1, pos = cx.pos();
+      const int hd = cx.hd(), pos = cx.pos();
       const int qn = cx.qn(), kn = cx.kn();
       if (si < 2) {
         const int rr = si == 0 ? r : r - qn;
-        const int i2 = (rr % hd) >> 1;
-        const float cs = __ldg(cx.cos_t() + (size_t)pos * half + i2);
-        const float sn = __ldg(cx.sin_t() + (size_t)pos * half + i2);
         // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
         const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
         const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));

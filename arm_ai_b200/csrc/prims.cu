@@ -1,12 +1,16 @@
-// prims.cu — the int8 / int4 / rmsnorm / flash-attention primitive NIFs on
-// sm_100a (reference: native/arm_ai_nif/src/shape_ops.rs, x86 scalar paths).
+// prims.cu — the int8 / int4 / rmsnorm / flash-attention primitive NIFs and
+// the LLM helpers (rope, softmax, silu(gate) * up, Q6_K dequantisation,
+// f16-weight matmul) on sm_100a (reference: native/arm_ai_nif/src/
+// shape_ops.rs, x86 scalar paths).
 //
 // Exactness: every integer result is bit-exact. Where the reference's f32
 // arithmetic is a short, fixed-order chain (int8 scale products, the int4
 // group sums and their sequential fold over groups, the weight-only int8
 // dot), the kernels reproduce that order with non-contracted __f*_rn ops, so
-// those f32 outputs are bit-exact too. rmsnorm (one 4096-long serial sum per
-// row) and flash attention use parallel reductions and are checked to a
+// those f32 outputs are bit-exact too (also the Q6_K dequantisation and the
+// f16-weight matmul). rmsnorm (one 4096-long serial sum per row), softmax
+// (parallel sum) and flash attention use parallel reductions, rope CUDA's
+// cosf / sinf and silu(gate) * up CUDA's expf: those are checked to a
 // tolerance.
 #include <cuda_fp16.h>
 
@@ -531,6 +535,157 @@ __global__ void k_dequant_i8(const float* __restrict__ act, const int8_t* __rest
   out[o] = __fmul_rn(acc, sc[j]);
 }
 
+// ---------------------------------------------------------------------------
+// LLM helper primitives (lib.rs:147-354 -> shape_ops.rs).
+// ---------------------------------------------------------------------------
+// rope_f32 (shape_ops.rs:1040-1100): thread per (row, pair k). pos =
+// positions[row / heads_per_token] as f32, theta = pos * inv_freq[k], then
+// (x0 cos - x1 sin, x0 sin + x1 cos), each product and sum rounded on its own.
+__global__ void k_rope(const float* __restrict__ x, const int64_t* __restrict__ pos,
+                       const float* __restrict__ inv_freq, float* out, int64_t n_rows, int half,
+                       int64_t heads_per_token) {
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= n_rows * half) return;
+  const int64_t row = o / half;
+  const int k = (int)(o % half);
+  const float p = (float)pos[row / heads_per_token];
+  const float theta = __fmul_rn(p, inv_freq[k]);
+  const float c = cosf(theta), s = sinf(theta);
+  const float2 v = reinterpret_cast<const float2*>(x)[o];
+  reinterpret_cast<float2*>(out)[o] = make_float2(__fsub_rn(__fmul_rn(v.x, c), __fmul_rn(v.y, s)),
+                                                  __fadd_rn(__fmul_rn(v.x, s), __fmul_rn(v.y, c)));
+}
+
+// softmax_last_axis_f32 (shape_ops.rs:2719-2751): block per row. max as the
+// reference scans it (start at src[0], replace on v > max: a NaN at src[0]
+// stays, later NaNs are skipped), e = exp(x - max), sum (parallel), then
+// e * (1 / sum).
+__global__ void k_softmax(const float* __restrict__ x, float* out, int inner) {
+  __shared__ float red[32];
+  __shared__ float bc;
+  const float* src = x + (int64_t)blockIdx.x * inner;
+  float* dst = out + (int64_t)blockIdx.x * inner;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  float m = -INFINITY;
+  for (int i = tid; i < inner; i += blockDim.x) m = fmaxf(m, src[i]);  // fmaxf skips NaN
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[wid] = m;
+  __syncthreads();
+  if (tid == 0) {
+    float mm = red[0];
+    for (int w = 1; w < nw; w++) mm = fmaxf(mm, red[w]);
+    const float s0 = src[0];
+    bc = isnan(s0) ? s0 : fmaxf(s0, mm);
+  }
+  __syncthreads();
+  const float mx = bc;
+  float sum = 0.f;
+  for (int i = tid; i < inner; i += blockDim.x) {
+    const float e = expf(__fsub_rn(src[i], mx));
+    dst[i] = e;
+    sum = __fadd_rn(sum, e);
+  }
+  sum = warp_sum(sum);
+  __syncthreads();
+  if (lane == 0) red[wid] = sum;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < nw; w++) t = __fadd_rn(t, red[w]);
+    bc = __fdiv_rn(1.0f, t);
+  }
+  __syncthreads();
+  const float inv = bc;
+  for (int i = tid; i < inner; i += blockDim.x) dst[i] = __fmul_rn(dst[i], inv);
+}
+
+// silu_gate_mul_up_f32 (shape_ops.rs:2755-2770): g * (1 / (1 + exp(-g))) * u.
+__global__ void k_silu_gate_mul_up(const float* __restrict__ g, const float* __restrict__ u, float* out,
+                                   int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = g[i];
+  const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+  out[i] = __fmul_rn(__fmul_rn(gv, sig), u[i]);
+}
+
+// dequantize_q6_k (shape_ops.rs:2848-2899): thread per (block, half n,
+// l < 32), four outputs like the reference's inner loop. The reference takes
+// the sub-scales scales[8n + {0, 2, 4, 6}] for all 32 values of each group
+// (ggml's dequantize_row_q6_K uses 8n + l/16 + {0, 2, 4, 6}); this follows
+// the reference. value = d * (float)(scale * q), one rounding.
+__global__ void k_dequant_q6k(const uint8_t* __restrict__ in, float* out, int64_t n_blocks) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n_blocks * 64) return;
+  const int64_t b = t >> 6;
+  const int n = (int)(t >> 5) & 1, l = (int)t & 31;
+  const uint8_t* blk = in + b * 210;
+  const uint8_t* ql = blk + 64 * n;
+  const uint8_t qh = blk[128 + 32 * n + l];
+  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
+  const float d = __half2float(__ushort_as_half((uint16_t)(blk[208] | (blk[209] << 8))));
+  const int q1 = ((ql[l] & 0xF) | (((qh >> 0) & 3) << 4)) - 32;
+  const int q2 = ((ql[l + 32] & 0xF) | (((qh >> 2) & 3) << 4)) - 32;
+  const int q3 = ((ql[l] >> 4) | (((qh >> 4) & 3) << 4)) - 32;
+  const int q4 = ((ql[l + 32] >> 4) | (((qh >> 6) & 3) << 4)) - 32;
+  float* o = out + b * 256 + 128 * n + l;
+  o[0] = __fmul_rn(d, (float)(sc[0] * q1));
+  o[32] = __fmul_rn(d, (float)(sc[2] * q2));
+  o[64] = __fmul_rn(d, (float)(sc[4] * q3));
+  o[96] = __fmul_rn(d, (float)(sc[6] * q4));
+}
+
+// dequant_matmul_f16_f32 (shape_ops.rs:1462-1490, the x86 path): out[r][j] =
+// sum over k in order of a[r][k] * f32(w[j][k]), product and sum rounded
+// separately (bit-exact with the reference's serial loop). A CTA of 8 warps
+// covers JW * 32 weight rows (lane = row) and 4 * 8 / JW activation rows per
+// thread group; weights and activations pass through shared memory in chunks
+// of 32 along K, converted to f32 and padded so lanes read distinct banks.
+constexpr int F16_KC = 32;
+template <int JW>
+__global__ void __launch_bounds__(256) k_dequant_f16(const float* __restrict__ act,
+                                                     const uint16_t* __restrict__ w, float* out, int64_t rows,
+                                                     int n, int k) {
+  constexpr int RW = 8 / JW;          // warps along activation rows
+  constexpr int JT = 32 * JW;         // weight rows per CTA
+  constexpr int RT = 4 * RW;          // activation rows per CTA
+  __shared__ float ws[JT][F16_KC + 1];
+  __shared__ float as[RT][F16_KC];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int jw = wid % JW, rw = wid / JW;
+  const int64_t j0 = (int64_t)blockIdx.x * JT, r0 = (int64_t)blockIdx.y * RT;
+  const int64_t j = j0 + jw * 32 + lane;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int kc = 0; kc < k; kc += F16_KC) {
+    const int kn = min(F16_KC, k - kc);
+    for (int e = tid; e < JT * F16_KC; e += 256) {
+      const int jr = e / F16_KC, kk = e % F16_KC;
+      const int64_t jj = j0 + jr;
+      ws[jr][kk] = (jj < n && kk < kn) ? __half2float(__ushort_as_half(w[jj * k + kc + kk])) : 0.f;
+    }
+    for (int e = tid; e < RT * F16_KC; e += 256) {
+      const int rr = e / F16_KC, kk = e % F16_KC;
+      const int64_t r = r0 + rr;
+      as[rr][kk] = (r < rows && kk < kn) ? act[r * k + kc + kk] : 0.f;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kn; kk++) {
+      const float wv = ws[jw * 32 + lane][kk];
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[i] = __fadd_rn(acc[i], __fmul_rn(as[rw * 4 + i][kk], wv));
+    }
+    __syncthreads();
+  }
+  if (j < n) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int64_t r = r0 + rw * 4 + i;
+      if (r < rows) out[r * n + j] = acc[i];
+    }
+  }
+}
+
 int finish(cudaStream_t s, void* dst, const void* src, size_t bytes) {
   ARMAI_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s));
   ARMAI_CUDA(cudaStreamSynchronize(s));
@@ -879,4 +1034,151 @@ extern "C" int armai_dev_int8_matmul_f32(const int8_t* a, const int8_t* w, const
   if (!m || !n) return ARMAI_OK;
   return launch_int8_gemm(a, w, nullptr, out, act_scales, per_token, act_scale, w_scales, m, n, k,
                           (cudaStream_t)stream);
+}
+
+// ===========================================================================
+// LLM helper primitives: rope, softmax, silu(gate) * up, Q6_K dequantisation,
+// f16-weight matmul.
+// ===========================================================================
+extern "C" int armai_dev_rope_f32(const float* x, const int64_t* positions, const float* inv_freq, float* out,
+                                  int64_t n_rows, int64_t head_dim, int64_t heads_per_token, void* stream) {
+  if (head_dim % 2) return fail(ARMAI_E_INVALID, "rope: head_dim " + std::to_string(head_dim) + " must be even");
+  const int64_t pairs = n_rows * (head_dim / 2);
+  if (!pairs) return ARMAI_OK;
+  if (heads_per_token <= 0) return fail(ARMAI_E_INVALID, "rope: heads_per_token must be positive");
+  k_rope<<<(unsigned)((pairs + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, positions, inv_freq, out, n_rows,
+                                                                           (int)(head_dim / 2), heads_per_token);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+extern "C" int armai_rope_f32(const float* input, size_t input_len, const int64_t* positions, size_t n_positions,
+                              const float* inv_freq, size_t inv_freq_len, size_t n_rows, size_t head_dim,
+                              size_t heads_per_token, float* out) {
+  if (input_len != n_rows * head_dim)
+    return fail(ARMAI_E_INVALID, lenmsg("rope: input", input_len, "n_rows*head_dim", n_rows * head_dim));
+  if (head_dim % 2) return fail(ARMAI_E_INVALID, "rope: head_dim " + std::to_string(head_dim) + " must be even");
+  if (inv_freq_len != head_dim / 2)
+    return fail(ARMAI_E_INVALID, lenmsg("rope: inv_freq", inv_freq_len, "head_dim/2", head_dim / 2));
+  if (n_rows != n_positions * heads_per_token)
+    return fail(ARMAI_E_INVALID, "rope: n_rows " + std::to_string(n_rows) + " != n_tokens * heads_per_token = " +
+                                     std::to_string(n_positions * heads_per_token));
+  if (!input_len) return ARMAI_OK;
+  cudaStream_t s;
+  ARMAI_TRY(thread_stream(&s));
+  Scoped dx(s), dp(s), df(s), dout(s);
+  ARMAI_TRY(h2d(dx, input, input_len * 4));
+  ARMAI_TRY(h2d(dp, positions, n_positions * 8));
+  ARMAI_TRY(h2d(df, inv_freq, inv_freq_len * 4));
+  ARMAI_TRY(dalloc(dout, input_len * 4));
+  ARMAI_TRY(armai_dev_rope_f32((float*)dx.p, (int64_t*)dp.p, (float*)df.p, (float*)dout.p, (int64_t)n_rows,
+                               (int64_t)head_dim, (int64_t)heads_per_token, s));
+  return finish(s, out, dout.p, input_len * 4);
+}
+
+extern "C" int armai_dev_softmax_last_axis_f32(const float* x, float* out, int64_t outer, int64_t inner,
+                                               void* stream) {
+  if (inner <= 0) return fail(ARMAI_E_INVALID, "softmax: inner must be positive");
+  if (!outer) return ARMAI_OK;
+  if (outer > 0x7fffffff) return fail(ARMAI_E_INVALID, "softmax: outer exceeds 2^31 - 1 rows");
+  const int threads = inner >= 1024 ? 256 : 128;
+  k_softmax<<<(unsigned)outer, threads, 0, (cudaStream_t)stream>>>(x, out, (int)inner);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+extern "C" int armai_softmax_last_axis_f32(const float* input, size_t input_len, size_t outer, size_t inner,
+                                           float* out) {
+  if (inner == 0) return fail(ARMAI_E_INVALID, "softmax: inner must be positive");
+  if (input_len != outer * inner)
+    return fail(ARMAI_E_INVALID, lenmsg("softmax: input", input_len, "outer*inner", outer * inner));
+  if (!outer) return ARMAI_OK;
+  cudaStream_t s;
+  ARMAI_TRY(thread_stream(&s));
+  Scoped dx(s), dout(s);
+  ARMAI_TRY(h2d(dx, input, input_len * 4));
+  ARMAI_TRY(dalloc(dout, input_len * 4));
+  ARMAI_TRY(armai_dev_softmax_last_axis_f32((float*)dx.p, (float*)dout.p, (int64_t)outer, (int64_t)inner, s));
+  return finish(s, out, dout.p, input_len * 4);
+}
+
+extern "C" int armai_dev_silu_gate_mul_up_f32(const float* gate, const float* up, float* out, int64_t n,
+                                              void* stream) {
+  if (n <= 0) return ARMAI_OK;
+  k_silu_gate_mul_up<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(gate, up, out, n);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+extern "C" int armai_silu_gate_mul_up_f32(const float* gate, size_t gate_len, const float* up, size_t up_len,
+                                          float* out) {
+  if (up_len != gate_len)
+    return fail(ARMAI_E_INVALID, "silu_gate_mul_up: up len " + std::to_string(up_len) + " != gate len " +
+                                     std::to_string(gate_len));
+  if (!gate_len) return ARMAI_OK;
+  cudaStream_t s;
+  ARMAI_TRY(thread_stream(&s));
+  Scoped dg(s), du(s), dout(s);
+  ARMAI_TRY(h2d(dg, gate, gate_len * 4));
+  ARMAI_TRY(h2d(du, up, up_len * 4));
+  ARMAI_TRY(dalloc(dout, gate_len * 4));
+  ARMAI_TRY(armai_dev_silu_gate_mul_up_f32((float*)dg.p, (float*)du.p, (float*)dout.p, (int64_t)gate_len, s));
+  return finish(s, out, dout.p, gate_len * 4);
+}
+
+extern "C" int armai_dev_dequantize_q6_k(const uint8_t* in, float* out, int64_t n_blocks, void* stream) {
+  if (n_blocks <= 0) return ARMAI_OK;
+  const int64_t threads = n_blocks * 64;
+  k_dequant_q6k<<<(unsigned)((threads + 255) / 256), 256, 0, (cudaStream_t)stream>>>(in, out, n_blocks);
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+extern "C" int armai_dequantize_q6_k(const uint8_t* input, size_t input_len, size_t n_elements, float* out) {
+  const size_t n_blocks = input_len / 210;
+  if (n_elements != n_blocks * 256)
+    return fail(ARMAI_E_INVALID, lenmsg("dequantize_q6_k: n_elements", n_elements, "256 * blocks", n_blocks * 256));
+  if (!n_blocks) return ARMAI_OK;
+  cudaStream_t s;
+  ARMAI_TRY(thread_stream(&s));
+  Scoped din(s), dout(s);
+  ARMAI_TRY(h2d(din, input, n_blocks * 210));
+  ARMAI_TRY(dalloc(dout, n_elements * 4));
+  ARMAI_TRY(armai_dev_dequantize_q6_k((uint8_t*)din.p, (float*)dout.p, (int64_t)n_blocks, s));
+  return finish(s, out, dout.p, n_elements * 4);
+}
+
+extern "C" int armai_dev_dequant_matmul_f16_f32(const float* act, const uint16_t* w, float* out, int64_t rows,
+                                                int64_t n, int64_t k, void* stream) {
+  if (rows <= 0 || n <= 0) return ARMAI_OK;
+  if (n > 0x7fffffff || k > 0x7fffffff) return fail(ARMAI_E_INVALID, "dequant_matmul_f16: N or K too large");
+  const cudaStream_t s = (cudaStream_t)stream;
+  if (rows <= 4) {  // decode: one activation row group, 256 weight rows per CTA
+    const dim3 grid((unsigned)((n + 255) / 256), 1);
+    k_dequant_f16<8><<<grid, 256, 0, s>>>(act, w, out, rows, (int)n, (int)k);
+  } else {
+    const dim3 grid((unsigned)((n + 31) / 32), (unsigned)((rows + 31) / 32));
+    k_dequant_f16<1><<<grid, 256, 0, s>>>(act, w, out, rows, (int)n, (int)k);
+  }
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
+}
+
+extern "C" int armai_dequant_matmul_f16_f32(const float* act, size_t act_len, const uint16_t* weights,
+                                            size_t weights_len, size_t b, size_t m, size_t n, size_t k,
+                                            float* out) {
+  if (act_len != b * m * k) return fail(ARMAI_E_INVALID, lenmsg("dequant_matmul_f16: act", act_len, "B*M*K", b * m * k));
+  if (weights_len != n * k)
+    return fail(ARMAI_E_INVALID, lenmsg("dequant_matmul_f16: weights", weights_len, "N*K", n * k));
+  const size_t rows = b * m;
+  if (!rows || !n) return ARMAI_OK;
+  cudaStream_t s;
+  ARMAI_TRY(thread_stream(&s));
+  Scoped da(s), dw(s), dout(s);
+  ARMAI_TRY(h2d(da, act, act_len * 4));
+  ARMAI_TRY(h2d(dw, weights, weights_len * 2));
+  ARMAI_TRY(dalloc(dout, rows * n * 4));
+  ARMAI_TRY(armai_dev_dequant_matmul_f16_f32((float*)da.p, (uint16_t*)dw.p, (float*)dout.p, (int64_t)rows,
+                                             (int64_t)n, (int64_t)k, s));
+  return finish(s, out, dout.p, rows * n * 4);
 }

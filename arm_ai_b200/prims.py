@@ -104,3 +104,50 @@ def dequant_matmul_int8_f32_op(act, weights, scales, b, m, n, k):
     _chk(load_cuda().armai_dequant_matmul_int8_f32(ptr(a), a.size, ptr(w), w.size, ptr(s), s.size, b, m, n, k,
                                                    ptr(out)))
     return out[: b * m * n]
+
+
+# ---- LLM helper NIFs (lib.rs:147-354) ----------------------------------
+
+def rope_f32_op(input, positions, inv_freq, n_rows, head_dim, heads_per_token):
+    """rope_f32_op/6: input [n_rows, head_dim] f32, positions i64 per token,
+    inv_freq [head_dim / 2] f32; interleaved pairs (shape_ops.rs:1040-1100)."""
+    x, p, f = _c(input, np.float32), _c(positions, np.int64), _c(inv_freq, np.float32)
+    out = np.empty(max(x.size, 1), np.float32)
+    _chk(load_cuda().armai_rope_f32(ptr(x), x.size, ptr(p), p.size, ptr(f), f.size, n_rows, head_dim,
+                                    heads_per_token, ptr(out)))
+    return out[: x.size]
+
+
+def dequant_matmul_f16_f32_op(act, weights_f16, b, m, n, k):
+    """dequant_matmul_f16_f32_op/6: act [B,M,K] f32, weights [N,K] f16 (or
+    their u16 bits) -> [B*M*N] f32 (shape_ops.rs:1462-1490)."""
+    a = _c(act, np.float32)
+    w = np.asarray(weights_f16)
+    w = _c(w.view(np.uint16) if w.dtype == np.float16 else w, np.uint16)
+    out = np.empty(max(b * m * n, 1), np.float32)
+    _chk(load_cuda().armai_dequant_matmul_f16_f32(ptr(a), a.size, ptr(w), w.size, b, m, n, k, ptr(out)))
+    return out[: b * m * n]
+
+
+def softmax_last_axis_f32_op(input, outer, inner):
+    """softmax_last_axis_f32_op/3 (shape_ops.rs:2719-2751)."""
+    x = _c(input, np.float32)
+    out = np.empty(max(x.size, 1), np.float32)
+    _chk(load_cuda().armai_softmax_last_axis_f32(ptr(x), x.size, outer, inner, ptr(out)))
+    return out[: x.size]
+
+
+def silu_gate_mul_up_f32_op(gate, up):
+    """silu_gate_mul_up_f32_op/2: silu(gate) * up (shape_ops.rs:2755-2770)."""
+    g, u = _c(gate, np.float32), _c(up, np.float32)
+    out = np.empty(max(g.size, 1), np.float32)
+    _chk(load_cuda().armai_silu_gate_mul_up_f32(ptr(g), g.size, ptr(u), u.size, ptr(out)))
+    return out[: g.size]
+
+
+def dequantize_q6_k_op(input, n_elements):
+    """dequantize_q6_k_op/2: GGML Q6_K bytes -> n_elements f32 (shape_ops.rs:2848-2899)."""
+    b = np.frombuffer(bytes(input), np.uint8) if isinstance(input, (bytes, bytearray)) else _c(input, np.uint8)
+    out = np.empty(max(n_elements, 1), np.float32)
+    _chk(load_cuda().armai_dequantize_q6_k(ptr(b), b.size, n_elements, ptr(out)))
+    return out[:n_elements]

@@ -230,6 +230,32 @@ ARMAI_API int armai_dequant_matmul_int8_f32(const float* act, size_t act_len, co
                                   const float* scales, size_t scales_len, size_t b, size_t m,
                                   size_t n, size_t k, float* out);
 
+/* rope_f32_op (lib.rs:147-171 -> shape_ops.rs:1040-1100): input [n_rows, head_dim],
+ * positions i64 per token (row r uses positions[r / heads_per_token]),
+ * inv_freq [head_dim / 2]; interleaved pairs (2k, 2k + 1). */
+ARMAI_API int armai_rope_f32(const float* input, size_t input_len, const int64_t* positions,
+                             size_t n_positions, const float* inv_freq, size_t inv_freq_len,
+                             size_t n_rows, size_t head_dim, size_t heads_per_token, float* out);
+
+/* dequant_matmul_f16_f32_op (lib.rs:173-196 -> shape_ops.rs:1462-1490):
+ * act [B,M,K] f32 x weights [N,K] f16 bits -> out [B,M,N]. */
+ARMAI_API int armai_dequant_matmul_f16_f32(const float* act, size_t act_len, const uint16_t* weights,
+                                           size_t weights_len, size_t b, size_t m, size_t n, size_t k,
+                                           float* out);
+
+/* softmax_last_axis_f32_op (lib.rs:298-318 -> shape_ops.rs:2719-2751). */
+ARMAI_API int armai_softmax_last_axis_f32(const float* input, size_t input_len, size_t outer,
+                                          size_t inner, float* out);
+
+/* silu_gate_mul_up_f32_op (lib.rs:320-342 -> shape_ops.rs:2755-2770). */
+ARMAI_API int armai_silu_gate_mul_up_f32(const float* gate, size_t gate_len, const float* up,
+                                         size_t up_len, float* out);
+
+/* dequantize_q6_k_op (lib.rs:344-354 -> shape_ops.rs:2848-2899): 210-byte
+ * blocks -> n_elements f32 (n_elements = 256 * whole blocks in input). */
+ARMAI_API int armai_dequantize_q6_k(const uint8_t* input, size_t input_len, size_t n_elements,
+                                    float* out);
+
 /* ------------------------------------------------------------------ */
 /* Device-pointer variants (benchmarks, and callers that keep tensors     */
 /* resident). `stream` is a cudaStream_t.                                   */
@@ -269,6 +295,18 @@ ARMAI_API int armai_dev_flash_attention_f16(const uint16_t* q, const uint16_t* k
 ARMAI_API int armai_dev_flash_attention_f32(const float* q, const float* k, const float* v, float* out,
                                   float scale, int64_t b, int64_t h, int64_t sq, int64_t sk,
                                   int64_t d, int causal, void* stream);
+ARMAI_API int armai_dev_rope_f32(const float* x, const int64_t* positions, const float* inv_freq,
+                                 float* out, int64_t n_rows, int64_t head_dim, int64_t heads_per_token,
+                                 void* stream);
+ARMAI_API int armai_dev_softmax_last_axis_f32(const float* x, float* out, int64_t outer, int64_t inner,
+                                              void* stream);
+ARMAI_API int armai_dev_silu_gate_mul_up_f32(const float* gate, const float* up, float* out, int64_t n,
+                                             void* stream);
+/* n_blocks 210-byte Q6_K blocks -> 256 * n_blocks f32. */
+ARMAI_API int armai_dev_dequantize_q6_k(const uint8_t* in, float* out, int64_t n_blocks, void* stream);
+/* act [rows, K] f32 x weights [N, K] f16 bits -> out [rows, N]. */
+ARMAI_API int armai_dev_dequant_matmul_f16_f32(const float* act, const uint16_t* w, float* out,
+                                               int64_t rows, int64_t n, int64_t k, void* stream);
 
 /* ------------------------------------------------------------------ */
 /* k-quant building blocks, exposed for bit-exact parity tests.           */

@@ -915,3 +915,101 @@ int orc_dequant_matmul_int8_f32(const float* act, const int8_t* w, const float* 
     }
   return 0;
 }
+
+/* shape_ops.rs:1040-1100 rope_f32: row r uses positions[r / heads_per_token];
+ * pairs (2k, 2k+1) rotated by theta = (f32)pos * inv_freq[k]. */
+int orc_rope_f32(const float* x, const int64_t* positions, const float* inv_freq, int64_t n_rows,
+                 int64_t head_dim, int64_t heads_per_token, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t row = 0; row < n_rows; row++) {
+    const float pos = (float)positions[row / heads_per_token];
+    const float* in = x + row * head_dim;
+    float* o = out + row * head_dim;
+    for (int64_t k = 0; k < head_dim / 2; k++) {
+      const float theta = pos * inv_freq[k];
+      const float c = cosf(theta), s = sinf(theta);
+      const float x0 = in[2 * k], x1 = in[2 * k + 1];
+      o[2 * k] = x0 * c - x1 * s;
+      o[2 * k + 1] = x0 * s + x1 * c;
+    }
+  }
+  return 0;
+}
+
+/* shape_ops.rs:2719-2751 softmax_last_axis_f32: max scanned from src[0]
+ * (replaced on v > max), e = exp(x - max) summed in order, then e * (1/sum). */
+int orc_softmax_last_axis_f32(const float* x, int64_t outer, int64_t inner, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < outer; r++) {
+    const float* src = x + r * inner;
+    float* row = out + r * inner;
+    float max = src[0];
+    for (int64_t i = 1; i < inner; i++)
+      if (src[i] > max) max = src[i];
+    float sum = 0.f;
+    for (int64_t i = 0; i < inner; i++) {
+      const float e = expf(src[i] - max);
+      row[i] = e;
+      sum += e;
+    }
+    const float inv = 1.0f / sum;
+    for (int64_t i = 0; i < inner; i++) row[i] *= inv;
+  }
+  return 0;
+}
+
+/* shape_ops.rs:2755-2770 silu_gate_mul_up_f32: g * (1 / (1 + exp(-g))) * u. */
+int orc_silu_gate_mul_up_f32(const float* gate, const float* up, int64_t n, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; i++) {
+    const float g = gate[i];
+    const float sig = 1.0f / (1.0f + expf(-g));
+    out[i] = g * sig * up[i];
+  }
+  return 0;
+}
+
+/* shape_ops.rs:2848-2899 dequantize_q6_k, as the reference writes it: the
+ * sub-scales of each 32-value group are scales[8n + {0, 2, 4, 6}] for every
+ * l (ggml's dequantize_row_q6_K would add l / 16). */
+int orc_dequantize_q6_k(const uint8_t* in, int64_t n_blocks, float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < n_blocks; b++) {
+    const uint8_t* blk = in + b * 210;
+    float* o = out + b * 256;
+    const uint8_t* ql = blk;
+    const uint8_t* qh = blk + 128;
+    const int8_t* sc = (const int8_t*)(blk + 192);
+    const float d = orc_f16_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
+    for (int n = 0; n < 2; n++) {
+      for (int l = 0; l < 32; l++) {
+        const uint8_t qhi = qh[32 * n + l];
+        const int q1 = ((ql[64 * n + l] & 0xF) | (((qhi >> 0) & 3) << 4)) - 32;
+        const int q2 = ((ql[64 * n + l + 32] & 0xF) | (((qhi >> 2) & 3) << 4)) - 32;
+        const int q3 = (((ql[64 * n + l] >> 4) & 0xF) | (((qhi >> 4) & 3) << 4)) - 32;
+        const int q4 = (((ql[64 * n + l + 32] >> 4) & 0xF) | (((qhi >> 6) & 3) << 4)) - 32;
+        o[128 * n + l] = d * (float)(sc[8 * n + 0] * q1);
+        o[128 * n + l + 32] = d * (float)(sc[8 * n + 2] * q2);
+        o[128 * n + l + 64] = d * (float)(sc[8 * n + 4] * q3);
+        o[128 * n + l + 96] = d * (float)(sc[8 * n + 6] * q4);
+      }
+    }
+  }
+  return 0;
+}
+
+/* shape_ops.rs:1462-1490 dequant_matmul_f16_f32 (x86 path): out[r][j] = sum
+ * over k in order of a[r][k] * f32(w[j][k]). */
+int orc_dequant_matmul_f16_f32(const float* act, const uint16_t* w, int64_t b, int64_t m, int64_t n,
+                               int64_t k, float* out) {
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t r = 0; r < b * m; r++)
+    for (int64_t j = 0; j < n; j++) {
+      const float* a = act + r * k;
+      const uint16_t* wr = w + j * k;
+      float total = 0.f;
+      for (int64_t kk = 0; kk < k; kk++) total += a[kk] * orc_f16_to_f32(wr[kk]);
+      out[r * n + j] = total;
+    }
+  return 0;
+}

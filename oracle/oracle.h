@@ -132,6 +132,14 @@ int orc_flash_attention_f32(const float* q, const float* k, const float* v, floa
                             float* out);
 int orc_dequant_matmul_int8_f32(const float* act, const int8_t* w, const float* scales, int64_t b,
                                 int64_t m, int64_t n, int64_t k, float* out);
+/* LLM helper primitives (lib.rs:147-354); lengths are the caller's to check. */
+int orc_rope_f32(const float* x, const int64_t* positions, const float* inv_freq, int64_t n_rows,
+                 int64_t head_dim, int64_t heads_per_token, float* out);
+int orc_softmax_last_axis_f32(const float* x, int64_t outer, int64_t inner, float* out);
+int orc_silu_gate_mul_up_f32(const float* gate, const float* up, int64_t n, float* out);
+int orc_dequantize_q6_k(const uint8_t* in, int64_t n_blocks, float* out);
+int orc_dequant_matmul_f16_f32(const float* act, const uint16_t* w, int64_t b, int64_t m, int64_t n,
+                               int64_t k, float* out);
 
 #ifdef __cplusplus
 }

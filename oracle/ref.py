@@ -63,6 +63,11 @@ def lib() -> ctypes.CDLL:
             "orc_rmsnorm_f32": (c_int, [V, V, I64, I64, c_float, V]),
             "orc_flash_attention_f32": (c_int, [V, V, V, c_float, I64, I64, I64, I64, I64, c_int, V]),
             "orc_dequant_matmul_int8_f32": (c_int, [V, V, V, I64, I64, I64, I64, V]),
+            "orc_rope_f32": (c_int, [V, V, V, I64, I64, I64, V]),
+            "orc_softmax_last_axis_f32": (c_int, [V, I64, I64, V]),
+            "orc_silu_gate_mul_up_f32": (c_int, [V, V, I64, V]),
+            "orc_dequantize_q6_k": (c_int, [V, I64, V]),
+            "orc_dequant_matmul_f16_f32": (c_int, [V, V, I64, I64, I64, I64, V]),
         }
         for k, (r, a) in sigs.items():
             f = getattr(L, k)
@@ -301,4 +306,42 @@ def flash_attention_f32(q, k, v, scale, b, h, sq, sk, d, causal):
 def dequant_matmul_int8_f32(act, w, scales, b, m, n, k):
     out = np.empty((b * m, n), dtype=np.float32)
     check(lib().orc_dequant_matmul_int8_f32(P(act), P(w), P(scales), b, m, n, k, P(out)))
+    return out
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def rope_f32(x, positions, inv_freq, n_rows, head_dim, heads_per_token):
+    out = np.empty((n_rows, head_dim), dtype=np.float32)
+    pos = np.ascontiguousarray(positions, dtype=np.int64)
+    check(lib().orc_rope_f32(P(_f32(x)), P(pos), P(_f32(inv_freq)), n_rows, head_dim, heads_per_token, P(out)))
+    return out
+
+
+def softmax_last_axis_f32(x, outer, inner):
+    out = np.empty((outer, inner), dtype=np.float32)
+    check(lib().orc_softmax_last_axis_f32(P(_f32(x)), outer, inner, P(out)))
+    return out
+
+
+def silu_gate_mul_up_f32(gate, up):
+    g, u = _f32(gate).reshape(-1), _f32(up).reshape(-1)
+    out = np.empty(g.size, dtype=np.float32)
+    check(lib().orc_silu_gate_mul_up_f32(P(g), P(u), g.size, P(out)))
+    return out
+
+
+def dequantize_q6_k(raw, n_blocks):
+    b = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1)
+    out = np.empty(n_blocks * 256, dtype=np.float32)
+    check(lib().orc_dequantize_q6_k(P(b), n_blocks, P(out)))
+    return out
+
+
+def dequant_matmul_f16_f32(act, w_bits, b, m, n, k):
+    out = np.empty((b * m, n), dtype=np.float32)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    check(lib().orc_dequant_matmul_f16_f32(P(_f32(act)), P(w), b, m, n, k, P(out)))
     return out
