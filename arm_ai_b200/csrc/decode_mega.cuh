@@ -505,27 +505,88 @@ struct MkCtx {
   }
 };
 
-// All chunks of this CTA's rows in one matvec phase: wait for each stage,
-// compute, hand the stage back to the producer.
+// The units of two staged chunks A and B, dealt over the consumer warps as
+// one list (A's units, then B's): with at most MK_CW units each warp takes
+// one; with more, warp w takes units w and w + MK_CW together (four dot
+// chains over one activation slice) — so a phase whose rows arrive in
+// several stages does not serialise one unit per warp per stage.
+template <int MODE>
+__device__ __forceinline__ void mk_group_units(const MkCtx& cx, const uint8_t* sa, int a0, int a1,
+                                               const Part (&pa)[3], const uint8_t* sb, int b0, int b1,
+                                               const Part (&pb)[3], const ActQ8& act, int cw, int lane,
+                                               float& best_v, int& best_i) {
+  const int nb = cx.nb();
+  const int nA = chunk_nunits<MODE>(a0, a1), U = nA + chunk_nunits<MODE>(b0, b1);
+  const int step = U <= MK_CW ? MK_CW : 2 * MK_CW;
+  for (int g = cw; g < U; g += step) {
+    const UnitRows w1 = g < nA ? unit_rows<MODE>(cx, sa, a0, a1, pa, g) : unit_rows<MODE>(cx, sb, b0, b1, pb, g - nA);
+    const int g2 = g + MK_CW;
+    float d[4];
+    if (step > MK_CW && g2 < U) {
+      const UnitRows w2 =
+          g2 < nA ? unit_rows<MODE>(cx, sa, a0, a1, pa, g2) : unit_rows<MODE>(cx, sb, b0, b1, pb, g2 - nA);
+      if (w1.ty0 == w2.ty0 && w1.ty1 == w2.ty1) {
+        if (MODE != MODE_GATEUP || w1.ty0 == w1.ty1) {
+          if (w1.ty0 == GGML_Q4_K)
+            unit_dots2<GGML_Q4_K, GGML_Q4_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
+          else
+            unit_dots2<GGML_Q6_K, GGML_Q6_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
+        } else if (w1.ty0 == GGML_Q4_K) {
+          unit_dots2<GGML_Q4_K, GGML_Q6_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
+        } else {
+          unit_dots2<GGML_Q6_K, GGML_Q4_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
+        }
+      } else {
+        unit_dot_any<MODE>(w1, nb, act, lane, d[0], d[1]);
+        unit_dot_any<MODE>(w2, nb, act, lane, d[2], d[3]);
+      }
+      if (lane == 0) {
+        unit_epilogue<MODE>(cx, w1, d[0], d[1], 0.f, 0.f, best_v, best_i);
+        unit_epilogue<MODE>(cx, w2, d[2], d[3], 0.f, 0.f, best_v, best_i);
+      }
+    } else {
+      unit_dot_any<MODE>(w1, nb, act, lane, d[0], d[1]);
+      if (lane == 0) unit_epilogue<MODE>(cx, w1, d[0], d[1], 0.f, 0.f, best_v, best_i);
+    }
+  }
+}
+
+// All chunks of this CTA's rows in one matvec phase: wait for the stages,
+// compute, hand the stages back to the producer. Except for QKV (few rows
+// per CTA), chunks are taken two at a time (mk_group_units).
 template <int MODE>
 __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, uint32_t tag, uint8_t* smem,
                           uint64_t* full, uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
                           float& best_v, int& best_i) {
   int r0, r1;
   phase_rows(ph, r0, r1);
-  for (int c0 = r0; c0 < r1; c0 += ph.chunk_rows) {
+  const MkCtx cx{p, ph, pos, phase, tag};
+  for (int c0 = r0; c0 < r1;) {
     const int c1 = min(c0 + ph.chunk_rows, r1);
-    const int s = cidx % p.ns;
-    if (!mk_wait(&full[s], (uint32_t)((cidx / p.ns) & 1), p.err)) return false;
+    const bool two = MODE != MODE_QKV && c1 < r1;
+    const int c2 = two ? min(c1 + ph.chunk_rows, r1) : c1;
+    const int sA = cidx % p.ns, sB = (cidx + 1) % p.ns;
+    if (!mk_wait(&full[sA], (uint32_t)((cidx / p.ns) & 1), p.err)) return false;
+    if (two && !mk_wait(&full[sB], (uint32_t)(((cidx + 1) / p.ns) & 1), p.err)) return false;
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
-    Part parts[3];
-    make_parts<MODE>(ph.seg, ph.nseg, c0, c1, parts);
-    chunk_units<MODE>(MkCtx{p, ph, pos, phase, tag}, smem + (size_t)s * MK_STAGE, c0, c1, parts, act, cw, MK_CW,
-                      lane, best_v, best_i);
+    Part pa[3];
+    make_parts<MODE>(ph.seg, ph.nseg, c0, c1, pa);
+    if (!two) {
+      chunk_units<MODE>(cx, smem + (size_t)sA * MK_STAGE, c0, c1, pa, act, cw, MK_CW, lane, best_v, best_i);
+    } else {
+      Part pb[3];
+      make_parts<MODE>(ph.seg, ph.nseg, c1, c2, pb);
+      mk_group_units<MODE>(cx, smem + (size_t)sA * MK_STAGE, c0, c1, pa, smem + (size_t)sB * MK_STAGE, c1, c2, pb,
+                           act, cw, lane, best_v, best_i);
+    }
     __syncwarp();
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
-    if (lane == 0) mbar_arrive(&empty[s]);
-    cidx++;
+    if (lane == 0) {
+      mbar_arrive(&empty[sA]);
+      if (two) mbar_arrive(&empty[sB]);
+    }
+    cidx += two ? 2 : 1;
+    c0 = c2;
   }
   return true;
 }

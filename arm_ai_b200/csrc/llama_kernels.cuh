@@ -327,94 +327,164 @@ __device__ __forceinline__ void unit_dots(const uint8_t* p0, const uint8_t* p1, 
   d1 = a1;
 }
 
+// Two units at once (four rows, one activation slice per pass): independent
+// dot chains that a warp interleaves. Unit a = rows a0 (type T0), a1 (T1);
+// unit b likewise.
+template <int T0, int T1>
+__device__ __forceinline__ void unit_dots2(const uint8_t* a0p, const uint8_t* a1p, bool hasa1, const uint8_t* b0p,
+                                           const uint8_t* b1p, bool hasb1, int nb, const ActQ8& act, int lane,
+                                           float (&d)[4]) {
+  const int t = lane & 3, bl = lane >> 2;
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  const int npass = (nb + 7) >> 3;
+  for (int ps = 0; ps < npass; ps++) {
+    const int blk = ps * 8 + bl;
+    if (blk < nb) {
+      ActSlice A;
+      load_slice(act, blk, t, A);
+      a0 += quarter_dot_t<T0>(a0p, nb, blk, t, A);
+      b0 += quarter_dot_t<T0>(b0p, nb, blk, t, A);
+      if (hasa1) a1 += quarter_dot_t<T1>(a1p, nb, blk, t, A);
+      if (hasb1) b1 += quarter_dot_t<T1>(b1p, nb, blk, t, A);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+    b0 += __shfl_xor_sync(0xffffffffu, b0, off);
+    b1 += __shfl_xor_sync(0xffffffffu, b1, off);
+  }
+  d[0] = a0; d[1] = a1; d[2] = b0; d[3] = b1;
+}
+
+// Unit u of a staged chunk [c0, c1): its two row pointers, their types, its
+// first row r, the QKV segment si and whether the second row exists.
+struct UnitRows {
+  const uint8_t *p0, *p1;
+  int ty0, ty1, r, si;
+  bool has1;
+};
+template <int MODE, class Ctx>
+__device__ __forceinline__ UnitRows unit_rows(const Ctx& cx, const uint8_t* stage, int c0, int c1,
+                                              const Part (&parts)[3], int u) {
+  UnitRows w;
+  w.si = 0;
+  w.has1 = true;
+  if (MODE == MODE_QKV) {
+    w.r = c0 + 2 * u;
+    const int qn = cx.qn(), kn = cx.kn();
+    w.si = w.r < qn ? 0 : (w.r < qn + kn ? 1 : 2);
+    const int sb = w.si == 0 ? 0 : (w.si == 1 ? qn : qn + kn);
+    const uint32_t off = w.si == 0 ? parts[0].off : (w.si == 1 ? parts[1].off : parts[2].off);
+    const int lo = w.si == 0 ? parts[0].lo : (w.si == 1 ? parts[1].lo : parts[2].lo);
+    const Seg& sg = cx.seg(w.si);
+    w.p0 = stage + off + (size_t)(w.r - sb - lo) * sg.row_bytes;
+    w.p1 = w.p0 + sg.row_bytes;
+    w.ty0 = w.ty1 = sg.type;
+  } else if (MODE == MODE_GATEUP) {
+    w.r = c0 + u;
+    w.p0 = stage + (size_t)u * cx.seg(0).row_bytes;
+    w.p1 = stage + parts[1].off + (size_t)u * cx.seg(1).row_bytes;
+    w.ty0 = cx.seg(0).type;
+    w.ty1 = cx.seg(1).type;
+  } else {
+    w.r = c0 + 2 * u;
+    w.p0 = stage + (size_t)(2 * u) * cx.seg(0).row_bytes;
+    w.p1 = w.p0 + cx.seg(0).row_bytes;
+    w.has1 = w.r + 1 < c1;
+    w.ty0 = w.ty1 = cx.seg(0).type;
+  }
+  return w;
+}
+
+template <int MODE>
+__device__ __forceinline__ int chunk_nunits(int c0, int c1) {
+  return MODE == MODE_GATEUP ? c1 - c0 : (c1 - c0 + 1) >> 1;
+}
+
+// Both dot products of one unit, dispatched on the rows' types.
+template <int MODE>
+__device__ __forceinline__ void unit_dot_any(const UnitRows& w, int nb, const ActQ8& act, int lane, float& d0,
+                                             float& d1) {
+  if (MODE != MODE_GATEUP || w.ty0 == w.ty1) {  // both rows of one matrix
+    if (w.ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
+    else unit_dots<GGML_Q6_K, GGML_Q6_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
+  } else if (w.ty0 == GGML_Q4_K) {
+    unit_dots<GGML_Q4_K, GGML_Q6_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
+  } else {
+    unit_dots<GGML_Q6_K, GGML_Q4_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
+  }
+}
+
+// RoPE factors of a q / k pair, loaded before the dots so that their latency
+// overlaps them (same address for the whole warp).
+template <int MODE, class Ctx>
+__device__ __forceinline__ void unit_rope(const Ctx& cx, const UnitRows& w, float& cs, float& sn) {
+  cs = 0.f;
+  sn = 0.f;
+  if (MODE == MODE_QKV && w.si < 2) {
+    const int hd = cx.hd(), rr = w.si == 0 ? w.r : w.r - cx.qn();
+    const size_t ti = (size_t)cx.pos() * (hd >> 1) + ((rr % hd) >> 1);
+    cs = __ldg(cx.cos_t() + ti);
+    sn = __ldg(cx.sin_t() + ti);
+  }
+}
+
+// The unit's epilogue (one lane).
+template <int MODE, class Ctx>
+__device__ __forceinline__ void unit_epilogue(const Ctx& cx, const UnitRows& w, float d0, float d1, float cs,
+                                              float sn, float& best_v, int& best_i) {
+  const int r = w.r;
+  if (MODE == MODE_QKV) {
+    const int hd = cx.hd();
+    const int qn = cx.qn(), kn = cx.kn();
+    if (w.si < 2) {
+      const int rr = w.si == 0 ? r : r - qn;
+      // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
+      const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
+      const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
+      if (w.si == 0) cx.put_q(r, o0, o1);
+      else cx.put_kv(0, rr / hd, rr % hd, o0, o1);
+    } else {
+      const int rv = r - qn - kn;
+      cx.put_kv(1, rv / hd, rv % hd, d0, d1);
+    }
+  } else if (MODE == MODE_GATEUP) {
+    // candle: silu(v) = v / (1 + exp(-v)); then * up
+    const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
+    cx.put_h(r, __fmul_rn(sl, d1));
+  } else {
+    float* out = cx.out();
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      if (k == 1 && !w.has1) break;
+      const float v = k == 0 ? d0 : d1;
+      if (MODE == MODE_RESID) cx.resid_add(out + r + k, r + k, v);
+      else if (out) out[r + k] = v;
+      if (MODE == MODE_HEAD && am_better(v, r + k, best_v, best_i)) {
+        best_v = v;
+        best_i = r + k;
+      }
+    }
+  }
+}
+
 template <int MODE, class Ctx>
 __device__ __forceinline__ void chunk_units(const Ctx& cx, const uint8_t* stage, int c0, int c1,
                                             const Part (&parts)[3], const ActQ8& act, int warp,
                                             int nwarps, int lane, float& best_v, int& best_i) {
   const int nb = cx.nb();
-  const int n = c1 - c0;
-  const int nunits = MODE == MODE_GATEUP ? n : (n + 1) >> 1;
+  const int nunits = chunk_nunits<MODE>(c0, c1);
   for (int u = warp; u < nunits; u += nwarps) {
-    const uint8_t *p0, *p1;
-    int ty0, ty1, r, si = 0;
-    bool has1 = true;
-    if (MODE == MODE_QKV) {
-      r = c0 + 2 * u;
-      const int qn = cx.qn(), kn = cx.kn();
-      si = r < qn ? 0 : (r < qn + kn ? 1 : 2);
-      const int sb = si == 0 ? 0 : (si == 1 ? qn : qn + kn);
-      const uint32_t off = si == 0 ? parts[0].off : (si == 1 ? parts[1].off : parts[2].off);
-      const int lo = si == 0 ? parts[0].lo : (si == 1 ? parts[1].lo : parts[2].lo);
-      const Seg& sg = cx.seg(si);
-      p0 = stage + off + (size_t)(r - sb - lo) * sg.row_bytes;
-      p1 = p0 + sg.row_bytes;
-      ty0 = ty1 = sg.type;
-    } else if (MODE == MODE_GATEUP) {
-      r = c0 + u;
-      p0 = stage + (size_t)u * cx.seg(0).row_bytes;
-      p1 = stage + parts[1].off + (size_t)u * cx.seg(1).row_bytes;
-      ty0 = cx.seg(0).type;
-      ty1 = cx.seg(1).type;
-    } else {
-      r = c0 + 2 * u;
-      p0 = stage + (size_t)(2 * u) * cx.seg(0).row_bytes;
-      p1 = p0 + cx.seg(0).row_bytes;
-      has1 = r + 1 < c1;
-      ty0 = ty1 = cx.seg(0).type;
-    }
-    // RoPE factors of a q / k pair: loaded before the dots so that their
-    // latency overlaps them (same address for the whole warp)
-    float cs = 0.f, sn = 0.f;
-    if (MODE == MODE_QKV && si < 2) {
-      const int hd = cx.hd(), rr = si == 0 ? r : r - cx.qn();
-      const size_t ti = (size_t)cx.pos() * (hd >> 1) + ((rr % hd) >> 1);
-      cs = __ldg(cx.cos_t() + ti);
-      sn = __ldg(cx.sin_t() + ti);
-    }
+    const UnitRows w = unit_rows<MODE>(cx, stage, c0, c1, parts, u);
+    float cs, sn;
+    unit_rope<MODE>(cx, w, cs, sn);
     float d0, d1;
-    if (MODE != MODE_GATEUP || ty0 == ty1) {  // both rows of one matrix
-      if (ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K>(p0, p1, has1, nb, act, lane, d0, d1);
-      else unit_dots<GGML_Q6_K, GGML_Q6_K>(p0, p1, has1, nb, act, lane, d0, d1);
-    } else if (ty0 == GGML_Q4_K) {
-      unit_dots<GGML_Q4_K, GGML_Q6_K>(p0, p1, has1, nb, act, lane, d0, d1);
-    } else {
-      unit_dots<GGML_Q6_K, GGML_Q4_K>(p0, p1, has1, nb, act, lane, d0, d1);
-    }
+    unit_dot_any<MODE>(w, nb, act, lane, d0, d1);
     if (lane != 0) continue;
     if (u == 0) cx.stamp(8);
-    float* out = cx.out();
-    if (MODE == MODE_QKV) {
-      const int hd = cx.hd(), pos = cx.pos();
-      const int qn = cx.qn(), kn = cx.kn();
-      if (si < 2) {
-        const int rr = si == 0 ? r : r - qn;
-        // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
-        const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
-        const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
-        if (si == 0) cx.put_q(r, o0, o1);
-        else cx.put_kv(0, rr / hd, rr % hd, o0, o1);
-      } else {
-        const int rv = r - qn - kn;
-        cx.put_kv(1, rv / hd, rv % hd, d0, d1);
-      }
-    } else if (MODE == MODE_GATEUP) {
-      // candle: silu(v) = v / (1 + exp(-v)); then * up
-      const float sl = __fdiv_rn(d0, __fadd_rn(1.0f, expf(-d0)));
-      cx.put_h(r, __fmul_rn(sl, d1));
-    } else {
-#pragma unroll
-      for (int k = 0; k < 2; k++) {
-        if (k == 1 && !has1) break;
-        const float v = k == 0 ? d0 : d1;
-        float* o = out + r + k;
-        if (MODE == MODE_RESID) cx.resid_add(o, r + k, v);
-        else *o = v;
-        if (MODE == MODE_HEAD && am_better(v, r + k, best_v, best_i)) {
-          best_v = v;
-          best_i = r + k;
-        }
-      }
-    }
+    unit_epilogue<MODE>(cx, w, d0, d1, cs, sn, best_v, best_i);
     if (u == 0) cx.stamp(9);
   }
 }

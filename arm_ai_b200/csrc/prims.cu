@@ -1137,7 +1137,8 @@ extern "C" int armai_dev_dequantize_q6_k(const uint8_t* in, float* out, int64_t 
 extern "C" int armai_dequantize_q6_k(const uint8_t* input, size_t input_len, size_t n_elements, float* out) {
   const size_t n_blocks = input_len / 210;
   if (n_elements != n_blocks * 256)
-    return fail(ARMAI_E_INVALID, lenmsg("dequantize_q6_k: n_elements", n_elements, "256 * blocks", n_blocks * 256));
+    return fail(ARMAI_E_INVALID, "dequantize_q6_k: n_elements " + std::to_string(n_elements) +
+                                     " != 256 * blocks = " + std::to_string(n_blocks * 256));
   if (!n_blocks) return ARMAI_OK;
   cudaStream_t s;
   ARMAI_TRY(thread_stream(&s));

@@ -47,9 +47,10 @@ def test_softmax_matches_oracle(built, outer, inner):
     got = prims.softmax_last_axis_f32_op(x, outer, inner).reshape(outer, inner)
     exp = ref.softmax_last_axis_f32(x, outer, inner)
     # the reference normalises by a serial f32 sum, whose relative error is
-    # bounded by inner * 2^-24; the parallel sum is far closer to exact
-    x64 = x.astype(np.float64)
-    exact = np.exp(x64 - x64.max(axis=1, keepdims=True))
+    # bounded by inner * 2^-24; the parallel sum is far closer to exact.
+    # "exact": f64 from the f32-rounded x - max that both compute
+    diff = (x - x.max(axis=1, keepdims=True)).astype(np.float32).astype(np.float64)
+    exact = np.exp(diff)
     exact /= exact.sum(axis=1, keepdims=True)
     np.testing.assert_allclose(got, exact, rtol=2e-6, atol=1e-30)
     np.testing.assert_allclose(got, exp, rtol=max(1e-5, inner * 2.0 ** -24), atol=1e-30)
