@@ -55,6 +55,8 @@ ARCHS = {
     # small shapes for CPU-checkable parity tests
     "tiny": LlamaArch(2, 256, 512, 4, 2, 1000, 10000.0, 1e-5, 4096),
     "small": LlamaArch(4, 512, 1536, 8, 2, 4096, 10000.0, 1e-5, 4096),
+    # head_dim 128 (the Mistral / Llama-3 attention shape) at CPU-checkable size
+    "tiny128": LlamaArch(2, 512, 1024, 4, 2, 1000, 500000.0, 1e-5, 8192),
 }
 
 

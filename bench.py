@@ -47,6 +47,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--no-clocks", action="store_true")
     p.add_argument("--no-config2", action="store_true", help="skip the batched-decode (config 2) figures")
+    p.add_argument("--no-config3", action="store_true", help="skip the Mistral-7B long-context (config 3) figures")
     p.add_argument("--no-config4", action="store_true", help="skip the Llama-3-8B tensor-parallel (config 4) figures")
     return p.parse_args()
 
@@ -294,6 +295,36 @@ def run_config4(d, peak):
             "timing": "decode: CUDA events over 127 back-to-back steps, max over ranks; prefill: host wall clock"}
 
 
+def run_config3(d, peak):
+    """Mistral-7B-architecture Q4_K_M, b = 1, 4096-token
+    seeded prompt with an f16 KV cache, then 256 decode tokens (split-K GQA
+    attention over the long context). One GPU (rank 0 of a single-process
+    run). Decode device-timed (CUDA events over 255 back-to-back steps)."""
+    from arm_ai_b200 import native, synth
+    arch, n_prompt, n_new = "mistral-7b", 4096, 256
+    path = synth.model_path(arch, seed=0)
+    gpu = native.llama_candle_load_op(path, device=d.local, max_seq_len=n_prompt + n_new + 64, kv_f16=1)
+    info = gpu.info()
+    prompt = synth.prompt_tokens(n_prompt, info.n_vocab, 4000)
+    native.llama_forward(gpu, prompt[:64], 0, want_logits=False)  # warm-up
+    t0 = time.time()
+    native.llama_forward(gpu, prompt, 0, want_logits=False)
+    pre_s = time.time() - t0
+    n_dec = n_new - 1
+    ms = native.llama_bench_decode(gpu, n_dec)
+    step_s = ms / 1e3 / n_dec
+    kv_row = 2 * info.n_layer * info.n_head_kv * info.head_dim * 2  # f16 K and V per position
+    bytes_tok = info.weight_bytes + kv_row * (n_prompt + n_prompt + n_dec) / 2
+    gpu.close()
+    return {"workload": f"{arch} Q4_K_M b=1: {n_prompt}-token prompt (f16 KV) + {n_new} new tokens, 1 GPU",
+            "decode_tokens_per_s": 1.0 / step_s, "ms_per_token": step_s * 1e3,
+            "prefill_tokens_per_s": n_prompt / pre_s,
+            "weight_and_kv_stream_gb_s": bytes_tok / step_s / 1e9,
+            "frac_of_hbm": bytes_tok / step_s / 1e9 / peak,
+            "bytes_per_token": bytes_tok,
+            "timing": "decode: CUDA events over 255 back-to-back steps; prefill: host wall clock"}
+
+
 def run_armai(args, d):
     from arm_ai_b200 import native, synth
     if d.rank == 0:
@@ -360,6 +391,7 @@ def run_armai(args, d):
     gpu_launches = int(args.steps * n_dec * info.n_kernels_per_step * d.world)
     gpu.close()
     cfg2 = None if args.no_config2 else run_config2(d)
+    cfg3 = run_config3(d, peak) if (d.world == 1 and not args.no_config3) else None
     cfg4 = None if args.no_config4 else run_config4(d, peak)
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
@@ -396,6 +428,7 @@ def run_armai(args, d):
             "gpu_launches": gpu_launches,
             "wall_s_timed_region": t_wall,
             "config2_batched": cfg2,
+            "config3_mistral_7b_long": cfg3,
             "config4_llama3_8b": cfg4,
         }
         print(json.dumps(out), flush=True)

@@ -39,3 +39,9 @@ def small_model(built):
 def tied_model(built):
     from arm_ai_b200 import synth
     return synth.model_path("tiny", seed=3, tie_output=True)
+
+
+@pytest.fixture(scope="session")
+def hd128_model(built):
+    from arm_ai_b200 import synth
+    return synth.model_path("tiny128", seed=4)
