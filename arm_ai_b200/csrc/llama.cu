@@ -8,6 +8,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "common.cuh"
@@ -23,6 +25,7 @@ namespace {
 
 constexpr int PREFILL_TILE = 8;       // tokens per prefill matvec launch
 constexpr int BATCH_NB = 16;          // sequences per batched-decode matvec launch
+constexpr int BATCH_NB_WIDE = 8;      // ... when 16 activation rows of K do not fit shared memory
 constexpr int TC_PREFILL_MIN = 64;    // prompts this long use the tensor-core GEMM (prefill_gemm 0)
 
 constexpr int ATTN_TOK_PER_LAUNCH = 64;
@@ -100,11 +103,11 @@ struct armai_llama {
   int tp = 1, tp_rank = 0;
   void* comm = nullptr;
   int v0 = 0, v_stride = 0;      // first vocab row of this rank; vocab rows per rank
-  float* tp_part = nullptr;      // [E] partial sum of a row-split matvec
-  float* best_val = nullptr;     // head winner: value and local row
+  float* tp_part = nullptr;      // [max_batch][E] partial sums of a row-split matvec
+  float* best_val = nullptr;     // [max_batch] head winner: value and local row
   int* best_idx = nullptr;
-  uint32_t* tp_send = nullptr;   // 2 words: winner bits, global row
-  uint32_t* tp_recv = nullptr;   // 2 * tp words
+  uint32_t* tp_send = nullptr;   // [max_batch][2]: winner bits, global row
+  uint32_t* tp_recv = nullptr;   // [tp][max_batch][2]
   float* logits_all = nullptr;   // [tp * v_stride] gathered logits
   void* xchg = nullptr;          // persistent kernel: this rank's exchange area (IPC-shared)
   void* peer_xchg[8] = {};       // the other ranks' exchange areas, mapped here
@@ -118,6 +121,7 @@ struct armai_llama {
   Plan pl_qkv1, pl_wo1, pl_gu1, pl_down1, pl_head1;
   Plan pl_qkvT, pl_woT, pl_guT, pl_downT;
   Plan pl_qkvB, pl_woB, pl_guB, pl_downB, pl_headB;  // batched decode (max_batch > 1)
+  int batch_nb = 16;             // sequences per batched matvec launch (BATCH_NB or BATCH_NB_WIDE)
   uint32_t* h_btok = nullptr;  // pinned [max_batch] tokens of a batched step
   size_t attn_smem = 0;
   int n_kernels_step = 0;
@@ -284,7 +288,7 @@ cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x,
 // row, pl_headB for a batch): token[b] = argmax, pos_out[b] = pos[b] + 1.
 template <int NB>
 cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const int* pos, int* pos_out,
-                        uint32_t* token, int nrows = NB) {
+                        uint32_t* token, int nrows = NB, int best_off = 0) {
   MvParams p = base_params(m, pl);
   p.x = x;
   p.gamma = m->out_norm;
@@ -302,8 +306,8 @@ cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const in
   p.pos = pos;
   p.pos_out = pos_out;
   if (m->tp > 1) {
-    p.best_val = m->best_val;
-    p.best_idx = m->best_idx;
+    p.best_val = m->best_val + best_off;
+    p.best_idx = m->best_idx + best_off;
   }
   return launch_mv<MODE_HEAD, NB>(m, pl, p, nrows);
 }
@@ -365,6 +369,7 @@ cudaError_t launch_mega(armai_llama* m) {
 // at XCHG_SLOTS_OFF) is shared with the other ranks through CUDA IPC; the
 // handles travel by one NCCL all-gather.
 constexpr size_t XCHG_SLOTS_OFF = 512;
+int wait_done(armai_llama* m, cudaEvent_t ev = nullptr);
 int setup_peer_exchange(armai_llama* m, MkParams& k) {
   if (m->tp > MK_TP_MAX) return fail(ARMAI_E_INVALID, "tensor parallel: at most 8 ranks");
   const size_t E = m->n_embd;
@@ -393,7 +398,7 @@ int setup_peer_exchange(armai_llama* m, MkParams& k) {
                             m->stream);
   if (e == cudaSuccess && rc == ARMAI_OK)
     e = cudaMemcpyAsync(all.data(), dh, (size_t)m->tp * sizeof(Rec), cudaMemcpyDeviceToHost, m->stream);
-  if (e == cudaSuccess && rc == ARMAI_OK) e = cudaStreamSynchronize(m->stream);
+  if (e == cudaSuccess && rc == ARMAI_OK) rc = wait_done(m);
   cudaFree(dh);
   if (rc != ARMAI_OK) return rc;
   if (e != cudaSuccess) return cuda_fail(e, "exchange of IPC handles", __FILE__, __LINE__);
@@ -571,27 +576,34 @@ int setup_mega(armai_llama* m, int nsm) {
 // Tensor parallelism, winner of the head across ranks: (value, global row)
 // of every rank, then the reference's argmax order (larger value, then the
 // smaller row; NaN never wins).
-__global__ void k_tp_pack(const float* best_val, const int* best_idx, int v0, uint32_t* send) {
-  const int bi = best_idx[0];
-  send[0] = __float_as_uint(best_val[0]);
-  send[1] = bi == 0x7fffffff ? 0xffffffffu : (uint32_t)(bi + v0);
+// For n sequences: send[2s], send[2s + 1] = sequence s's winner on this rank;
+// recv = every rank's send ([rank][n][2]).
+__global__ void k_tp_pack(const float* best_val, const int* best_idx, int v0, uint32_t* send, int n) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n) return;
+  const int bi = best_idx[s];
+  send[2 * s] = __float_as_uint(best_val[s]);
+  send[2 * s + 1] = bi == 0x7fffffff ? 0xffffffffu : (uint32_t)(bi + v0);
 }
-__global__ void k_tp_pick(const uint32_t* recv, int tp, uint32_t* token) {
+__global__ void k_tp_pick(const uint32_t* recv, int tp, int n, uint32_t* token) {
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n) return;
   float bv = -INFINITY;
   uint32_t bi = 0xffffffffu;
   for (int r = 0; r < tp; r++) {
-    const float v = __uint_as_float(recv[2 * r]);
-    const uint32_t i = recv[2 * r + 1];
+    const float v = __uint_as_float(recv[((size_t)r * n + s) * 2]);
+    const uint32_t i = recv[((size_t)r * n + s) * 2 + 1];
     if (i != 0xffffffffu && (bi == 0xffffffffu || v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
   }
-  token[0] = bi == 0xffffffffu ? 0u : bi;
+  token[s] = bi == 0xffffffffu ? 0u : bi;
 }
 
-int tp_head_merge(armai_llama* m, uint32_t* token) {
-  k_tp_pack<<<1, 1, 0, m->stream>>>(m->best_val, m->best_idx, m->v0, m->tp_send);
+int tp_head_merge(armai_llama* m, uint32_t* token, int n = 1) {
+  const unsigned blocks = (unsigned)((n + 127) / 128);
+  k_tp_pack<<<blocks, 128, 0, m->stream>>>(m->best_val, m->best_idx, m->v0, m->tp_send, n);
   ARMAI_CUDA(cudaGetLastError());
-  ARMAI_TRY(nccl_allgather_b32(m->tp_send, m->tp_recv, 2, m->comm, m->stream));
-  k_tp_pick<<<1, 1, 0, m->stream>>>(m->tp_recv, m->tp, token);
+  ARMAI_TRY(nccl_allgather_b32(m->tp_send, m->tp_recv, (size_t)2 * n, m->comm, m->stream));
+  k_tp_pick<<<blocks, 128, 0, m->stream>>>(m->tp_recv, m->tp, n, token);
   ARMAI_CUDA(cudaGetLastError());
   return ARMAI_OK;
 }
@@ -648,8 +660,38 @@ int run_decode_step(armai_llama* m) {
   return enqueue_decode_step(m);
 }
 
+// Host wait on the model's stream (ev == nullptr) or on an event recorded on
+// it. Tensor parallelism: a rank whose peer failed outside a collective would
+// wait inside NCCL for ever, so the wait is bounded; on expiry the
+// communicator is aborted (its kernels return), the model is marked broken and
+// the call fails. One GPU: a plain synchronize.
+constexpr double TP_WAIT_S = 120.0;
+int wait_done(armai_llama* m, cudaEvent_t ev) {
+  if (m->tp <= 1 || !m->comm) {
+    ARMAI_CUDA(ev ? cudaEventSynchronize(ev) : cudaStreamSynchronize(m->stream));
+    return ARMAI_OK;
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint32_t it = 0;; ++it) {
+    const cudaError_t e = ev ? cudaEventQuery(ev) : cudaStreamQuery(m->stream);
+    if (e != cudaErrorNotReady) {
+      ARMAI_CUDA(e);
+      return ARMAI_OK;
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > TP_WAIT_S) {
+      nccl_comm_abort(m->comm);
+      m->comm = nullptr;
+      m->broken = true;
+      cudaStreamSynchronize(m->stream);
+      return fail(ARMAI_E_DEVICE, "tensor parallel: no progress for " + std::to_string((int)TP_WAIT_S) +
+                                      " s (another rank failed?); communicator aborted, reload the model");
+    }
+    if (it > 2000) std::this_thread::sleep_for(std::chrono::microseconds(200));
+  }
+}
+
 int check_device_error(armai_llama* m) {
-  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_TRY(wait_done(m));
   ARMAI_CUDA(cudaMemcpy(m->h_misc, m->d_err, 4, cudaMemcpyDeviceToHost));
   if (m->h_misc[0] != 0) {
     m->broken = true;
@@ -704,7 +746,7 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
   uint32_t* ht = m->h_prompt;
   int* hp = reinterpret_cast<int*>(m->h_prompt + m->h_prompt_cap);
   // The pinned staging may still be read by an earlier async copy.
-  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_TRY(wait_done(m));
   for (int i = 0; i < S; i++) { ht[i] = tokens[i]; hp[i] = i; }
   ARMAI_CUDA(cudaMemcpyAsync(m->p_tok, ht, (size_t)S * 4, cudaMemcpyHostToDevice, m->stream));
   ARMAI_CUDA(cudaMemcpyAsync(m->p_pos, hp, (size_t)S * 4, cudaMemcpyHostToDevice, m->stream));
@@ -787,31 +829,65 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
 // One greedy decode step for sequence slots 0..n-1: token d_token[b] at
 // position d_pos[b] of slot b's KV cache; writes the next token and position
 // back. Matvecs run BATCH_NB sequences per weight pass.
-int enqueue_batch_step(armai_llama* m, int n) {
+// x[s] += W in[s] for the n sequences of a batched step (W = attn_output or
+// ffn_down, in = y or h with row stride W.cols). Tensor parallel: W is split
+// along K; rank 0 adds its part into x, the others store theirs in tp_part,
+// and one all-reduce of n rows sums them into x everywhere.
+template <int NB>
+int rowsplit_resid_batch(armai_llama* m, const Plan& pl, const DevMat& w, const float* in, int n) {
+  const size_t E = m->n_embd, K = (size_t)w.cols;
+  for (int g = 0; g < n; g += NB) {
+    const int nr = std::min(NB, n - g);
+    if (m->tp == 1 || m->tp_rank == 0) {
+      ARMAI_CUDA(launch_resid<NB>(m, pl, w, in + g * K, m->x + g * E, nr));
+    } else {
+      MvParams p = base_params(m, pl);
+      p.x = in + g * K;
+      p.K = w.cols;
+      p.nb = w.cols / QK_K;
+      p.seg[0] = w.seg();
+      p.nseg = 1;
+      p.total_rows = w.rows;
+      p.out = m->tp_part + g * E;
+      p.out_stride = m->n_embd;
+      const cudaError_t e = launch_mv<MODE_STORE, NB>(m, pl, p, nr);
+      ARMAI_CUDA(e);
+    }
+  }
+  if (m->tp == 1) return ARMAI_OK;
+  return nccl_allreduce_sum_f32(m->tp_rank == 0 ? m->x : m->tp_part, m->x, (size_t)n * E, m->comm, m->stream);
+}
+
+template <int NB>
+int enqueue_batch_step_nb(armai_llama* m, int n) {
   const size_t E = m->n_embd, QN = (size_t)m->n_head * m->head_dim, F = m->n_ff;
   ARMAI_CUDA(launch_embed(m, m->d_token, m->x, n));
   for (int l = 0; l < m->n_layer; l++) {
     const Layer& L = m->layers[l];
-    for (int g = 0; g < n; g += BATCH_NB)
-      ARMAI_CUDA(launch_qkv<BATCH_NB>(m, m->pl_qkvB, l, m->x + g * E, m->q + g * QN, m->d_pos + g,
-                                      m->kv_seq_stride, g, std::min(BATCH_NB, n - g)));
+    for (int g = 0; g < n; g += NB)
+      ARMAI_CUDA(launch_qkv<NB>(m, m->pl_qkvB, l, m->x + g * E, m->q + g * QN, m->d_pos + g, m->kv_seq_stride,
+                                g, std::min(NB, n - g)));
     ARMAI_CUDA(launch_attn(m, l, m->q, m->y, m->d_pos, n, m->kv_seq_stride, 0));
-    for (int g = 0; g < n; g += BATCH_NB)
-      ARMAI_CUDA(launch_resid<BATCH_NB>(m, m->pl_woB, L.wo, m->y + g * QN, m->x + g * E, std::min(BATCH_NB, n - g)));
-    for (int g = 0; g < n; g += BATCH_NB)
-      ARMAI_CUDA(launch_gateup<BATCH_NB>(m, m->pl_guB, l, m->x + g * E, m->h + g * F, std::min(BATCH_NB, n - g)));
-    for (int g = 0; g < n; g += BATCH_NB)
-      ARMAI_CUDA(launch_resid<BATCH_NB>(m, m->pl_downB, L.wd, m->h + g * F, m->x + g * E, std::min(BATCH_NB, n - g)));
+    ARMAI_TRY(rowsplit_resid_batch<NB>(m, m->pl_woB, L.wo, m->y, n));
+    for (int g = 0; g < n; g += NB)
+      ARMAI_CUDA(launch_gateup<NB>(m, m->pl_guB, l, m->x + g * E, m->h + g * F, std::min(NB, n - g)));
+    ARMAI_TRY(rowsplit_resid_batch<NB>(m, m->pl_downB, L.wd, m->h, n));
   }
-  for (int g = 0; g < n; g += BATCH_NB)
-    ARMAI_CUDA(launch_head<BATCH_NB>(m, m->pl_headB, m->x + g * E, m->d_pos + g, m->d_pos + g, m->d_token + g,
-                                     std::min(BATCH_NB, n - g)));
+  for (int g = 0; g < n; g += NB)
+    ARMAI_CUDA(launch_head<NB>(m, m->pl_headB, m->x + g * E, m->d_pos + g, m->d_pos + g, m->d_token + g,
+                               std::min(NB, n - g), g));
+  if (m->tp > 1) ARMAI_TRY(tp_head_merge(m, m->d_token, n));
   return ARMAI_OK;
+}
+
+int enqueue_batch_step(armai_llama* m, int n) {
+  return m->batch_nb == BATCH_NB ? enqueue_batch_step_nb<BATCH_NB>(m, n)
+                                 : enqueue_batch_step_nb<BATCH_NB_WIDE>(m, n);
 }
 
 // Single token at position `pos` through the decode kernels.
 int enqueue_single(armai_llama* m, uint32_t token, int pos) {
-  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_TRY(wait_done(m));
   m->h_misc[1] = (int)token;
   m->h_misc[2] = pos;
   ARMAI_CUDA(cudaMemcpyAsync(m->d_token, &m->h_misc[1], 4, cudaMemcpyHostToDevice, m->stream));
@@ -957,14 +1033,14 @@ int upload_tensors(armai_llama* m, const char* path, const GgufFile& g, std::vec
 void free_model(armai_llama* m) {
   if (!m) return;
   cudaSetDevice(m->device);
-  if (m->stream) cudaStreamSynchronize(m->stream);
+  if (m->stream) wait_done(m);
   if (m->graph) cudaGraphExecDestroy(m->graph);  // before the NCCL communicator it may hold
-  if (m->comm && m->xchg) {
+  if (m->comm && m->xchg && !m->broken) {
     // no rank may still write into this rank's exchange area: meet first
     float* one = nullptr;
     if (cudaMalloc(&one, 4) == cudaSuccess) {
       nccl_allreduce_sum_f32(one, one, 1, m->comm, m->stream);
-      cudaStreamSynchronize(m->stream);
+      wait_done(m);
       cudaFree(one);
     }
   }
@@ -1031,10 +1107,10 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
       delete m;
       return fail(ARMAI_E_INVALID, "tensor parallel: tp_rank must be in [0, tp_size) and tp_unique_id set");
     }
-    if (o.prefill_gemm == 1 || m->max_batch > 1) {
+    if (o.prefill_gemm == 1) {
       delete m;
-      return fail(ARMAI_E_INVALID, "tensor parallel: prompts run the GEMM path and batches are not sharded "
-                                   "(prefill_gemm 1 and max_batch > 1 are not available with tp_size > 1)");
+      return fail(ARMAI_E_INVALID, "tensor parallel: prompts run the GEMM path (prefill_gemm 1 is not "
+                                   "available with tp_size > 1)");
     }
     // decode: the persistent kernel sums the row-split products through peer
     // memory (decode_kernel 0), or the per-kernel chain through NCCL (1)
@@ -1245,11 +1321,11 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   LOAD_CUDA(cudaMalloc(&m->am_cnt, 64));
   LOAD_CUDA(cudaMemsetAsync(m->am_cnt, 0, 64, m->stream));
   if (m->tp > 1) {
-    LOAD_CUDA(cudaMalloc(&m->tp_part, (size_t)m->n_embd * 4));
-    LOAD_CUDA(cudaMalloc(&m->best_val, 64));
-    LOAD_CUDA(cudaMalloc(&m->best_idx, 64));
-    LOAD_CUDA(cudaMalloc(&m->tp_send, 64));
-    LOAD_CUDA(cudaMalloc(&m->tp_recv, (size_t)m->tp * 8));
+    LOAD_CUDA(cudaMalloc(&m->tp_part, (size_t)B * m->n_embd * 4));
+    LOAD_CUDA(cudaMalloc(&m->best_val, (size_t)B * 4));
+    LOAD_CUDA(cudaMalloc(&m->best_idx, (size_t)B * 4));
+    LOAD_CUDA(cudaMalloc(&m->tp_send, (size_t)B * 8));
+    LOAD_CUDA(cudaMalloc(&m->tp_recv, (size_t)m->tp * B * 8));
     LOAD_CUDA(cudaMalloc(&m->logits_all, (size_t)m->tp * m->v_stride * 4));
     const int nrc = nccl_comm_init(&m->comm, m->tp, opts->tp_unique_id, m->tp_rank);
     if (nrc != ARMAI_OK) { free_model(m); return nrc; }
@@ -1291,17 +1367,36 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
   if (!arc) arc = set_smem_attr<MODE_RESID, PREFILL_TILE>(std::max(m->pl_woT.smem, m->pl_downT.smem));
   if (!arc) arc = set_smem_attr<MODE_GATEUP, PREFILL_TILE>(m->pl_guT.smem);
   if (!arc && m->max_batch > 1) {
-    m->pl_qkvB = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
-    m->pl_woB = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, BATCH_NB, false, nsm, SMEM_LIMIT);
-    m->pl_guB = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
-    m->pl_downB = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, BATCH_NB, false, nsm, SMEM_LIMIT);
-    m->pl_headB = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, BATCH_NB, true, nsm, SMEM_LIMIT);
-    for (const Plan* pl : {&m->pl_qkvB, &m->pl_woB, &m->pl_guB, &m->pl_downB, &m->pl_headB})
-      if (pl->smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "model rows too wide for batched decode"); }
-    arc = set_smem_attr<MODE_QKV, BATCH_NB>(m->pl_qkvB.smem);
-    if (!arc) arc = set_smem_attr<MODE_RESID, BATCH_NB>(std::max(m->pl_woB.smem, m->pl_downB.smem));
-    if (!arc) arc = set_smem_attr<MODE_GATEUP, BATCH_NB>(m->pl_guB.smem);
-    if (!arc) arc = set_smem_attr<MODE_HEAD, BATCH_NB>(m->pl_headB.smem);
+    // 16 sequences per weight pass, or 8 where 16 activation rows of the
+    // widest K (ffn_down) do not fit shared memory
+    auto plans = [&](int nb) {
+      m->pl_qkvB = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
+      m->pl_woB = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, nb, false, nsm, SMEM_LIMIT);
+      m->pl_guB = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
+      m->pl_downB = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, nb, false, nsm, SMEM_LIMIT);
+      m->pl_headB = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
+      for (const Plan* pl : {&m->pl_qkvB, &m->pl_woB, &m->pl_guB, &m->pl_downB, &m->pl_headB})
+        if (pl->smem > SMEM_LIMIT) return false;
+      return true;
+    };
+    m->batch_nb = BATCH_NB;
+    if (!plans(BATCH_NB)) {
+      m->batch_nb = BATCH_NB_WIDE;
+      if (!plans(BATCH_NB_WIDE)) { free_model(m); return fail(ARMAI_E_INVALID, "model rows too wide for batched decode"); }
+    }
+    // ranks other than 0 of a tensor-parallel model store their row-split
+    // partial sums with MODE_STORE
+    auto attrs = [&](auto nbc) {
+      constexpr int NB = decltype(nbc)::value;
+      int a = set_smem_attr<MODE_QKV, NB>(m->pl_qkvB.smem);
+      if (!a) a = set_smem_attr<MODE_RESID, NB>(std::max(m->pl_woB.smem, m->pl_downB.smem));
+      if (!a) a = set_smem_attr<MODE_GATEUP, NB>(m->pl_guB.smem);
+      if (!a) a = set_smem_attr<MODE_HEAD, NB>(m->pl_headB.smem);
+      if (!a) a = set_smem_attr<MODE_STORE, NB>(std::max(m->pl_woB.smem, m->pl_downB.smem));
+      return a;
+    };
+    arc = m->batch_nb == BATCH_NB ? attrs(std::integral_constant<int, BATCH_NB>{})
+                                  : attrs(std::integral_constant<int, BATCH_NB_WIDE>{});
     if (!arc) {
       const cudaError_t he = cudaMallocHost(&m->h_btok, (size_t)m->max_batch * 4);
       if (he != cudaSuccess) arc = cuda_fail(he, "cudaMallocHost", __FILE__, __LINE__);
@@ -1431,7 +1526,7 @@ extern "C" int armai_llama_generate(armai_llama* m, const uint32_t* prompt, size
   const auto t0 = clk::now();
   ARMAI_TRY(forward_locked(m, prompt, (int)n_prompt, 0));
   ARMAI_CUDA(cudaMemcpyAsync(m->h_tok, m->d_token, 4, cudaMemcpyDeviceToHost, m->stream));
-  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_TRY(wait_done(m));
   *prefill_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(clk::now() - t0).count();
   uint32_t next = m->h_tok[0];
   size_t n = 0;
@@ -1459,13 +1554,16 @@ extern "C" int armai_llama_generate(armai_llama* m, const uint32_t* prompt, size
       rc = launch_step(i + 1);
       if (rc) break;
     }
-    cudaError_t e = cudaEventSynchronize(ev[i % RING]);
-    if (e != cudaSuccess) { rc = cuda_fail(e, "cudaEventSynchronize", __FILE__, __LINE__); break; }
+    rc = wait_done(m, ev[i % RING]);
+    if (rc) break;
     next = m->h_tok[i % RING];
     out[n++] = next;
     if (on_token) on_token(user, next);
   }
-  cudaStreamSynchronize(m->stream);
+  {
+    const int wr = wait_done(m);  // steps launched ahead
+    if (rc == ARMAI_OK) rc = wr;
+  }
   *decode_us = (uint64_t)std::chrono::duration_cast<std::chrono::microseconds>(clk::now() - t1).count();
   for (int i = 0; i < RING; i++) cudaEventDestroy(ev[i]);
   m->kv_len = (int)(n_prompt + n - 1);
@@ -1535,7 +1633,7 @@ extern "C" int armai_llama_generate_batch(armai_llama* m, const uint32_t* prompt
     }
   };
   ARMAI_CUDA(cudaMemcpyAsync(m->h_btok, m->d_token, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
-  ARMAI_CUDA(cudaStreamSynchronize(m->stream));
+  ARMAI_TRY(wait_done(m));
   record();
   while (live > 0) {
     ARMAI_TRY(enqueue_batch_step(m, n));
@@ -1560,7 +1658,7 @@ extern "C" int armai_llama_bench_decode(armai_llama* m, int32_t n_steps, float* 
   ARMAI_CUDA(cudaEventRecord(a, m->stream));
   for (int i = 0; i < n_steps; i++) ARMAI_TRY(run_decode_step(m));
   ARMAI_CUDA(cudaEventRecord(b, m->stream));
-  ARMAI_CUDA(cudaEventSynchronize(b));
+  ARMAI_TRY(wait_done(m, b));
   ARMAI_CUDA(cudaEventElapsedTime(ms, a, b));
   cudaEventDestroy(a);
   cudaEventDestroy(b);
@@ -1611,7 +1709,7 @@ extern "C" int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t ro
   cudaEventRecord(b, m->stream);
   m->use_pdl = pdl;
   if (rc != ARMAI_OK) { cudaEventDestroy(a); cudaEventDestroy(b); return rc; }
-  ARMAI_CUDA(cudaEventSynchronize(b));
+  ARMAI_TRY(wait_done(m, b));
   float ms = 0.f;
   ARMAI_CUDA(cudaEventElapsedTime(&ms, a, b));
   cudaEventDestroy(a);
@@ -1641,9 +1739,10 @@ extern "C" int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t ca
     m->mk.trace = nullptr;
   }
   if (e == cudaSuccess) e = cudaMemcpyAsync(out, d, n * 8, cudaMemcpyDeviceToHost, m->stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  int wrc = e == cudaSuccess ? wait_done(m) : ARMAI_OK;
   cudaFree(d);
   if (e != cudaSuccess) return cuda_fail(e, "trace_decode", __FILE__, __LINE__);
+  ARMAI_TRY(wrc);
   m->kv_len += 1;
   *n_phases = m->mk.n_ph + 1;
   *n_ctas = m->mk_grid;

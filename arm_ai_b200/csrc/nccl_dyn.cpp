@@ -23,6 +23,7 @@ struct NcclFns {
                              cudaStream_t) = nullptr;
   ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool ok = false;
   std::string why;
@@ -43,9 +44,10 @@ NcclFns& fns() {
     f.all_reduce = (decltype(f.all_reduce))dlsym(h, "ncclAllReduce");
     f.all_gather = (decltype(f.all_gather))dlsym(h, "ncclAllGather");
     f.comm_destroy = (decltype(f.comm_destroy))dlsym(h, "ncclCommDestroy");
+    f.comm_abort = (decltype(f.comm_abort))dlsym(h, "ncclCommAbort");
     f.error_string = (decltype(f.error_string))dlsym(h, "ncclGetErrorString");
     f.ok = f.get_unique_id && f.comm_init_rank && f.all_reduce && f.all_gather && f.comm_destroy &&
-           f.error_string;
+           f.comm_abort && f.error_string;
     if (!f.ok) f.why = "libnccl.so.2 lacks a required symbol";
   });
   return f;
@@ -92,6 +94,10 @@ int nccl_allgather_b32(const void* send, void* recv, size_t n_per_rank, void* co
 
 void nccl_comm_destroy(void* comm) {
   if (comm && fns().ok) fns().comm_destroy((ncclComm_t)comm);
+}
+
+void nccl_comm_abort(void* comm) {
+  if (comm && fns().ok) fns().comm_abort((ncclComm_t)comm);
 }
 
 }  // namespace armai

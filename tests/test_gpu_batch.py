@@ -67,3 +67,20 @@ def test_batch_stops_and_edges(models):
     # the handle still serves single-sequence calls
     single, _, _ = native.llama_candle_generate_op(gpu, prompts[0], 16, [])
     assert single == full[0]
+
+
+def test_batch_wide_model_8_row_kernels(built):
+    """ffn_down K = 12288: the batched step falls back to 8 sequences per
+    weight pass; still token for token the single-sequence chain."""
+    path = synth.model_path("wide", seed=6)
+    gpu = native.llama_candle_load_op(path, decode_kernel=1, max_batch=12)
+    vocab = gpu.info().n_vocab
+    prompts = _prompts(11, vocab, 1700)
+    toks, _, _ = native.llama_generate_batch(gpu, prompts, 12)
+    for p, t in zip(prompts, toks):
+        single, _, _ = native.llama_candle_generate_op(gpu, p, 12, [])
+        assert t == single
+    tol = 2 * flip_bound(path, lengths=(16, 24, 64))
+    for p, t in list(zip(prompts, toks))[:3]:
+        assert greedy_consistent(path, p, t, tol=tol) is None
+    gpu.close()

@@ -2,9 +2,11 @@
 test model: 8 query / 2 KV heads, FFN 1536, vocab 4096 split over 2 ranks).
 
 Each rank holds half the heads, gate/up rows and vocab rows and a K-half of
-attn_output / ffn_down; the halves are summed by NCCL. Against the oracle:
-prompt logits (gathered from both ranks) within the model's flip bound and
-greedy tokens consistent with the oracle, identical on both ranks. Skipped
+attn_output / ffn_down; the halves are summed through peer memory (the
+persistent decode kernel) or by NCCL (per-kernel chain, prefill, batched
+decode). Against the oracle: prompt logits (gathered from both ranks) within
+the model's flip bound and greedy tokens consistent with the oracle,
+identical on both ranks, for single-sequence and batched decode. Skipped
 with fewer than two GPUs.
 """
 import os
@@ -21,13 +23,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
+BATCH_PROMPTS = [(13, 21), (20, 22), (7, 23)]  # (length, seed)
+
+
 def _rank(rank, world, port, path, prompt, q):
     import datetime
 
     import numpy as np
     import torch.distributed as dist
 
-    from arm_ai_b200 import native, tp
+    from arm_ai_b200 import native, synth, tp
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")  # plain NVLink transfers, no multicast objects
@@ -44,7 +49,14 @@ def _rank(rank, world, port, path, prompt, q):
             lg2, _ = native.llama_forward(gpu, long_prompt, 0)
             gpu.close()
             out.append((np.asarray(lg), tok, toks, np.asarray(lg1), np.asarray(lg2)))
-        q.put((rank, out))
+        # batched decode (config 4's batch case): sharded weights, every
+        # sequence on every rank, row-split sums and head winners through NCCL
+        uid = tp.share_unique_id(rank)
+        gpu = tp.load_tp(path, rank, world, rank, uid, max_batch=4)
+        prompts = [synth.prompt_tokens(n, 4096, sd) for n, sd in BATCH_PROMPTS]
+        btoks = [[int(t) for t in seq] for seq in native.llama_generate_batch(gpu, prompts, 20)[0]]
+        gpu.close()
+        q.put((rank, out, btoks))
     except Exception as e:  # report instead of hanging the other rank
         q.put((rank, repr(e)))
     finally:
@@ -73,13 +85,20 @@ def test_tp2_matches_oracle(small_model):
         p.join(timeout=60)
     for r in res:
         assert not isinstance(r[1], str), r[1]
+    bt = [r[2] for r in res]
+    assert bt[0] == bt[1]  # both ranks decode the same batch
+    btol = 2 * flip_bound(small_model, lengths=(16, 24, 64))
+    for (n, sd), toks in zip(BATCH_PROMPTS, bt[0]):
+        assert len(toks) == 20
+        assert greedy_consistent(small_model, synth.prompt_tokens(n, 4096, sd), toks, tol=btol) is None
     bound = flip_bound(small_model, lengths=(16, 24, 64, 100, 128))
     orc = ref.OracleLlama(small_model)
     lo = orc.forward(prompt, 0)
     lo1 = orc.forward([77], len(prompt))
     lo2 = ref.OracleLlama(small_model).forward(list(prompt) * 8, 0)
     for kernel in (0, 1):
-        for _, out in res:
+        for r in res:
+            out = r[1]
             lg, tok, toks, lg1, lg2 = out[kernel]
             assert rel_maxabs(lg, lo) < bound, kernel
             assert rel_maxabs(lg1, lo1) < bound, kernel
