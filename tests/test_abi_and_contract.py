@@ -35,6 +35,22 @@ def test_library_exports_every_declared_symbol(built):
     assert not missing, missing
 
 
+def test_integration_rust_block_matches_header():
+    """INTEGRATION.md's FFI block declares exactly the header's functions and
+    the option / info structs' fields in the header's order."""
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    assert sorted(set(re.findall(r"pub fn (armai_\w+)\(", doc))) == declared_symbols()
+    hdr = re.sub(r"/\*.*?\*/", "", open(os.path.join(ROOT, "include", "armai.h")).read(), flags=re.S)
+    for name in ("armai_llama_opts", "armai_llama_info"):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (name, name), hdr, re.S).group(1)
+        c_fields = []
+        for decl in filter(str.strip, body.split(";")):
+            first, *more = decl.replace("*", " ").split(",")
+            c_fields += [n.strip().split("[")[0] for n in [first.split()[-1], *more]]
+        rs = re.search(r"pub struct %s \{(.*?)\}" % name, doc, re.S).group(1)
+        assert re.findall(r"pub (\w+):", rs) == c_fields, name
+
+
 def test_missing_gguf_returns_error(built):
     assert LlamaCandle.load("/tmp/__nope.gguf")[0] == "error"
 
