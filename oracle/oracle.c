@@ -64,6 +64,24 @@ float orc_f16_to_f32(uint16_t h) {
 }
 
 /* Rust `f32 as i8`: saturating, NaN -> 0. */
+/* IEEE binary32 -> binary16, round to nearest even (half::f16::from_f32). */
+uint16_t orc_f32_to_f16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7fffffffu;
+  if (ax >= 0x7f800000u) return (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0));
+  if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u);
+  if (ax < 0x38800000u) {
+    float a;
+    memcpy(&a, &ax, 4);
+    return (uint16_t)(sign | (uint32_t)nearbyintf(a * 16777216.0f));
+  }
+  uint32_t hh = (((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13);
+  uint32_t rem = ax & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (hh & 1u))) hh++;
+  return (uint16_t)(sign | hh);
+}
+
 static int8_t sat_i8(float v) {
   if (v != v) return 0;
   if (v >= 127.f) return 127;
@@ -221,6 +239,127 @@ float orc_vec_dot_q6k_q8k(int64_t n, const orc_block_q6k* xs, const orc_block_q8
 }
 
 /* Integer halves of the two dot products above, one pair per super-block. */
+/* candle-core 0.8.4 k_quants.rs: BlockQ5K::vec_dot_unopt — BlockQ4K's
+ * structure with the fifth bit of each value from qh (bit 2j of qh[l] for
+ * the low nibbles of the j-th 64-value group, bit 2j + 1 for the high). */
+float orc_vec_dot_q5k_q8k(int64_t n, const orc_block_q5k* xs, const orc_block_q8k* ys) {
+  uint8_t scales[8], mins[8];
+  int8_t aux8[ORC_QK_K];
+  int16_t aux16[8];
+  float sums[8] = {0};
+  int32_t aux32[8];
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / ORC_QK_K; b++) {
+    const orc_block_q5k* x = &xs[b];
+    const orc_block_q8k* y = &ys[b];
+    memset(aux32, 0, sizeof aux32);
+    int8_t* a = aux8;
+    const uint8_t* q4 = x->qs;
+    const uint8_t* hm = x->qh;
+    uint8_t m = 1;
+    for (int j = 0; j < ORC_QK_K / 64; j++) {
+      for (int l = 0; l < 32; l++) a[l] = (int8_t)(q4[l] & 0xF);
+      for (int l = 0; l < 32; l++) a[l] = (int8_t)(a[l] + ((hm[l] & m) ? 16 : 0));
+      a += 32;
+      m <<= 1;
+      for (int l = 0; l < 32; l++) a[l] = (int8_t)(q4[l] >> 4);
+      for (int l = 0; l < 32; l++) a[l] = (int8_t)(a[l] + ((hm[l] & m) ? 16 : 0));
+      a += 32;
+      m <<= 1;
+      q4 += 32;
+    }
+    q4k_scales_mins(x->scales, scales, mins);
+    int32_t sumi = 0;
+    for (int j = 0; j < ORC_QK_K / 16; j++) sumi += (int32_t)y->bsums[j] * (int32_t)mins[j / 2];
+    a = aux8;
+    const int8_t* q8 = y->qs;
+    for (int is = 0; is < 8; is++) {
+      int32_t scale = scales[is];
+      for (int r = 0; r < 4; r++) {
+        for (int l = 0; l < 8; l++) aux16[l] = (int16_t)(q8[l] * a[l]);
+        for (int l = 0; l < 8; l++) aux32[l] += scale * (int32_t)aux16[l];
+        q8 += 8;
+        a += 8;
+      }
+    }
+    float d = orc_f16_to_f32(x->d) * y->d;
+    for (int l = 0; l < 8; l++) sums[l] += d * (float)aux32[l];
+    float dmin = orc_f16_to_f32(x->dmin) * y->d;
+    sumf -= dmin * (float)sumi;
+  }
+  float s = -0.0f;
+  for (int l = 0; l < 8; l++) s += sums[l];
+  return sumf + s;
+}
+
+/* candle-core 0.8.4 k_quants.rs BlockQ8_0::from_float: per 32 values
+ * d = amax / 127, id = 1/d (0 when d = 0), q = round-half-away(x * id),
+ * d stored as f16. */
+int orc_quantize_row_q8_0(const float* x, int64_t k, orc_block_q8_0* y) {
+  if (k % ORC_QK8_0 != 0) {
+    set_err("quantize_row_q8_0: k is not divisible by 32");
+    return -1;
+  }
+  for (int64_t b = 0; b < k / ORC_QK8_0; b++) {
+    const float* xs = x + b * ORC_QK8_0;
+    float amax = 0.f;
+    for (int j = 0; j < ORC_QK8_0; j++) amax = fmaxf(amax, fabsf(xs[j]));
+    const float d = amax / 127.0f;
+    const float id = d != 0.f ? 1.0f / d : 0.f;
+    y[b].d = orc_f32_to_f16(d);
+    for (int j = 0; j < ORC_QK8_0; j++) y[b].qs[j] = sat_i8(roundf(xs[j] * id));
+  }
+  return 0;
+}
+
+/* k_quants.rs BlockQ4_0::vec_dot (generic): per block the integer sum of
+ * (nibble - 8) * q8 (low nibbles pair with q8[j], high with q8[j + 16]),
+ * then sumf += sumi * d_x * d_y. */
+float orc_vec_dot_q4_0_q8_0(int64_t n, const orc_block_q4_0* xs, const orc_block_q8_0* ys) {
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / ORC_QK8_0; b++) {
+    int32_t sumi = 0;
+    for (int j = 0; j < ORC_QK8_0 / 2; j++) {
+      const int32_t v0 = (int32_t)(xs[b].qs[j] & 0x0F) - 8;
+      const int32_t v1 = (int32_t)(xs[b].qs[j] >> 4) - 8;
+      sumi += v0 * (int32_t)ys[b].qs[j] + v1 * (int32_t)ys[b].qs[j + ORC_QK8_0 / 2];
+    }
+    sumf += (float)sumi * orc_f16_to_f32(xs[b].d) * orc_f16_to_f32(ys[b].d);
+  }
+  return sumf;
+}
+
+/* k_quants.rs BlockQ5_0::vec_dot (generic): the fifth bit of value j from
+ * bit j of qh (low nibbles) and bit j + 16 (high nibbles), values - 16. */
+float orc_vec_dot_q5_0_q8_0(int64_t n, const orc_block_q5_0* xs, const orc_block_q8_0* ys) {
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / ORC_QK8_0; b++) {
+    uint32_t qh;
+    memcpy(&qh, xs[b].qh, 4);
+    int32_t sumi = 0;
+    for (int j = 0; j < ORC_QK8_0 / 2; j++) {
+      const uint32_t xh0 = ((qh & (1u << j)) >> j) << 4;
+      const uint32_t xh1 = (qh & (1u << (j + 16))) >> (j + 12);
+      const int32_t x0 = (int32_t)((xs[b].qs[j] & 0x0Fu) | xh0) - 16;
+      const int32_t x1 = (int32_t)(((uint32_t)xs[b].qs[j] >> 4) | xh1) - 16;
+      sumi += x0 * (int32_t)ys[b].qs[j] + x1 * (int32_t)ys[b].qs[j + ORC_QK8_0 / 2];
+    }
+    sumf += (float)sumi * orc_f16_to_f32(xs[b].d) * orc_f16_to_f32(ys[b].d);
+  }
+  return sumf;
+}
+
+/* k_quants.rs BlockQ8_0::vec_dot (generic). */
+float orc_vec_dot_q8_0_q8_0(int64_t n, const orc_block_q8_0* xs, const orc_block_q8_0* ys) {
+  float sumf = 0.f;
+  for (int64_t b = 0; b < n / ORC_QK8_0; b++) {
+    int32_t sumi = 0;
+    for (int j = 0; j < ORC_QK8_0; j++) sumi += (int32_t)xs[b].qs[j] * (int32_t)ys[b].qs[j];
+    sumf += (float)sumi * orc_f16_to_f32(xs[b].d) * orc_f16_to_f32(ys[b].d);
+  }
+  return sumf;
+}
+
 void orc_q4k_block_ints(const orc_block_q4k* xs, const orc_block_q8k* ys, int64_t nb,
                         int32_t* isum, int32_t* msum) {
   uint8_t scales[8], mins[8];
@@ -318,9 +457,87 @@ void orc_dequant_row_q6k(const orc_block_q6k* xs, int64_t k, float* y) {
 static int64_t row_bytes(int type, int64_t k) {
   switch (type) {
     case ORC_F32: return 4 * k;
+    case ORC_F16: return 2 * k;
+    case ORC_Q4_0: return (k / ORC_QK8_0) * (int64_t)sizeof(orc_block_q4_0);
+    case ORC_Q5_0: return (k / ORC_QK8_0) * (int64_t)sizeof(orc_block_q5_0);
+    case ORC_Q8_0: return (k / ORC_QK8_0) * (int64_t)sizeof(orc_block_q8_0);
     case ORC_Q4_K: return (k / ORC_QK_K) * (int64_t)sizeof(orc_block_q4k);
+    case ORC_Q5_K: return (k / ORC_QK_K) * (int64_t)sizeof(orc_block_q5k);
     case ORC_Q6_K: return (k / ORC_QK_K) * (int64_t)sizeof(orc_block_q6k);
     default: return -1;
+  }
+}
+
+/* to_float of one row (k_quants.rs Block*::to_float; f16 via half). */
+int orc_dequant_row(int type, const void* row, int64_t k, float* y) {
+  switch (type) {
+    case ORC_F32:
+      memcpy(y, row, sizeof(float) * (size_t)k);
+      return 0;
+    case ORC_F16:
+      for (int64_t i = 0; i < k; i++) y[i] = orc_f16_to_f32(((const uint16_t*)row)[i]);
+      return 0;
+    case ORC_Q4_K:
+      orc_dequant_row_q4k((const orc_block_q4k*)row, k, y);
+      return 0;
+    case ORC_Q6_K:
+      orc_dequant_row_q6k((const orc_block_q6k*)row, k, y);
+      return 0;
+    case ORC_Q4_0:
+      for (int64_t b = 0; b < k / ORC_QK8_0; b++) {
+        const orc_block_q4_0* x = (const orc_block_q4_0*)row + b;
+        const float d = orc_f16_to_f32(x->d);
+        for (int j = 0; j < ORC_QK8_0 / 2; j++) {
+          y[b * ORC_QK8_0 + j] = (float)((int)(x->qs[j] & 0x0F) - 8) * d;
+          y[b * ORC_QK8_0 + j + ORC_QK8_0 / 2] = (float)((int)(x->qs[j] >> 4) - 8) * d;
+        }
+      }
+      return 0;
+    case ORC_Q5_0:
+      for (int64_t b = 0; b < k / ORC_QK8_0; b++) {
+        const orc_block_q5_0* x = (const orc_block_q5_0*)row + b;
+        const float d = orc_f16_to_f32(x->d);
+        uint32_t qh;
+        memcpy(&qh, x->qh, 4);
+        for (int j = 0; j < ORC_QK8_0 / 2; j++) {
+          const uint32_t xh0 = ((qh >> j) << 4) & 0x10u;
+          const uint32_t xh1 = (qh >> (j + 12)) & 0x10u;
+          y[b * ORC_QK8_0 + j] = (float)((int)((x->qs[j] & 0x0Fu) | xh0) - 16) * d;
+          y[b * ORC_QK8_0 + j + ORC_QK8_0 / 2] = (float)((int)(((uint32_t)x->qs[j] >> 4) | xh1) - 16) * d;
+        }
+      }
+      return 0;
+    case ORC_Q8_0:
+      for (int64_t b = 0; b < k / ORC_QK8_0; b++) {
+        const orc_block_q8_0* x = (const orc_block_q8_0*)row + b;
+        const float d = orc_f16_to_f32(x->d);
+        for (int j = 0; j < ORC_QK8_0; j++) y[b * ORC_QK8_0 + j] = (float)x->qs[j] * d;
+      }
+      return 0;
+    case ORC_Q5_K:
+      for (int64_t b = 0; b < k / ORC_QK_K; b++) {
+        const orc_block_q5k* x = (const orc_block_q5k*)row + b;
+        const float d = orc_f16_to_f32(x->d), mn = orc_f16_to_f32(x->dmin);
+        const uint8_t* ql = x->qs;
+        float* o = y + b * ORC_QK_K;
+        uint8_t u1 = 1, u2 = 2;
+        for (int j = 0, is = 0; j < ORC_QK_K; j += 64, is += 2) {
+          uint8_t sc, m;
+          get_scale_min_k4(is, x->scales, &sc, &m);
+          const float d1 = d * (float)sc, m1 = mn * (float)m;
+          get_scale_min_k4(is + 1, x->scales, &sc, &m);
+          const float d2 = d * (float)sc, m2 = mn * (float)m;
+          for (int l = 0; l < 32; l++) *o++ = d1 * (float)((ql[l] & 0xF) + ((x->qh[l] & u1) ? 16 : 0)) - m1;
+          for (int l = 0; l < 32; l++) *o++ = d2 * (float)((ql[l] >> 4) + ((x->qh[l] & u2) ? 16 : 0)) - m2;
+          ql += 32;
+          u1 <<= 2;
+          u2 <<= 2;
+        }
+      }
+      return 0;
+    default:
+      set_err("dequant_row: unsupported type");
+      return -1;
   }
 }
 
@@ -341,6 +558,37 @@ int orc_qmatmul(const void* w, int wtype, int64_t n, int64_t k, const float* x, 
     }
     return 0;
   }
+  if (wtype == ORC_Q4_0 || wtype == ORC_Q5_0 || wtype == ORC_Q8_0) {
+    /* the legacy types' VecDotType is Q8_0 */
+    if (k % ORC_QK8_0 != 0) {
+      set_err("qmatmul: k is not divisible by 32");
+      return -1;
+    }
+    const int64_t nb0 = k / ORC_QK8_0;
+    orc_block_q8_0* l0 = (orc_block_q8_0*)calloc((size_t)(m * nb0), sizeof(orc_block_q8_0));
+    if (!l0) {
+      set_err("qmatmul: out of memory");
+      return -1;
+    }
+    for (int64_t r = 0; r < m; r++) orc_quantize_row_q8_0(x + r * k, k, l0 + r * nb0);
+    const int64_t rb0 = row_bytes(wtype, k);
+    for (int64_t r = 0; r < m; r++) {
+      const orc_block_q8_0* lr = l0 + r * nb0;
+#pragma omp parallel for schedule(static)
+      for (int64_t c = 0; c < n; c++) {
+        const void* wr = (const uint8_t*)w + c * rb0;
+        out[r * n + c] = wtype == ORC_Q4_0   ? orc_vec_dot_q4_0_q8_0(k, (const orc_block_q4_0*)wr, lr)
+                         : wtype == ORC_Q5_0 ? orc_vec_dot_q5_0_q8_0(k, (const orc_block_q5_0*)wr, lr)
+                                             : orc_vec_dot_q8_0_q8_0(k, (const orc_block_q8_0*)wr, lr);
+      }
+    }
+    free(l0);
+    return 0;
+  }
+  if (wtype != ORC_Q4_K && wtype != ORC_Q5_K && wtype != ORC_Q6_K) {
+    set_err("qmatmul: unsupported weight type");
+    return -1;
+  }
   if (k % ORC_QK_K != 0) {
     set_err("qmatmul: k is not divisible by 256");
     return -1;
@@ -358,9 +606,9 @@ int orc_qmatmul(const void* w, int wtype, int64_t n, int64_t k, const float* x, 
 #pragma omp parallel for schedule(static)
     for (int64_t c = 0; c < n; c++) {
       const void* wr = (const uint8_t*)w + c * rb;
-      out[r * n + c] = (wtype == ORC_Q4_K)
-                           ? orc_vec_dot_q4k_q8k(k, (const orc_block_q4k*)wr, lr)
-                           : orc_vec_dot_q6k_q8k(k, (const orc_block_q6k*)wr, lr);
+      out[r * n + c] = wtype == ORC_Q4_K   ? orc_vec_dot_q4k_q8k(k, (const orc_block_q4k*)wr, lr)
+                       : wtype == ORC_Q5_K ? orc_vec_dot_q5k_q8k(k, (const orc_block_q5k*)wr, lr)
+                                           : orc_vec_dot_q6k_q8k(k, (const orc_block_q6k*)wr, lr);
     }
   }
   free(lhs);
@@ -392,25 +640,7 @@ struct orc_llama {
 };
 
 /* f32 -> binary16 (round to nearest even) -> f32. */
-static float round_f16(float f) {
-  uint32_t x;
-  memcpy(&x, &f, 4);
-  uint32_t sign = (x >> 16) & 0x8000u, ax = x & 0x7fffffffu;
-  uint16_t h;
-  if (ax >= 0x7f800000u) h = (uint16_t)(sign | 0x7c00u | (ax > 0x7f800000u ? 0x200u : 0));
-  else if (ax >= 0x477ff000u) h = (uint16_t)(sign | 0x7c00u);
-  else if (ax < 0x38800000u) {
-    float a;
-    memcpy(&a, &ax, 4);
-    h = (uint16_t)(sign | (uint32_t)nearbyintf(a * 16777216.0f));
-  } else {
-    uint32_t hh = (((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13);
-    uint32_t rem = ax & 0x1fffu;
-    if (rem > 0x1000u || (rem == 0x1000u && (hh & 1u))) hh++;
-    h = (uint16_t)(sign | hh);
-  }
-  return orc_f16_to_f32(h);
-}
+static float round_f16(float f) { return orc_f16_to_f32(orc_f32_to_f16(f)); }
 
 void orc_llama_set_kv_f16(orc_llama* m, int on) { m->kv_f16 = on ? 1 : 0; }
 
@@ -532,9 +762,7 @@ static void embed_row(const orc_llama* m, uint32_t tok, float* out) {
   const orc_tensor* t = &m->tok_embd;
   int64_t rb = row_bytes(t->type, t->cols);
   const uint8_t* row = (const uint8_t*)t->p + (int64_t)tok * rb;
-  if (t->type == ORC_Q4_K) orc_dequant_row_q4k((const orc_block_q4k*)row, t->cols, out);
-  else if (t->type == ORC_Q6_K) orc_dequant_row_q6k((const orc_block_q6k*)row, t->cols, out);
-  else memcpy(out, row, sizeof(float) * (size_t)t->cols);
+  orc_dequant_row(t->type, row, t->cols, out);
 }
 
 static int qmm(const orc_tensor* t, const float* x, int64_t m, float* out) {

@@ -8,9 +8,11 @@
  * What it restates:
  *   - candle-core 0.8.4 k-quants (generic, non-SIMD paths — the ones an
  *     x86_64 build without target-cpu=native runs): BlockQ8K::from_float,
- *     BlockQ4K/BlockQ6K vec_dot_unopt, BlockQ4K/BlockQ6K to_float, and the
- *     CPU QMatMul driver (quantise each lhs row to Q8_K, one vec_dot per
- *     output column). The crate is pinned in the reference at
+ *     BlockQ4K/BlockQ5K/BlockQ6K vec_dot_unopt and to_float, the legacy
+ *     BlockQ4_0/BlockQ5_0/BlockQ8_0 (to_float, vec_dot with a Q8_0 lhs) and
+ *     BlockQ8_0::from_float, and the CPU QMatMul driver (quantise each lhs
+ *     row to the weight's VecDotType — Q8_K or Q8_0 — one vec_dot per output
+ *     column). The crate is pinned in the reference at
  *     native/arm_ai_nif/Cargo.lock:175-178 (candle-core 0.8.4); it is not
  *     vendored under the reference tree.
  *   - candle-transformers 0.8.4 models::quantized_llama::ModelWeights
@@ -20,8 +22,9 @@
  *     native/arm_ai_nif/src/shape_ops.rs (file:line cited per function in
  *     oracle.c).
  *
- * Parity status: the Q4_K / Q6_K block layouts and dequantisation are pinned
- * against gguf-py 0.19.0's independent dequantize(); the GGUF container is
+ * Parity status: the Q4_K / Q5_K / Q6_K / Q4_0 / Q5_0 / Q8_0 block layouts
+ * and dequantisation, and Q8_0 quantisation, are pinned against gguf-py
+ * 0.19.0's independent dequantize() / quantize(); the GGUF container is
  * read by gguf-py's GGUFReader. Q8_K quantisation rounding, the vec_dot
  * combine order and the forward-pass details are restated from candle's
  * published source and are NOT pinned by any reference-run output (no Rust
@@ -38,7 +41,8 @@ extern "C" {
 #endif
 
 /* GGML tensor type ids (GGUF spec). */
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_K = 12, ORC_Q6_K = 14 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q5_0 = 6, ORC_Q8_0 = 8, ORC_Q4_K = 12, ORC_Q5_K = 13,
+       ORC_Q6_K = 14 };
 
 #define ORC_QK_K 256
 
@@ -62,11 +66,45 @@ typedef struct {
   int16_t bsums[16];
 } orc_block_q8k; /* 292 bytes */
 
+typedef struct {
+  uint16_t d;
+  uint16_t dmin;
+  uint8_t scales[12];
+  uint8_t qh[32];
+  uint8_t qs[128];
+} orc_block_q5k; /* 176 bytes */
+
+/* 32-value blocks of the legacy types; their matmuls quantise the lhs to Q8_0. */
+#define ORC_QK8_0 32
+typedef struct {
+  uint16_t d;
+  uint8_t qs[16];
+} orc_block_q4_0; /* 18 bytes */
+
+typedef struct {
+  uint16_t d;
+  uint8_t qh[4];
+  uint8_t qs[16];
+} orc_block_q5_0; /* 22 bytes */
+
+typedef struct {
+  uint16_t d;
+  int8_t qs[32];
+} orc_block_q8_0; /* 34 bytes */
+
 /* ---- k-quant block math (candle-core 0.8.4 k_quants.rs) ---- */
 float orc_f16_to_f32(uint16_t h);
 int orc_quantize_row_q8k(const float* x, int64_t k, orc_block_q8k* y);
 float orc_vec_dot_q4k_q8k(int64_t n, const orc_block_q4k* x, const orc_block_q8k* y);
 float orc_vec_dot_q6k_q8k(int64_t n, const orc_block_q6k* x, const orc_block_q8k* y);
+float orc_vec_dot_q5k_q8k(int64_t n, const orc_block_q5k* x, const orc_block_q8k* y);
+uint16_t orc_f32_to_f16(float f);
+int orc_quantize_row_q8_0(const float* x, int64_t k, orc_block_q8_0* y);
+float orc_vec_dot_q4_0_q8_0(int64_t n, const orc_block_q4_0* x, const orc_block_q8_0* y);
+float orc_vec_dot_q5_0_q8_0(int64_t n, const orc_block_q5_0* x, const orc_block_q8_0* y);
+float orc_vec_dot_q8_0_q8_0(int64_t n, const orc_block_q8_0* x, const orc_block_q8_0* y);
+/* to_float of one row of k values of any type above (F32 and F16 too); -1 if unsupported. */
+int orc_dequant_row(int type, const void* row, int64_t k, float* y);
 void orc_dequant_row_q4k(const orc_block_q4k* x, int64_t k, float* y);
 void orc_dequant_row_q6k(const orc_block_q6k* x, int64_t k, float* y);
 /* Integer per-super-block dot products (the exact integers candle combines

@@ -19,6 +19,9 @@ sys.path.insert(0, HERE)
 from build import LIB, build  # noqa: E402
 
 Q4_K, Q6_K, F32, F16 = 12, 14, 0, 1
+Q4_0, Q5_0, Q8_0, Q5_K = 2, 6, 8, 13
+Q8_0_DTYPE = np.dtype([("d", "<u2"), ("qs", "i1", (32,))])
+assert Q8_0_DTYPE.itemsize == 34
 Q8K_DTYPE = np.dtype([("d", "<f4"), ("qs", "i1", (256,)), ("bsums", "<i2", (16,))])
 assert Q8K_DTYPE.itemsize == 292
 
@@ -40,6 +43,9 @@ def lib() -> ctypes.CDLL:
             "orc_q4k_block_ints": (None, [V, V, I64, V, V]),
             "orc_q6k_block_ints": (None, [V, V, I64, V]),
             "orc_qmatmul": (c_int, [V, c_int, I64, I64, V, I64, V]),
+            "orc_quantize_row_q8_0": (c_int, [V, I64, V]),
+            "orc_dequant_row": (c_int, [c_int, V, I64, V]),
+            "orc_vec_dot_q5k_q8k": (c_float, [I64, V, V]),
             "orc_llama_new": (V, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_float, c_float, c_int]),
             "orc_llama_set_tensor": (c_int, [V, c_char_p, c_int, V, c_int, I64, I64]),
             "orc_llama_finalize": (c_int, [V]),
@@ -119,17 +125,28 @@ def quantize_q8k(x: np.ndarray) -> np.ndarray:
     return out
 
 
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """candle BlockQ8_0::from_float of each row (k % 32 == 0)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    k = x.shape[-1]
+    rows = x.reshape(-1, k)
+    out = np.zeros((rows.shape[0], k // 32), dtype=Q8_0_DTYPE)
+    for r in range(rows.shape[0]):
+        check(lib().orc_quantize_row_q8_0(P(rows[r]), k, P(out[r])))
+    return out
+
+
 def vec_dot(wtype: int, w_row: np.ndarray, q8_row: np.ndarray, k: int) -> float:
-    f = lib().orc_vec_dot_q4k_q8k if wtype == Q4_K else lib().orc_vec_dot_q6k_q8k
+    f = {Q4_K: lib().orc_vec_dot_q4k_q8k, Q5_K: lib().orc_vec_dot_q5k_q8k}.get(wtype, lib().orc_vec_dot_q6k_q8k)
     return float(f(k, P(np.ascontiguousarray(w_row)), P(np.ascontiguousarray(q8_row))))
 
 
 def dequant_rows(wtype: int, raw: np.ndarray, k: int) -> np.ndarray:
+    """to_float of each row of raw GGML blocks (any type orc_dequant_row knows)."""
     raw = np.ascontiguousarray(raw, dtype=np.uint8).reshape(-1, raw.shape[-1])
     out = np.empty((raw.shape[0], k), dtype=np.float32)
-    f = lib().orc_dequant_row_q4k if wtype == Q4_K else lib().orc_dequant_row_q6k
     for r in range(raw.shape[0]):
-        f(P(raw[r]), k, P(out[r]))
+        check(lib().orc_dequant_row(wtype, P(raw[r]), k, P(out[r])))
     return out
 
 
