@@ -148,3 +148,13 @@ def test_generate_stats_and_stop_trim(monkeypatch):
     monkeypatch.setattr(native, "llama_candle_generate_op", lambda *a: ([2], 0, 0))
     toks, stats = LlamaCandle.generate(m, prompt_tokens=[1], stop_tokens=[2])
     assert toks == [] and stats["decode_ms_per_tok"] is None and stats["prefill_tokens_per_sec"] == 1e6
+
+
+def test_bench_reads_profiled_traffic():
+    """bench.py's roofline `traffic` comes from the committed ncu summary of the
+    decode kernel; the summary must keep the line it parses."""
+    import sys
+    sys.path.insert(0, ROOT)
+    import bench
+    t = bench.profiled_traffic("k_decode_mega")
+    assert t is not None and 600e6 < t < 700e6  # ~one TinyLlama token's weights
