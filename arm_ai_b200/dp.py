@@ -1,4 +1,4 @@
-"""Data-parallel batched decode across the GPUs of one node.
+"""Data-parallel batched decode across the GPUs of one node (many independent sequences, e.g. 16 x 512-token prompts).
 
 Independent sequences shard with no data-path collective: rank r of W takes
 a contiguous block of the sequences, decodes it with one batched call on its

@@ -117,7 +117,7 @@ def llama_candle_stream_op(model: LlamaResource, prompt, max_new: int, stop_toke
 
 
 def llama_generate_batch(model: LlamaResource, prompts, max_new: int, stop_tokens=()):
-    """Batched greedy decode of independent sequences (no
+    """Batched greedy decode of independent sequences (several independent sequences; no
     reference counterpart, the reference holds one cache per handle):
     ([tokens per sequence], prefill_us, decode_us). Each sequence behaves as
     one llama_candle_generate_op call; the model must be loaded with

@@ -2,7 +2,7 @@
 
 The reference's headline numbers use real model files that are not available
 here, so benchmarks and parity tests run on random-init models with the
-architectures BASELINE.json names. Every tensor is drawn N(0, 0.02) from a
+architectures the benchmarks use. Every tensor is drawn N(0, 0.02) from a
 seed derived from (model seed, tensor name) and quantised by
 ``csrc/synth.c``: Q4_K for every 2-D tensor, Q6_K for ``output`` and for
 ``attn_v`` / ``ffn_down`` on even layers (a stated simplification of
@@ -46,7 +46,7 @@ class LlamaArch:
 
 
 ARCHS = {
-    # BASELINE.json configs[0] / [1]
+    # the headline b=1 decode and the batched decode workloads
     "tinyllama-1.1b": LlamaArch(22, 2048, 5632, 32, 4, 32000, 10000.0, 1e-5, 2048),
     # configs[2]
     "mistral-7b": LlamaArch(32, 4096, 14336, 32, 8, 32000, 10000.0, 1e-5, 32768),

@@ -1,4 +1,4 @@
-"""Tensor-parallel model loading across the GPUs of one
+"""Tensor-parallel model loading (7B/8B-class models such as Llama-3-8B) across the GPUs of one
 node: one process per GPU, every rank loads the same GGUF with its
 tp_rank, all ranks share rank 0's NCCL unique id (armai_nccl_unique_id)
 through the already-initialised torch.distributed group. The reference runs

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 quantized-Llama decode path (BASELINE.json metric).
+"""Benchmark of the B200 quantized-Llama decode path (decode tokens/s and weight-stream GB/s, b = 1).
 
-Workload (the configuration the metric is quoted
+Workload (the configuration the reference's headline metric is quoted
 on): TinyLlama-1.1B-architecture, Q4_K_M, batch 1, greedy; 32-token seeded
 prompt, 128 new tokens. A "step" is one generation's decode phase: 127
 single-token decode steps after the prompt's prefill.
@@ -35,7 +35,7 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tokens/s and weight-stream HBM GB/s (% peak), Q4_K_M Llama, b=1"
 ARCH = "tinyllama-1.1b"
 PROMPT, MAX_NEW = 32, 128
-PUBLISHED_TOK_S = 4.71  # TinyLlama 1.1B Q4_K_M b=1 decode (Snapdragon 632)
+PUBLISHED_TOK_S = 4.71  # the reference's published TinyLlama 1.1B Q4_K_M b=1 decode rate (Snapdragon 632)
 
 
 def parse():
@@ -224,7 +224,7 @@ def run_reference(args, d):
 
 
 def run_config2(d):
-    """16 independent sequences, 512-token seeded prompts,
+    """Batched decode: 16 independent sequences, 512-token seeded prompts,
     128 new tokens each, sharded over the ranks (dp.generate_batch_dp); each
     rank decodes its sequences in one batched call. Reported beside the
     headline, measured after it."""
@@ -252,7 +252,7 @@ def run_config2(d):
 
 
 def run_config4(d, peak):
-    """Llama-3-8B-architecture Q4_K_M, b = 1, 1024-token
+    """Tensor-parallel decode: Llama-3-8B-architecture Q4_K_M, b = 1, 1024-token
     seeded prompt, 128 new tokens, tensor-parallel over the N ranks: decode
     by the persistent kernel, whose attn_output / ffn_down partial sums cross
     NVLink as generation-tagged peer-memory stores; prefill by the tensor-core
@@ -323,7 +323,7 @@ def run_config4_batch32(d, path, info, n_dec):
 
 
 def run_config3(d, peak):
-    """Mistral-7B-architecture Q4_K_M, b = 1, 4096-token
+    """Long-context decode: Mistral-7B-architecture Q4_K_M, b = 1, 4096-token
     seeded prompt with an f16 KV cache, then 256 decode tokens (split-K GQA
     attention over the long context). One GPU (rank 0 of a single-process
     run). Decode device-timed (CUDA events over 255 back-to-back steps)."""

@@ -66,13 +66,17 @@ typedef struct armai_llama_opts {
   int32_t reserved[6];
 } armai_llama_opts;
 
-/* Tensor parallelism (tp_size > 1): every rank calls
+/* Tensor parallelism (tp_size > 1; 7B/8B-class models): every rank calls
  * armai_llama_load with the same path, its tp_rank and the same 128-byte
  * NCCL unique id, which rank 0 creates with armai_nccl_unique_id and shares
  * out of band (no reference counterpart: the reference runs on one CPU).
  * Query/KV heads, gate/up rows and vocab rows are split over the ranks;
- * attn_output and ffn_down are split along K and summed by an NCCL
- * all-reduce; prompts run the tensor-core GEMM path. */
+ * attn_output and ffn_down are split along K. The persistent decode kernel
+ * adds their partial sums through peer memory (CUDA IPC); the per-kernel
+ * chain, prompts (tensor-core GEMM path) and batched decode use NCCL
+ * all-reduces. Ranks must be on distinct GPUs and make the same calls in the
+ * same order; host waits are bounded (the communicator is aborted after
+ * 120 s without progress). */
 ARMAI_API int armai_nccl_unique_id(void* out128);
 
 /* Fill `o` with the defaults above. */
@@ -81,7 +85,9 @@ ARMAI_API void armai_llama_default_opts(armai_llama_opts* o);
 /* Replaces llama_candle::load_model (native/arm_ai_nif/src/llama_candle.rs:35-48)
  * behind llama_candle_load_op (native/arm_ai_nif/src/lib.rs:1659-1665).
  * Parses the GGUF file, uploads the Q4_K / Q6_K super-blocks to HBM,
- * allocates the KV cache and captures the decode graph. `opts` may be NULL. */
+ * allocates the KV cache and prepares the decode step (the persistent
+ * kernel's phase table, or the per-kernel chain captured as a CUDA graph).
+ * Other weight types are rejected, naming the tensor. `opts` may be NULL. */
 ARMAI_API int armai_llama_load(const char* path, const armai_llama_opts* opts, armai_llama** out);
 
 /* Releases every device and host resource of the model (the NIF resource's
@@ -115,7 +121,7 @@ ARMAI_API int armai_llama_generate(armai_llama* m, const uint32_t* prompt, size_
                          armai_token_cb on_token, void* user, uint32_t* out, size_t* n_out,
                          uint64_t* prefill_us, uint64_t* decode_us);
 
-/* Batched greedy decode of n_seq independent sequences:
+/* Batched greedy decode of n_seq independent sequences (e.g. 16 sequences per GPU):
  * prompts are concatenated in `prompts` with lengths in `n_prompt[n_seq]`.
  * Each sequence behaves exactly like one armai_llama_generate call; decode
  * steps of all live sequences run as one batched step. out is
@@ -283,7 +289,7 @@ ARMAI_API int armai_dev_int4_gemv_q4_x_q8(const float* a, const uint8_t* w_packe
 ARMAI_API int armai_dev_int4_gemv_q4_x_q8_noalloc(const float* a, const uint8_t* w_packed,
                                                   const float* w_scales, float* out, int64_t n, int64_t k,
                                                   void* stream);
-/* BASELINE config 5's int4 variant: per-32-group f16 scales [N,K/32]. */
+/* The int4 gemv with per-32-group f16 scales [N,K/32] (instead of f32). */
 ARMAI_API int armai_dev_int4_gemv_f16s(const float* a, const uint8_t* w_packed, const uint16_t* w_scales,
                              float* out, int64_t n, int64_t k, void* stream);
 ARMAI_API int armai_dev_rmsnorm_f32(const float* x, const float* gamma, float* out, int64_t n_outer,

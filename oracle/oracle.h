@@ -125,7 +125,7 @@ int orc_llama_set_tensor(orc_llama* m, const char* role, int layer, const void* 
                          int ggml_type, int64_t rows, int64_t cols);
 int orc_llama_finalize(orc_llama* m);
 /* Store K/V cache entries rounded to IEEE binary16 (round to nearest even)
- * and read them back as f32: the f16 KV cache of BASELINE config 3. candle's
+ * and read them back as f32: the f16 KV cache of the long-context configuration. candle's
  * quantized_llama keeps an f32 cache; this mode is off by default. */
 void orc_llama_set_kv_f16(orc_llama* m, int on);
 void orc_llama_free(orc_llama* m);

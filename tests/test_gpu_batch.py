@@ -1,4 +1,4 @@
-"""Batched greedy decode: armai_llama_generate_batch.
+"""Batched greedy decode (independent sequences per GPU): armai_llama_generate_batch.
 
 Each sequence must behave as one armai_llama_generate call. The batched step
 runs the same per-row arithmetic as the per-kernel decode chain (one weight

@@ -1,6 +1,6 @@
 """head_dim 128 (the Mistral-7B / Llama-3-8B attention shape) on a
 CPU-checkable model: the persistent decode kernel's HD = 128 instantiation
-and BASELINE config 3's structure — f16 KV cache, a ~4096-token prompt and
+and the long-context configuration's structure — f16 KV cache, a ~4096-token prompt and
 decode steps across position 4096 (split attention of 16 context slices of
 several 32-position tiles) — against the oracle, under the same flip-bound
 criteria as tests/test_gpu_llama.py."""

@@ -1,6 +1,6 @@
 """Parity of the CUDA decode path with the CPU oracle, through the C ABI.
 
-Bar (BASELINE.json north star): final logits within 1e-2 relative max-abs
+Bar: final logits within 1e-2 relative max-abs
 (max |ours - oracle| / max |oracle|), greedy token ids identical for the
 first 32 tokens. The integer parts are bit-exact (test_gpu_kquant.py); the
 remaining differences are f32 summation orders, which now and then flip one

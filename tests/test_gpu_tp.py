@@ -1,4 +1,4 @@
-"""Tensor parallelism on two GPUs (BASELINE config 4's structure on the small
+"""Tensor parallelism on two GPUs (the Llama-3-8B sharding on the small
 test model: 8 query / 2 KV heads, FFN 1536, vocab 4096 split over 2 ranks).
 
 Each rank holds half the heads, gate/up rows and vocab rows and a K-half of
