@@ -14,7 +14,6 @@
 // tolerance.
 #include <cuda_fp16.h>
 
-#include <atomic>
 #include <cstring>
 #include <string>
 
@@ -614,7 +613,10 @@ __global__ void k_silu_gate_mul_up(const float* __restrict__ g, const float* __r
 // l < 32), four outputs like the reference's inner loop. The reference takes
 // the sub-scales scales[8n + {0, 2, 4, 6}] for all 32 values of each group
 // (ggml's dequantize_row_q6_K uses 8n + l/16 + {0, 2, 4, 6}); this follows
-// the reference. value = d * (float)(scale * q), one rounding.
+// the reference. The reference reads the sub-scales from a `&[u8]` and
+// widens them with `as i32` (shape_ops.rs:2860,2887-2890), so they are
+// unsigned 0..255 here (ggml's Q6_K scales are int8).
+// value = d * (float)(scale * q), one rounding.
 __global__ void k_dequant_q6k(const uint8_t* __restrict__ in, float* out, int64_t n_blocks) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= n_blocks * 64) return;
@@ -623,17 +625,17 @@ __global__ void k_dequant_q6k(const uint8_t* __restrict__ in, float* out, int64_
   const uint8_t* blk = in + b * 210;
   const uint8_t* ql = blk + 64 * n;
   const uint8_t qh = blk[128 + 32 * n + l];
-  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * n);
+  const uint8_t* sc = blk + 192 + 8 * n;  // u8 -> i32: zero-extended
   const float d = __half2float(__ushort_as_half((uint16_t)(blk[208] | (blk[209] << 8))));
   const int q1 = ((ql[l] & 0xF) | (((qh >> 0) & 3) << 4)) - 32;
   const int q2 = ((ql[l + 32] & 0xF) | (((qh >> 2) & 3) << 4)) - 32;
   const int q3 = ((ql[l] >> 4) | (((qh >> 4) & 3) << 4)) - 32;
   const int q4 = ((ql[l + 32] >> 4) | (((qh >> 6) & 3) << 4)) - 32;
   float* o = out + b * 256 + 128 * n + l;
-  o[0] = __fmul_rn(d, (float)(sc[0] * q1));
-  o[32] = __fmul_rn(d, (float)(sc[2] * q2));
-  o[64] = __fmul_rn(d, (float)(sc[4] * q3));
-  o[96] = __fmul_rn(d, (float)(sc[6] * q4));
+  o[0] = __fmul_rn(d, (float)((int)sc[0] * q1));
+  o[32] = __fmul_rn(d, (float)((int)sc[2] * q2));
+  o[64] = __fmul_rn(d, (float)((int)sc[4] * q3));
+  o[96] = __fmul_rn(d, (float)((int)sc[6] * q4));
 }
 
 // dequant_matmul_f16_f32 (shape_ops.rs:1462-1490, the x86 path): out[r][j] =
@@ -854,24 +856,15 @@ constexpr int64_t Q4Q8_NOALLOC_MAX_K = 32LL * 32 * MAX_GROUPS_PER_LANE;  // 1638
 static __device__ __align__(256) uint8_t g_q4q8_scratch[Q4Q8_NOALLOC_MAX_K + Q4Q8_NOALLOC_MAX_K / 32 * 4];
 
 namespace {
-constexpr int NOALLOC_MAX_DEVICES = 64;
-std::atomic<void*> g_q4q8_scratch_ptr[NOALLOC_MAX_DEVICES];
-
-// Device address of this device's copy of the scratch; looked up once per
-// device (the first call, which may also load the module).
+// Device address of the current device's copy of the scratch. Looked up on
+// every call rather than cached: the lookup is cheap once the module is
+// loaded, and an address cached per device number would go stale if the
+// host program reset the device (cudaDeviceReset) and made a new context.
+// The first call on a device may load the module.
 int q4q8_scratch(uint8_t** out) {
-  int dev = 0;
-  ARMAI_CUDA(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= NOALLOC_MAX_DEVICES)
-    return fail(ARMAI_E_INVALID, "int4_gemv_q4_x_q8_noalloc: device ordinal " + std::to_string(dev) +
-                                     " beyond " + std::to_string(NOALLOC_MAX_DEVICES));
-  void* p = g_q4q8_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!p) {
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_q4q8_scratch);
-    if (e != cudaSuccess)
-      return cuda_fail(e, "cudaGetSymbolAddress(g_q4q8_scratch)", __FILE__, __LINE__);
-    g_q4q8_scratch_ptr[dev].store(p, std::memory_order_release);
-  }
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_q4q8_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_q4q8_scratch)", __FILE__, __LINE__);
   *out = static_cast<uint8_t*>(p);
   return ARMAI_OK;
 }

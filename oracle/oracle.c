@@ -1199,7 +1199,9 @@ int orc_silu_gate_mul_up_f32(const float* gate, const float* up, int64_t n, floa
 
 /* shape_ops.rs:2848-2899 dequantize_q6_k, as the reference writes it: the
  * sub-scales of each 32-value group are scales[8n + {0, 2, 4, 6}] for every
- * l (ggml's dequantize_row_q6_K would add l / 16). */
+ * l (ggml's dequantize_row_q6_K would add l / 16), and they are read from a
+ * `&[u8]` slice and widened with `as i32` (shape_ops.rs:2860,2887-2890), so
+ * they are UNSIGNED 0..255 (ggml's block_q6_K holds int8 scales). */
 int orc_dequantize_q6_k(const uint8_t* in, int64_t n_blocks, float* out) {
 #pragma omp parallel for schedule(static)
   for (int64_t b = 0; b < n_blocks; b++) {
@@ -1207,7 +1209,7 @@ int orc_dequantize_q6_k(const uint8_t* in, int64_t n_blocks, float* out) {
     float* o = out + b * 256;
     const uint8_t* ql = blk;
     const uint8_t* qh = blk + 128;
-    const int8_t* sc = (const int8_t*)(blk + 192);
+    const uint8_t* sc = blk + 192; /* u8 -> i32: zero-extended */
     const float d = orc_f16_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
     for (int n = 0; n < 2; n++) {
       for (int l = 0; l < 32; l++) {
@@ -1216,10 +1218,10 @@ int orc_dequantize_q6_k(const uint8_t* in, int64_t n_blocks, float* out) {
         const int q2 = ((ql[64 * n + l + 32] & 0xF) | (((qhi >> 2) & 3) << 4)) - 32;
         const int q3 = (((ql[64 * n + l] >> 4) & 0xF) | (((qhi >> 4) & 3) << 4)) - 32;
         const int q4 = (((ql[64 * n + l + 32] >> 4) & 0xF) | (((qhi >> 6) & 3) << 4)) - 32;
-        o[128 * n + l] = d * (float)(sc[8 * n + 0] * q1);
-        o[128 * n + l + 32] = d * (float)(sc[8 * n + 2] * q2);
-        o[128 * n + l + 64] = d * (float)(sc[8 * n + 4] * q3);
-        o[128 * n + l + 96] = d * (float)(sc[8 * n + 6] * q4);
+        o[128 * n + l] = d * (float)((int)sc[8 * n + 0] * q1);
+        o[128 * n + l + 32] = d * (float)((int)sc[8 * n + 2] * q2);
+        o[128 * n + l + 64] = d * (float)((int)sc[8 * n + 4] * q3);
+        o[128 * n + l + 96] = d * (float)((int)sc[8 * n + 6] * q4);
       }
     }
   }

@@ -83,8 +83,23 @@ def q6k_blocks(nb):
 @pytest.mark.parametrize("nb", [1, 3, 4096])
 def test_dequantize_q6_k_bit_exact(built, nb):
     raw = q6k_blocks(nb)
+    # at least half of the sub-scale bytes at or above 0x80, where an int8
+    # reading of the reference's u8 scales would differ
+    raw[:, 192:208:2] |= 0x80
+    assert (raw[:, 192:208] >= 0x80).mean() >= 0.5
     got = prims.dequantize_q6_k_op(raw.tobytes(), nb * 256)
     assert np.array_equal(got, ref.dequantize_q6_k(raw, nb))
+
+
+def test_dequantize_q6_k_known_answer(built):
+    """Hand-derived values (tests/test_oracle_llm_pins.py: q6k_known_answer)
+    for sub-scale bytes 0x80, 0xC0 and 0xFF, read unsigned as the reference's
+    `scales[i] as i32` over a `&[u8]` does."""
+    from test_oracle_llm_pins import q6k_known_answer, q6k_known_block
+    raw = np.stack([q6k_known_block(0x3C00), q6k_known_block(0x3000), q6k_known_block(0xB800)])
+    got = prims.dequantize_q6_k_op(raw.tobytes(), 3 * 256).reshape(3, 256)
+    for i, d in enumerate((1.0, 0.125, -0.5)):
+        assert np.array_equal(got[i], q6k_known_answer(d))
 
 
 @pytest.mark.parametrize("b,m,n,k", [(1, 1, 4096, 4096), (1, 3, 100, 33), (2, 16, 512, 1024), (1, 64, 2048, 256)])

@@ -45,11 +45,13 @@ def test_rope_known_answers(built):
 
 
 def q6k_reference_loop(raw):
-    """shape_ops.rs:2848-2899 transcribed: scales[8n + {0,2,4,6}] for every l."""
+    """shape_ops.rs:2848-2899 transcribed: scales[8n + {0,2,4,6}] for every l,
+    and `let scales = &block[192..208]` is a `&[u8]`, so `scales[i] as i32`
+    zero-extends: the sub-scales are unsigned 0..255."""
     nb = raw.shape[0]
     out = np.empty((nb, 256), np.float32)
     d = raw[:, 208:210].copy().view(np.float16).astype(np.float32).reshape(nb)
-    sc = raw[:, 192:208].view(np.int8).astype(np.int32)
+    sc = raw[:, 192:208].astype(np.int32)
     for n in range(2):
         ql, qh = raw[:, 64 * n: 64 * n + 64].astype(np.int32), raw[:, 128 + 32 * n: 160 + 32 * n].astype(np.int32)
         q1 = ((ql[:, :32] & 0xF) | ((qh & 3) << 4)) - 32
@@ -74,15 +76,69 @@ def test_dequantize_q6_k_follows_reference_loop(built):
     assert np.array_equal(ref.dequantize_q6_k(raw, 37).reshape(37, 256), q6k_reference_loop(raw))
 
 
+def q6k_known_block(d_bits):
+    """One hand-built Q6_K block: ql[0] = 0x21, ql[32] = 0x43, qh[0] = 0xE4,
+    every other ql/qh byte 0; sub-scale bytes scales[0] = 0x80,
+    scales[2] = 0xC0, scales[4] = 0xFF, scales[6] = 0x01, scales[8] = 0x7F,
+    the rest 0; f16 d from `d_bits`."""
+    blk = np.zeros(210, np.uint8)
+    blk[0], blk[32], blk[128] = 0x21, 0x43, 0xE4
+    blk[192], blk[194], blk[196], blk[198], blk[200] = 0x80, 0xC0, 0xFF, 0x01, 0x7F
+    blk[208], blk[209] = d_bits & 0xFF, d_bits >> 8
+    return blk
+
+
+def q6k_known_answer(d):
+    """Expected output of q6k_known_block, written out from the Rust loop
+    (shape_ops.rs:2870-2895) by hand. For n = 0, l = 0:
+      q1 = (0x21 & 0xF | ((0xE4 >> 0) & 3) << 4) - 32 = (1 | 0) - 32 = -31
+      q2 = (0x43 & 0xF | ((0xE4 >> 2) & 3) << 4) - 32 = (3 | 16) - 32 = -13
+      q3 = (0x21 >> 4  | ((0xE4 >> 4) & 3) << 4) - 32 = (2 | 32) - 32 = 2
+      q4 = (0x43 >> 4  | ((0xE4 >> 6) & 3) << 4) - 32 = (4 | 48) - 32 = 20
+    and the sub-scales `scales[i] as i32` of u8 bytes: s1 = 0x80 = 128,
+    s2 = 0xC0 = 192, s3 = 0xFF = 255, s4 = 0x01 = 1 (int8 would read -128,
+    -64, -1, 1). out = d * (s * q) as f32:
+      out[0] = 128 * -31 = -3968, out[32] = 192 * -13 = -2496,
+      out[64] = 255 * 2 = 510,     out[96] = 1 * 20 = 20.
+    Every other l of n = 0 has ql = qh = 0, q = -32: 128 * -32 = -4096,
+    192 * -32 = -6144, 255 * -32 = -8160, 1 * -32 = -32. For n = 1 all q are
+    -32 with s = scales[8] = 127 (values 128..159: -4064) and
+    scales[10 / 12 / 14] = 0 (values 160..255: 0)."""
+    out = np.zeros(256, np.float64)
+    out[0:32], out[32:64], out[64:96], out[96:128] = -4096, -6144, -8160, -32
+    out[0], out[32], out[64], out[96] = -3968, -2496, 510, 20
+    out[128:160] = -4064
+    return (out * d).astype(np.float32)
+
+
+@pytest.mark.parametrize("d_bits,d", [(0x3C00, 1.0), (0x3000, 0.125), (0xB800, -0.5)])
+def test_dequantize_q6_k_known_answer_unsigned_subscales(built, d_bits, d):
+    got = ref.dequantize_q6_k(q6k_known_block(d_bits)[None, :], 1).reshape(256)
+    assert np.array_equal(got, q6k_known_answer(d))
+
+
 def test_dequantize_q6_k_subscale_order_vs_ggml(built):
     """The reference uses sub-scale 2g for the whole 32-value group; ggml uses
-    2g + l/16. They agree exactly when the paired sub-scales are equal."""
+    2g + l/16. It also reads the sub-scale bytes unsigned where ggml reads
+    int8. The two agree exactly when the paired sub-scales are equal and
+    every sub-scale byte is below 0x80."""
     gguf = pytest.importorskip("gguf")
     from gguf.quants import dequantize
     same = q6k_blocks(8, equal_pairs=True)
+    same[:, 192:208] &= 0x7F
     ggml = dequantize(same.reshape(-1), gguf.GGMLQuantizationType.Q6_K).reshape(8, 256)
     assert np.array_equal(ref.dequantize_q6_k(same, 8).reshape(8, 256), ggml.astype(np.float32))
+    # a sub-scale byte >= 0x80 is s under the reference, s - 256 under ggml
+    neg = same.copy()
+    neg[:, 192:194] |= 0x80
+    ggml = dequantize(neg.reshape(-1), gguf.GGMLQuantizationType.Q6_K).reshape(8, 256).astype(np.float32)
+    ours = ref.dequantize_q6_k(neg, 8).reshape(8, 256)
+    assert np.array_equal(ours[:, 32:], ggml[:, 32:])
+    s = neg[:, 192].astype(np.float64)
+    np.testing.assert_allclose(ours[:, :32].astype(np.float64) * (s - 256)[:, None] / s[:, None],
+                               ggml[:, :32], rtol=1e-6)
     diff = q6k_blocks(8)
+    diff[:, 192:208] &= 0x7F
     ggml = dequantize(diff.reshape(-1), gguf.GGMLQuantizationType.Q6_K).reshape(8, 256).astype(np.float32)
     ours = ref.dequantize_q6_k(diff, 8).reshape(8, 256)
     first_half = np.concatenate([np.arange(32 * g, 32 * g + 16) for g in range(8)])
