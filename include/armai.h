@@ -283,9 +283,10 @@ ARMAI_API int armai_dev_int4_gemv_q4_x_q8(const float* a, const uint8_t* w_packe
  * latency or its failure in mid-step. Same arguments and results as
  * armai_dev_int4_gemv_q4_x_q8; the stage-1 scratch is a static device array
  * sized for K <= 16384 (ARMAI_E_RANGE above that). Calls on one device share
- * that scratch: they must not overlap (use one stream, or order them). The
- * first call on each device looks the scratch up (and may load the module);
- * make it before any stream capture. */
+ * that scratch: they must not overlap (use one stream, or order them). Each
+ * call looks up the current device's scratch address (so a device reset
+ * between calls is harmless); the first call on a device may load the
+ * module, so make it before any stream capture. */
 ARMAI_API int armai_dev_int4_gemv_q4_x_q8_noalloc(const float* a, const uint8_t* w_packed,
                                                   const float* w_scales, float* out, int64_t n, int64_t k,
                                                   void* stream);
