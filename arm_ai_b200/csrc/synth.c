@@ -133,14 +133,23 @@ static void quant_block_q4k(const float* x, uint8_t* out) {
     for (int l = 0; l < 32; l++) qs[32 * c + l] = (uint8_t)(q[64 * c + l] | (q[64 * c + 32 + l] << 4));
 }
 
-/* One Q6_K super-block from 256 floats. */
+/* One Q6_K super-block from 256 floats. Signed sub-scales, as llama.cpp's
+ * quantiser makes them: each 16-value group's scale maps the group's value of
+ * largest magnitude (the first one on ties) to -32, so a sub-scale's sign is
+ * the opposite of that value's and about half of them are negative. */
 static void quant_block_q6k(const float* x, uint8_t* out) {
   float scale[16], max_abs_scale = 0.f;
   for (int j = 0; j < 16; j++) {
-    float amax = 0.f;
-    for (int l = 0; l < 16; l++) amax = fmaxf(amax, fabsf(x[16 * j + l]));
-    scale[j] = amax / 31.f;
-    if (scale[j] > max_abs_scale) max_abs_scale = scale[j];
+    float amax = 0.f, mx = 0.f;
+    for (int l = 0; l < 16; l++) {
+      const float v = x[16 * j + l];
+      if (fabsf(v) > amax) {
+        amax = fabsf(v);
+        mx = v;
+      }
+    }
+    scale[j] = mx / -32.f;
+    if (amax / 32.f > max_abs_scale) max_abs_scale = amax / 32.f;
   }
   uint16_t dh = f32_to_f16(max_abs_scale / 127.f);
   float d = f16_to_f32(dh);

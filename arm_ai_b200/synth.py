@@ -6,7 +6,8 @@ architectures the benchmarks use. Every tensor is drawn N(0, 0.02) from a
 seed derived from (model seed, tensor name) and quantised by
 ``csrc/synth.c``: Q4_K for every 2-D tensor, Q6_K for ``output`` and for
 ``attn_v`` / ``ffn_down`` on even layers (a stated simplification of
-llama.cpp's Q4_K_M mix). Norm gains are f32, 1 + N(0, 0.05).
+llama.cpp's Q4_K_M mix). Q6_K sub-scales are signed as llama.cpp makes them
+(about half negative). Norm gains are f32, 1 + N(0, 0.05).
 
 The file is written with gguf-py's ``GGUFWriter``; the loader in
 ``libarmai_cuda.so`` parses it with its own reader, so the container format is
@@ -146,7 +147,8 @@ def model_path(arch_name: str, seed: int = 0, cache_dir: str | None = None, tie_
     cache_dir = cache_dir or os.environ.get("ARMAI_MODEL_CACHE", "/tmp/armai_models")
     os.makedirs(cache_dir, exist_ok=True)
     arch = ARCHS[arch_name]
-    key = hashlib.sha256(repr((asdict(arch), seed, tie_output, 1)).encode()).hexdigest()[:12]
+    # the last field versions the quantiser (2: signed Q6_K sub-scales)
+    key = hashlib.sha256(repr((asdict(arch), seed, tie_output, 2)).encode()).hexdigest()[:12]
     p = os.path.join(cache_dir, f"{arch_name}-s{seed}{'-tied' if tie_output else ''}-{key}.gguf")
     if not os.path.exists(p):
         tmp = f"{p}.{os.getpid()}.tmp"  # complete files only, even if interrupted or raced

@@ -51,10 +51,35 @@ def test_q8k_quantize_bit_exact(built, k):
     assert np.array_equal(ours["d"].view(np.uint32), theirs["d"].view(np.uint32))
 
 
-@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K])
+def _q6k_subscales(w):
+    """The int8 sub-scales of every Q6_K super-block of rows `w`."""
+    return w.reshape(-1, 210)[:, 192:208].view(np.int8)
+
+
+def _random_q6k_rows(rows, k, seed):
+    """Q6_K rows of random bytes (every ql / qh / sub-scale byte, so sub-scales
+    span -128..127) with finite f16 d of either sign."""
+    rng = np.random.default_rng(seed)
+    raw = rng.integers(0, 256, (rows * (k // 256), 210), dtype=np.uint8)
+    d = (rng.uniform(1e-5, 1e-3, raw.shape[0]) * rng.choice([-1, 1], raw.shape[0])).astype(np.float16)
+    raw[:, 208:210] = d.view(np.uint8).reshape(-1, 2)
+    return raw.reshape(rows, -1)
+
+
+def test_synthetic_q6k_has_negative_subscales(built):
+    sc = _q6k_subscales(_rows(kquant.Q6_K, 64, 2048, seed=1))
+    assert 0.3 < (sc < 0).mean() < 0.7
+
+
+@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K, "q6k_random"])
 @pytest.mark.parametrize("k", [2048, 5632])
 def test_block_dots_bit_exact(built, qtype, k):
-    w = _rows(qtype, 37, k, seed=k + qtype)
+    if qtype == "q6k_random":
+        qtype, w = kquant.Q6_K, _random_q6k_rows(37, k, seed=k)
+    else:
+        w = _rows(qtype, 37, k, seed=k + qtype)
+    if qtype == kquant.Q6_K:
+        assert (_q6k_subscales(w) < 0).mean() > 0.3
     q8 = ref.quantize_q8k(_activations(3, k, 7))
     isum, msum = kquant.block_dots(qtype, w, k, q8)
     risum, rmsum = ref.block_ints(qtype, w, q8, k)
@@ -87,12 +112,19 @@ def _f16_operands(qtype, w, k, x):
     return a, wd
 
 
-@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K])
+@pytest.mark.parametrize("qtype", [kquant.Q4_K, kquant.Q6_K, "q6k_random"])
 @pytest.mark.parametrize("k,n,m", [(256, 128, 128), (2048, 384, 200), (5632, 256, 77), (2048, 1000, 5)])
 def test_qgemm_tensor_cores(built, qtype, k, n, m):
     """tcgen05 prefill GEMM: exactly the f16 operands' product up to the f32
-    summation order (2e-6 of the magnitude sum), ragged m and n included."""
-    w = _rows(qtype, n, k, seed=7 * n + k)
+    summation order (2e-6 of the magnitude sum), ragged m and n included.
+    Q6_K rows carry negative sub-scales (synthetic: about half; random bytes:
+    the full int8 range)."""
+    if qtype == "q6k_random":
+        qtype, w = kquant.Q6_K, _random_q6k_rows(n, k, seed=7 * n + k)
+    else:
+        w = _rows(qtype, n, k, seed=7 * n + k)
+    if qtype == kquant.Q6_K:
+        assert (_q6k_subscales(w) < 0).mean() > 0.3
     x = _activations(m, k, 5)
     ours = kquant.qgemm(qtype, w, k, x)
     a, wd = _f16_operands(qtype, w, k, x)
