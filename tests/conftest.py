@@ -45,3 +45,21 @@ def tied_model(built):
 def hd128_model(built):
     from arm_ai_b200 import synth
     return synth.model_path("tiny128", seed=4)
+
+
+# Measured parity figures that tests record (e.g. the benchmarked
+# configuration's logit error and greedy-id agreement), printed at the end of
+# the run so that the summary of a quiet (-q) run carries them.
+PARITY_REPORT: list[str] = []
+
+
+@pytest.fixture(scope="session")
+def parity_report():
+    return PARITY_REPORT
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    if PARITY_REPORT:
+        terminalreporter.section("parity report")
+        for line in PARITY_REPORT:
+            terminalreporter.write_line(line)
