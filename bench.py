@@ -104,12 +104,18 @@ class Clocks:
         self.dev, self.proc, self.lines = dev, None, []
         self.enabled = enabled
 
+    def _smi_id(self):
+        """nvidia-smi's id of CUDA device `dev`: its UUID, since nvidia-smi
+        numbers GPUs in its own order and ignores CUDA_VISIBLE_DEVICES."""
+        import torch
+        return f"GPU-{torch.cuda.get_device_properties(self.dev).uuid}"
+
     def __enter__(self):
         if self.enabled:
             try:
                 self.proc = subprocess.Popen(
                     ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
-                     "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                     "-i", self._smi_id()], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
                 self.th = threading.Thread(target=self._read, daemon=True)
                 self.th.start()
             except Exception:
@@ -170,6 +176,28 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def bench_config(world):
+    """The `config` object of both arms' JSON lines (identical, so that the
+    two lines describe the same workload)."""
+    return {"workload": f"{ARCH} Q4_K_M greedy decode b=1: {PROMPT}-token prompt + {MAX_NEW} new "
+                        f"tokens ({MAX_NEW - 1} timed decode steps per step)",
+            "arch": "22 layers, hidden 2048, FFN 5632, 32/4 heads, head_dim 64, vocab 32000",
+            "l2": "inputs larger than L2: every decode token streams all 633 MB of weights",
+            "timed": "decode steps of one generation per step; prefill between steps untimed",
+            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"}
+
+
 def cpu_baseline_sample(path, prompt, max_new=6):
     """The oracle (candle's generic kernels restated in C, OpenMP over output
     columns as rayon does) on all host threads: decode tokens/s."""
@@ -183,13 +211,19 @@ def cpu_baseline_sample(path, prompt, max_new=6):
     wall = time.time() - t0
     m.close()
     v = (len(toks) - 1) * 1e6 / max(dec_us, 1)
-    return {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+    return {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
             "sample": f"{ARCH} Q4_K_M b=1: {len(prompt)}-token prompt + {max_new} new tokens "
                       f"(decode {len(toks) - 1} steps, {dec_us / 1e6:.1f} s; prefill {pre_us / 1e6:.1f} s; "
                       f"wall {wall:.1f} s)"}
 
 
 def run_reference(args, d):
+    """The reference's CPU path (the oracle restatement of candle 0.8.4's
+    generic kernels, OpenMP over output columns as rayon does, all host
+    threads) on the same workload as the GPU arm: per step one generation of
+    a 32-token prompt + 128 new tokens, decode tokens/s measured as the
+    reference measures it ((n_new - 1) / decode_us). Warm-up steps are
+    shortened (8 new tokens): they only page the model in."""
     if d.rank != 0:
         return
     from arm_ai_b200 import synth
@@ -200,25 +234,26 @@ def run_reference(args, d):
     ref.set_threads(cores)
     m = ref.OracleLlama(path)
     prompt = synth.prompt_tokens(PROMPT, m.n_vocab, 1000)
-    per_step_new = 4  # bounded sample: 3 decode steps per step
     for _ in range(args.warmup):
-        m.generate(prompt, per_step_new)
+        m.generate(prompt, 8)
     tok, dec = 0, 0
     t0 = time.time()
     for _ in range(args.steps):
-        toks, _, dec_us = m.generate(prompt, per_step_new)
+        toks, _, dec_us = m.generate(prompt, MAX_NEW)
         tok += len(toks) - 1
         dec += dec_us
     wall = time.time() - t0
+    m.close()
     v = tok * 1e6 / max(dec, 1)
     out = {"metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall * 1000 / args.steps,
            "higher_is_better": True, "scaling": "weak", "vs_baseline": v / PUBLISHED_TOK_S, "dtype": "int8",
-           "data": "synthetic (seeded random-init weights, Q4_K_M mix)",
-           "config": {"workload": f"{ARCH} Q4_K_M greedy decode b=1, {PROMPT}-token prompt; CPU sample of "
-                                  f"{per_step_new} new tokens per step"},
-           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": f"{args.steps} x ({PROMPT}-token prompt + {per_step_new} new tokens)"},
+           "data": "synthetic (seeded random-init N(0,0.02) weights quantised Q4_K/Q6_K (Q4_K_M mix); "
+                   "prompt ids uniform in [3, 32000))",
+           "config": bench_config(args.gpus),
+           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                            "sample": f"{args.steps} x ({PROMPT}-token prompt + {MAX_NEW} new tokens), "
+                                      f"{tok} decode steps in {dec / 1e6:.1f} s"},
            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -435,12 +470,7 @@ def run_armai(args, d):
             "scaling": "weak", "vs_baseline": value / d.world / PUBLISHED_TOK_S, "dtype": "int8",
             "data": "synthetic (seeded random-init N(0,0.02) weights quantised Q4_K/Q6_K (Q4_K_M mix); "
                     "prompt ids uniform in [3, 32000))",
-            "config": {"workload": f"{ARCH} Q4_K_M greedy decode b=1: {PROMPT}-token prompt + {MAX_NEW} new "
-                                   f"tokens ({n_dec} timed decode steps per step)",
-                       "arch": "22 layers, hidden 2048, FFN 5632, 32/4 heads, head_dim 64, vocab 32000",
-                       "l2": f"inputs larger than L2: {bytes_tok / 1e6:.0f} MB of weights streamed per token",
-                       "timed": "decode steps back to back on device (CUDA events); prefill between steps untimed",
-                       "parallelism": f"replicas x{d.world}" if d.world > 1 else "1 GPU"},
+            "config": bench_config(d.world),
             "weight_stream": {"gb_s_per_gpu": ws_gbs, "frac_of_hbm": ws_gbs / peak,
                               "bytes_per_token": bytes_tok + kv_bytes, "peak_gbs": peak, "peak_source": peak_kind},
             "decode_kernel": kname,
