@@ -116,7 +116,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // 3 producer issued the phase's first chunk, 4 first chunk's data ready,
 // 5 first chunk computed, 6 prologue's first pass done, 7 rms scale known,
 // 8 / 9 first unit's dot products / epilogue done.
-constexpr int MK_TRACE_SLOTS = 10;
+constexpr int MK_TRACE_SLOTS = 12;
 __device__ __forceinline__ void mk_stamp(const MkParams& p, int phase, int slot) {
   if (p.trace) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * MK_TRACE_SLOTS + slot] = global_ns();
 }
@@ -165,7 +165,7 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Bounded mbarrier wait that also gives up when another CTA flagged an error.
-__device__ __forceinline__ bool mk_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
+__device__ __forceinline__ bool mk_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t* iters = nullptr) {
   const uint32_t addr = smem_u32(bar);
   for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
     uint32_t ok;
@@ -176,6 +176,7 @@ __device__ __forceinline__ bool mk_wait(uint64_t* bar, uint32_t parity, uint32_t
         : "=r"(ok)
         : "r"(addr), "r"(parity)
         : "memory");
+    if (iters) *iters = i + 1;
     if (ok) return true;
     if (i > 8) {
       if ((i & 63) == 0 && dev_failed(err)) return false;
@@ -196,10 +197,12 @@ __device__ __forceinline__ int mode_of(int kind) {
 // no larger than the smallest phase's unit count, so every CTA owns rows in
 // every matvec phase (which the buffer reuse relies on).
 __device__ __forceinline__ void phase_rows(const MkPhase& ph, int& r0, int& r1) {
+  // 32-bit arithmetic: units (at most a vocabulary's rows) x grid stays far
+  // below 2^31, and a 64-bit division is a long software routine
   const int unit = ph.kind == PH_QKV ? 2 : 1;
-  const long long U = (ph.total_rows + unit - 1) / unit, G = gridDim.x, b = blockIdx.x;
-  r0 = min((int)(b * U / G) * unit, ph.total_rows);
-  r1 = min((int)((b + 1) * U / G) * unit, ph.total_rows);
+  const int U = (ph.total_rows + unit - 1) / unit, G = gridDim.x, b = blockIdx.x;
+  r0 = min((b * U / G) * unit, ph.total_rows);
+  r1 = min(((b + 1) * U / G) * unit, ph.total_rows);
 }
 
 // ---------------------------------------------------------------------------
@@ -344,8 +347,9 @@ __device__ __forceinline__ float wait_word(const unsigned long long* p, uint32_t
 // embedding (layer 0's QKV), y (attn_output), h (ffn_down), or the residual
 // stream x = this CTA's copy + the previous phase's row sums of every rank,
 // added in rank order (QKV of later layers, gate/up, the head).
-__device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8],
-                                             uint32_t want, const float* xrep) {
+__device__ __forceinline__ F8 mk_load_vals_ool(const MkParams& p, const MkPhase& ph, int j, int lane, uint32_t want,
+                                            const float* xrep) {
+  float vv[8];
   if (ph.kind == PH_WO || ph.kind == PH_DOWN) {
     unsigned long long w[8];
     wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err);
@@ -370,6 +374,16 @@ __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& p
 #pragma unroll
     for (int e = 0; e < 8; e++) vv[e] = acc[e];
   }
+  F8 r;
+#pragma unroll
+  for (int e = 0; e < 8; e++) r.v[e] = vv[e];
+  return r;
+}
+__device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& ph, int j, int lane, float (&vv)[8],
+                                             uint32_t want, const float* xrep) {
+  const F8 r = mk_load_vals_ool(p, ph, j, lane, want, xrep);
+#pragma unroll
+  for (int e = 0; e < 8; e++) vv[e] = r.v[e];
 }
 
 // Q8_K activation of phase i's input in shared memory (rmsnorm first when
@@ -378,32 +392,24 @@ __device__ __forceinline__ void mk_load_vals(const MkParams& p, const MkPhase& p
 // passes; any further ones (K > MK_REGJ * 256 * consumer warps) are read
 // again in the second pass (from the copy of x, or the same tagged words).
 __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, uint8_t* smem,
-                             ActQ8& act, int cw, int lane, float* xrep, uint64_t* gbar, uint32_t gpar,
+                             const ActQ8 act, int cw, int lane, float* xrep, uint64_t* gbar, uint32_t gpar,
                              uint32_t want) {
   const int K = ph.K, nb = ph.nb;
   float* part = reinterpret_cast<float*>(smem + p.off_red) + 64;
-  act.qs = reinterpret_cast<int8_t*>(smem + p.off_act_qs);
-  act.d = reinterpret_cast<float*>(smem + p.off_act_d);
-  act.bs = reinterpret_cast<int32_t*>(smem + p.off_act_bs);
   const bool norm = ph.gamma != nullptr;
   const bool is_x = ph.kind != PH_WO && ph.kind != PH_DOWN;
+  // One call site per loader: every copy of the (inlined) loaders would be
+  // instruction-cache footprint of every phase.
   float v[MK_REGJ][8];
-  // the register-held blocks' loads are all issued before any is used
-#pragma unroll
-  for (int r = 0; r < MK_REGJ; r++)
-    if (cw + r * MK_CW < nb) mk_load_vals(p, ph, cw + r * MK_CW, lane, v[r], want, xrep);
   for (int j = cw, jj = 0; j < nb; j += MK_CW, jj++) {
     float vv[8];
-    if (jj < MK_REGJ) {
+    mk_load_vals(p, ph, j, lane, vv, want, xrep);
 #pragma unroll
-      for (int r = 0; r < MK_REGJ; r++)
-        if (jj == r) {
+    for (int r = 0; r < MK_REGJ; r++)
+      if (jj == r) {
 #pragma unroll
-          for (int k = 0; k < 8; k++) vv[k] = v[r][k];
-        }
-    } else {
-      mk_load_vals(p, ph, j, lane, vv, want, xrep);
-    }
+        for (int k = 0; k < 8; k++) v[r][k] = vv[k];
+      }
     if (is_x) {
       float4* xw = reinterpret_cast<float4*>(xrep + j * QK_K + 8 * lane);
       xw[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
@@ -445,8 +451,11 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
       const float4 a = xr[0], b = xr[1];
       vv[0] = a.x; vv[1] = a.y; vv[2] = a.z; vv[3] = a.w;
       vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
-    } else {
-      mk_load_vals(p, ph, j, lane, vv, want, xrep);
+    } else {  // y / h blocks beyond the register-held ones: read again
+      unsigned long long w[8];
+      wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err);
+#pragma unroll
+      for (int e = 0; e < 8; e++) vv[e] = word_val(w[e]);
     }
     if (norm) {
       const float4* gr = reinterpret_cast<const float4*>(gs + j * QK_K + 8 * lane);
@@ -505,79 +514,145 @@ struct MkCtx {
   }
 };
 
-// The units of two staged chunks A and B, dealt over the consumer warps as
-// one list (A's units, then B's): with at most MK_CW units each warp takes
-// one; with more, warp w takes units w and w + MK_CW together (four dot
-// chains over one activation slice) — so a phase whose rows arrive in
-// several stages does not serialise one unit per warp per stage.
-template <int MODE>
-__device__ __forceinline__ void mk_group_units(const MkCtx& cx, const uint8_t* sa, int a0, int a1,
-                                               const Part (&pa)[3], const uint8_t* sb, int b0, int b1,
-                                               const Part (&pb)[3], const ActQ8& act, int cw, int lane,
-                                               float& best_v, int& best_i) {
-  const int nb = cx.nb();
-  const int nA = chunk_nunits<MODE>(a0, a1), U = nA + chunk_nunits<MODE>(b0, b1);
-  const int step = U <= MK_CW ? MK_CW : 2 * MK_CW;
-  for (int g = cw; g < U; g += step) {
-    const UnitRows w1 = g < nA ? unit_rows<MODE>(cx, sa, a0, a1, pa, g) : unit_rows<MODE>(cx, sb, b0, b1, pb, g - nA);
-    const int g2 = g + MK_CW;
-    float d[4];
-    if (step > MK_CW && g2 < U) {
-      const UnitRows w2 =
-          g2 < nA ? unit_rows<MODE>(cx, sa, a0, a1, pa, g2) : unit_rows<MODE>(cx, sb, b0, b1, pb, g2 - nA);
-      if (w1.ty0 == w2.ty0 && w1.ty1 == w2.ty1) {
-        if (MODE != MODE_GATEUP || w1.ty0 == w1.ty1) {
-          if (w1.ty0 == GGML_Q4_K)
-            unit_dots2<GGML_Q4_K, GGML_Q4_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
-          else
-            unit_dots2<GGML_Q6_K, GGML_Q6_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
-        } else if (w1.ty0 == GGML_Q4_K) {
-          unit_dots2<GGML_Q4_K, GGML_Q6_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
-        } else {
-          unit_dots2<GGML_Q6_K, GGML_Q4_K>(w1.p0, w1.p1, w1.has1, w2.p0, w2.p1, w2.has1, nb, act, lane, d);
-        }
-      } else {
-        unit_dot_any<MODE>(w1, nb, act, lane, d[0], d[1]);
-        unit_dot_any<MODE>(w2, nb, act, lane, d[2], d[3]);
-      }
-      if (lane == 0) {
-        unit_epilogue<MODE>(cx, w1, d[0], d[1], 0.f, 0.f, best_v, best_i);
-        unit_epilogue<MODE>(cx, w2, d[2], d[3], 0.f, 0.f, best_v, best_i);
-      }
-    } else {
-      unit_dot_any<MODE>(w1, nb, act, lane, d[0], d[1]);
-      if (lane == 0) unit_epilogue<MODE>(cx, w1, d[0], d[1], 0.f, 0.f, best_v, best_i);
+// ---------------------------------------------------------------------------
+// The matvec phases share one copy of their code: the mode (q/k/v, residual,
+// gate/up, head) and the weight types are runtime values. The whole decode
+// step then executes a few tens of KB of instructions per layer, which stay
+// in the SM's instruction cache; per-mode and per-type template copies made
+// every phase start from cold code (an instruction fetched from outside the
+// cache costs about ten cycles, so a latency-bound chain runs several times
+// slower).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mk_parts(const MkPhase& ph, int mode, int c0, int c1, Part (&parts)[3]) {
+  if (mode == MODE_QKV) make_parts<MODE_QKV>(ph.seg, ph.nseg, c0, c1, parts);
+  else if (mode == MODE_GATEUP) make_parts<MODE_GATEUP>(ph.seg, ph.nseg, c0, c1, parts);
+  else make_parts<MODE_RESID>(ph.seg, ph.nseg, c0, c1, parts);
+}
+__device__ __forceinline__ int mk_nunits(int mode, int c0, int c1) {
+  return mode == MODE_GATEUP ? c1 - c0 : (c1 - c0 + 1) >> 1;
+}
+// Unit u of a staged chunk [c0, c1) (see unit_rows): its two rows.
+__device__ __forceinline__ UnitRows mk_unit(const MkPhase& ph, int mode, const uint8_t* stage, int c0, int c1,
+                                            const Part (&parts)[3], int u) {
+  UnitRows w;
+  w.si = 0;
+  w.has1 = true;
+  if (mode == MODE_QKV) {
+    w.r = c0 + 2 * u;
+    const int qn = ph.seg[0].rows, kn = ph.seg[1].rows;
+    w.si = w.r < qn ? 0 : (w.r < qn + kn ? 1 : 2);
+    const int sb = w.si == 0 ? 0 : (w.si == 1 ? qn : qn + kn);
+    const uint32_t off = w.si == 0 ? parts[0].off : (w.si == 1 ? parts[1].off : parts[2].off);
+    const int lo = w.si == 0 ? parts[0].lo : (w.si == 1 ? parts[1].lo : parts[2].lo);
+    const int rb = ph.seg[w.si].row_bytes;
+    w.p0 = stage + off + (size_t)(w.r - sb - lo) * rb;
+    w.p1 = w.p0 + rb;
+    w.ty0 = w.ty1 = ph.seg[w.si].type;
+  } else if (mode == MODE_GATEUP) {
+    w.r = c0 + u;
+    w.p0 = stage + (size_t)u * ph.seg[0].row_bytes;
+    w.p1 = stage + parts[1].off + (size_t)u * ph.seg[1].row_bytes;
+    w.ty0 = ph.seg[0].type;
+    w.ty1 = ph.seg[1].type;
+  } else {
+    w.r = c0 + 2 * u;
+    w.p0 = stage + (size_t)(2 * u) * ph.seg[0].row_bytes;
+    w.p1 = w.p0 + ph.seg[0].row_bytes;
+    w.has1 = w.r + 1 < c1;
+    w.ty0 = w.ty1 = ph.seg[0].type;
+  }
+  return w;
+}
+// Both dot products of a unit; each row's type dispatched per quarter (the
+// type is the same for the whole warp).
+__device__ __forceinline__ float2 mk_dot2(const UnitRows& w, int nb, const ActQ8& act, int lane) {
+  const int t = lane & 3, bl = lane >> 2;
+  float a0 = 0.f, a1 = 0.f;
+  const int npass = (nb + 7) >> 3;
+  for (int ps = 0; ps < npass; ps++) {
+    const int blk = ps * 8 + bl;
+    if (blk < nb) {
+      ActSlice A;
+      load_slice(act, blk, t, A);
+      a0 += quarter_dot(w.ty0, w.p0, nb, blk, t, A);
+      if (w.has1) a1 += quarter_dot(w.ty1, w.p1, nb, blk, t, A);
     }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+  }
+  return make_float2(a0, a1);
+}
+
+// Per-warp state carried from phase to phase: the ring position (stage,
+// mbarrier parity) and the head's running argmax.
+struct MkRun {
+  int s, par;
+  float best_v;
+  int best_i;
+};
+__device__ __forceinline__ void mk_advance(MkRun& run, int ns) {
+  if (++run.s == ns) {
+    run.s = 0;
+    run.par ^= 1;
   }
 }
 
 // All chunks of this CTA's rows in one matvec phase: wait for the stages,
 // compute, hand the stages back to the producer. Except for QKV (few rows
-// per CTA), chunks are taken two at a time (mk_group_units).
-template <int MODE>
-__device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int pos, uint32_t tag, uint8_t* smem,
-                          uint64_t* full, uint64_t* empty, int& cidx, const ActQ8& act, int cw, int lane,
-                          float& best_v, int& best_i) {
+// per CTA), chunks are taken two at a time and their units dealt over the
+// consumer warps as one list, so a phase whose rows arrive in several stages
+// does not serialise one unit per warp per stage.
+__device__ MkRun mk_chunks(const MkParams& p, const MkPhase& ph, int mode, int phase, int pos, uint32_t tag,
+                           uint8_t* smem, uint64_t* full, uint64_t* empty, MkRun run, const ActQ8 act, int cw,
+                           int lane) {
   int r0, r1;
   phase_rows(ph, r0, r1);
   const MkCtx cx{p, ph, pos, phase, tag};
+  const int nb = ph.nb;
   for (int c0 = r0; c0 < r1;) {
     const int c1 = min(c0 + ph.chunk_rows, r1);
-    const bool two = MODE != MODE_QKV && c1 < r1;
+    const bool two = mode != MODE_QKV && c1 < r1;
     const int c2 = two ? min(c1 + ph.chunk_rows, r1) : c1;
-    const int sA = cidx % p.ns, sB = (cidx + 1) % p.ns;
-    if (!mk_wait(&full[sA], (uint32_t)((cidx / p.ns) & 1), p.err)) return false;
-    if (two && !mk_wait(&full[sB], (uint32_t)(((cidx + 1) / p.ns) & 1), p.err)) return false;
+    const int sA = run.s, pA = run.par;
+    mk_advance(run, p.ns);
+    const int sB = run.s, pB = run.par;
+    if (two) mk_advance(run, p.ns);
+    uint32_t iters = 0;
+    const bool tr = p.trace && c0 == r0 && cw == 0 && lane == 0;
+    if (tr) mk_stamp(p, phase, 10);
+    if (!mk_wait(&full[sA], (uint32_t)pA, p.err, tr ? &iters : nullptr)) return run;
+    if (tr) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * MK_TRACE_SLOTS + 11] = iters;
+    if (two && !mk_wait(&full[sB], (uint32_t)pB, p.err)) return run;
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
-    Part pa[3];
-    make_parts<MODE>(ph.seg, ph.nseg, c0, c1, pa);
-    if (!two) {
-      chunk_units<MODE>(cx, smem + (size_t)sA * MK_STAGE, c0, c1, pa, act, cw, MK_CW, lane, best_v, best_i);
-    } else {
-      Part pb[3];
-      make_parts<MODE>(ph.seg, ph.nseg, c1, c2, pb);
-      mk_group_units<MODE>(cx, smem + (size_t)sA * MK_STAGE, c0, c1, pa, smem + (size_t)sB * MK_STAGE, c1, c2, pb,
-                           act, cw, lane, best_v, best_i);
+    Part pa[3], pb[3];
+    mk_parts(ph, mode, c0, c1, pa);
+    if (two) mk_parts(ph, mode, c1, c2, pb);
+    const int nA = mk_nunits(mode, c0, c1), U = nA + (two ? mk_nunits(mode, c1, c2) : 0);
+    const uint8_t* stA = smem + (size_t)sA * MK_STAGE;
+    const uint8_t* stB = smem + (size_t)sB * MK_STAGE;
+    for (int g = cw; g < U; g += MK_CW) {
+      const bool inA = g < nA;
+      Part q[3];
+#pragma unroll
+      for (int k = 0; k < 3; k++) q[k] = inA ? pa[k] : pb[k];
+      const UnitRows w = mk_unit(ph, mode, inA ? stA : stB, inA ? c0 : c1, inA ? c1 : c2, q, inA ? g : g - nA);
+      float cs = 0.f, sn = 0.f;
+      if (mode == MODE_QKV && w.si < 2) {  // RoPE factors, loaded before the dots
+        const int hd = p.hd, rr = w.si == 0 ? w.r : w.r - ph.seg[0].rows;
+        const size_t ti = (size_t)pos * (hd >> 1) + ((rr % hd) >> 1);
+        cs = __ldg(p.cos_t + ti);
+        sn = __ldg(p.sin_t + ti);
+      }
+      const float2 d = mk_dot2(w, nb, act, lane);
+      if (lane == 0) {
+        if (mode == MODE_QKV) unit_epilogue<MODE_QKV>(cx, w, d.x, d.y, cs, sn, run.best_v, run.best_i);
+        else if (mode == MODE_GATEUP) unit_epilogue<MODE_GATEUP>(cx, w, d.x, d.y, cs, sn, run.best_v, run.best_i);
+        else if (mode == MODE_HEAD) unit_epilogue<MODE_HEAD>(cx, w, d.x, d.y, cs, sn, run.best_v, run.best_i);
+        else unit_epilogue<MODE_RESID>(cx, w, d.x, d.y, cs, sn, run.best_v, run.best_i);
+      }
     }
     __syncwarp();
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 5);
@@ -585,10 +660,9 @@ __device__ bool mk_chunks(const MkParams& p, const MkPhase& ph, int phase, int p
       mbar_arrive(&empty[sA]);
       if (two) mbar_arrive(&empty[sB]);
     }
-    cidx += two ? 2 : 1;
     c0 = c2;
   }
-  return true;
+  return run;
 }
 
 template <typename KV>
@@ -662,7 +736,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
       float4 kv, vv;
       if (tb + tt == T - 1) {  // this step's row
         unsigned long long kw[4], vw[4];
-        wait_words<false, 4>(p.fkv + (size_t)g * HD + c, want, kw, p.err);
+                wait_words<false, 4>(p.fkv + (size_t)g * HD + c, want, kw, p.err);
         wait_words<false, 4>(p.fkv + ((size_t)p.n_kv + g) * HD + c, want, vw, p.err);
         kv = make_float4(word_val(kw[0]), word_val(kw[1]), word_val(kw[2]), word_val(kw[3]));
         vv = make_float4(word_val(vw[0]), word_val(vw[1]), word_val(vw[2]), word_val(vw[3]));
@@ -728,11 +802,12 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
     }
     named_sync(1, MK_CT);
   }
+  const int y0 = (g * nrep + r0) * HD;  // this unit's rows of y
   if (splits == 1) {
 #pragma unroll
     for (int k = 0; k < MAXE; k++) {
       const int e = tid + k * MK_CT;
-      if (e < nh * HD) st_word_gpu(p.fy + (size_t)(g * nrep + r0) * HD + e, tag_word(tag, o[k] / lrow[e / HD]));
+      if (e < nh * HD) st_word_gpu(p.fy + y0 + e, tag_word(tag, o[k] / lrow[e / HD]));
     }
     return;
   }
@@ -791,15 +866,172 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
 }
 
 // ---------------------------------------------------------------------------
+// Consumer: short-context attention, one unit per query head hq, no tiles or
+// splits (T <= MK_ATT_SHORT_PASSES * positions per pass). Thread (pi, di)
+// holds dims [8 di, 8 di + 8) of positions pi, pi + P, ... (P = positions per
+// pass): the K rows of the cache are loaded into registers before the unit
+// waits for q, each score is a dot over 8 dims reduced across the HD / 8
+// threads of its position, softmax max and sum are block reductions, and the
+// V rows are loaded while those run. P.V partials are reduced across the
+// positions of a warp by shuffles, then across warps in shared memory.
+// ---------------------------------------------------------------------------
+constexpr int MK_ATT_SHORT_PASSES = 4;
+template <int HD>
+__host__ __device__ constexpr int mk_att_short_max_t() { return MK_ATT_SHORT_PASSES * (MK_CT / (HD / 8)); }
+
+template <typename KV>
+__device__ __forceinline__ void kv_load8(const KV* base, size_t idx, float (&v)[8]) {
+  if constexpr (sizeof(KV) == 4) {
+    const float4* s = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + idx);
+    const float4 a = __ldcg(s), b = __ldcg(s + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 r = __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(base) + idx));
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <int HD, typename KV>
+__device__ void mk_attn_short(const MkParams& p, const MkPhase& ph, int phase, int hq, int T, float* sm, int cw,
+                              int lane, uint32_t want, uint32_t tag) {
+  constexpr int TPP = HD / 8;       // threads per position
+  constexpr int PPP = MK_CT / TPP;  // positions per pass
+  constexpr int NP = MK_ATT_SHORT_PASSES;
+  const int tid = cw * 32 + lane, pi = tid / TPP, di = tid % TPP;
+  const int g = hq / (p.n_head / p.n_kv);
+  const int64_t kvbase = (int64_t)g * p.max_seq * HD;
+  const KV* kc = reinterpret_cast<const KV*>(ph.kc) + kvbase;
+  const KV* vc = reinterpret_cast<const KV*>(ph.vc) + kvbase;
+  float* red = sm;               // [2][MK_CW] warp maxima / sums
+  float* opart = sm + 2 * MK_CW; // [MK_CW][HD] P.V partials
+  // K rows written by earlier steps: loads issued before q is awaited
+  float kr[NP][8];
+#pragma unroll
+  for (int k = 0; k < NP; k++) {
+    const int t = pi + k * PPP;
+    if (t < T - 1) kv_load8(kc, (size_t)t * HD + 8 * di, kr[k]);
+  }
+  if (tid == 0) mk_stamp(p, phase, 3);
+  float q[8];
+  {
+    unsigned long long w[8];
+    wait_words<false, 8>(p.fq + (size_t)hq * HD + 8 * di, want, w, p.err);
+#pragma unroll
+    for (int e = 0; e < 8; e++) q[e] = word_val(w[e]);
+  }
+  if (tid == 0) mk_stamp(p, phase, 4);
+  const int tl = T - 1;  // this step's K/V row, from the QKV phase
+  if (tl % PPP == pi) {
+    unsigned long long w[8];
+    wait_words<false, 8>(p.fkv + (size_t)g * HD + 8 * di, want, w, p.err);
+#pragma unroll
+    for (int k = 0; k < NP; k++)
+      if (k == tl / PPP) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) kr[k][e] = word_val(w[e]);
+      }
+  }
+  float sc[NP];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < NP; k++) {
+    float a = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; e++) a += q[e] * kr[k][e];
+#pragma unroll
+    for (int off = TPP / 2; off >= 1; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+    sc[k] = pi + k * PPP < T ? a * p.att_scale : -INFINITY;
+    mx = fmaxf(mx, sc[k]);
+  }
+  if (tid == 0) mk_stamp(p, phase, 5);
+  // V rows: loads issued before the softmax reductions
+  float vr[NP][8];
+#pragma unroll
+  for (int k = 0; k < NP; k++) {
+    const int t = pi + k * PPP;
+    if (t < T - 1) kv_load8(vc, (size_t)t * HD + 8 * di, vr[k]);
+  }
+  if (tl % PPP == pi) {
+    unsigned long long w[8];
+    wait_words<false, 8>(p.fkv + ((size_t)p.n_kv + g) * HD + 8 * di, want, w, p.err);
+#pragma unroll
+    for (int k = 0; k < NP; k++)
+      if (k == tl / PPP) {
+#pragma unroll
+        for (int e = 0; e < 8; e++) vr[k][e] = word_val(w[e]);
+      }
+  }
+#pragma unroll
+  for (int off = 16; off >= TPP; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) red[cw] = mx;
+  named_sync(1, MK_CT);
+  float M = red[0];
+  for (int w = 1; w < MK_CW; w++) M = fmaxf(M, red[w]);
+  if (tid == 0) mk_stamp(p, phase, 6);
+  float l = 0.f, o[8];
+#pragma unroll
+  for (int e = 0; e < 8; e++) o[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < NP; k++) {
+    if (pi + k * PPP < T) {
+      const float pe = expf(sc[k] - M);
+      l += pe;
+#pragma unroll
+      for (int e = 0; e < 8; e++) o[e] += pe * vr[k][e];
+    }
+  }
+  // each position's weight is held by all TPP threads of it: count it once
+#pragma unroll
+  for (int off = 16; off >= TPP; off >>= 1) {
+    l += __shfl_xor_sync(0xffffffffu, l, off);
+#pragma unroll
+    for (int e = 0; e < 8; e++) o[e] += __shfl_xor_sync(0xffffffffu, o[e], off);
+  }
+  if (lane == 0) red[MK_CW + cw] = l;
+  if (lane < TPP) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) opart[cw * HD + 8 * lane + e] = o[e];
+  }
+  named_sync(1, MK_CT);
+  if (tid == 0) mk_stamp(p, phase, 7);
+  if (tid < HD) {
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < MK_CW; w++) {
+      L += red[MK_CW + w];
+      O += opart[w * HD + tid];
+    }
+    st_word_gpu(p.fy + (size_t)hq * HD + tid, tag_word(tag, O / L));
+  }
+  named_sync(1, MK_CT);
+  if (tid == 0) mk_stamp(p, phase, 8);
+}
+
+// ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
 template <int HD, typename KV>
-__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p) {
+__global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_constant__ MkParams params) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_flag;
   __shared__ __align__(16) MkPhase s_ph[2];
   __shared__ int s_pos;  // position of this step's token (constant during the step)
+  // The launch parameters live in shared memory for the whole step: read
+  // through the constant cache, which shares its backing store with the
+  // instruction cache, they missed again and again.
+  __shared__ __align__(16) MkParams p;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(&params);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(&p);
+    for (int w = tid; w < (int)(sizeof(MkParams) / 4); w += blockDim.x) dst[w] = src[w];
+  }
+  __syncthreads();
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
   uint64_t* empty = full + MK_MAX_NS;
   if (tid == 0) {
@@ -819,14 +1051,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
   const int ctid = tid - 32, cw = warp - 1;
   if (ctid == 0) s_pos = (int)__ldcg(p.pos);
   float* xrep = reinterpret_cast<float*>(smem + p.off_xrep);
-  ActQ8 act;
-  int cidx = 0;
+  const ActQ8 act{reinterpret_cast<int8_t*>(smem + p.off_act_qs), reinterpret_cast<float*>(smem + p.off_act_d),
+                  reinterpret_cast<int32_t*>(smem + p.off_act_bs)};
+  MkRun run{0, 0, -INFINITY, 0x7fffffff};
   uint64_t* gbar = empty + MK_MAX_NS;
   uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
   // phase i's outputs carry tag gen + i + 1; its inputs gen + i
   const uint32_t gen = (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.n_ph + 1));
-  float best_v = -INFINITY;
-  int best_i = 0x7fffffff;
+
   for (int i = 0; i < p.n_ph; i++) {
     // Copy the phase descriptor into shared memory (double-buffered by
     // parity: no warp can still read phase i-1's copy once all passed the
@@ -869,6 +1101,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       const int hpu = T <= MK_ATT_PER_HEAD_MAX_T ? 1 : nrep, hsplit = nrep / hpu;
       const int nunits = p.n_kv * hsplit * splits;
       float* asm_ = reinterpret_cast<float*>(smem + p.off_att);
+      if (T <= mk_att_short_max_t<HD>()) {
+        // one unit per query head, spread over the grid
+        for (int u = blockIdx.x; u < p.n_head; u += gridDim.x)
+          mk_attn_short<HD, KV>(p, ph, i, u, T, asm_, cw, lane, want, tag);
+      } else
       for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
         const int hu = u / splits;  // head unit: (KV head, first query head of the unit)
         mk_attn_unit<HD, KV>(p, ph, hu / hsplit, (hu % hsplit) * hpu, hpu, u % splits, splits, T, asm_, cw, lane,
@@ -881,21 +1118,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const MkParams p)
       // a wait that gives up flags the error and goes on (in bounds); all
       // warps leave at the next phase start
       const int mode = mode_of(ph.kind);
-      if (mode == MODE_QKV)
-        mk_chunks<MODE_QKV>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_GATEUP)
-        mk_chunks<MODE_GATEUP>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else if (mode == MODE_HEAD)
-        mk_chunks<MODE_HEAD>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
-      else
-        mk_chunks<MODE_RESID>(p, ph, i, s_pos, tag, smem, full, empty, cidx, act, cw, lane, best_v, best_i);
+      run = mk_chunks(p, ph, mode, i, s_pos, tag, smem, full, empty, run, act, cw, lane);
     }
     if (ctid == 0) mk_stamp(p, i, 2);
   }
   // HEAD: CTA argmax partial, the last CTA reduces all partials.
   float* rv = reinterpret_cast<float*>(smem + p.off_red);
   int* ri = reinterpret_cast<int*>(rv + 32);
-  if (lane == 0) { rv[cw] = best_v; ri[cw] = best_i; }
+  if (lane == 0) { rv[cw] = run.best_v; ri[cw] = run.best_i; }
   named_sync(1, MK_CT);
   if (ctid == 0) {
     float bv = -INFINITY;

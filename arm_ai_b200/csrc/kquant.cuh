@@ -53,28 +53,29 @@ struct ActQ8 {
 // block & 7, which spreads the 32 lanes of a slice load over all banks.
 __device__ __forceinline__ void q8k_quant_block_warp(const float (&v)[8], int lane, int8_t* qs,
                                                      float* d, int32_t* bs, int swz = 0) {
-  float amax = 0.f, mx = 0.f;
-  int idx = 0x7fffffff;
+  // The first value of largest magnitude: |x| compared through its bits
+  // (non-negative floats order as unsigned integers), a NaN never chosen (as
+  // candle's `amax < |x|` never takes one); the warp's largest key, then the
+  // lowest index holding it, then that lane's signed value.
+  uint32_t key = 0u;
+  int ib = 0;
 #pragma unroll
   for (int i = 0; i < 8; i++) {
-    float a = fabsf(v[i]);
-    if (amax < a) {
-      amax = a;
-      mx = v[i];
-      idx = 8 * lane + i;
+    const float a = fabsf(v[i]);
+    const uint32_t k = isnan(a) ? 0u : __float_as_uint(a);
+    if (k > key) {
+      key = k;
+      ib = i;
     }
   }
+  float mine = v[0];
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-    float om = __shfl_xor_sync(0xffffffffu, mx, off);
-    int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-    if (oa > amax || (oa == amax && oi < idx)) {
-      amax = oa;
-      mx = om;
-      idx = oi;
-    }
-  }
+  for (int i = 1; i < 8; i++)
+    if (ib == i) mine = v[i];
+  const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+  const uint32_t first = __reduce_min_sync(0xffffffffu, (kmax != 0u && key == kmax) ? (uint32_t)(8 * lane + ib) : 0xffffffffu);
+  const float amax = __uint_as_float(kmax);
+  const float mx = __shfl_sync(0xffffffffu, mine, (int)((first >> 3) & 31u));
   uint32_t w0 = 0, w1 = 0;
   int32_t s = 0;
   if (amax != 0.f) {

@@ -172,13 +172,13 @@ def llama_bench_kernel(model: LlamaResource, kind: str, rounds: int = 3):
 
 def llama_trace_decode(model: LlamaResource):
     """One decode step of the persistent kernel with per-phase, per-CTA
-    globaltimer stamps: uint64 array [n_phases, n_ctas, 10] (ns)."""
+    globaltimer stamps: uint64 array [n_phases, n_ctas, 12] (ns)."""
     cap = 1 << 20
     buf = np.zeros(cap, dtype=np.uint64)
     nph, nct = ctypes.c_int32(0), ctypes.c_int32(0)
     check(load_cuda().armai_llama_trace_decode(model.handle, buf.ctypes.data, cap, ctypes.byref(nph),
                                                ctypes.byref(nct)))
-    return buf[: nph.value * nct.value * 10].reshape(nph.value, nct.value, 10)
+    return buf[: nph.value * nct.value * 12].reshape(nph.value, nct.value, 12)
 
 
 __all__ = ["llama_bench_kernel", "llama_trace_decode", "llama_generate_batch", "NifError", "LlamaResource", "llama_candle_load_op", "llama_candle_generate_op",
