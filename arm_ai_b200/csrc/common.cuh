@@ -48,8 +48,17 @@ enum : uint32_t {
 constexpr int QK_K = 256;
 constexpr int GGML_F32 = 0;
 constexpr int GGML_F16 = 1;
+constexpr int GGML_Q4_0 = 2;
+constexpr int GGML_Q5_0 = 6;
+constexpr int GGML_Q8_0 = 8;
 constexpr int GGML_Q4_K = 12;
+constexpr int GGML_Q5_K = 13;
 constexpr int GGML_Q6_K = 14;
+constexpr int QK8_0 = 32;              // values per legacy block (Q4_0 / Q5_0 / Q8_0)
+constexpr int Q4_0_BLOCK_BYTES = 18;   // f16 d, 16 B nibbles
+constexpr int Q5_0_BLOCK_BYTES = 22;   // f16 d, 4 B high bits, 16 B nibbles
+constexpr int Q8_0_BLOCK_BYTES = 34;   // f16 d, 32 i8
+constexpr int Q5K_BLOCK_BYTES = 176;   // f16 d, f16 dmin, 12 B scales, 32 B qh, 128 B qs
 constexpr int Q4K_BLOCK_BYTES = 144;  // f16 d, f16 dmin, 12 B scales, 128 B qs
 constexpr int Q6K_BLOCK_BYTES = 210;  // 128 B ql, 64 B qh, 16 i8 scales, f16 d
 // Q6_K as laid out in HBM: per row, nb blocks of [ql|qh|scales] (208 B each)
@@ -57,10 +66,23 @@ constexpr int Q6K_BLOCK_BYTES = 210;  // 128 B ql, 64 B qh, 16 i8 scales, f16 d
 // then a 16-byte-aligned unit for bulk (TMA) copies.
 constexpr int Q6K_BODY_BYTES = 208;
 inline int64_t q6k_dpad_bytes(int64_t nb) { return ((nb * 2 + 15) / 16) * 16; }
+// The weight types whose dot products take a Q8_K activation (k-quants) or
+// a Q8_0 activation (legacy 32-value blocks), as candle's VecDotType.
+__host__ __device__ inline bool is_kquant(int type) {
+  return type == GGML_Q4_K || type == GGML_Q5_K || type == GGML_Q6_K;
+}
+__host__ __device__ inline bool is_legacy(int type) {
+  return type == GGML_Q4_0 || type == GGML_Q5_0 || type == GGML_Q8_0;
+}
+__host__ __device__ inline int legacy_block_bytes(int type) {
+  return type == GGML_Q4_0 ? Q4_0_BLOCK_BYTES : type == GGML_Q5_0 ? Q5_0_BLOCK_BYTES : Q8_0_BLOCK_BYTES;
+}
 inline int64_t dev_row_bytes(int type, int64_t k) {
   const int64_t nb = k / QK_K;
   if (type == GGML_Q4_K) return nb * Q4K_BLOCK_BYTES;
+  if (type == GGML_Q5_K) return nb * Q5K_BLOCK_BYTES;
   if (type == GGML_Q6_K) return nb * Q6K_BODY_BYTES + q6k_dpad_bytes(nb);
+  if (is_legacy(type)) return (k / QK8_0) * legacy_block_bytes(type);
   if (type == GGML_F32) return 4 * k;
   return -1;
 }

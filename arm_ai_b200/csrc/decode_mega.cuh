@@ -60,6 +60,7 @@ struct MkPhase {
   int rows_per_cta;   // multiple of 2 for QKV
   int chunk_rows;     // multiple of 2 for QKV
   int K, nb;
+  int acts;           // activations the rows need: 1 Q8_K (k-quants), 2 Q8_0 (legacy types)
   const float* gamma; // rmsnorm weight, or nullptr
   float* out;         // HEAD: logits (nullptr: not kept)
   void* kc;           // layer KV cache
@@ -94,6 +95,7 @@ struct MkParams {
   uint32_t* err;
   unsigned long long* trace;  // nullptr, or [n_ph][grid][MK_TRACE_SLOTS] globaltimer stamps
   size_t off_bars, off_act_qs, off_act_d, off_act_bs, off_red, off_att;  // smem layout
+  size_t off_act0_qs, off_act0_d, off_act0_s;  // Q8_0 activation (0: no phase needs one)
   int kmax;
   size_t off_xrep;  // smem: this CTA's copy of the residual stream x [n_embd]
   unsigned long long* epoch;            // decode steps completed (generation base)
@@ -245,31 +247,7 @@ struct F8 {
 __device__ __forceinline__ F8 mk_embed_vals(const MkParams& p, int j, int lane, int nb) {
   F8 out;
   const uint32_t tok = min(__ldcg(p.token), (uint32_t)(0x7fffffff));
-  const uint8_t* row = p.embd + (int64_t)tok * p.embd_row_bytes;
-#pragma unroll
-  for (int k = 0; k < 8; k++) {
-    const int i = 8 * lane + k;
-    if (p.embd_type == GGML_Q4_K) {
-      const uint8_t* blk = row + (int64_t)j * Q4K_BLOCK_BYTES;
-      const int c = i / 64, l = i % 64, sj = 2 * c + (l >= 32);
-      const uint8_t byte = blk[16 + 32 * c + (l & 31)];
-      const int q = l >= 32 ? (byte >> 4) : (byte & 0xF);
-      int sc, m;
-      q4k_scale_min(blk + 4, sj, sc, m);
-      const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
-      const float dmin = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
-      out.v[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
-    } else {
-      const uint8_t* body = row + (int64_t)j * Q6K_BODY_BYTES;
-      const uint16_t* dv = reinterpret_cast<const uint16_t*>(row + (int64_t)nb * Q6K_BODY_BYTES);
-      const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
-      const uint8_t qlb = body[64 * n + l + (g & 1) * 32];
-      const int lo = (g < 2) ? (qlb & 0xF) : (qlb >> 4);
-      const int hi = (body[128 + 32 * n + l] >> (2 * g)) & 3;
-      const int8_t sc = reinterpret_cast<const int8_t*>(body + 192)[8 * n + l / 16 + 2 * g];
-      out.v[k] = __fmul_rn(__fmul_rn(h2f(dv[j]), (float)sc), (float)((lo | (hi << 4)) - 32));
-    }
-  }
+  dequant8(p.embd_type, p.embd + (int64_t)tok * p.embd_row_bytes, nb, j, lane, out.v);
   return out;
 }
 
@@ -464,7 +442,8 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
 #pragma unroll
       for (int k = 0; k < 8; k++) vv[k] = __fmul_rn(__fdiv_rn(vv[k], m), g[k]);
     }
-    q8k_quant_block_warp(vv, lane, act.qs + j * QK_K, act.d + j, act.bs + j * 16, j & 7);
+    if (ph.acts & 1) q8k_quant_block_warp(vv, lane, act.qs + j * QK_K, act.d + j, act.bs + j * 16, j & 7);
+    if (ph.acts & 2) q80_quant_block_warp(vv, lane, act.qs0 + j * QK_K, act.d0 + 8 * j, act.s0 + 8 * j, j & 7);
   }
   named_sync(1, MK_CT);
 }
@@ -563,27 +542,10 @@ __device__ __forceinline__ UnitRows mk_unit(const MkPhase& ph, int mode, const u
   }
   return w;
 }
-// Both dot products of a unit; each row's type dispatched per quarter (the
-// type is the same for the whole warp).
+// Both dot products of a unit (row_pair_dots: each row's type dispatched at
+// run time; the Q4_K / Q6_K rows of a Q4_K_M model take the first branches).
 __device__ __forceinline__ float2 mk_dot2(const UnitRows& w, int nb, const ActQ8& act, int lane) {
-  const int t = lane & 3, bl = lane >> 2;
-  float a0 = 0.f, a1 = 0.f;
-  const int npass = (nb + 7) >> 3;
-  for (int ps = 0; ps < npass; ps++) {
-    const int blk = ps * 8 + bl;
-    if (blk < nb) {
-      ActSlice A;
-      load_slice(act, blk, t, A);
-      a0 += quarter_dot(w.ty0, w.p0, nb, blk, t, A);
-      if (w.has1) a1 += quarter_dot(w.ty1, w.p1, nb, blk, t, A);
-    }
-  }
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    a0 += __shfl_xor_sync(0xffffffffu, a0, off);
-    a1 += __shfl_xor_sync(0xffffffffu, a1, off);
-  }
-  return make_float2(a0, a1);
+  return row_pair_dots(w.ty0, w.p0, w.ty1, w.p1, w.has1, nb, act, lane);
 }
 
 // Per-warp state carried from phase to phase: the ring position (stage,
@@ -1052,7 +1014,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
   if (ctid == 0) s_pos = (int)__ldcg(p.pos);
   float* xrep = reinterpret_cast<float*>(smem + p.off_xrep);
   const ActQ8 act{reinterpret_cast<int8_t*>(smem + p.off_act_qs), reinterpret_cast<float*>(smem + p.off_act_d),
-                  reinterpret_cast<int32_t*>(smem + p.off_act_bs)};
+                  reinterpret_cast<int32_t*>(smem + p.off_act_bs), reinterpret_cast<int8_t*>(smem + p.off_act0_qs),
+                  reinterpret_cast<float*>(smem + p.off_act0_d), reinterpret_cast<int32_t*>(smem + p.off_act0_s)};
   MkRun run{0, 0, -INFINITY, 0x7fffffff};
   uint64_t* gbar = empty + MK_MAX_NS;
   uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)

@@ -40,6 +40,12 @@ struct ActQ8 {
   int8_t* qs;
   float* d;
   int32_t* bs;
+  // The same values as candle's Q8_0 (the VecDotType of Q4_0 / Q5_0 /
+  // Q8_0 weights): qs0[k] int8, d0[k/32] the f16 scale as f32, s0[k/32] the
+  // block's sum of qs0. nullptr when no matrix of the phase needs them.
+  int8_t* qs0;
+  float* d0;
+  int32_t* s0;
 };
 
 // One 256-value Q8_K block, computed by one warp. Lane l owns values
@@ -97,6 +103,40 @@ __device__ __forceinline__ void q8k_quant_block_warp(const float (&v)[8], int la
   reinterpret_cast<uint2*>(qs)[(((lane >> 1) ^ swz) << 1) | (lane & 1)] = make_uint2(w0, w1);
   s += __shfl_xor_sync(0xffffffffu, s, 1);
   if ((lane & 1) == 0) bs[lane >> 1] = s;
+}
+
+// The same 256 values as eight Q8_0 blocks of 32 (lanes 4b..4b+3 hold block
+// b). Matches BlockQ8_0::from_float: d = amax / 127 (amax ignores NaN, as
+// f32::max does), id = 1/d (0 when d is 0), q = round_half_away(x * id)
+// saturated to i8 (NaN -> 0, as `as i8`), d kept as f16. Same chunk swizzle
+// as the Q8_K bytes.
+__device__ __forceinline__ void q80_quant_block_warp(const float (&v)[8], int lane, int8_t* qs, float* d,
+                                                     int32_t* s, int swz = 0) {
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float dd = __fdiv_rn(amax, 127.0f);
+  const float id = dd != 0.f ? __fdiv_rn(1.0f, dd) : 0.f;
+  uint32_t w0 = 0, w1 = 0;
+  int32_t sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float r = roundf(__fmul_rn(v[i], id));
+    const int q = isnan(r) ? 0 : (int)fmaxf(fminf(r, 127.f), -128.f);
+    sum += q;
+    const uint32_t b = (uint32_t)(q & 0xff);
+    if (i < 4) w0 |= b << (8 * i);
+    else w1 |= b << (8 * (i - 4));
+  }
+  reinterpret_cast<uint2*>(qs)[(((lane >> 1) ^ swz) << 1) | (lane & 1)] = make_uint2(w0, w1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if ((lane & 3) == 0) {
+    d[lane >> 2] = __half2float(__float2half_rn(dd));
+    s[lane >> 2] = sum;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -224,13 +264,205 @@ __device__ __forceinline__ int q6k_quarter(const uint8_t* body, int t, const Act
   return tot;
 }
 
+// Integers of one Q5_K quarter: Q4_K's plus the fifth bit of each value
+// (qh byte l, bit 2t for the low nibbles, 2t + 1 for the high), as
+// BlockQ5K::vec_dot; the same scales / mins and combine as Q4_K.
+__device__ __forceinline__ void q5k_quarter(const uint8_t* blk, int t, const ActSlice& A, int& isum, int& msum,
+                                            float& dx, float& dmx) {
+  const int4 hd = *reinterpret_cast<const int4*>(blk);
+  const int4 h0 = *reinterpret_cast<const int4*>(blk + 16);
+  const int4 h1 = *reinterpret_cast<const int4*>(blk + 32);
+  const int4 qa = *reinterpret_cast<const int4*>(blk + 48 + 32 * t);
+  const int4 qb = *reinterpret_cast<const int4*>(blk + 64 + 32 * t);
+  const uint32_t w[8] = {(uint32_t)qa.x, (uint32_t)qa.y, (uint32_t)qa.z, (uint32_t)qa.w,
+                         (uint32_t)qb.x, (uint32_t)qb.y, (uint32_t)qb.z, (uint32_t)qb.w};
+  const uint32_t h[8] = {(uint32_t)h0.x, (uint32_t)h0.y, (uint32_t)h0.z, (uint32_t)h0.w,
+                         (uint32_t)h1.x, (uint32_t)h1.y, (uint32_t)h1.z, (uint32_t)h1.w};
+  int dlo = 0, dhi16 = 0, blo = 0, bhi = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    dlo = __dp4a((int)(w[i] & 0x0F0F0F0Fu), (int)A.q[i], dlo);
+    dhi16 = dp4a_us(w[i] & 0xF0F0F0F0u, A.q[8 + i], dhi16);
+    blo = __dp4a((int)((h[i] >> (2 * t)) & 0x01010101u), (int)A.q[i], blo);
+    bhi = __dp4a((int)((h[i] >> (2 * t + 1)) & 0x01010101u), (int)A.q[8 + i], bhi);
+  }
+  const int vlo = dlo + 16 * blo, vhi = (dhi16 >> 4) + 16 * bhi;
+  const uint32_t s03 = (uint32_t)hd.y, s47 = (uint32_t)hd.z, s811 = (uint32_t)hd.w;
+  const uint32_t scw = t < 2 ? (s03 & 0x3f3f3f3fu) : ((s811 & 0x0f0f0f0fu) | ((s03 >> 2) & 0x30303030u));
+  const uint32_t mw = t < 2 ? (s47 & 0x3f3f3f3fu) : (((s811 >> 4) & 0x0f0f0f0fu) | ((s47 >> 2) & 0x30303030u));
+  const int sh = 16 * (t & 1);
+  const int sa = (int)((scw >> sh) & 0xffu), sb = (int)((scw >> (sh + 8)) & 0xffu);
+  const int ma = (int)((mw >> sh) & 0xffu), mb = (int)((mw >> (sh + 8)) & 0xffu);
+  isum = sa * vlo + sb * vhi;
+  msum = ma * (A.bs[0] + A.bs[1]) + mb * (A.bs[2] + A.bs[3]);
+  dx = h2f((uint16_t)((uint32_t)hd.x & 0xffffu));
+  dmx = h2f((uint16_t)((uint32_t)hd.x >> 16));
+}
+
+// Q8_0 activation slice of lane (super-block blk, quarter t): values
+// [256 blk + 64 t, + 64) = legacy blocks 8 blk + 2t and 8 blk + 2t + 1.
+struct ActSlice0 {
+  uint32_t q[16];
+  float d[2];
+  int s[2];
+};
+__device__ __forceinline__ void load_slice0(const ActQ8& a, int blk, int t, ActSlice0& s) {
+  const int4* qv = reinterpret_cast<const int4*>(a.qs0 + (size_t)blk * QK_K);
+  const int swz = blk & 7;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int4 v = qv[(4 * t + i) ^ swz];
+    s.q[4 * i] = (uint32_t)v.x;
+    s.q[4 * i + 1] = (uint32_t)v.y;
+    s.q[4 * i + 2] = (uint32_t)v.z;
+    s.q[4 * i + 3] = (uint32_t)v.w;
+  }
+  const float2 dd = *reinterpret_cast<const float2*>(a.d0 + 8 * blk + 2 * t);
+  const int2 ss = *reinterpret_cast<const int2*>(a.s0 + 8 * blk + 2 * t);
+  s.d[0] = dd.x;
+  s.d[1] = dd.y;
+  s.s[0] = ss.x;
+  s.s[1] = ss.y;
+}
+
+// Words [i0, i0 + n) of a byte sequence that starts 2 bytes past a 4-byte
+// boundary (w = the aligned words covering it).
+__device__ __forceinline__ uint32_t shr16(uint32_t lo, uint32_t hi) { return __funnelshift_r(lo, hi, 16); }
+
+// One lane's share of a legacy-type row against the Q8_0 activation: two
+// 32-value blocks, each sumf += (float)sumi * d_x * d_y in candle's order
+// (k_quants.rs BlockQ4_0 / BlockQ5_0 / BlockQ8_0 ::vec_dot); the two blocks'
+// terms are added here and across lanes afterwards. `row` is 4-byte aligned
+// (rows start 16-byte aligned; two blocks span a multiple of 4 bytes).
+__device__ __forceinline__ float legacy_pair_dot(int type, const uint8_t* row, int blk, int t, const ActSlice0& B) {
+  const int bb = legacy_block_bytes(type);
+  const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + (size_t)(8 * blk + 2 * t) * bb);
+  int sumi[2];
+  float dx[2];
+  if (type == GGML_Q4_0) {  // 36 bytes: d | 16 qs | d | 16 qs
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; i++) w[i] = wp[i];
+    const uint32_t qa[4] = {shr16(w[0], w[1]), shr16(w[1], w[2]), shr16(w[2], w[3]), shr16(w[3], w[4])};
+    const uint32_t qb[4] = {w[5], w[6], w[7], w[8]};
+    dx[0] = h2f((uint16_t)(w[0] & 0xffffu));
+    dx[1] = h2f((uint16_t)(w[4] >> 16));
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t* q = h ? qb : qa;
+      int acc = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        acc = __dp4a((int)(q[i] & 0x0F0F0F0Fu), (int)B.q[8 * h + i], acc);
+        acc = __dp4a((int)((q[i] >> 4) & 0x0F0F0F0Fu), (int)B.q[8 * h + 4 + i], acc);
+      }
+      sumi[h] = acc - 8 * B.s[h];
+    }
+  } else if (type == GGML_Q5_0) {  // 44 bytes: d | qh(4) | 16 qs | d | qh(4) | 16 qs
+    uint32_t w[11];
+#pragma unroll
+    for (int i = 0; i < 11; i++) w[i] = wp[i];
+    const uint32_t qha = shr16(w[0], w[1]);
+    const uint32_t qa[4] = {shr16(w[1], w[2]), shr16(w[2], w[3]), shr16(w[3], w[4]), shr16(w[4], w[5])};
+    const uint32_t qhb = w[6];
+    const uint32_t qb[4] = {w[7], w[8], w[9], w[10]};
+    dx[0] = h2f((uint16_t)(w[0] & 0xffffu));
+    dx[1] = h2f((uint16_t)(w[5] >> 16));
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const uint32_t* q = h ? qb : qa;
+      const uint32_t qh = h ? qhb : qha;
+      int acc = 0;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        // bit j of qh -> bit 4 of value j's byte (values 4i..4i+3), and
+        // bit j + 16 for the high nibbles
+        const uint32_t lo = (q[i] & 0x0F0F0F0Fu) | ((((qh >> (4 * i)) & 0xFu) * 0x00204081u & 0x01010101u) << 4);
+        const uint32_t hi = ((q[i] >> 4) & 0x0F0F0F0Fu) |
+                            ((((qh >> (16 + 4 * i)) & 0xFu) * 0x00204081u & 0x01010101u) << 4);
+        acc = __dp4a((int)lo, (int)B.q[8 * h + i], acc);
+        acc = __dp4a((int)hi, (int)B.q[8 * h + 4 + i], acc);
+      }
+      sumi[h] = acc - 16 * B.s[h];
+    }
+  } else {  // Q8_0, 68 bytes: d | 32 qs | d | 32 qs
+    uint32_t w[17];
+#pragma unroll
+    for (int i = 0; i < 17; i++) w[i] = wp[i];
+    dx[0] = h2f((uint16_t)(w[0] & 0xffffu));
+    dx[1] = h2f((uint16_t)(w[8] >> 16));
+    int a = 0, b = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      a = __dp4a((int)shr16(w[i], w[i + 1]), (int)B.q[i], a);
+      b = __dp4a((int)w[9 + i], (int)B.q[8 + i], b);
+    }
+    sumi[0] = a;
+    sumi[1] = b;
+  }
+  return __fmul_rn(__fmul_rn((float)sumi[0], dx[0]), B.d[0]) + __fmul_rn(__fmul_rn((float)sumi[1], dx[1]), B.d[1]);
+}
+
+// Values [8 lane, 8 lane + 8) of 256-value group j of a device row (token
+// embedding rows), each as the type's to_float computes it.
+__device__ __forceinline__ void dequant8(int type, const uint8_t* row, int nb, int j, int lane, float (&out)[8]) {
+  if (is_legacy(type)) {
+    const int bb = legacy_block_bytes(type);
+    const uint8_t* blk = row + (size_t)(8 * j + (lane >> 2)) * bb;
+    const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+    uint32_t qh = 0;
+    if (type == GGML_Q5_0) qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+    const uint8_t* qs = blk + (type == GGML_Q5_0 ? 6 : 2);
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int v = 8 * (lane & 3) + k;  // value within the 32-block
+      int q;
+      if (type == GGML_Q8_0) {
+        q = (int)(int8_t)qs[v];
+      } else {
+        const int nib = v < 16 ? (qs[v] & 0xF) : (qs[v - 16] >> 4);
+        q = type == GGML_Q4_0 ? nib - 8 : (nib | (int)(((qh >> v) & 1u) << 4)) - 16;
+      }
+      out[k] = __fmul_rn((float)q, d);
+    }
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k++) {
+    const int i = 8 * lane + k;
+    if (type == GGML_Q4_K || type == GGML_Q5_K) {
+      const int bb = type == GGML_Q4_K ? Q4K_BLOCK_BYTES : Q5K_BLOCK_BYTES, qo = type == GGML_Q4_K ? 16 : 48;
+      const uint8_t* blk = row + (int64_t)j * bb;
+      const int c = i / 64, l = i % 64, sj = 2 * c + (l >= 32);
+      const uint8_t byte = blk[qo + 32 * c + (l & 31)];
+      int q = l >= 32 ? (byte >> 4) : (byte & 0xF);
+      if (type == GGML_Q5_K) q += ((blk[16 + (l & 31)] >> sj) & 1) << 4;
+      int sc, m;
+      q4k_scale_min(blk + 4, sj, sc, m);
+      const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+      const float dmin = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
+      out[k] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)m));
+    } else {
+      const uint8_t* body = row + (int64_t)j * Q6K_BODY_BYTES;
+      const uint16_t* dv = reinterpret_cast<const uint16_t*>(row + (int64_t)nb * Q6K_BODY_BYTES);
+      const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
+      const uint8_t qlb = body[64 * n + l + (g & 1) * 32];
+      const int lo = (g < 2) ? (qlb & 0xF) : (qlb >> 4);
+      const int hi = (body[128 + 32 * n + l] >> (2 * g)) & 3;
+      const int8_t sc = reinterpret_cast<const int8_t*>(body + 192)[8 * n + l / 16 + 2 * g];
+      out[k] = __fmul_rn(__fmul_rn(h2f(dv[j]), (float)sc), (float)((lo | (hi << 4)) - 32));
+    }
+  }
+}
+
 // One lane's f32 share of <weight row, activation> over pass `pass`.
 __device__ __forceinline__ float quarter_dot(int type, const uint8_t* row, int nb, int blk, int t,
                                              const ActSlice& A) {
-  if (type == GGML_Q4_K) {
+  if (type == GGML_Q4_K || type == GGML_Q5_K) {
     int is, ms;
     float dx, dmx;
-    q4k_quarter(row + (size_t)blk * Q4K_BLOCK_BYTES, t, A, is, ms, dx, dmx);
+    if (type == GGML_Q4_K) q4k_quarter(row + (size_t)blk * Q4K_BLOCK_BYTES, t, A, is, ms, dx, dmx);
+    else q5k_quarter(row + (size_t)blk * Q5K_BLOCK_BYTES, t, A, is, ms, dx, dmx);
     return __fmul_rn(dx, A.dy) * (float)is - __fmul_rn(dmx, A.dy) * (float)ms;
   }
   const uint16_t dh = reinterpret_cast<const uint16_t*>(row + (size_t)nb * Q6K_BODY_BYTES)[blk];
@@ -251,6 +483,49 @@ __device__ __forceinline__ float quarter_dot_t(const uint8_t* row, int nb, int b
     const uint16_t dh = reinterpret_cast<const uint16_t*>(row + (size_t)nb * Q6K_BODY_BYTES)[blk];
     return __fmul_rn(h2f(dh), A.dy) * (float)q6k_quarter(row + (size_t)blk * Q6K_BODY_BYTES, t, A);
   }
+}
+
+// Both dot products of a row pair of any supported types (each row's type
+// is the same for the whole warp): k-quant rows against the Q8_K slice,
+// legacy rows against the Q8_0 slice; the per-lane shares are then summed
+// across the warp. Shared by the persistent kernel and the per-kernel chain's
+// generic path.
+__device__ __forceinline__ float2 row_pair_dots(int ty0, const uint8_t* p0, int ty1, const uint8_t* p1, bool has1,
+                                                int nb, const ActQ8& act, int lane) {
+  const int t = lane & 3, bl = lane >> 2;
+  const bool k0 = is_kquant(ty0), k1 = has1 && is_kquant(ty1);
+  const bool l0 = !k0, l1 = has1 && !k1;
+  float a0 = 0.f, a1 = 0.f;
+  const int npass = (nb + 7) >> 3;
+  // one loop per activation type, so that only one slice is live at a time
+  if (k0 || k1) {
+    for (int ps = 0; ps < npass; ps++) {
+      const int blk = ps * 8 + bl;
+      if (blk < nb) {
+        ActSlice A;
+        load_slice(act, blk, t, A);
+        if (k0) a0 += quarter_dot(ty0, p0, nb, blk, t, A);
+        if (k1) a1 += quarter_dot(ty1, p1, nb, blk, t, A);
+      }
+    }
+  }
+  if (l0 || l1) {
+    for (int ps = 0; ps < npass; ps++) {
+      const int blk = ps * 8 + bl;
+      if (blk < nb) {
+        ActSlice0 B;
+        load_slice0(act, blk, t, B);
+        if (l0) a0 += legacy_pair_dot(ty0, p0, blk, t, B);
+        if (l1) a1 += legacy_pair_dot(ty1, p1, blk, t, B);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, off);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, off);
+  }
+  return make_float2(a0, a1);
 }
 
 }  // namespace armai

@@ -185,6 +185,7 @@ int qmm_launch(const uint8_t* w, int type, int n, int k, int rb, const float* x,
   p.nb = k / QK_K;
   p.seg[0] = Seg{w, type, n, k / QK_K, rb};
   p.nseg = 1;
+  p.acts = is_legacy(type) ? 2 : 1;
   p.total_rows = n;
   p.nrows = NB;
   p.rows_per_cta = per;

@@ -98,6 +98,7 @@ struct armai_llama {
   float* pG = nullptr;         // GEMM output [cap][g_cols]
   int g_cols = 0;
   int prefill_gemm = 0;        // armai_llama_opts.prefill_gemm
+  bool q80 = false;            // a matrix takes Q8_0 activations (Q4_0 / Q5_0 / Q8_0)
   // tensor parallelism (tp > 1): this rank holds a slice of every matrix, the
   // residual stream x is replicated, row-split products are summed by NCCL
   int tp = 1, tp_rank = 0;
@@ -138,6 +139,14 @@ struct armai_llama {
 
 namespace {
 
+// Activations a launch's rows need (candle's VecDotType): bit 1 Q8_K for
+// k-quant rows, bit 2 Q8_0 for legacy-type rows.
+int seg_acts(const Seg* seg, int nseg) {
+  int a = 0;
+  for (int i = 0; i < nseg; i++) a |= is_legacy(seg[i].type) ? 2 : 1;
+  return a;
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                      bool pdl, Args&&... args) {
@@ -157,14 +166,14 @@ cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
 // Row plan for a k_matvec launch: contiguous row ranges per CTA, chunks that
 // fit a stage, a ring of up to 3 stages within the shared-memory budget.
 Plan make_plan(int total_rows, int unit, int row_bytes_per_unit_row, int rows_per_unit_in_stage,
-               int K, int NB, bool norm, int nsm, size_t budget) {
+               int K, int NB, bool norm, int nsm, size_t budget, bool q80) {
   Plan p;
   // rows of the virtual row space per CTA, rounded up to `unit`
   int per = (total_rows + nsm - 1) / nsm;
   per = ((per + unit - 1) / unit) * unit;
   p.rows_per_cta = per;
   p.grid = (total_rows + per - 1) / per;
-  const size_t act = mv_smem_layout(0, 0, K, NB, norm).total;
+  const size_t act = mv_smem_layout(0, 0, K, NB, norm, q80).total;
   const size_t unit_bytes = (size_t)row_bytes_per_unit_row * rows_per_unit_in_stage;  // bytes per row of the chunk
   const size_t room = budget > act + 1024 ? budget - act - 1024 : 0;
   size_t stage_cap = std::min<size_t>(STAGE_MAX, room);
@@ -178,7 +187,7 @@ Plan make_plan(int total_rows, int unit, int row_bytes_per_unit_row, int rows_pe
   int ns = std::min(nchunks, 3);
   while (ns > 1 && act + (size_t)ns * p.stage_bytes + 1024 > budget) ns--;
   p.ns = ns;
-  p.smem = mv_smem_layout(ns, p.stage_bytes, K, NB, norm).total;
+  p.smem = mv_smem_layout(ns, p.stage_bytes, K, NB, norm, q80).total;
   return p;
 }
 
@@ -238,6 +247,7 @@ cudaError_t launch_qkv(armai_llama* m, const Plan& pl, int l, const float* x, fl
   p.seg[1] = L.wk.seg();
   p.seg[2] = L.wv.seg();
   p.nseg = 3;
+  p.acts = seg_acts(p.seg, p.nseg);
   p.qn = L.wq.rows;
   p.kn = L.wk.rows;
   p.total_rows = L.wq.rows + L.wk.rows + L.wv.rows;
@@ -260,6 +270,7 @@ cudaError_t launch_resid(armai_llama* m, const Plan& pl, const DevMat& w, const 
   p.nb = w.cols / QK_K;
   p.seg[0] = w.seg();
   p.nseg = 1;
+  p.acts = seg_acts(p.seg, p.nseg);
   p.total_rows = w.rows;
   p.out = x;
   p.out_stride = m->n_embd;
@@ -278,6 +289,7 @@ cudaError_t launch_gateup(armai_llama* m, const Plan& pl, int l, const float* x,
   p.seg[0] = L.wg.seg();
   p.seg[1] = L.wu.seg();
   p.nseg = 2;
+  p.acts = seg_acts(p.seg, p.nseg);
   p.total_rows = L.wg.rows;
   p.out = h;
   p.out_stride = m->n_ff;
@@ -296,6 +308,7 @@ cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const in
   p.nb = m->n_embd / QK_K;
   p.seg[0] = m->output.seg();
   p.nseg = 1;
+  p.acts = seg_acts(p.seg, p.nseg);
   p.total_rows = m->output.rows;
   p.out = m->logits;
   p.out_stride = m->n_vocab;
@@ -458,6 +471,7 @@ int setup_mega(armai_llama* m, int nsm) {
     int i = 0;
     for (const DevMat* d : mats) p.seg[i++] = d->seg();
     p.nseg = i;
+    p.acts = seg_acts(p.seg, p.nseg);
     p.total_rows = total;
     p.rows_per_cta = per_cta(total, unit);
     p.chunk_rows = chunk_for(unit_bytes, unit, p.rows_per_cta);
@@ -497,9 +511,11 @@ int setup_mega(armai_llama* m, int nsm) {
   const int nrep = m->n_head / m->n_head_kv;
   // the attention region also holds the staged rmsnorm weights (n_embd f32)
   const size_t att_bytes = std::max(mk_att_floats(m->head_dim, nrep) * 4, (size_t)m->n_embd * 4) + 64;
+  // Q8_0 activation buffers only when a matrix takes them (legacy types)
+  const size_t act0 = m->q80 ? al16((size_t)kmax) + 2 * al16((size_t)kmax / QK8_0 * 4) : 0;
   size_t fixed = al16((size_t)(2 * MK_MAX_NS + 1) * 8) + al16((size_t)kmax) + al16((size_t)kmax / QK_K * 4) +
                  al16((size_t)kmax / 16 * 4) + al16((64 + (size_t)kmax / QK_K + 8) * 4) + al16(att_bytes) +
-                 al16((size_t)E * 4);
+                 al16((size_t)E * 4) + act0;
   // 2 KB of headroom for the kernel's static shared memory (phase copies etc.)
   int ns = (int)std::min<size_t>(MK_MAX_NS, (SMEM_LIMIT - fixed - 2048) / MK_STAGE);
   if (ns < 2) return fail(ARMAI_E_INVALID, "persistent decode kernel: not enough shared memory");
@@ -512,6 +528,11 @@ int setup_mega(armai_llama* m, int nsm) {
   k.off_red = o;    o += al16((64 + (size_t)kmax / QK_K + 8) * 4);
   k.off_att = o;    o += al16(att_bytes);
   k.off_xrep = o;   o += al16((size_t)E * 4);
+  if (m->q80) {
+    k.off_act0_qs = o; o += al16((size_t)kmax);
+    k.off_act0_d = o;  o += al16((size_t)kmax / QK8_0 * 4);
+    k.off_act0_s = o;  o += al16((size_t)kmax / QK8_0 * 4);
+  }
   m->mk_smem = o;
   k.kmax = kmax;
   // Tagged words, zeroed (tag 0 is never awaited): q, the K/V row, y, h,
@@ -625,6 +646,7 @@ int rowsplit_resid(armai_llama* m, const Plan& pl, const DevMat& w, const float*
     p.nb = w.cols / QK_K;
     p.seg[0] = w.seg();
     p.nseg = 1;
+    p.acts = seg_acts(p.seg, p.nseg);
     p.total_rows = w.rows;
     p.out = m->tp_part;
     p.out_stride = m->n_embd;
@@ -847,6 +869,7 @@ int rowsplit_resid_batch(armai_llama* m, const Plan& pl, const DevMat& w, const 
       p.nb = w.cols / QK_K;
       p.seg[0] = w.seg();
       p.nseg = 1;
+      p.acts = seg_acts(p.seg, p.nseg);
       p.total_rows = w.rows;
       p.out = m->tp_part + g * E;
       p.out_stride = m->n_embd;
@@ -1153,9 +1176,9 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     const GgufTensor* t = find(name);
     if (!t) return fail(ARMAI_E_FORMAT, "ModelWeights::from_gguf failed: cannot find tensor info for " + name);
     if (t->dims.size() != 2) return fail(ARMAI_E_FORMAT, "tensor " + name + " is not 2-D");
-    if (t->type != GGML_Q4_K && t->type != GGML_Q6_K)
+    if (!is_kquant((int)t->type) && !is_legacy((int)t->type))
       return fail(ARMAI_E_FORMAT, std::string("tensor ") + name + " has type " + ggml_type_name(t->type) +
-                                      "; this build supports Q4_K and Q6_K matrices");
+                                      "; this build supports Q4_0, Q5_0, Q8_0, Q4_K, Q5_K and Q6_K matrices");
     if ((want_cols > 0 && t->cols() != want_cols) || (want_rows > 0 && t->rows() != want_rows))
       return fail(ARMAI_E_FORMAT, "tensor " + name + " has an unexpected shape");
     dm.type = (int)t->type;
@@ -1243,6 +1266,29 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     if (!rc && (m->n_ff % QK_K)) rc = fail(ARMAI_E_FORMAT, "feed-forward length must be a multiple of 256");
   }
   if (rc != ARMAI_OK) { delete m; return rc; }
+  // Matrices other than Q4_K / Q6_K (Q5_K, and the legacy Q4_0 / Q5_0 /
+  // Q8_0 whose dot products take Q8_0 activations): their prompts run the
+  // integer per-kernel chain, as candle computes them, not the tensor-core
+  // GEMM (whose shared activation operand serves one activation type).
+  {
+    std::vector<const DevMat*> mats{&m->tok_embd};
+    if (find("output.weight")) mats.push_back(&m->output);
+    for (const Layer& L : m->layers)
+      for (const DevMat* d : {&L.wq, &L.wk, &L.wv, &L.wo, &L.wg, &L.wu, &L.wd}) mats.push_back(d);
+    const DevMat* other = nullptr;
+    for (const DevMat* d : mats) {
+      if (is_legacy(d->type)) m->q80 = true;
+      if (d->type != GGML_Q4_K && d->type != GGML_Q6_K && !other) other = d;
+    }
+    if (other) {
+      if (T > 1) {
+        delete m;
+        return fail(ARMAI_E_INVALID, std::string("tensor parallel needs Q4_K / Q6_K matrices (its prompts run the "
+                                                 "tensor-core GEMM); this model has ") + ggml_type_name(other->type));
+      }
+      m->prefill_gemm = 1;
+    }
+  }
   if (T > 1) {  // from here on the model is this rank's shard
     m->n_head /= T;
     m->n_head_kv /= T;
@@ -1346,15 +1392,15 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     dn_rb = std::max(dn_rb, L.wd.row_bytes);
   }
   const int qkv_rows = L0.wq.rows + L0.wk.rows + L0.wv.rows;
-  m->pl_qkv1 = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
-  m->pl_wo1 = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, 1, false, nsm, SMEM_DECODE);
-  m->pl_gu1 = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
-  m->pl_down1 = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, 1, false, nsm, SMEM_DECODE);
-  m->pl_head1 = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, 1, true, nsm, SMEM_DECODE);
-  m->pl_qkvT = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT);
-  m->pl_woT = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, PREFILL_TILE, false, nsm, SMEM_LIMIT);
-  m->pl_guT = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT);
-  m->pl_downT = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, PREFILL_TILE, false, nsm, SMEM_LIMIT);
+  m->pl_qkv1 = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE, m->q80);
+  m->pl_wo1 = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, 1, false, nsm, SMEM_DECODE, m->q80);
+  m->pl_gu1 = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, 1, true, nsm, SMEM_DECODE, m->q80);
+  m->pl_down1 = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, 1, false, nsm, SMEM_DECODE, m->q80);
+  m->pl_head1 = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, 1, true, nsm, SMEM_DECODE, m->q80);
+  m->pl_qkvT = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT, m->q80);
+  m->pl_woT = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, PREFILL_TILE, false, nsm, SMEM_LIMIT, m->q80);
+  m->pl_guT = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, PREFILL_TILE, true, nsm, SMEM_LIMIT, m->q80);
+  m->pl_downT = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, PREFILL_TILE, false, nsm, SMEM_LIMIT, m->q80);
   for (const Plan* pl : {&m->pl_qkv1, &m->pl_wo1, &m->pl_gu1, &m->pl_down1, &m->pl_head1, &m->pl_qkvT,
                          &m->pl_woT, &m->pl_guT, &m->pl_downT})
     if (pl->smem > SMEM_LIMIT) { free_model(m); return fail(ARMAI_E_INVALID, "model rows too wide for shared memory"); }
@@ -1370,11 +1416,11 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     // 16 sequences per weight pass, or 8 where 16 activation rows of the
     // widest K (ffn_down) do not fit shared memory
     auto plans = [&](int nb) {
-      m->pl_qkvB = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
-      m->pl_woB = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, nb, false, nsm, SMEM_LIMIT);
-      m->pl_guB = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
-      m->pl_downB = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, nb, false, nsm, SMEM_LIMIT);
-      m->pl_headB = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT);
+      m->pl_qkvB = make_plan(qkv_rows, 2, qkv_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT, m->q80);
+      m->pl_woB = make_plan(m->n_embd, 1, wo_rb, 1, (int)QN, nb, false, nsm, SMEM_LIMIT, m->q80);
+      m->pl_guB = make_plan(m->n_ff, 1, gu_rb, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT, m->q80);
+      m->pl_downB = make_plan(m->n_embd, 1, dn_rb, 1, m->n_ff, nb, false, nsm, SMEM_LIMIT, m->q80);
+      m->pl_headB = make_plan(m->output.rows, 1, m->output.row_bytes, 1, m->n_embd, nb, true, nsm, SMEM_LIMIT, m->q80);
       for (const Plan* pl : {&m->pl_qkvB, &m->pl_woB, &m->pl_guB, &m->pl_downB, &m->pl_headB})
         if (pl->smem > SMEM_LIMIT) return false;
       return true;

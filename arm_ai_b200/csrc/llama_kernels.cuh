@@ -105,6 +105,7 @@ struct MvParams {
   int K, nb;
   Seg seg[3];
   int nseg;
+  int acts;            // activations the rows need: 1 Q8_K (k-quants), 2 Q8_0 (legacy types)
   int nrows;           // activation rows (tokens / sequences) of this launch, <= NB
   int total_rows;      // QKV: q+k+v rows; GATEUP: rows of one of the pair; else rows
   int rows_per_cta, chunk_rows, ns;
@@ -132,13 +133,14 @@ struct MvParams {
 
 // Shared-memory layout of k_matvec (bytes), host and device agree on it.
 struct MvSmem {
-  size_t stages, act_qs, act_d, act_bs, gamma, bars, red, total;
+  size_t stages, act_qs, act_d, act_bs, gamma, bars, red, act0_qs, act0_d, act0_s, total;
 };
 __host__ __device__ inline size_t al16(size_t v) { return (v + 15) & ~size_t(15); }
 // red: 64 floats of scratch, NB*(K/256) per-block partial sums of squares,
 // NB rms values.
+// The Q8_0 buffers exist only when a matrix of the launch needs them.
 __host__ __device__ inline MvSmem mv_smem_layout(int ns, uint32_t stage_bytes, int K, int NB,
-                                                 bool norm) {
+                                                 bool norm, bool q80 = false) {
   MvSmem L;
   size_t o = 0;
   L.stages = o;  o += al16((size_t)ns * stage_bytes);
@@ -148,6 +150,9 @@ __host__ __device__ inline MvSmem mv_smem_layout(int ns, uint32_t stage_bytes, i
   L.gamma = o;   o += norm ? al16((size_t)K * 4) : 0;
   L.bars = o;    o += al16((size_t)(ns + 1) * 8);
   L.red = o;     o += al16((64 + (size_t)NB * (K / QK_K) + NB) * 4);
+  L.act0_qs = o; o += q80 ? al16((size_t)NB * K) : 0;
+  L.act0_d = o;  o += q80 ? al16((size_t)NB * (K / QK8_0) * 4) : 0;
+  L.act0_s = o;  o += q80 ? al16((size_t)NB * (K / QK8_0) * 4) : 0;
   L.total = o;
   return L;
 }
@@ -232,6 +237,9 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
     act[b].qs = reinterpret_cast<int8_t*>(smem + L.act_qs) + (size_t)b * K;
     act[b].d = reinterpret_cast<float*>(smem + L.act_d) + (size_t)b * nb;
     act[b].bs = reinterpret_cast<int32_t*>(smem + L.act_bs) + (size_t)b * (K / 16);
+    act[b].qs0 = reinterpret_cast<int8_t*>(smem + L.act0_qs) + (size_t)b * K;
+    act[b].d0 = reinterpret_cast<float*>(smem + L.act0_d) + (size_t)b * (K / QK8_0);
+    act[b].s0 = reinterpret_cast<int32_t*>(smem + L.act0_s) + (size_t)b * (K / QK8_0);
   }
   const float* src = p.x;
   const bool norm = p.gamma != nullptr;
@@ -270,7 +278,9 @@ __device__ void build_act(const MvParams& p, uint8_t* smem, const MvSmem& L, Act
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], m), g[i]);
     }
-    q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16, j & 7);
+    if (p.acts & 1) q8k_quant_block_warp(v, lane, act[b].qs + j * QK_K, act[b].d + j, act[b].bs + j * 16, j & 7);
+    if (p.acts & 2)
+      q80_quant_block_warp(v, lane, act[b].qs0 + j * QK_K, act[b].d0 + 8 * j, act[b].s0 + 8 * j, j & 7);
   }
   __syncthreads();
 }
@@ -407,7 +417,12 @@ __device__ __forceinline__ int chunk_nunits(int c0, int c1) {
 template <int MODE>
 __device__ __forceinline__ void unit_dot_any(const UnitRows& w, int nb, const ActQ8& act, int lane, float& d0,
                                              float& d1) {
-  if (MODE != MODE_GATEUP || w.ty0 == w.ty1) {  // both rows of one matrix
+  if ((w.ty0 != GGML_Q4_K && w.ty0 != GGML_Q6_K) || (w.ty1 != GGML_Q4_K && w.ty1 != GGML_Q6_K)) {
+    // Q5_K / legacy types: the generic runtime-typed path
+    const float2 r = row_pair_dots(w.ty0, w.p0, w.ty1, w.p1, w.has1, nb, act, lane);
+    d0 = r.x;
+    d1 = r.y;
+  } else if (MODE != MODE_GATEUP || w.ty0 == w.ty1) {  // both rows of one matrix
     if (w.ty0 == GGML_Q4_K) unit_dots<GGML_Q4_K, GGML_Q4_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
     else unit_dots<GGML_Q6_K, GGML_Q6_K>(w.p0, w.p1, w.has1, nb, act, lane, d0, d1);
   } else if (w.ty0 == GGML_Q4_K) {
@@ -527,7 +542,7 @@ template <int MODE, int NB>
 __global__ void __launch_bounds__(MV_THREADS, 2) k_matvec(const MvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const MvSmem L = mv_smem_layout(p.ns, p.stage_bytes, p.K, NB, p.gamma != nullptr);
+  const MvSmem L = mv_smem_layout(p.ns, p.stage_bytes, p.K, NB, p.gamma != nullptr, (p.acts & 2) != 0);
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(r0 + p.rows_per_cta, p.total_rows);
   const int nchunks = r1 > r0 ? (r1 - r0 + p.chunk_rows - 1) / p.chunk_rows : 0;
@@ -857,33 +872,12 @@ static __global__ void __launch_bounds__(256) k_embed(const uint8_t* table, int 
   const uint8_t* row = table + (int64_t)tok * row_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* y = x + (size_t)b * K;
-  // one warp per 256-value block
+  // one warp per 256-value block, 8 values per lane (each type's to_float)
   for (int j = warp; j < nb; j += blockDim.x >> 5) {
-    if (type == GGML_Q4_K) {
-      const uint8_t* blk = row + (int64_t)j * Q4K_BLOCK_BYTES;
-      const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
-      const float dmin = h2f(*reinterpret_cast<const uint16_t*>(blk + 2));
-      for (int i = lane; i < QK_K; i += 32) {
-        const int c = i / 64, l = i % 64, sj = 2 * c + (l >= 32);
-        const uint8_t byte = blk[16 + 32 * c + (l & 31)];
-        const int q = l >= 32 ? (byte >> 4) : (byte & 0xF);
-        int sc, m;
-        q4k_scale_min(blk + 4, sj, sc, m);
-        y[j * QK_K + i] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q),
-                                    __fmul_rn(dmin, (float)m));
-      }
-    } else {
-      const uint8_t* body = row + (int64_t)j * Q6K_BODY_BYTES;
-      const uint16_t* dv = reinterpret_cast<const uint16_t*>(row + (int64_t)nb * Q6K_BODY_BYTES);
-      for (int i = lane; i < QK_K; i += 32) {
-        const int n = i / 128, r = i % 128, g = r / 32, l = r % 32;
-        const uint8_t qlb = body[64 * n + l + (g & 1) * 32];
-        const int lo = (g < 2) ? (qlb & 0xF) : (qlb >> 4);
-        const int hi = (body[128 + 32 * n + l] >> (2 * g)) & 3;
-        const int8_t sc = reinterpret_cast<const int8_t*>(body + 192)[8 * n + l / 16 + 2 * g];
-        y[j * QK_K + i] = __fmul_rn(__fmul_rn(h2f(dv[j]), (float)sc), (float)((lo | (hi << 4)) - 32));
-      }
-    }
+    float v[8];
+    dequant8(type, row, nb, j, lane, v);
+#pragma unroll
+    for (int k = 0; k < 8; k++) y[j * QK_K + 8 * lane + k] = v[k];
   }
 }
 

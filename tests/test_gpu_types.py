@@ -1,8 +1,8 @@
 """Weight types beyond Q4_K / Q6_K (Q5_K with Q8_K activations; Q4_0, Q5_0,
 Q8_0 with candle's Q8_0 activations) through the GPU path, against the
-oracle, on tiny models that use one type throughout or mix them. While the
-loader rejects a type (it names the tensor and the type) its case is skipped;
-the oracle side of these types is pinned in tests/test_oracle_types_pins.py."""
+oracle, on tiny models that use one type throughout or mix them (prompts of
+these models run the integer per-kernel chain; decode the persistent kernel).
+The oracle side of these types is pinned in tests/test_oracle_types_pins.py."""
 import os
 
 import numpy as np
@@ -10,7 +10,6 @@ import pytest
 
 import ref
 from arm_ai_b200 import native, synth
-from arm_ai_b200.native import NifError
 from mixed_models import write_mixed_model
 from parity import check_errors, flip_bound, greedy_consistent, rel_maxabs
 
@@ -32,12 +31,7 @@ def test_weight_types_match_oracle(built, case):
     d = os.environ.get("ARMAI_MODEL_CACHE", "/tmp/armai_models")
     os.makedirs(d, exist_ok=True)
     path = write_mixed_model(os.path.join(d, f"tiny-{case}-s21-v1.gguf"), "tiny", 21, CASES[case])
-    try:
-        gpu = native.llama_candle_load_op(path)
-    except NifError as e:
-        if "this build supports Q4_K and Q6_K" in str(e):
-            pytest.skip(f"no GPU kernels for this weight type yet: {e}")
-        raise
+    gpu = native.llama_candle_load_op(path)
     orc = ref.OracleLlama(path)
     bound = flip_bound(path, lengths=(16, 24, 64, 100, 128))
     errs = []

@@ -1,6 +1,7 @@
-"""The loader's weight-type check, on the CPU: a GGUF whose attn_q is Q8_0
-(a type candle accepts but this build's kernels do not) is rejected before
-any device work, with the tensor and its type in the message."""
+"""The loader's weight-type check, on the CPU: a GGUF whose attn_q has a type
+outside the ones the reference's loader documents (Q4_0, Q5_0, Q8_0, Q4_K,
+Q5_K, Q6_K; lib/arm_ai/native.ex:551-556) is rejected before any device
+work, with the tensor and its type in the message."""
 import numpy as np
 import pytest
 
@@ -55,9 +56,10 @@ def _write_model(path, q_type_name):
     w.close()
 
 
-@pytest.mark.parametrize("qtype", ["Q8_0", "Q4_0", "Q5_0"])
+@pytest.mark.parametrize("qtype", ["Q4_1", "Q5_1"])
 def test_unsupported_weight_type_rejected(built, tmp_path, qtype):
     p = tmp_path / f"attn_q_{qtype}.gguf"
     _write_model(p, qtype)
-    with pytest.raises(NifError, match=rf"tensor blk\.0\.attn_q\.weight has type {qtype}; this build supports Q4_K and Q6_K"):
+    with pytest.raises(NifError, match=rf"tensor blk\.0\.attn_q\.weight has type {qtype}; this build supports "
+                                       r"Q4_0, Q5_0, Q8_0, Q4_K, Q5_K and Q6_K matrices"):
         native.llama_candle_load_op(str(p))
