@@ -15,6 +15,7 @@
 #include <cuda_fp16.h>
 
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -50,8 +51,37 @@ struct Scoped {
   ~Scoped() { if (p) cudaFreeAsync(p, s); }
 };
 
+// Stream-ordered allocations come from the library's own memory pool per
+// device, which keeps freed memory for the next call (release threshold at
+// its maximum): with a threshold of 0, as the default pool has, every call
+// after a synchronisation paid for a fresh device allocation.
+int lib_pool(cudaMemPool_t* out) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  ARMAI_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(ARMAI_E_INVALID, "device ordinal beyond 64");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    ARMAI_CUDA(cudaMemPoolCreate(&pool, &props));
+    uint64_t keep = ~0ull;
+    ARMAI_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    pools[dev] = pool;
+  }
+  *out = pools[dev];
+  return ARMAI_OK;
+}
+
 int dalloc(Scoped& b, size_t bytes) {
-  ARMAI_CUDA(cudaMallocAsync(&b.p, bytes ? bytes : 16, b.s));
+  cudaMemPool_t pool;
+  ARMAI_TRY(lib_pool(&pool));
+  ARMAI_CUDA(cudaMallocFromPoolAsync(&b.p, bytes ? bytes : 16, pool, b.s));
   return ARMAI_OK;
 }
 int h2d(Scoped& b, const void* src, size_t bytes) {
@@ -145,6 +175,19 @@ __global__ void __launch_bounds__(256) k_int8_gemm(const int8_t* __restrict__ a,
     }
 }
 
+}  // namespace
+namespace armai {
+int launch_int8_gemm_tc(const int8_t* a, const int8_t* w, int32_t* o32, float* of32, const float* act_scales,
+                        int per_token, float act_scale, const float* w_scales, int64_t m, int64_t n, int64_t k,
+                        cudaStream_t s);
+int int8_gemm_tc_check();
+}  // namespace armai
+namespace {
+
+// M >= 64 (GEMM-shaped): the tcgen05 kind::i8 kernel (i8gemm_tc.cu); smaller
+// M (matrix-vector shaped, bound by streaming W): the dp4a kernels below.
+constexpr int64_t I8_TC_MIN_M = 64;
+
 int launch_int8_gemm(const int8_t* a, const int8_t* w, int32_t* o32, float* of32, const float* act_scales,
                      int per_token, float act_scale, const float* w_scales, int64_t m, int64_t n,
                      int64_t k, cudaStream_t s) {
@@ -152,6 +195,9 @@ int launch_int8_gemm(const int8_t* a, const int8_t* w, int32_t* o32, float* of32
     // rows are read 16 bytes at a time
     return fail(ARMAI_E_INVALID, "int8_matmul: K must be a multiple of 16 on this path");
   }
+  const bool aligned = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
+  if (m >= I8_TC_MIN_M && aligned && m <= INT32_MAX && n <= INT32_MAX && k <= INT32_MAX)
+    return launch_int8_gemm_tc(a, w, o32, of32, act_scales, per_token, act_scale, w_scales, m, n, k, s);
   if (m <= 4) {
     dim3 g((unsigned)((n + 31) / 32), (unsigned)m);
     k_int8_gemm<1><<<g, 256, 0, s>>>(a, w, o32, of32, act_scales, per_token, act_scale, w_scales, (int)m, (int)n, (int)k);
@@ -712,7 +758,8 @@ extern "C" int armai_int8_matmul_s32(const int8_t* a, size_t a_len, const int8_t
   ARMAI_TRY(dalloc(dout, m * n * 4));
   ARMAI_TRY(launch_int8_gemm((int8_t*)da.p, (int8_t*)dw.p, (int32_t*)dout.p, nullptr, nullptr, 0, 0.f,
                              nullptr, (int64_t)m, (int64_t)n, (int64_t)k, s));
-  return finish(s, out, dout.p, m * n * 4);
+  ARMAI_TRY(finish(s, out, dout.p, m * n * 4));
+  return int8_gemm_tc_check();
 }
 
 static int int8_f32_common(const int8_t* a, size_t a_len, const int8_t* w, size_t w_len,
@@ -736,7 +783,8 @@ static int int8_f32_common(const int8_t* a, size_t a_len, const int8_t* w, size_
   ARMAI_TRY(dalloc(dout, m * n * 4));
   ARMAI_TRY(launch_int8_gemm((int8_t*)da.p, (int8_t*)dw.p, nullptr, (float*)dout.p, (float*)das.p,
                              per_token, act_scale, (float*)dws.p, (int64_t)m, (int64_t)n, (int64_t)k, s));
-  return finish(s, out, dout.p, m * n * 4);
+  ARMAI_TRY(finish(s, out, dout.p, m * n * 4));
+  return int8_gemm_tc_check();
 }
 
 extern "C" int armai_int8_matmul_f32(const int8_t* a, size_t a_len, const int8_t* w, size_t w_len,

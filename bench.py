@@ -49,6 +49,7 @@ def parse():
     p.add_argument("--no-config2", action="store_true", help="skip the batched-decode (config 2) figures")
     p.add_argument("--no-config3", action="store_true", help="skip the Mistral-7B long-context (config 3) figures")
     p.add_argument("--no-config4", action="store_true", help="skip the Llama-3-8B tensor-parallel (config 4) figures")
+    p.add_argument("--no-config5", action="store_true", help="skip the primitive sweep (config 5) figures")
     return p.parse_args()
 
 
@@ -387,6 +388,106 @@ def run_config3(d, peak):
             "timing": "decode: CUDA events over 255 back-to-back steps; prefill: host wall clock"}
 
 
+def measured_tc_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_config5(d, peak_hbm):
+    """BASELINE configs[4], the primitive sweep, through the device-pointer
+    entry points (inputs resident in HBM): per call device time from CUDA
+    events on the call's stream, L2 flushed (a 256 MB write) before every
+    timed call, 3 warm-up calls, median of 10. Roofline per primitive: HBM
+    for the matrix-vector shapes (int8 M <= 16, int4 matvecs, RMSNorm),
+    tensor cores for the int8 GEMM at M = 512 (s8 dense peak taken as 2 x the
+    measured bf16 GEMM peak, the nominal ratio) and for flash attention
+    (measured bf16 peak)."""
+    import ctypes
+
+    import torch
+    from arm_ai_b200._lib import load_cuda
+    lib = load_cuda()
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    st = torch.cuda.current_stream()
+    sp = ctypes.c_void_p(st.cuda_stream)
+    tc_peak, tc_src = measured_tc_peak()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(10):
+            flush.fill_(1.0)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            rc = fn()
+            b.record(st)
+            if rc != 0:
+                raise RuntimeError(f"primitive call failed ({rc})")
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    P = lambda t: ctypes.c_void_p(t.data_ptr())
+    out = {"timing": "device time per call (CUDA events on the call's stream), L2 flushed before each, median of 10",
+           "tensor_peak_tflops": tc_peak, "tensor_peak_source": tc_src, "hbm_peak_gbs": peak_hbm}
+    i8 = {}
+    for K in (2048, 4096):
+        w = torch.randint(-127, 128, (K, K), dtype=torch.int8, device=dev, generator=gen)
+        ws = torch.rand(K, device=dev, generator=gen) * 0.1
+        for M in (1, 16, 512):
+            a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev, generator=gen)
+            o = torch.empty(M, K, dtype=torch.float32, device=dev)
+            ms = timeit(lambda: lib.armai_dev_int8_matmul_f32(P(a), P(w), None, 0, ctypes.c_float(0.0125), P(ws),
+                                                              P(o), M, K, K, sp))
+            ops, byt = 2 * M * K * K, K * K + M * K + 4 * K + 4 * M * K
+            e = {"us": ms * 1e3, "tops": ops / ms / 1e9, "gb_s": byt / ms / 1e6}
+            if M >= 64:
+                e.update(bound="tensor", kernel="k_i8gemm (tcgen05 kind::i8)", frac=e["tops"] / (2 * tc_peak))
+            else:
+                e.update(bound="hbm", kernel="k_int8_gemm (dp4a)", frac=e["gb_s"] / peak_hbm)
+            i8[f"M{M}_K{K}_N{K}"] = e
+    out["int8_matmul_f32"] = i8
+    i4 = {}
+    for N, K in ((4096, 4096), (14336, 4096)):
+        wp = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=gen)
+        sc = torch.rand(N, K // 32, device=dev, generator=gen) * 0.01
+        a = torch.rand(1, K, device=dev, generator=gen) * 2 - 1
+        o = torch.empty(N, device=dev)
+        byt = N * K // 2 + 4 * N * K // 32 + 4 * K + 4 * N
+        for name, fn in (("int4_gemv_q4_x_q8", lambda: lib.armai_dev_int4_gemv_q4_x_q8(P(a), P(wp), P(sc), P(o), N,
+                                                                                        K, sp)),
+                         ("int4_matmul_f32_m1", lambda: lib.armai_dev_int4_matmul_f32(P(a), P(wp), P(sc), P(o), 1,
+                                                                                        N, K, sp))):
+            ms = timeit(fn)
+            i4[f"{name}_N{N}_K{K}"] = {"us": ms * 1e3, "gb_s": byt / ms / 1e6, "bound": "hbm",
+                                        "frac": byt / ms / 1e6 / peak_hbm}
+    out["int4_matvec"] = i4
+    x = torch.rand(512, 4096, device=dev, generator=gen)
+    g = torch.rand(4096, device=dev, generator=gen)
+    o = torch.empty_like(x)
+    ms = timeit(lambda: lib.armai_dev_rmsnorm_f32(P(x), P(g), P(o), 512, 4096, ctypes.c_float(1e-5), sp))
+    byt = 2 * 4 * 512 * 4096 + 4 * 4096
+    out["rmsnorm_f32_512x4096"] = {"us": ms * 1e3, "gb_s": byt / ms / 1e6, "bound": "hbm",
+                                   "frac": byt / ms / 1e6 / peak_hbm}
+    H, S, D = 32, 2048, 128
+    q, k, v = (torch.rand(1, H, S, D, device=dev, generator=gen).half() * 2 - 1 for _ in range(3))
+    o = torch.empty(1, H, S, D, device=dev)
+    ms = timeit(lambda: lib.armai_dev_flash_attention_f16(P(q), P(k), P(v), P(o), ctypes.c_float(D ** -0.5), 1, H,
+                                                          S, S, D, 1, sp))
+    fl = 4 * S * S * D * H / 2
+    out["flash_attention_f16_h32_s2048_d128_causal"] = {"us": ms * 1e3, "tflops": fl / ms / 1e9, "bound": "tensor",
+                                                        "frac": fl / ms / 1e9 / tc_peak}
+    return out
+
+
 def run_armai(args, d):
     from arm_ai_b200 import native, synth
     if d.rank == 0:
@@ -460,6 +561,7 @@ def run_armai(args, d):
     cfg2 = None if args.no_config2 else guard(run_config2, d)
     cfg3 = guard(run_config3, d, peak) if (d.world == 1 and not args.no_config3) else None
     cfg4 = None if args.no_config4 else guard(run_config4, d, peak)
+    cfg5 = guard(run_config5, d, peak) if (d.rank == 0 and not args.no_config5) else None
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(path, prompt)
@@ -492,6 +594,7 @@ def run_armai(args, d):
             "config2_batched": cfg2,
             "config3_mistral_7b_long": cfg3,
             "config4_llama3_8b": cfg4,
+            "config5_primitives": cfg5,
         }
         print(json.dumps(out), flush=True)
 

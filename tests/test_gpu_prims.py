@@ -22,7 +22,10 @@ def i8(shape):
     return RNG.integers(-127, 128, size=shape, dtype=np.int8)
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 2048, 2048), (16, 4096, 4096), (512, 2048, 2048), (3, 100, 48)])
+# M >= 64 runs the tcgen05 kind::i8 kernel (TMA boxes of 128 x 128 bytes,
+# zero-filled past the edges): ragged M / N / K cover its tile edges.
+@pytest.mark.parametrize("m,n,k", [(1, 2048, 2048), (16, 4096, 4096), (512, 2048, 2048), (3, 100, 48),
+                                   (512, 4096, 4096), (64, 256, 272), (200, 300, 144), (130, 129, 4112)])
 def test_int8_gemm_bit_exact(built, m, n, k):
     a, w = i8((m, k)), i8((n, k))
     ws = RNG.uniform(1e-3, 1e-1, n).astype(np.float32)
