@@ -53,6 +53,7 @@ _SIGS = {
     "armai_llama_bench_decode": (c_int, [c_void_p, c_int32, POINTER(c_float)]),
     "armai_llama_bench_kernel": (c_int, [c_void_p, c_int32, c_int32, POINTER(c_float), POINTER(c_int64)]),
     "armai_llama_trace_decode": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_int32), POINTER(c_int32)]),
+    "armai_llama_test_stall": (c_int, [c_void_p, c_int32, c_uint32]),
     "armai_int8_matmul_f32": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p, c_size_t,
                                       c_double, c_size_t, c_size_t, c_size_t, c_void_p]),
     "armai_int8_matmul_f32_per_token": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_void_p,

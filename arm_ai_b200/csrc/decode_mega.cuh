@@ -93,6 +93,12 @@ struct MkParams {
   uint32_t* token;
   int* pos;
   uint32_t* err;
+  // Polls of a tagged word before a wait gives up (sets the error word and
+  // lets the launch end); MK_BAR_LIMIT unless a test shortens it.
+  uint32_t poll_limit;
+  // Test injection: the phase whose outputs are never published (-1: none),
+  // so that its consumers' bounded waits run out.
+  int test_stall_phase;
   unsigned long long* trace;  // nullptr, or [n_ph][grid][MK_TRACE_SLOTS] globaltimer stamps
   size_t off_bars, off_act_qs, off_act_d, off_act_bs, off_red, off_att;  // smem layout
   size_t off_act0_qs, off_act0_d, off_act0_s;  // Q8_0 activation (0: no phase needs one)
@@ -210,11 +216,39 @@ __device__ __forceinline__ void phase_rows(const MkPhase& ph, int& r0, int& r1) 
 // ---------------------------------------------------------------------------
 // Producer: one lane streams this CTA's rows of every weight phase.
 // ---------------------------------------------------------------------------
+// Bounded wait for a copy's completion that does not give up early when
+// another CTA failed: a CTA must not exit with its own copies in flight.
+__device__ __forceinline__ void mk_drain(uint64_t* bar, uint32_t parity) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (ok) return;
+    if (i > 8) __nanosleep(128);
+  }
+}
+
 __device__ void mk_producer(const MkParams& p, uint8_t* smem) {
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bars);
   uint64_t* empty = full + MK_MAX_NS;
   const uint64_t pol = l2_evict_first_policy();
   int sidx = 0;
+  // On every exit (normal, or a wait that gave up): the stages issued last
+  // have landed before this thread leaves (normally they were consumed).
+  struct Drain {
+    uint64_t* full;
+    const int& sidx;
+    int ns;
+    __device__ ~Drain() {
+      for (int j = sidx > ns ? sidx - ns : 0; j < sidx; j++) mk_drain(&full[j % ns], (uint32_t)((j / ns) & 1));
+    }
+  } drain{full, sidx, p.ns};
   for (int i = 0; i < p.n_ph; i++) {
     const MkPhase& ph = p.ph[i];
     if (ph.kind == PH_ATTN) continue;
@@ -289,8 +323,8 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long* 
 }
 // Bounded poll: false (and the error flag) when it gives up or another CTA
 // failed.
-__device__ __forceinline__ bool poll_continue(uint32_t it, uint32_t* err) {
-  if (it > MK_BAR_LIMIT || (((it & 255) == 255) && dev_failed(err))) {
+__device__ __forceinline__ bool poll_continue(uint32_t it, uint32_t* err, uint32_t limit) {
+  if (it > limit || (((it & 255) == 255) && dev_failed(err))) {
     atomicOr(err, DEVERR_COUNTER_TIMEOUT);
     return false;
   }
@@ -300,14 +334,14 @@ __device__ __forceinline__ bool poll_continue(uint32_t it, uint32_t* err) {
 // N (even) consecutive words (16-byte aligned) carrying tag `want`.
 template <bool SYS, int N>
 __device__ __forceinline__ void wait_words(const unsigned long long* p, uint32_t want, unsigned long long (&w)[N],
-                                           uint32_t* err) {
+                                           uint32_t* err, uint32_t limit) {
 #pragma unroll
   for (int e = 0; e < N; e += 2) ld_words2<SYS>(p + e, w[e], w[e + 1]);
   for (uint32_t it = 0;; ++it) {
     bool ok = true;
 #pragma unroll
     for (int e = 0; e < N; e++) ok &= (uint32_t)w[e] == want;
-    if (ok || !poll_continue(it, err)) return;
+    if (ok || !poll_continue(it, err, limit)) return;
 #pragma unroll
     for (int e = 0; e < N; e += 2)
       if ((uint32_t)w[e] != want || (uint32_t)w[e + 1] != want) ld_words2<SYS>(p + e, w[e], w[e + 1]);
@@ -315,9 +349,10 @@ __device__ __forceinline__ void wait_words(const unsigned long long* p, uint32_t
 }
 // One word carrying tag `want`; its value.
 template <bool SYS>
-__device__ __forceinline__ float wait_word(const unsigned long long* p, uint32_t want, uint32_t* err) {
+__device__ __forceinline__ float wait_word(const unsigned long long* p, uint32_t want, uint32_t* err,
+                                           uint32_t limit) {
   unsigned long long w = ld_word<SYS>(p);
-  for (uint32_t it = 0; (uint32_t)w != want && poll_continue(it, err); ++it) w = ld_word<SYS>(p);
+  for (uint32_t it = 0; (uint32_t)w != want && poll_continue(it, err, limit); ++it) w = ld_word<SYS>(p);
   return word_val(w);
 }
 
@@ -330,7 +365,7 @@ __device__ __forceinline__ F8 mk_load_vals_ool(const MkParams& p, const MkPhase&
   float vv[8];
   if (ph.kind == PH_WO || ph.kind == PH_DOWN) {
     unsigned long long w[8];
-    wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err);
+    wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err, p.poll_limit);
 #pragma unroll
     for (int e = 0; e < 8; e++) vv[e] = word_val(w[e]);
   } else if (ph.kind == PH_QKV && ph.layer == 0) {
@@ -345,7 +380,7 @@ __device__ __forceinline__ F8 mk_load_vals_ool(const MkParams& p, const MkPhase&
     const unsigned long long* sl = p.xslot[p.tp_rank] + (size_t)par * p.tp * E + j * QK_K + 8 * lane;
     for (int k = 0; k < p.tp; k++) {
       unsigned long long w[8];
-      wait_words<true, 8>(sl + (size_t)k * E, want, w, p.err);
+      wait_words<true, 8>(sl + (size_t)k * E, want, w, p.err, p.poll_limit);
 #pragma unroll
       for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(acc[e], word_val(w[e]));
     }
@@ -431,7 +466,7 @@ __device__ void mk_build_act(const MkParams& p, const MkPhase& ph, int phase, ui
       vv[4] = b.x; vv[5] = b.y; vv[6] = b.z; vv[7] = b.w;
     } else {  // y / h blocks beyond the register-held ones: read again
       unsigned long long w[8];
-      wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err);
+      wait_words<false, 8>((ph.kind == PH_WO ? p.fy : p.fh) + j * QK_K + 8 * lane, want, w, p.err, p.poll_limit);
 #pragma unroll
       for (int e = 0; e < 8; e++) vv[e] = word_val(w[e]);
     }
@@ -468,7 +503,9 @@ struct MkCtx {
   __device__ const float* cos_t() const { return p.cos_t; }
   __device__ const float* sin_t() const { return p.sin_t; }
   __device__ void stamp(int slot) const { mk_stamp(p, phase, slot); }
+  __device__ bool stalled() const { return phase == p.test_stall_phase; }
   __device__ void put_q(int r, float a, float b) const {
+    if (stalled()) return;
     st_word_gpu(p.fq + r, tag_word(tag, a));
     st_word_gpu(p.fq + r + 1, tag_word(tag, b));
   }
@@ -480,15 +517,19 @@ struct MkCtx {
       a = __half2float(__float2half_rn(a));
       b = __half2float(__float2half_rn(b));
     }
+    if (stalled()) return;
     unsigned long long* w = p.fkv + ((size_t)which * p.n_kv + kvh) * p.hd + dd;
     st_word_gpu(w, tag_word(tag, a));
     st_word_gpu(w + 1, tag_word(tag, b));
   }
-  __device__ void put_h(int r, float v) const { st_word_gpu(p.fh + r, tag_word(tag, v)); }
+  __device__ void put_h(int r, float v) const {
+    if (!stalled()) st_word_gpu(p.fh + r, tag_word(tag, v));
+  }
   // attn_output / ffn_down row r: this rank's sum into every rank's slot
   __device__ void resid_add(float*, int r, float v) const {
     const size_t off = ((size_t)(ph.kind == PH_WO ? 1 : 0) * p.tp + p.tp_rank) * p.n_embd + r;
     const unsigned long long w = tag_word(tag, v);
+    if (stalled()) return;
     for (int k = 0; k < p.tp; k++) st_word_sys(p.xslot[k] + off, w);
   }
 };
@@ -685,7 +726,7 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
   const KV* kc = reinterpret_cast<const KV*>(ph.kc) + kvbase;
   const KV* vc = reinterpret_cast<const KV*>(ph.vc) + kvbase;
   const unsigned long long* qw = p.fq + (size_t)(g * nrep + r0) * HD;
-  for (int i = tid; i < nh * HD; i += MK_CT) qs[i] = wait_word<false>(qw + i, want, p.err);
+  for (int i = tid; i < nh * HD; i += MK_CT) qs[i] = wait_word<false>(qw + i, want, p.err, p.poll_limit);
   if (tid < nh) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
   float o[MAXE];
 #pragma unroll
@@ -698,8 +739,8 @@ __device__ void mk_attn_unit(const MkParams& p, const MkPhase& ph, int g, int r0
       float4 kv, vv;
       if (tb + tt == T - 1) {  // this step's row
         unsigned long long kw[4], vw[4];
-                wait_words<false, 4>(p.fkv + (size_t)g * HD + c, want, kw, p.err);
-        wait_words<false, 4>(p.fkv + ((size_t)p.n_kv + g) * HD + c, want, vw, p.err);
+                wait_words<false, 4>(p.fkv + (size_t)g * HD + c, want, kw, p.err, p.poll_limit);
+        wait_words<false, 4>(p.fkv + ((size_t)p.n_kv + g) * HD + c, want, vw, p.err, p.poll_limit);
         kv = make_float4(word_val(kw[0]), word_val(kw[1]), word_val(kw[2]), word_val(kw[3]));
         vv = make_float4(word_val(vw[0]), word_val(vw[1]), word_val(vw[2]), word_val(vw[3]));
       } else {
@@ -883,7 +924,7 @@ __device__ void mk_attn_short(const MkParams& p, const MkPhase& ph, int phase, i
   float q[8];
   {
     unsigned long long w[8];
-    wait_words<false, 8>(p.fq + (size_t)hq * HD + 8 * di, want, w, p.err);
+    wait_words<false, 8>(p.fq + (size_t)hq * HD + 8 * di, want, w, p.err, p.poll_limit);
 #pragma unroll
     for (int e = 0; e < 8; e++) q[e] = word_val(w[e]);
   }
@@ -891,7 +932,7 @@ __device__ void mk_attn_short(const MkParams& p, const MkPhase& ph, int phase, i
   const int tl = T - 1;  // this step's K/V row, from the QKV phase
   if (tl % PPP == pi) {
     unsigned long long w[8];
-    wait_words<false, 8>(p.fkv + (size_t)g * HD + 8 * di, want, w, p.err);
+    wait_words<false, 8>(p.fkv + (size_t)g * HD + 8 * di, want, w, p.err, p.poll_limit);
 #pragma unroll
     for (int k = 0; k < NP; k++)
       if (k == tl / PPP) {
@@ -921,7 +962,7 @@ __device__ void mk_attn_short(const MkParams& p, const MkPhase& ph, int phase, i
   }
   if (tl % PPP == pi) {
     unsigned long long w[8];
-    wait_words<false, 8>(p.fkv + ((size_t)p.n_kv + g) * HD + 8 * di, want, w, p.err);
+    wait_words<false, 8>(p.fkv + ((size_t)p.n_kv + g) * HD + 8 * di, want, w, p.err, p.poll_limit);
 #pragma unroll
     for (int k = 0; k < NP; k++)
       if (k == tl / PPP) {
@@ -1018,7 +1059,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
                   reinterpret_cast<float*>(smem + p.off_act0_d), reinterpret_cast<int32_t*>(smem + p.off_act0_s)};
   MkRun run{0, 0, -INFINITY, 0x7fffffff};
   uint64_t* gbar = empty + MK_MAX_NS;
-  uint32_t gcount = 0;  // gamma stagings consumed so far (mbarrier parity)
+  uint32_t gcount = 0;   // gamma stagings consumed so far (mbarrier parity)
+  uint32_t gissued = 0;  // gamma stagings issued (consumer thread 0)
   // phase i's outputs carry tag gen + i + 1; its inputs gen + i
   const uint32_t gen = (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.n_ph + 1));
 
@@ -1035,7 +1077,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
     }
     if (ctid == 0) s_flag = dev_failed(p.err);
     named_sync(1, MK_CT);
-    if (s_flag) return;  // a wait gave up somewhere: all consumer warps leave together
+    if (s_flag) {  // a wait gave up somewhere: all consumer warps leave together
+      if (ctid == 0 && gissued > gcount) mk_drain(gbar, (gissued - 1u) & 1u);  // no copy left in flight
+      return;
+    }
     // Stage the rmsnorm weights of the next phase (gate/up after attn_output,
     // q/k/v or the head after ffn_down; phase 0 its own) in the attention
     // region, idle until then, so the prologue reads them from shared memory.
@@ -1048,6 +1093,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
         fence_proxy_async();
         mbar_expect_tx(gbar, bytes);
         bulk_g2s(smem + p.off_att, g, bytes, gbar, l2_evict_first_policy());
+        gissued++;
       }
     }
     if (ctid == 0) mk_stamp(p, i, 0);

@@ -575,6 +575,8 @@ int setup_mega(armai_llama* m, int nsm) {
   k.token = m->d_token;
   k.pos = m->d_pos;
   k.err = m->d_err;
+  k.poll_limit = MK_BAR_LIMIT;
+  k.test_stall_phase = -1;
   m->mk_grid = grid;
   if (m->head_dim == 64) {
     ARMAI_CUDA(cudaFuncSetAttribute(k_decode_mega<64, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)o));
@@ -1793,6 +1795,16 @@ extern "C" int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t ca
   *n_phases = m->mk.n_ph + 1;
   *n_ctas = m->mk_grid;
   return check_device_error(m);
+}
+
+extern "C" int armai_llama_test_stall(armai_llama* m, int32_t phase, uint32_t poll_limit) {
+  if (!m) return fail(ARMAI_E_INVALID, "test_stall: null model");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->use_mega) return fail(ARMAI_E_INVALID, "test_stall: needs the persistent decode kernel");
+  if (phase < 0 || phase >= m->mk.n_ph) return fail(ARMAI_E_RANGE, "test_stall: no such phase");
+  m->mk.test_stall_phase = phase;
+  m->mk.poll_limit = poll_limit ? poll_limit : MK_BAR_LIMIT;
+  return ARMAI_OK;
 }
 
 extern "C" int armai_nccl_unique_id(void* out128) {

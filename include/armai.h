@@ -172,6 +172,16 @@ ARMAI_API int armai_llama_bench_kernel(armai_llama* m, int32_t kind, int32_t rou
 ARMAI_API int armai_llama_trace_decode(armai_llama* m, uint64_t* out, size_t cap, int32_t* n_phases,
                                        int32_t* n_ctas);
 
+/* Test-only error injection for the persistent decode kernel (no reference
+ * counterpart). From the next decode step on, phase `phase` (numbered as in
+ * armai_llama_trace_decode) publishes none of its outputs, and every wait on
+ * another CTA's output gives up after `poll_limit` polls (0 keeps the
+ * default): the consumers of that phase run out their bounded waits, the
+ * launch ends with the device error word set, and the call returns
+ * ARMAI_E_DEVICE; the model then answers every call with "reload the
+ * model". No GPU fault is involved: the kernel only stops waiting. */
+ARMAI_API int armai_llama_test_stall(armai_llama* m, int32_t phase, uint32_t poll_limit);
+
 /* ------------------------------------------------------------------ */
 /* Primitive NIFs (nx_arm building blocks). Host buffers in, caller-owned  */
 /* host output buffer out; same argument order as the NIFs.                */

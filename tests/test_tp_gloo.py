@@ -70,3 +70,42 @@ def test_loader_rejects_unrunnable_shardings(built, tiny_model, small_model):
     # tiny: 4 x 64-wide heads -> 2 ranks leave half a 256-value block of attn_output each
     with pytest.raises(NifError, match=r"whole 256-value blocks of attn_output per rank"):
         _load(tiny_model, tp_size=2, tp_rank=1)
+
+
+def _worker_absent(rank, world, port, q):
+    """Rank 1 never takes part in the id exchange (it leaves right after
+    joining the group); rank 0's exchange must end with an error within the
+    group's short timeout instead of waiting for ever."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        return
+    t0 = time.time()
+    try:
+        tp.share_unique_id(rank)
+        q.put((rank, "completed"))
+    except Exception as e:
+        q.put((rank, ("error", type(e).__name__, time.time() - t0)))
+
+
+def test_unique_id_exchange_ends_when_a_rank_never_joins(built):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_absent, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert got[1] == "left"
+    assert isinstance(got[0], tuple) and got[0][0] == "error", got[0]
+    assert got[0][2] < 60, got[0]
