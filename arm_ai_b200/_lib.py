@@ -24,7 +24,8 @@ class LlamaOpts(Structure):
     _fields_ = [("device", c_int32), ("max_seq_len", c_int32), ("kv_f16", c_int32),
                 ("max_batch", c_int32), ("use_graph", c_int32), ("use_pdl", c_int32),
                 ("tp_size", c_int32), ("tp_rank", c_int32), ("tp_unique_id", c_void_p),
-                ("decode_kernel", c_int32), ("prefill_gemm", c_int32), ("reserved", c_int32 * 6)]
+                ("decode_kernel", c_int32), ("prefill_gemm", c_int32), ("batch_gemm", c_int32),
+                ("reserved", c_int32 * 5)]
 
 
 class LlamaInfo(Structure):

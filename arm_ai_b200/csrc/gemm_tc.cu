@@ -1,16 +1,40 @@
-// gemm_tc.cu — device code and launchers of the tensor-core prefill GEMM
-// (interface and design notes in gemm_tc.cuh).
+// gemm_tc.cu — device code and launchers of the tensor-core GEMM for
+// prompts and batched decode (interface and design notes in gemm_tc.cuh).
 #include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
 
 #include "kquant.cuh"
 #include "llama_kernels.cuh"
 
 namespace armai {
 
+namespace {
+template <typename... KArgs, typename... Args>
+cudaError_t qg_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+}  // namespace
+
 // ---- tcgen05 / mbarrier helpers (PTX) --------------------------------------
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
@@ -31,20 +55,22 @@ __device__ __forceinline__ uint64_t qg_smem_desc(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: f16 A and B (K-major), f32 D, M = 128, N = 128.
-__host__ __device__ constexpr uint32_t qg_instr_desc() {
+// kind::f16 instruction descriptor: f16 A (tensor memory) and B (shared
+// memory, K-major), f32 D, M = 128 weight rows, N = ntok tokens.
+__host__ __device__ constexpr uint32_t qg_instr_desc(int ntok) {
   return (1u << 4)                 // D format f32
          | (0u << 7) | (0u << 10)  // A, B format f16
-         | ((uint32_t)(QG_N >> 3) << 17) | ((uint32_t)(QG_M >> 4) << 24);
+         | ((uint32_t)(ntok >> 3) << 17) | ((uint32_t)(QG_W >> 4) << 24);
 }
 
-__device__ __forceinline__ void qg_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] x B[smem desc]
+__device__ __forceinline__ void qg_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -71,112 +97,177 @@ __device__ __forceinline__ bool qg_wait(uint64_t* bar, uint32_t parity, uint32_t
   atomicOr(err, DEVERR_MBAR_TIMEOUT);
   return false;
 }
+// The same for a whole warp: every lane waits, the warp goes on only if all saw the phase.
+__device__ __forceinline__ bool qg_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* err) {
+  return __all_sync(0xffffffffu, qg_wait(bar, parity, err));
+}
 
-// 16 consecutive accumulator columns of this warp's 32 lanes.
-__device__ __forceinline__ void qg_tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+// 8 consecutive accumulator columns (tokens) of this warp's 32 lanes (rows).
+__device__ __forceinline__ void qg_tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// ---- W dequantisation: 64 values [k0, k0 + 64) of one row, as 8 x 8 f16 ----
-__device__ __forceinline__ void qg_store_row(uint8_t* tile, int r, const float (&v)[64]) {
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
-    __half2 h[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(v[8 * c + 2 * i], v[8 * c + 2 * i + 1]);
-    *reinterpret_cast<uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4)) = *reinterpret_cast<uint4*>(h);
-  }
+// 16 columns of f16 pairs (32 K values) of this warp's 32 lanes into tensor memory.
+__device__ __forceinline__ void qg_tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
-// BlockQ4K::to_float of values [64c, 64c + 64) of one super-block: bytes
-// qs[32c .. 32c + 32) hold them (low nibbles: sub-block 2c, high: 2c + 1).
-__device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, int c, float (&v)[64]) {
-  const uint4 hd = __ldg(reinterpret_cast<const uint4*>(blk));
-  const uint4 q0 = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * c));
-  const uint4 q1 = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * c));
+// ---- packed f32 pairs (sm_100 f32x2 arithmetic) ----------------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint32_t f2_to_h2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// 2^23 + byte i of x: an f32 whose value is exact (bytes are at most 255).
+__device__ __forceinline__ float qg_byte_f(uint32_t x, int i) {
+  return __uint_as_float(__byte_perm(x, 0x4B000000u, 0x7440u | (uint32_t)i));
+}
+
+// ---- W dequantisation from raw super-blocks in shared memory --------------
+// Q4_K (BlockQ4K::to_float): stage c of a super-block holds values
+// [64c, 64c + 64): sub-block 2c (low nibbles of qs[32c .. 32c + 32)) and
+// 2c + 1 (high nibbles). K half hh = sub-block 2c + hh: value l is
+// d * sc * q_l - dmin * m (the products d * sc and dmin * m rounded in f32
+// as candle does; the last step fused), rounded to f16 in pairs.
+__device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, uint4 hd, int c, int hh, uint32_t (&o)[16]) {
   uint8_t sc8[12];
   const uint32_t sw[3] = {hd.y, hd.z, hd.w};
 #pragma unroll
   for (int i = 0; i < 12; i++) sc8[i] = (uint8_t)(sw[i >> 2] >> (8 * (i & 3)));
-  int sc0, m0, sc1, m1;
-  q4k_scale_min(sc8, 2 * c, sc0, m0);
-  q4k_scale_min(sc8, 2 * c + 1, sc1, m1);
+  int sc, mn;
+  q4k_scale_min(sc8, 2 * c + hh, sc, mn);
   const float d = h2f((uint16_t)(hd.x & 0xffffu)), dmin = h2f((uint16_t)(hd.x >> 16));
-  const float d0 = __fmul_rn(d, (float)sc0), mm0 = __fmul_rn(dmin, (float)m0);
-  const float d1 = __fmul_rn(d, (float)sc1), mm1 = __fmul_rn(dmin, (float)m1);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+  const uint64_t dd = f2_pack(d1, d1), mm = f2_pack(-m1, -m1), bias = f2_pack(-8388608.f, -8388608.f);
+  const uint4 q0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
+  const uint4 q1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c);
   const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-  for (int l = 0; l < 32; l++) {
-    const uint32_t b = (qw[l >> 2] >> (8 * (l & 3))) & 0xffu;
-    v[l] = __fsub_rn(__fmul_rn(d0, (float)(b & 0xF)), mm0);
-    v[32 + l] = __fsub_rn(__fmul_rn(d1, (float)(b >> 4)), mm1);
+  for (int w = 0; w < 8; w++) {
+    const uint32_t x = (qw[w] >> (4 * hh)) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const uint64_t n = f2_add(f2_pack(qg_byte_f(x, 2 * i), qg_byte_f(x, 2 * i + 1)), bias);
+      o[2 * w + i] = f2_to_h2(f2_fma(n, dd, mm));
+    }
   }
 }
 
-// BlockQ6K::to_float of values [64t, 64t + 64) of one super-block (device
-// body: ql 128, qh 64, i8 scales 16; d from the row's f16 array). With
-// t = 2n + h, value 64t + i takes ql[64n + i] nibble h and qh[32n + (i & 31)]
-// bits 4h + 2 (i >> 5); its scale is sc[4t + i / 16].
-__device__ __forceinline__ void qg_deq_q6k(const uint8_t* body, float d, int t, float (&v)[64]) {
-  const int n = t >> 1, h = t & 1;
-  uint32_t lw[16], hw[8];
+// Q6_K (BlockQ6K::to_float; device body: ql 128, qh 64, i8 scales 16, d from
+// the row's f16 array): stage t = 2n + hq holds values 128n + 64hq + [0, 64);
+// K half h: value 32h + l takes ql[64n + 32h + l] nibble hq and
+// qh[32n + l] bits 4hq + 2h, scale sc[4t + 2h + l / 16]; (d * sc) * (q - 32).
+__device__ __forceinline__ void qg_deq_q6k(const uint8_t* body, float d, int t, int h, uint32_t (&o)[16]) {
+  const int n = t >> 1, hq = t & 1;
+  const uint4 l0 = *reinterpret_cast<const uint4*>(body + 64 * n + 32 * h);
+  const uint4 l1 = *reinterpret_cast<const uint4*>(body + 64 * n + 32 * h + 16);
+  const uint4 h0 = *reinterpret_cast<const uint4*>(body + 128 + 32 * n);
+  const uint4 h1 = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + 16);
+  const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const uint32_t sc2 = *reinterpret_cast<const uint16_t*>(body + 192 + 4 * t + 2 * h);
+  const float s0 = __fmul_rn(d, (float)(int8_t)(sc2 & 0xffu)), s1 = __fmul_rn(d, (float)(int8_t)(sc2 >> 8));
+  const uint64_t bias = f2_pack(-8388640.f, -8388640.f);  // -(2^23 + 32)
+  const uint64_t ss0 = f2_pack(s0, s0), ss1 = f2_pack(s1, s1);
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(body + 64 * n) + i);
-    lw[4 * i] = a.x; lw[4 * i + 1] = a.y; lw[4 * i + 2] = a.z; lw[4 * i + 3] = a.w;
-  }
+  for (int w = 0; w < 8; w++) {
+    const uint32_t x = ((lw[w] >> (4 * hq)) & 0x0F0F0F0Fu) | (((hw[w] >> (4 * hq + 2 * h)) & 0x03030303u) << 4);
 #pragma unroll
-  for (int i = 0; i < 2; i++) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(body + 128 + 32 * n) + i);
-    hw[4 * i] = a.x; hw[4 * i + 1] = a.y; hw[4 * i + 2] = a.z; hw[4 * i + 3] = a.w;
-  }
-  const uint32_t sc4 = __ldg(reinterpret_cast<const uint32_t*>(body + 192 + 4 * t));
-#pragma unroll
-  for (int i = 0; i < 64; i++) {
-    const uint32_t lo = (lw[i >> 2] >> (8 * (i & 3) + 4 * h)) & 0xFu;
-    const uint32_t hi = (hw[(i & 31) >> 2] >> (8 * (i & 3) + 4 * h + 2 * (i >> 5))) & 0x3u;
-    const int q = (int)(lo | (hi << 4)) - 32;
-    const float sc = (float)(int8_t)((sc4 >> (8 * (i >> 4))) & 0xffu);
-    v[i] = __fmul_rn(__fmul_rn(d, sc), (float)q);
+    for (int i = 0; i < 2; i++) {
+      const uint64_t q = f2_add(f2_pack(qg_byte_f(x, 2 * i), qg_byte_f(x, 2 * i + 1)), bias);
+      o[2 * w + i] = f2_to_h2(f2_mul(w < 4 ? ss0 : ss1, q));
+    }
   }
 }
 
-__global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const QgParams p) {
+// 2-D TMA load (no multicast) of a box of raw weight rows into shared memory.
+__device__ __forceinline__ void qg_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Segment holding weight row n (its index and the row within it), -1 past the end.
+__device__ __forceinline__ int qg_find_seg(const QgParams& p, int n, int& local) {
+  int base = 0, si = -1;
+  local = 0;
+  for (int s2 = 0; s2 < p.nseg; s2++) {
+    if (n >= base && n < base + p.seg[s2].rows) { si = s2; local = n - base; }
+    base += p.seg[s2].rows;
+  }
+  return si;
+}
+
+// Grid: x = 128-row weight tiles, y = token tiles (p.ntok tokens), z = K
+// splits (p.kb_split super-blocks each).
+__global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgMaps maps, const QgParams p) {
   extern __shared__ uint8_t qg_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 1024-byte aligned tiles (the swizzle pattern repeats every 1024 bytes)
   const uint32_t raw_addr = smem_u32(qg_raw);
   uint8_t* smem = qg_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* a_st = smem;
-  uint8_t* b_st = smem + QG_STAGES * QG_TILE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * QG_STAGES * QG_TILE_BYTES);
+  const int ntok = p.ntok;
+  const uint32_t b_bytes = (uint32_t)ntok * 128u;
+  uint8_t* b_st = smem;                            // token tiles: QG_STAGES x ntok rows x 128 B
+  uint8_t* rw = b_st + QG_STAGES * b_bytes;        // raw weight slots (128-byte aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(rw + QG_RAW_SLOTS * QG_RAW_SLOT_BYTES);
   uint64_t* empty = full + QG_STAGES;
-  uint64_t* accb = empty + QG_STAGES;
+  uint64_t* rfull = empty + QG_STAGES;
+  uint64_t* rempty = rfull + QG_RAW_SLOTS;
+  uint64_t* accb = rempty + QG_RAW_SLOTS;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(accb + 1);
-  __shared__ int s_fail;
 
-  const int n0 = blockIdx.x * QG_N, m0 = blockIdx.y * QG_M;
-  const int nk = p.k / QG_K;
+  const int n0 = blockIdx.x * QG_W, t0 = blockIdx.y * ntok;
+  const int nb_all = p.k / QK_K;
+  const int kb0 = blockIdx.z * p.kb_split, nblk = min(nb_all, kb0 + p.kb_split) - kb0;
+  const int nk = 4 * nblk;
   if (tid == 0) {
     for (int s = 0; s < QG_STAGES; s++) {
-      mbar_init(&full[s], 1 + 4);   // A copy (arrive + tx) and the 4 dequantising warps
-      mbar_init(&empty[s], 1);      // tcgen05.commit after the stage's MMAs
+      mbar_init(&full[s], 1 + QG_DEQ_WARPS);  // token copy (arrive + tx) and the dequantising warps
+      mbar_init(&empty[s], 1);                // tcgen05.commit after the stage's MMAs
+    }
+    for (int r = 0; r < QG_RAW_SLOTS; r++) {
+      mbar_init(&rfull[r], 1);                // the raw loader's arrival + tx
+      mbar_init(&rempty[r], QG_DEQ_WARPS);    // every dequantising warp done with the slot
     }
     mbar_init(accb, 1);
     fence_mbar_init();
-    s_fail = 0;
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                 "r"(QG_N)
+                 "r"(p.tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -184,17 +275,31 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const QgParams p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t taddr = *tslot;
+  const uint32_t t_a = taddr + (uint32_t)p.acc_cols;  // A stages: 32 columns each
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint8_t* asrc = p.a_tiles + (size_t)blockIdx.y * nk * QG_TILE_BYTES;
-      const uint64_t pol = l2_evict_first_policy();
+      // token rows [t0, t0 + ntok) of k-chunk kc: within one 128-token tile
+      // (ntok <= 128, t0 = 0) or two whole tiles (ntok = 256)
+      const int nkc_all = p.k / QG_K;
+      const int parts = ntok > 128 ? 2 : 1;
+      const uint32_t part_bytes = ntok > 128 ? QG_TILE_BYTES : b_bytes;
+      // the activation tiles come from the previous kernel (programmatic
+      // dependent launch: everything before this point overlaps it; the
+      // epilogue's stores follow the MMAs, which follow these copies)
+      pdl_wait();
+      const uint64_t pol = l2_evict_last_policy();
       int issued = 0;
       for (int kc = 0; kc < nk; kc++) {
         const int s = kc % QG_STAGES;
         if (kc >= QG_STAGES && !qg_wait(&empty[s], (uint32_t)((kc / QG_STAGES - 1) & 1), p.err)) break;
-        mbar_arrive_tx(&full[s], QG_TILE_BYTES);
-        bulk_g2s(a_st + s * QG_TILE_BYTES, asrc + (size_t)kc * QG_TILE_BYTES, QG_TILE_BYTES, &full[s], pol);
+        mbar_arrive_tx(&full[s], b_bytes);
+        const int kcg = 4 * kb0 + kc;
+        for (int part = 0; part < parts; part++) {
+          const int mt = t0 / 128 + part;
+          bulk_g2s(b_st + s * b_bytes + part * QG_TILE_BYTES,
+                   p.a_tiles + ((size_t)mt * nkc_all + kcg) * QG_TILE_BYTES, part_bytes, &full[s], pol);
+        }
         issued = kc + 1;
       }
       // every copy this thread issued has landed before the CTA may exit
@@ -203,74 +308,112 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const QgParams p) {
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = qg_instr_desc();
+      const uint32_t idesc = qg_instr_desc(ntok);
       for (int kc = 0; kc < nk; kc++) {
         const int s = kc % QG_STAGES;
         if (!qg_wait(&full[s], (uint32_t)((kc / QG_STAGES) & 1), p.err)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(a_st + s * QG_TILE_BYTES), b0 = smem_u32(b_st + s * QG_TILE_BYTES);
+        const uint32_t b0 = smem_u32(b_st + s * b_bytes);
 #pragma unroll
-        for (int kk = 0; kk < QG_K / 16; kk++)   // K = 16 per MMA: 32 bytes along the swizzled row
-          qg_mma(taddr, qg_smem_desc(a0 + 32 * kk), qg_smem_desc(b0 + 32 * kk), idesc, (kc | kk) != 0);
+        for (int kk = 0; kk < QG_K / 16; kk++)   // K = 16 per MMA: 8 columns of A, 32 bytes along B's rows
+          qg_mma_ts(taddr, t_a + 32 * s + 8 * kk, qg_smem_desc(b0 + 32 * kk), idesc, (kc | kk) != 0);
         qg_commit(&empty[s]);
       }
       qg_commit(accb);  // also on an early exit: completes once the issued MMAs have
     }
     __syncwarp();
-  } else {
-    // ---- W producers: thread r owns weight row n0 + r of the tile ----
-    const int r = tid - 64;
-    const int n = n0 + r;
-    int si = -1, nl = 0;
-    {
-      int base = 0;
-      for (int s = 0; s < p.nseg; s++) {
-        if (n >= base && n < base + p.seg[s].rows) { si = s; nl = n - base; }
-        base += p.seg[s].rows;
-      }
-    }
-    const uint8_t* wrow = si >= 0 ? p.seg[si].w + (size_t)nl * p.seg[si].row_bytes : nullptr;
-    const int wtype = si >= 0 ? p.seg[si].type : 0;
-    const int nb = p.k / QK_K;
-    bool ok = true;
-    for (int kc = 0; kc < nk; kc++) {
-      const int s = kc % QG_STAGES;
-      if (kc >= QG_STAGES && !qg_wait(&empty[s], (uint32_t)((kc / QG_STAGES - 1) & 1), p.err)) { ok = false; break; }
-      float v[64];
-      const int blk = kc >> 2, c = kc & 3;
-      if (!wrow) {
+  } else if (warp == 2) {
+    if (lane == 0) {
+      // raw super-blocks: 32-row groups g of the tile, each from the segment
+      // holding it (segments before the last hold multiples of 32 rows; rows
+      // past a segment's end or the matrix are zero-filled by the TMA unit)
+      int gseg[4], grow[4], gbb[4];
+      uint32_t tx = 0;
 #pragma unroll
-        for (int i = 0; i < 64; i++) v[i] = 0.f;
-      } else if (wtype == GGML_Q4_K) {
-        qg_deq_q4k(wrow + (size_t)blk * Q4K_BLOCK_BYTES, c, v);
-      } else {
-        const float d = h2f(__ldg(reinterpret_cast<const uint16_t*>(wrow + (size_t)nb * Q6K_BODY_BYTES) + blk));
-        qg_deq_q6k(wrow + (size_t)blk * Q6K_BODY_BYTES, d, c, v);
+      for (int g = 0; g < 4; g++) {
+        int nl;
+        int si = qg_find_seg(p, n0 + 32 * g, nl);
+        if (si < 0) { si = p.nseg - 1; nl = p.seg[si].rows; }  // past the matrix: all fill
+        gseg[g] = si;
+        grow[g] = nl;
+        gbb[g] = p.seg[si].type == GGML_Q4_K ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES;
+        tx += 32u * (uint32_t)gbb[g];
       }
-      qg_store_row(b_st + s * QG_TILE_BYTES, r, v);
-      fence_async_smem();  // generic-proxy writes -> visible to the tensor cores
+      int issued = 0;
+      for (int b = 0; b < nblk; b++) {
+        const int r = b % QG_RAW_SLOTS;
+        if (b >= QG_RAW_SLOTS && !qg_wait(&rempty[r], (uint32_t)((b / QG_RAW_SLOTS - 1) & 1), p.err)) break;
+        mbar_arrive_tx(&rfull[r], tx);
+#pragma unroll
+        for (int g = 0; g < 4; g++)
+          qg_tma_load(rw + r * QG_RAW_SLOT_BYTES + g * QG_RAW_GROUP_BYTES, &maps.m[gseg[g]], (kb0 + b) * gbb[g],
+                      grow[g], &rfull[r]);
+        issued = b + 1;
+      }
+      for (int b = issued > QG_RAW_SLOTS ? issued - QG_RAW_SLOTS : 0; b < issued; b++)
+        qg_wait(&rfull[b % QG_RAW_SLOTS], (uint32_t)((b / QG_RAW_SLOTS) & 1), p.err);
+    }
+  } else {
+    // ---- W dequantisers: warp -> tensor-memory lane quarter q, K half hh ----
+    const int q = warp & 3, hh = (warp - 3) >> 2;
+    const int r = 32 * q + lane, n = n0 + r;
+    int nl;
+    const int si = qg_find_seg(p, n, nl);
+    const int wtype = si >= 0 ? p.seg[si].type : 0;
+    const int bb = wtype == GGML_Q4_K ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES;
+    const uint16_t* q6d = (si >= 0 && wtype == GGML_Q6_K)
+                              ? reinterpret_cast<const uint16_t*>(p.seg[si].w + (size_t)nl * p.seg[si].row_bytes +
+                                                                  (size_t)nb_all * Q6K_BODY_BYTES)
+                              : nullptr;
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    uint4 hd = make_uint4(0, 0, 0, 0);
+    float d6 = 0.f;
+    for (int kc = 0; kc < nk; kc++) {
+      const int s = kc % QG_STAGES, b = kc >> 2, c = kc & 3, rs = b % QG_RAW_SLOTS;
+      const uint8_t* row = rw + rs * QG_RAW_SLOT_BYTES + q * QG_RAW_GROUP_BYTES + lane * bb;
+      if (c == 0) {
+        if (!qg_wait_warp(&rfull[rs], (uint32_t)((b / QG_RAW_SLOTS) & 1), p.err)) break;
+        if (q6d) d6 = h2f(__ldg(q6d + kb0 + b));
+        else hd = *reinterpret_cast<const uint4*>(row);
+      }
+      uint32_t o[16];
+      if (si < 0) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) o[i] = 0u;
+      } else if (wtype == GGML_Q4_K) {
+        qg_deq_q4k(row, hd, c, hh, o);
+      } else {
+        qg_deq_q6k(row, d6, c, hh, o);
+      }
+      __syncwarp();
+      if (lane == 0 && c == 3) mbar_arrive1(&rempty[rs]);  // the raw slot's last stage has been read
+      // the MMAs of the stage that last used these columns have completed
+      if (kc >= QG_STAGES && !qg_wait_warp(&empty[s], (uint32_t)((kc / QG_STAGES - 1) & 1), p.err)) break;
+      tc_fence_after();
+      qg_tmem_st16(t_a + lane_base + 32 * s + 16 * hh, o);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive1(&full[s]);
     }
-    if (!ok) atomicExch(&s_fail, 1);
-    // ---- epilogue: this warp's 32 tokens x 128 columns ----
-    const bool acc_ok = qg_wait(accb, 0, p.err);
+    // ---- epilogue: this warp's 32 weight rows x token half hh ----
+    const bool acc_ok = qg_wait_warp(accb, 0, p.err);
     tc_fence_after();
-    const int q = warp & 3;                 // tensor-memory lane quarter of this warp
-    const int m = m0 + 32 * q + lane;
     if (acc_ok) {
+      float* out = p.out + (size_t)blockIdx.z * p.split_stride;
+      const int half = ntok >> 1;
 #pragma unroll 1
-      for (int c0 = 0; c0 < QG_N; c0 += 16) {
-        float v[16];
-        qg_tmem_ld16(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-        if (m < p.m) {
-          float* o = p.out + (size_t)m * p.ldo + n0 + c0;
-          if (n0 + c0 + 16 <= p.n) {
+      for (int c0 = hh * half; c0 < (hh + 1) * half; c0 += 8) {
+        float v[8];
+        qg_tmem_ld8(taddr + lane_base + (uint32_t)c0, v);
+        if (n < p.n) {
 #pragma unroll
-            for (int i = 0; i < 16; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-            for (int i = 0; i < 16; i++)
-              if (n0 + c0 + i < p.n) o[i] = v[i];
+          for (int j = 0; j < 8; j++) {
+            const int t = t0 + c0 + j;
+            if (t < p.m) {
+              float* o = out + (size_t)t * p.ldo + n;
+              *o = p.add ? __fadd_rn(v[j], *o) : v[j];
+            }
           }
         }
       }
@@ -280,105 +423,171 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const QgParams p) {
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(QG_N) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(p.tmem_cols) : "memory");
   }
 }
 
-// ---- A operand: (rms-norm +) Q8_K + f16 expansion into swizzled tiles ------
-// One CTA (256 threads) per token row; rows m..m_pad-1 are zero. The norm
-// follows candle's rms_norm with per-block partial sums added in block order
-// (as the decode kernels); Q8_K as BlockQ8K::from_float.
-__global__ void __launch_bounds__(256) k_qgemm_act(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                   float eps, int m, int k, uint8_t* __restrict__ a_tiles) {
+// ---- B operand: (rms-norm +) Q8_K + f16 expansion into swizzled tiles ------
+// Q8_K (BlockQ8K::from_float: the first value of largest magnitude sets the
+// scale) of one 256-value block j held 8 per lane (values 8 lane .. + 7),
+// expanded to f16 q * d, into token row r of the block's four k-chunk tiles.
+__device__ __forceinline__ void qg_act_block(const float (&v)[8], int lane, int j, int r, uint8_t* tbase) {
+  float amax = 0.f, mx = 0.f;
+  int idx = 0x7fffffff;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const float av = fabsf(v[i]);
+    if (amax < av) { amax = av; mx = v[i]; idx = 8 * lane + i; }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
+    const float om = __shfl_xor_sync(0xffffffffu, mx, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
+    if (oa > amax || (oa == amax && oi < idx)) { amax = oa; mx = om; idx = oi; }
+  }
+  __half2 h[4];
+  if (amax != 0.f) {
+    const float iscale = __fdiv_rn(-128.f, mx);
+    const float d = __fdiv_rn(1.0f, iscale);
+    float q[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) q[i] = __fmul_rn(fmaxf(fminf(roundf(__fmul_rn(iscale, v[i])), 127.f), -128.f), d);
+#pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(q[2 * i], q[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(0.f, 0.f);
+  }
+  // values [j*256 + 8 lane, +8): k-chunk 4j + lane/8, 16-byte chunk lane % 8
+  const int kc = 4 * j + (lane >> 3), c = lane & 7;
+  *reinterpret_cast<uint4*>(tbase + (size_t)kc * QG_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
+      *reinterpret_cast<uint4*>(h);
+}
+
+__device__ __forceinline__ void qg_ld8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// The split sums of 8 consecutive columns, added in split order.
+__device__ __forceinline__ void qg_split_sum8(const QgSplit& g, size_t off, float (&v)[8]) {
+  qg_ld8(g.ws + off, v);
+  int sp = 1;
+  for (; sp + 4 <= g.splits; sp += 4) {  // four partials in flight
+    float w[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++) qg_ld8(g.ws + (size_t)(sp + u) * g.stride + off, w[u]);
+#pragma unroll
+    for (int u = 0; u < 4; u++)
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], w[u][i]);
+  }
+  for (; sp < g.splits; sp++) {
+    float w[8];
+    qg_ld8(g.ws + (size_t)sp * g.stride + off, w);
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], w[i]);
+  }
+}
+
+enum { ACT_X = 0, ACT_RESID = 1, ACT_SILU = 2 };
+struct RowAct {
+  const float* x;    // ACT_X: input rows [m][k]
+  float* xo;         // ACT_RESID: residual rows [m][k], updated in place
+  const float* gamma;
+  float eps;
+  int k;
+  QgSplit g;         // ACT_RESID, ACT_SILU
+  uint8_t* a_tiles;  // null: no tiles (ACT_RESID only)
+};
+
+// One CTA (256 threads) per token row: the row's values (ACT_X: x;
+// ACT_RESID: x + the split sums, stored back; ACT_SILU: silu(gate) * up from
+// the split sums), optionally rms-normalised with gamma, as activation tiles.
+// The norm follows candle's rms_norm with per-block partial sums added in
+// block order (as the decode kernels).
+template <int KIND>
+__global__ void __launch_bounds__(256) k_row_act(const RowAct p) {
+  pdl_launch();
+  pdl_wait();
   __shared__ float part[64];  // K <= 16384
   __shared__ float s_rms;
   const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nb = k / QK_K, nkc = k / QG_K;
-  uint8_t* tbase = a_tiles + (size_t)(row / QG_M) * nkc * QG_TILE_BYTES;
-  const int r = row % QG_M;
-  if (row >= m) {
-    for (int c = tid; c < nkc * 8; c += blockDim.x)
-      *reinterpret_cast<uint4*>(tbase + (size_t)(c >> 3) * QG_TILE_BYTES + r * 128 + (((c & 7) ^ (r & 7)) << 4)) =
-          make_uint4(0, 0, 0, 0);
-    return;
-  }
-  const float* xr = x + (size_t)row * k;
-  float inv_m = 1.f;
-  if (gamma) {
-    for (int j = warp; j < nb; j += 8) {
-      const float4 a = *reinterpret_cast<const float4*>(xr + j * QK_K + 8 * lane);
-      const float4 b = *reinterpret_cast<const float4*>(xr + j * QK_K + 8 * lane + 4);
-      float ss = a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x + b.y * b.y + b.z * b.z + b.w * b.w;
+  const int k = p.k, nb = k / QK_K, nkc = k / QG_K;
+  uint8_t* tbase = p.a_tiles ? p.a_tiles + (size_t)(row / 128) * nkc * QG_TILE_BYTES : nullptr;
+  const int r = row % 128;
+  const float* xr = KIND == ACT_X ? p.x + (size_t)row * k : p.xo + (size_t)row * k;
+  const bool norm = p.gamma != nullptr && tbase != nullptr;
+  for (int j = warp; j < nb; j += 8) {
+    const int col = j * QK_K + 8 * lane;
+    float v[8];
+    if (KIND == ACT_X) {
+      qg_ld8(xr + col, v);
+    } else if (KIND == ACT_RESID) {
+      float x0[8];
+      qg_split_sum8(p.g, (size_t)row * p.g.ld + col, v);
+      qg_ld8(xr + col, x0);
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], x0[i]);
+      float* xw = p.xo + (size_t)row * k + col;
+      *reinterpret_cast<float4*>(xw) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(xw + 4) = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+      float u[8];
+      qg_split_sum8(p.g, (size_t)row * p.g.ld + col, v);
+      qg_split_sum8(p.g, (size_t)row * p.g.ld + k + col, u);
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), u[i]);
+    }
+    if (norm) {
+      float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3] + v[4] * v[4] + v[5] * v[5] + v[6] * v[6] +
+                 v[7] * v[7];
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (lane == 0) part[j] = ss;
+    } else if (tbase) {
+      qg_act_block(v, lane, j, r, tbase);
     }
-    __syncthreads();
-    if (tid == 0) {
-      float sum2 = 0.f;
-      for (int j = 0; j < nb; j++) sum2 += part[j];
-      s_rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)k), eps));
-    }
-    __syncthreads();
-    inv_m = s_rms;
   }
+  if (!norm) return;
+  __syncthreads();
+  if (tid == 0) {
+    float sum2 = 0.f;
+    for (int j = 0; j < nb; j++) sum2 += part[j];
+    s_rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(sum2, (float)k), p.eps));
+  }
+  __syncthreads();
+  const float rms = s_rms;
   for (int j = warp; j < nb; j += 8) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + j * QK_K + 8 * lane);
-    const float4 b = *reinterpret_cast<const float4*>(xr + j * QK_K + 8 * lane + 4);
-    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    if (gamma) {
-      const float4 g0 = *reinterpret_cast<const float4*>(gamma + j * QK_K + 8 * lane);
-      const float4 g1 = *reinterpret_cast<const float4*>(gamma + j * QK_K + 8 * lane + 4);
-      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const int col = j * QK_K + 8 * lane;
+    float v[8], g[8];
+    qg_ld8(xr + col, v);  // ACT_RESID: this thread's own stores above
+    qg_ld8(p.gamma + col, g);
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], inv_m), g[i]);
-    }
-    // BlockQ8K::from_float: first value of largest magnitude sets the scale
-    float amax = 0.f, mx = 0.f;
-    int idx = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float av = fabsf(v[i]);
-      if (amax < av) { amax = av; mx = v[i]; idx = 8 * lane + i; }
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-      const float om = __shfl_xor_sync(0xffffffffu, mx, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-      if (oa > amax || (oa == amax && oi < idx)) { amax = oa; mx = om; idx = oi; }
-    }
-    __half2 h[4];
-    if (amax != 0.f) {
-      const float iscale = __fdiv_rn(-128.f, mx);
-      const float d = __fdiv_rn(1.0f, iscale);
-      float q[8];
-#pragma unroll
-      for (int i = 0; i < 8; i++) q[i] = __fmul_rn(fmaxf(fminf(roundf(__fmul_rn(iscale, v[i])), 127.f), -128.f), d);
-#pragma unroll
-      for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(q[2 * i], q[2 * i + 1]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 4; i++) h[i] = __floats2half2_rn(0.f, 0.f);
-    }
-    // values [j*256 + 8 lane, +8): k-chunk 4j + lane/8, 16-byte chunk lane % 8
-    const int kc = 4 * j + (lane >> 3), c = lane & 7;
-    *reinterpret_cast<uint4*>(tbase + (size_t)kc * QG_TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) =
-        *reinterpret_cast<uint4*>(h);
+    for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], rms), g[i]);
+    qg_act_block(v, lane, j, r, tbase);
   }
 }
 
-// ---- prefill epilogues --------------------------------------------------
-__global__ void k_qkv_post(const float* __restrict__ g, int ldg, int S, const int* __restrict__ pos, int qn,
-                           int kn, int hd, int max_seq, const float* __restrict__ cos_t,
-                           const float* __restrict__ sin_t, float* __restrict__ q_out, void* kc, void* vc,
-                           int kv_f16) {
+// ---- q|k|v epilogue -------------------------------------------------------
+__global__ void k_qkv_post(const QgSplit g, int S, const int* __restrict__ pos, int qn, int kn, int hd,
+                           int max_seq, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                           float* __restrict__ q_out, void* kc, void* vc, int kv_f16, int64_t slot_stride) {
+  pdl_launch();
+  pdl_wait();
   const int t = blockIdx.y;
   const int pr = blockIdx.x * blockDim.x + threadIdx.x;  // row pair
-  const int rows = ldg;
+  const int rows = g.ld;
   if (t >= S || 2 * pr >= rows) return;
   const int r = 2 * pr;
-  const float d0 = g[(size_t)t * ldg + r], d1 = g[(size_t)t * ldg + r + 1];
+  const float* w = g.ws + (size_t)t * g.ld + r;
+  float d0 = w[0], d1 = w[1];
+  for (int sp = 1; sp < g.splits; sp++) {
+    d0 = __fadd_rn(d0, w[(size_t)sp * g.stride]);
+    d1 = __fadd_rn(d1, w[(size_t)sp * g.stride + 1]);
+  }
   const int p = pos[t], half = hd >> 1;
   if (r < qn + kn) {
     const int rr = r < qn ? r : r - qn;
@@ -391,12 +600,12 @@ __global__ void k_qkv_post(const float* __restrict__ g, int ldg, int S, const in
       *reinterpret_cast<float2*>(q_out + (size_t)t * qn + r) = make_float2(o0, o1);
     } else {
       const int kvh = rr / hd, dd = rr % hd;
-      store_kv(kc, kv_f16, ((int64_t)kvh * max_seq + p) * hd + dd, o0, o1);
+      store_kv(kc, kv_f16, t * slot_stride + ((int64_t)kvh * max_seq + p) * hd + dd, o0, o1);
     }
   } else {
     const int rv = r - qn - kn;
     const int kvh = rv / hd, dd = rv % hd;
-    store_kv(vc, kv_f16, ((int64_t)kvh * max_seq + p) * hd + dd, d0, d1);
+    store_kv(vc, kv_f16, t * slot_stride + ((int64_t)kvh * max_seq + p) * hd + dd, d0, d1);
   }
 }
 
@@ -405,19 +614,103 @@ __global__ void k_resid_add(float* __restrict__ x, const float* __restrict__ g, 
   if (t < S && i < n) x[(size_t)t * n + i] = __fadd_rn(g[(size_t)t * ldg + i], x[(size_t)t * n + i]);
 }
 
-__global__ void k_silu_mul(const float* __restrict__ g, int S, int n, float* __restrict__ h) {
+// out[t][j] = sum over splits of ws (split order), then the job's consumer.
+__global__ void k_qg_finish(const float* __restrict__ ws, int splits, size_t split_stride, int m, int ncols, int ldw,
+                            int mode, float* __restrict__ dst, int ldd) {
+  pdl_launch();
+  pdl_wait();
   const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= S || i >= n) return;
-  const float v = g[(size_t)t * 2 * n + i], u = g[(size_t)t * 2 * n + n + i];
-  h[(size_t)t * n + i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))), u);
+  if (t >= m || i >= ncols) return;
+  const float* w = ws + (size_t)t * ldw + i;
+  float a = w[0];
+  for (int sp = 1; sp < splits; sp++) a = __fadd_rn(a, w[(size_t)sp * split_stride]);
+  float* o = dst + (size_t)t * ldd + i;
+  if (mode == QG_STORE) {
+    *o = a;
+  } else if (mode == QG_RESID) {
+    *o = __fadd_rn(a, *o);
+  } else {
+    float u = w[ncols];
+    for (int sp = 1; sp < splits; sp++) u = __fadd_rn(u, w[(size_t)sp * split_stride + ncols]);
+    *o = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), u);
+  }
 }
 
-int qkv_post_launch(const float* g, int ldg, int S, const int* pos, int qn, int kn, int hd, int max_seq,
+// token[t] = argmax of logits row t (am_better order), pos[t] += 1. Each
+// thread scans a strided slice, 4 loads in flight.
+__global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ logits, int n, uint32_t* token,
+                                                     int* pos) {
+  pdl_launch();
+  pdl_wait();
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
+  const float* row = logits + (size_t)t * n;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  int i = tid;
+  for (; i + 3 * nt < n; i += 4 * nt) {
+    const float v0 = __ldg(row + i), v1 = __ldg(row + i + nt), v2 = __ldg(row + i + 2 * nt),
+                v3 = __ldg(row + i + 3 * nt);
+    if (am_better(v0, i, bv, bi)) { bv = v0; bi = i; }
+    if (am_better(v1, i + nt, bv, bi)) { bv = v1; bi = i + nt; }
+    if (am_better(v2, i + 2 * nt, bv, bi)) { bv = v2; bi = i + 2 * nt; }
+    if (am_better(v3, i + 3 * nt, bv, bi)) { bv = v3; bi = i + 3 * nt; }
+  }
+  for (; i < n; i += nt) {
+    const float v = __ldg(row + i);
+    if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+  }
+  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  __syncthreads();
+  if (tid == 0) {
+    for (int w = 1; w < (nt >> 5); w++)
+      if (am_better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+    token[t] = (uint32_t)(bi == 0x7fffffff ? 0 : bi);
+    pos[t] += 1;
+  }
+}
+
+// ---- launchers --------------------------------------------------------------
+int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int hd, int max_seq,
                     const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
-                    cudaStream_t s) {
-  const dim3 grid((unsigned)((ldg / 2 + 127) / 128), (unsigned)S);
-  k_qkv_post<<<grid, 128, 0, s>>>(g, ldg, S, pos, qn, kn, hd, max_seq, cos_t, sin_t, q_out, kc, vc, kv_f16);
-  ARMAI_CUDA(cudaGetLastError());
+                    int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl) {
+  if (S <= 0) return ARMAI_OK;
+  const dim3 grid((unsigned)((g.ld / 2 + 127) / 128), (unsigned)S);
+  ARMAI_CUDA(qg_launch(k_qkv_post, grid, dim3(128), 0, s, pdl, g, S, pos, qn, kn, hd, max_seq, cos_t, sin_t,
+                       q_out, kc, vc, kv_f16, (int64_t)(kv_seq_stride * seq_step)));
+  return ARMAI_OK;
+}
+
+int resid_act_launch(const QgSplit& g, float* x, int S, int n, const float* gamma, float eps, uint8_t* a_tiles,
+                     cudaStream_t s, bool pdl) {
+  if (n % QK_K || n / QK_K > 64) return fail(ARMAI_E_INVALID, "resid_act: n must be a multiple of 256, at most 16384");
+  if (S <= 0) return ARMAI_OK;
+  RowAct p{};
+  p.xo = x;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.k = n;
+  p.g = g;
+  p.a_tiles = a_tiles;
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_RESID>, dim3(S), dim3(256), 0, s, pdl, p));
+  return ARMAI_OK;
+}
+
+int silu_act_launch(const QgSplit& g, int S, int F, uint8_t* a_tiles, cudaStream_t s, bool pdl) {
+  if (F % QK_K || F / QK_K > 64) return fail(ARMAI_E_INVALID, "silu_act: F must be a multiple of 256, at most 16384");
+  if (S <= 0) return ARMAI_OK;
+  RowAct p{};
+  p.k = F;
+  p.g = g;
+  p.a_tiles = a_tiles;
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_SILU>, dim3(S), dim3(256), 0, s, pdl, p));
   return ARMAI_OK;
 }
 
@@ -427,32 +720,169 @@ int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream
   return ARMAI_OK;
 }
 
-int silu_mul_launch(const float* g, int S, int n, float* h, cudaStream_t s) {
-  k_silu_mul<<<dim3((unsigned)((n + 255) / 256), (unsigned)S), 256, 0, s>>>(g, S, n, h);
-  ARMAI_CUDA(cudaGetLastError());
+int row_argmax_launch(const float* logits, int S, int n, uint32_t* token, int* pos, cudaStream_t s, bool pdl) {
+  if (S <= 0) return ARMAI_OK;
+  ARMAI_CUDA(qg_launch(k_row_argmax, dim3(S), dim3(1024), 0, s, pdl, logits, n, token, pos));
   return ARMAI_OK;
 }
 
 int qgemm_act_launch(const float* x, const float* gamma, float eps, int m, int k, uint8_t* a_tiles,
-                     cudaStream_t s) {
+                     cudaStream_t s, bool pdl) {
   if (k % QK_K || k / QK_K > 64) return fail(ARMAI_E_INVALID, "qgemm: K must be a multiple of 256, at most 16384");
-  const int m_pad = ((m + QG_M - 1) / QG_M) * QG_M;
-  k_qgemm_act<<<m_pad, 256, 0, s>>>(x, gamma, eps, m, k, a_tiles);
-  ARMAI_CUDA(cudaGetLastError());
+  if (m <= 0) return ARMAI_OK;
+  RowAct p{};
+  p.x = x;
+  p.gamma = gamma;
+  p.eps = eps;
+  p.k = k;
+  p.a_tiles = a_tiles;
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_X>, dim3(m), dim3(256), 0, s, pdl, p));
   return ARMAI_OK;
 }
 
-int qgemm_launch(const QgParams& p, cudaStream_t s) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 qg_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// The tensor map of one weight segment, built once per (address, shape,
+// type): weights do not move while a model is loaded, so the maps are reused
+// by every later launch (and by captured graphs, which hold them by value).
+int qg_weight_map(const QgSeg& sg, CUtensorMap* out) {
+  struct Key {
+    const void* w;
+    int type, rows, row_bytes;
+    bool operator==(const Key& o) const {
+      return w == o.w && type == o.type && rows == o.rows && row_bytes == o.row_bytes;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.w) ^ ((size_t)k.rows << 20) ^ ((size_t)k.row_bytes << 40) ^ (size_t)k.type;
+    }
+  };
+  static std::mutex mu;
+  static std::unordered_map<Key, CUtensorMap, Hash> cache;
+  const Key key{sg.w, sg.type, sg.rows, sg.row_bytes};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return ARMAI_OK;
+  }
+  auto enc = qg_encoder();
+  if (!enc) return fail(ARMAI_E_CUDA, "qgemm: cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {(cuuint64_t)sg.row_bytes, (cuuint64_t)sg.rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)sg.row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)(sg.type == GGML_Q4_K ? Q4K_BLOCK_BYTES : Q6K_BODY_BYTES), 32u};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap m;
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(sg.w), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ARMAI_E_CUDA, "qgemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  cache.emplace(key, m);
+  *out = m;
+  return ARMAI_OK;
+}
+
+}  // namespace
+
+int qgemm_run(const QgJob& j, cudaStream_t s, QgSplit* split) {
   static thread_local int attr_dev = -1;
+  static thread_local int n_sms = 148;
   int dev = 0;
   ARMAI_CUDA(cudaGetDevice(&dev));
   if (attr_dev != dev) {
-    ARMAI_CUDA(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QG_SMEM));
+    ARMAI_CUDA(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)qg_smem_bytes(QG_TOK_MAX)));
+    ARMAI_CUDA(cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev));
     attr_dev = dev;
   }
-  const dim3 grid((unsigned)((p.n + QG_N - 1) / QG_N), (unsigned)((p.m + QG_M - 1) / QG_M));
-  k_qgemm<<<grid, QG_THREADS, QG_SMEM, s>>>(p);
-  ARMAI_CUDA(cudaGetLastError());
+  if (j.k <= 0 || j.k % QK_K || j.k > 16384)
+    return fail(ARMAI_E_INVALID, "qgemm: K must be a multiple of 256, at most 16384");
+  if (j.nseg < 1 || j.nseg > 3) return fail(ARMAI_E_INVALID, "qgemm: 1 to 3 weight segments");
+  if (j.mode == QG_SILU && (j.nseg != 2 || j.seg[0].rows != j.seg[1].rows))
+    return fail(ARMAI_E_INVALID, "qgemm: SiLU jobs take gate and up segments of equal rows");
+  if ((j.mode == QG_PARTIAL) != (split != nullptr))
+    return fail(ARMAI_E_INVALID, "qgemm: a QgSplit goes with QG_PARTIAL jobs");
+  QgParams p;
+  std::memset(&p, 0, sizeof p);
+  QgMaps maps;
+  std::memset(&maps, 0, sizeof maps);
+  for (int i = 0; i < j.nseg; i++) {
+    const QgSeg& sg = j.seg[i];
+    if (sg.type != GGML_Q4_K && sg.type != GGML_Q6_K)
+      return fail(ARMAI_E_INVALID, "qgemm: Q4_K / Q6_K matrices only");
+    // every segment but the last starts a 32-row group of its own
+    if ((i + 1 < j.nseg && sg.rows % 32) || sg.row_bytes % 16 || (reinterpret_cast<uintptr_t>(sg.w) & 15))
+      return fail(ARMAI_E_INVALID,
+                  "qgemm: segments before the last need rows in multiples of 32; rows 16-byte aligned");
+    ARMAI_TRY(qg_weight_map(sg, &maps.m[i]));
+    p.seg[i] = sg;
+    p.n += sg.rows;
+  }
+  if (j.m <= 0 || p.n == 0) return ARMAI_OK;
+  p.a_tiles = j.a_tiles;
+  p.m = j.m;
+  p.k = j.k;
+  p.nseg = j.nseg;
+  p.err = j.err;
+  p.ntok = j.m <= 128 ? ((j.m + 15) / 16) * 16 : QG_TOK_MAX;
+  p.acc_cols = std::max(32, p.ntok);
+  p.tmem_cols = 32;
+  while (p.tmem_cols < p.acc_cols + 32 * QG_STAGES) p.tmem_cols <<= 1;
+  const uint32_t smem = qg_smem_bytes(p.ntok);
+  int occ = 1;
+  ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_qgemm, QG_THREADS, smem));
+  occ = std::max(1, std::min(occ, 512 / p.tmem_cols));
+  const int tiles_n = (p.n + QG_W - 1) / QG_W, tiles_t = (j.m + p.ntok - 1) / p.ntok;
+  const int ctas = tiles_n * tiles_t, slots = n_sms * occ, nb = j.k / QK_K;
+  // K split: fewest (waves x (super-blocks per CTA + 1 for the CTA's fill
+  // and drain)), within the workspace
+  const size_t part = (size_t)j.m * p.n;
+  int splits = 1;
+  long best = -1;
+  for (int sp = 1; sp <= std::min(nb, 32); sp++) {
+    const int per = (nb + sp - 1) / sp, real = (nb + per - 1) / per;
+    if (real != sp) continue;
+    const bool need_ws = sp > 1 || j.mode == QG_SILU || j.mode == QG_PARTIAL;
+    if (need_ws && (!j.ws || (size_t)sp * part > j.ws_floats)) continue;
+    const long waves = ((long)ctas * sp + slots - 1) / slots;
+    const long cost = waves * (per + 1);
+    if (best < 0 || cost < best) { best = cost; splits = sp; }
+  }
+  if (best < 0) return fail(ARMAI_E_INVALID, "qgemm: workspace too small for this job");
+  p.kb_split = (nb + splits - 1) / splits;
+  const bool direct = splits == 1 && (j.mode == QG_STORE || j.mode == QG_RESID);
+  if (direct) {
+    p.out = j.dst;
+    p.ldo = j.ldd;
+    p.add = j.mode == QG_RESID;
+  } else {
+    p.out = j.ws;
+    p.ldo = p.n;
+    p.split_stride = part;
+  }
+  const dim3 grid((unsigned)tiles_n, (unsigned)tiles_t, (unsigned)splits);
+  ARMAI_CUDA(qg_launch(k_qgemm, grid, dim3(QG_THREADS), smem, s, j.pdl != 0, maps, p));
+  if (split) {
+    *split = QgSplit{j.ws, splits, part, p.n};
+  } else if (!direct) {
+    const int ncols = j.mode == QG_SILU ? p.n / 2 : p.n;
+    ARMAI_CUDA(qg_launch(k_qg_finish, dim3((unsigned)((ncols + 255) / 256), (unsigned)j.m), dim3(256), 0, s,
+                         j.pdl != 0, (const float*)j.ws, splits, part, j.m, ncols, p.n, j.mode, j.dst, j.ldd));
+  }
   return ARMAI_OK;
 }
 

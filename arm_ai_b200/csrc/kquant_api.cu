@@ -245,19 +245,25 @@ extern "C" int armai_qgemm(const void* w, int type, size_t n, size_t k, const fl
   ARMAI_CUDA(cudaMalloc(&dout.p, m * n * 4));
   ARMAI_CUDA(cudaMalloc(&derr.p, 4));
   ARMAI_CUDA(cudaMemset(derr.p, 0, 4));
+  // split-K partials: up to 8 splits
+  const size_t ws_floats = 8 * m * n;
+  DevBuf dws;
+  ARMAI_CUDA(cudaMalloc(&dws.p, ws_floats * 4));
   ARMAI_TRY(qgemm_act_launch((const float*)dx.p, (const float*)dg.p, eps, (int)m, (int)k, (uint8_t*)da.p, 0));
-  QgParams p;
-  std::memset(&p, 0, sizeof p);
-  p.a_tiles = (const uint8_t*)da.p;
-  p.m = (int)m;
-  p.n = (int)n;
-  p.k = (int)k;
-  p.seg[0] = QgSeg{(const uint8_t*)dw.p, type, (int)n, rb};
-  p.nseg = 1;
-  p.out = (float*)dout.p;
-  p.ldo = (int)n;
-  p.err = (uint32_t*)derr.p;
-  ARMAI_TRY(qgemm_launch(p, 0));
+  QgJob j;
+  std::memset(&j, 0, sizeof j);
+  j.a_tiles = (const uint8_t*)da.p;
+  j.m = (int)m;
+  j.k = (int)k;
+  j.seg[0] = QgSeg{(const uint8_t*)dw.p, type, (int)n, rb};
+  j.nseg = 1;
+  j.mode = QG_STORE;
+  j.dst = (float*)dout.p;
+  j.ldd = (int)n;
+  j.ws = (float*)dws.p;
+  j.ws_floats = ws_floats;
+  j.err = (uint32_t*)derr.p;
+  ARMAI_TRY(qgemm_run(j, 0));
   uint32_t herr = 0;
   ARMAI_CUDA(cudaMemcpy(&herr, derr.p, 4, cudaMemcpyDeviceToHost));
   if (herr) return fail(ARMAI_E_DEVICE, "qgemm: device error flag set");

@@ -97,7 +97,10 @@ struct armai_llama {
   uint8_t* pA = nullptr;       // tensor-core GEMM A tiles
   float* pG = nullptr;         // GEMM output [cap][g_cols]
   int g_cols = 0;
+  float* pWs = nullptr;        // GEMM split-K partials
+  size_t ws_floats = 0;
   int prefill_gemm = 0;        // armai_llama_opts.prefill_gemm
+  int batch_gemm = 0;          // armai_llama_opts.batch_gemm
   bool q80 = false;            // a matrix takes Q8_0 activations (Q4_0 / Q5_0 / Q8_0)
   // tensor parallelism (tp > 1): this rank holds a slice of every matrix, the
   // residual stream x is replicated, row-split products are summed by NCCL
@@ -730,17 +733,21 @@ int ensure_prefill(armai_llama* m, int S) {
   int cap = std::max(S, 64);
   cap = ((cap + PREFILL_TILE - 1) / PREFILL_TILE) * PREFILL_TILE;
   cudaFree(m->pX); cudaFree(m->pQ); cudaFree(m->pY); cudaFree(m->pH);
-  cudaFree(m->p_pos); cudaFree(m->p_tok); cudaFree(m->pA); cudaFree(m->pG);
-  m->pX = m->pQ = m->pY = m->pH = m->pG = nullptr;
+  cudaFree(m->p_pos); cudaFree(m->p_tok); cudaFree(m->pA); cudaFree(m->pG); cudaFree(m->pWs);
+  m->pX = m->pQ = m->pY = m->pH = m->pG = m->pWs = nullptr;
   m->pA = nullptr;
   m->pf_cap = 0;
+  m->ws_floats = 0;
   const size_t qn = (size_t)m->n_head * m->head_dim;
-  if (m->prefill_gemm != 1) {
+  if (m->prefill_gemm != 1 || m->batch_gemm != 1) {
     const Layer& L0 = m->layers[0];
     const int kmax = std::max(m->n_embd, std::max(m->n_ff, (int)qn));
     m->g_cols = std::max(L0.wq.rows + L0.wk.rows + L0.wv.rows, std::max(2 * m->n_ff, m->n_embd));
     ARMAI_CUDA(cudaMalloc(&m->pA, qgemm_a_bytes(cap, kmax)));
     ARMAI_CUDA(cudaMalloc(&m->pG, (size_t)cap * m->g_cols * 4));
+    // split-K partials: a few splits of long prompts, many of short ones
+    m->ws_floats = (size_t)m->g_cols * (size_t)std::max(2 * cap, 2048);
+    ARMAI_CUDA(cudaMalloc(&m->pWs, m->ws_floats * 4));
   }
   ARMAI_CUDA(cudaMalloc(&m->pX, (size_t)cap * m->n_embd * 4));
   ARMAI_CUDA(cudaMalloc(&m->pQ, (size_t)cap * qn * 4));
@@ -755,6 +762,69 @@ int ensure_prefill(armai_llama* m, int S) {
     m->h_prompt_cap = cap;
   }
   m->pf_cap = cap;
+  return ARMAI_OK;
+}
+
+// One weight GEMM of the tensor-core path over the activation tiles in pA.
+int gemm_job(armai_llama* m, std::initializer_list<const DevMat*> mats, int S, int K, int mode, float* dst,
+             int ldd, QgSplit* split = nullptr) {
+  QgJob j;
+  std::memset(&j, 0, sizeof j);
+  j.a_tiles = m->pA;
+  j.m = S;
+  j.k = K;
+  for (const DevMat* d : mats) j.seg[j.nseg++] = QgSeg{d->w, d->type, d->rows, d->row_bytes};
+  j.mode = mode;
+  j.dst = dst;
+  j.ldd = ldd;
+  j.ws = m->pWs;
+  j.ws_floats = m->ws_floats;
+  j.err = m->d_err;
+  j.pdl = m->use_pdl;
+  return qgemm_run(j, m->stream, split);
+}
+
+// One layer of S tokens through the tensor-core GEMMs. On entry pA holds the
+// activation tiles of x normalised with L.attn_norm; on return x[S][E] has
+// the layer's two residual adds and pA the tiles of the new x normalised with
+// next_gamma (none when next_gamma is null). q/y are scratch rows. Token t
+// sits at position pos[t] of sequence slot seq + t * seq_step (a prompt: one
+// slot; a decode batch: slot t).
+int gemm_layer(armai_llama* m, const Layer& L, int l, int S, float* x, float* q, float* y, const int* pos,
+               int seq_step, int seq, const float* next_gamma) {
+  const int E = m->n_embd, QN = m->n_head * m->head_dim, F = m->n_ff;
+  const bool pdl = m->use_pdl;
+  QgSplit g;
+  ARMAI_TRY(gemm_job(m, {&L.wq, &L.wk, &L.wv}, S, E, QG_PARTIAL, nullptr, 0, &g));
+  ARMAI_TRY(qkv_post_launch(g, S, pos, L.wq.rows, L.wk.rows, m->head_dim, m->max_seq, m->cos_t, m->sin_t, q,
+                            kv_seq_ptr(m, m->kc, l, seq), kv_seq_ptr(m, m->vc, l, seq), m->kv_f16,
+                            m->kv_seq_stride, seq_step, m->stream, pdl));
+  if (seq_step) {
+    ARMAI_CUDA(launch_attn(m, l, q, y, pos, S, m->kv_seq_stride, seq));
+  } else {
+    for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
+      const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
+      ARMAI_CUDA(launch_attn(m, l, q + (size_t)t0 * QN, y + (size_t)t0 * QN, pos + t0, n, 0, seq));
+    }
+  }
+  // x += W in (attn_output / ffn_down), then the next activation tiles;
+  // tensor parallel: the ranks' partial products are summed by NCCL first
+  auto resid = [&](const DevMat& w, int K, const float* gamma) -> int {
+    QgSplit r;
+    if (m->tp == 1) {
+      ARMAI_TRY(gemm_job(m, {&w}, S, K, QG_PARTIAL, nullptr, 0, &r));
+    } else {
+      ARMAI_TRY(gemm_job(m, {&w}, S, K, QG_STORE, m->pG, E));
+      ARMAI_TRY(nccl_allreduce_sum_f32(m->pG, m->pG, (size_t)S * E, m->comm, m->stream));
+      r = QgSplit{m->pG, 1, 0, E};
+    }
+    return resid_act_launch(r, x, S, E, gamma, m->eps, gamma ? m->pA : nullptr, m->stream, pdl);
+  };
+  ARMAI_TRY(qgemm_act_launch(y, nullptr, m->eps, S, QN, m->pA, m->stream, pdl));
+  ARMAI_TRY(resid(L.wo, QN, L.ffn_norm));
+  ARMAI_TRY(gemm_job(m, {&L.wg, &L.wu}, S, E, QG_PARTIAL, nullptr, 0, &g));
+  ARMAI_TRY(silu_act_launch(g, S, F, m->pA, m->stream, pdl));
+  ARMAI_TRY(resid(L.wd, F, next_gamma));
   return ARMAI_OK;
 }
 
@@ -777,46 +847,11 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
   const size_t E = m->n_embd, QN = (size_t)m->n_head * m->head_dim, F = m->n_ff;
   ARMAI_CUDA(launch_embed(m, m->p_tok, m->pX, S));
   const bool gemm = m->prefill_gemm == 2 || (m->prefill_gemm == 0 && S >= TC_PREFILL_MIN);
+  if (gemm)
+    ARMAI_TRY(qgemm_act_launch(m->pX, m->layers[0].attn_norm, m->eps, S, (int)E, m->pA, m->stream, m->use_pdl));
   for (int l = 0; l < m->n_layer && gemm; l++) {
-    const Layer& L = m->layers[l];
-    auto gemm_into = [&](std::initializer_list<const DevMat*> mats, int K, int ldo) -> int {
-      QgParams p;
-      std::memset(&p, 0, sizeof p);
-      p.a_tiles = m->pA;
-      p.m = S;
-      p.k = K;
-      int i = 0;
-      for (const DevMat* d : mats) {
-        p.seg[i++] = QgSeg{d->w, d->type, d->rows, d->row_bytes};
-        p.n += d->rows;
-      }
-      p.nseg = i;
-      p.out = m->pG;
-      p.ldo = ldo;
-      p.err = m->d_err;
-      return qgemm_launch(p, m->stream);
-    };
-    const int qkv_rows = L.wq.rows + L.wk.rows + L.wv.rows;
-    ARMAI_TRY(qgemm_act_launch(m->pX, L.attn_norm, m->eps, S, (int)E, m->pA, m->stream));
-    ARMAI_TRY(gemm_into({&L.wq, &L.wk, &L.wv}, (int)E, qkv_rows));
-    ARMAI_TRY(qkv_post_launch(m->pG, qkv_rows, S, m->p_pos, L.wq.rows, L.wk.rows, m->head_dim, m->max_seq,
-                              m->cos_t, m->sin_t, m->pQ, kv_seq_ptr(m, m->kc, l, seq), kv_seq_ptr(m, m->vc, l, seq),
-                              m->kv_f16, m->stream));
-    for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
-      const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
-      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0, seq));
-    }
-    ARMAI_TRY(qgemm_act_launch(m->pY, nullptr, m->eps, S, (int)QN, m->pA, m->stream));
-    ARMAI_TRY(gemm_into({&L.wo}, (int)QN, (int)E));
-    if (m->tp > 1) ARMAI_TRY(nccl_allreduce_sum_f32(m->pG, m->pG, (size_t)S * E, m->comm, m->stream));
-    ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
-    ARMAI_TRY(qgemm_act_launch(m->pX, L.ffn_norm, m->eps, S, (int)E, m->pA, m->stream));
-    ARMAI_TRY(gemm_into({&L.wg, &L.wu}, (int)E, (int)(2 * F)));
-    ARMAI_TRY(silu_mul_launch(m->pG, S, (int)F, m->pH, m->stream));
-    ARMAI_TRY(qgemm_act_launch(m->pH, nullptr, m->eps, S, (int)F, m->pA, m->stream));
-    ARMAI_TRY(gemm_into({&L.wd}, (int)F, (int)E));
-    if (m->tp > 1) ARMAI_TRY(nccl_allreduce_sum_f32(m->pG, m->pG, (size_t)S * E, m->comm, m->stream));
-    ARMAI_TRY(resid_add_launch(m->pX, m->pG, S, (int)E, (int)E, m->stream));
+    const float* next = l + 1 < m->n_layer ? m->layers[l + 1].attn_norm : nullptr;
+    ARMAI_TRY(gemm_layer(m, m->layers[l], l, S, m->pX, m->pQ, m->pY, m->p_pos, 0, seq, next));
   }
   for (int l = 0; l < m->n_layer && !gemm; l++) {
     int t = 0;
@@ -905,7 +940,25 @@ int enqueue_batch_step_nb(armai_llama* m, int n) {
   return ARMAI_OK;
 }
 
+// The batched step through the tensor-core GEMMs (one GPU, Q4_K / Q6_K):
+// per layer one GEMM per weight group for all n sequences, attention per
+// sequence slot, then the logits GEMM (its activation tiles carry the output
+// norm) and a row argmax.
+int enqueue_batch_step_gemm(armai_llama* m, int n) {
+  ARMAI_TRY(ensure_prefill(m, std::max(n, 64)));
+  const int E = m->n_embd;
+  ARMAI_CUDA(launch_embed(m, m->d_token, m->x, n));
+  ARMAI_TRY(qgemm_act_launch(m->x, m->layers[0].attn_norm, m->eps, n, E, m->pA, m->stream, m->use_pdl));
+  for (int l = 0; l < m->n_layer; l++) {
+    const float* next = l + 1 < m->n_layer ? m->layers[l + 1].attn_norm : m->out_norm;
+    ARMAI_TRY(gemm_layer(m, m->layers[l], l, n, m->x, m->q, m->y, m->d_pos, 1, 0, next));
+  }
+  ARMAI_TRY(gemm_job(m, {&m->output}, n, E, QG_STORE, m->logits, m->n_vocab));
+  return row_argmax_launch(m->logits, n, m->n_vocab, m->d_token, m->d_pos, m->stream, m->use_pdl);
+}
+
 int enqueue_batch_step(armai_llama* m, int n) {
+  if (m->batch_gemm != 1) return enqueue_batch_step_gemm(m, n);
   return m->batch_nb == BATCH_NB ? enqueue_batch_step_nb<BATCH_NB>(m, n)
                                  : enqueue_batch_step_nb<BATCH_NB_WIDE>(m, n);
 }
@@ -1075,7 +1128,7 @@ void free_model(armai_llama* m) {
   void* dptrs[] = {m->arena, m->cos_t, m->sin_t, m->kc, m->vc, m->x, m->q, m->y, m->h, m->logits,
                    m->d_token, m->d_pos, m->d_err, m->attn_part, m->attn_cnt, m->am_val, m->am_idx,
                    m->am_cnt, m->pX, m->pQ, m->pY, m->pH, m->p_pos, m->p_tok, m->d_phases, m->flow,
-                   m->pA, m->pG, m->tp_part, m->best_val, m->best_idx, m->tp_send, m->tp_recv,
+                   m->pA, m->pG, m->pWs, m->tp_part, m->best_val, m->best_idx, m->tp_send, m->tp_recv,
                    m->logits_all, m->xchg};
   for (void* p : dptrs)
     if (p) cudaFree(p);
@@ -1125,6 +1178,11 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     delete m;
     return fail(ARMAI_E_INVALID, "prefill_gemm must be 0, 1 or 2");
   }
+  m->batch_gemm = o.batch_gemm;
+  if (o.batch_gemm < 0 || o.batch_gemm > 2) {
+    delete m;
+    return fail(ARMAI_E_INVALID, "batch_gemm must be 0, 1 or 2");
+  }
   m->tp = std::max(1, o.tp_size);
   m->tp_rank = o.tp_rank;
   if (m->tp > 1) {
@@ -1141,6 +1199,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     // memory (decode_kernel 0), or the per-kernel chain through NCCL (1)
     m->use_pdl = false;
     m->prefill_gemm = 2;
+    m->batch_gemm = 1;  // the batched GEMM step runs on one GPU
   }
   m->n_layer = (int)block_count;
   m->n_embd = (int)embd;
@@ -1289,6 +1348,7 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
                                                  "tensor-core GEMM); this model has ") + ggml_type_name(other->type));
       }
       m->prefill_gemm = 1;
+      m->batch_gemm = 1;
     }
   }
   if (T > 1) {  // from here on the model is this rank's shard

@@ -63,7 +63,12 @@ typedef struct armai_llama_opts {
   int32_t prefill_gemm; /* prompt matmuls: 0 = tensor-core GEMM for prompts of
                            at least 64 tokens, dp4a matvec below (default);
                            1 = always the dp4a matvec; 2 = always the GEMM */
-  int32_t reserved[6];
+  int32_t batch_gemm;   /* batched decode steps (armai_llama_generate_batch):
+                           0 = tensor-core GEMM for Q4_K / Q6_K models on one
+                           GPU, integer matvec otherwise (default); 1 = always
+                           the integer matvec (token for token the
+                           single-sequence chain); 2 = the GEMM where available */
+  int32_t reserved[5];
 } armai_llama_opts;
 
 /* Tensor parallelism (tp_size > 1; 7B/8B-class models): every rank calls
