@@ -1,0 +1,52 @@
+// fa_tc.cuh — attention on the 5th-generation tensor cores (sm_100a):
+// out = softmax(scale * Q K^T [causal]) V for a block of queries against a
+// key/value sequence: the prompt attention of candle's quantized_llama
+// (candle-transformers 0.8.4 ModelWeights::forward at offset 0, reached from
+// native/arm_ai_nif/src/llama_candle.rs:69-137: q.matmul(k^T) / sqrt(d),
+// masked_fill(-inf) above the diagonal, softmax, @ v) and the reference's
+// flash_attention_f32_op (native/arm_ai_nif/src/shape_ops.rs:464-558),
+// computed with an online softmax over key tiles.
+//
+// One CTA = 128 queries of one head (tensor-memory lanes). Per key tile of
+// 128: S = Q K^T by tcgen05.mma (kind::f16, f32 in tensor memory), the
+// softmax warps (thread = query row) read S with tcgen05.ld, keep the running
+// max / sum in f32, write P = exp(S - max) as f16 back into the same tensor
+// memory columns, rescale the f32 output accumulator in tensor memory when
+// the max moves, and O += P V is a second MMA with P as the A operand from
+// tensor memory and V^T from shared memory. Q, K and V (f32 or f16 in
+// global memory) are converted to f16 and written K-major, 128-byte
+// swizzled, by four loader warps, two key/value tiles ahead.
+//
+// Precision: f16 operands (2^-11 relative) and f32 accumulation; the
+// reference computes in f32. Every wait is bounded and sets an error flag.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace armai {
+
+struct FaParams {
+  const void* q;         // q[b][t][h][d]: element (b, t, h, d) at b*q_bs + t*q_ts + h*q_hs + d
+  int64_t q_bs, q_ts, q_hs;
+  const void* k;         // k/v: (b, key, kvh, d) at b*kv_bs + key*kv_ts + kvh*kv_hs + d
+  const void* v;
+  int64_t kv_bs, kv_ts, kv_hs;
+  float* o;              // f32 output, strides as q
+  int64_t o_bs, o_ts, o_hs;
+  int sq, sk;            // queries, keys (causal: query i sees keys 0 .. i)
+  int n_head, group;     // heads; query heads per key/value head
+  float scale;
+  int causal;
+  uint32_t* err;
+};
+
+// Launch for head dim 64 or 128 and batch b (gridDim.z); q_f16 / kv_f16
+// select f16 inputs (else f32). Returns ARMAI_E_INVALID for other head dims.
+int fa_tc_launch(const FaParams& p, int hd, int batch, bool q_f16, bool kv_f16, cudaStream_t s, bool pdl = false);
+
+}  // namespace armai

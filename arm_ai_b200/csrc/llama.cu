@@ -16,6 +16,7 @@
 #include "decode_mega.cuh"
 #include "gguf.h"
 #include "gemm_tc.cuh"
+#include "fa_tc.cuh"
 #include "nccl_dyn.h"
 #include "llama_kernels.cuh"
 
@@ -801,6 +802,26 @@ int gemm_layer(armai_llama* m, const Layer& L, int l, int S, float* x, float* q,
                             m->kv_seq_stride, seq_step, m->stream, pdl));
   if (seq_step) {
     ARMAI_CUDA(launch_attn(m, l, q, y, pos, S, m->kv_seq_stride, seq));
+  } else if (m->head_dim == 64 || m->head_dim == 128) {
+    // the prompt's causal attention on the tensor cores (positions 0 .. S-1)
+    FaParams a{};
+    a.q = q;
+    a.q_ts = QN;
+    a.q_hs = m->head_dim;
+    a.k = kv_seq_ptr(m, m->kc, l, seq);
+    a.v = kv_seq_ptr(m, m->vc, l, seq);
+    a.kv_ts = m->head_dim;
+    a.kv_hs = (int64_t)m->max_seq * m->head_dim;
+    a.o = y;
+    a.o_ts = QN;
+    a.o_hs = m->head_dim;
+    a.sq = a.sk = S;
+    a.n_head = m->n_head;
+    a.group = m->n_head / m->n_head_kv;
+    a.scale = (float)(1.0 / sqrt((double)m->head_dim));
+    a.causal = 1;
+    a.err = m->d_err;
+    ARMAI_TRY(fa_tc_launch(a, m->head_dim, 1, false, m->kv_f16 != 0, m->stream, pdl));
   } else {
     for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
       const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);

@@ -19,6 +19,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "fa_tc.cuh"
 
 using namespace armai;
 
@@ -1017,6 +1018,26 @@ extern "C" int armai_dev_flash_attention_f16(const uint16_t* q, const uint16_t* 
                                              float* out, float scale, int64_t b, int64_t h, int64_t sq,
                                              int64_t sk, int64_t d, int causal, void* stream) {
   if (!b || !h || !sq) return ARMAI_OK;
+  if ((d == 64 || d == 128) && sk > 0) {  // tensor cores (f16 operands are the inputs' own type)
+    FaParams p{};
+    p.q = q;
+    p.k = k;
+    p.v = v;
+    p.o = out;
+    p.q_bs = p.o_bs = h * sq * d;
+    p.q_hs = p.o_hs = sq * d;
+    p.q_ts = p.o_ts = d;
+    p.kv_bs = h * sk * d;
+    p.kv_hs = sk * d;
+    p.kv_ts = d;
+    p.sq = (int)sq;
+    p.sk = (int)sk;
+    p.n_head = (int)h;
+    p.group = 1;
+    p.scale = scale;
+    p.causal = causal;
+    return fa_tc_launch(p, (int)d, (int)b, true, true, (cudaStream_t)stream);
+  }
   return launch_flash<__half>(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
                               reinterpret_cast<const __half*>(v), out, scale, b, h, sq, sk, d, causal,
                               (cudaStream_t)stream);

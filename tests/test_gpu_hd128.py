@@ -14,12 +14,20 @@ from parity import check_errors, flip_bound, greedy_consistent, rel_maxabs
 pytestmark = pytest.mark.gpu
 
 
-def test_hd128_prefill_and_decode_match_oracle(hd128_model):
+@pytest.mark.parametrize("prefill_gemm", [1, 0])
+def test_hd128_prefill_and_decode_match_oracle(hd128_model, prefill_gemm):
+    """prefill_gemm=1: every prompt through the integer matvec kernels, held
+    to the flip bound. prefill_gemm=0 (the default): prompts of 64 tokens or
+    more run the tensor-core GEMMs and attention (f16 operands), held to
+    1.5 x the flip bound as in tests/test_gpu_llama.py, and so are the decode
+    steps that read the KV cache those prompts wrote."""
     path = hd128_model
-    gpu = native.llama_candle_load_op(path)
+    gpu = native.llama_candle_load_op(path, prefill_gemm=prefill_gemm)
     assert gpu.info().head_dim == 128
     orc = ref.OracleLlama(path)
     bound = flip_bound(path, lengths=(16, 24, 64, 100, 128))
+    if prefill_gemm == 0:
+        bound *= 1.5
     errs = []
     for n in (1, 20, 70, 129):
         prompt = synth.prompt_tokens(n, orc.n_vocab, 300 + n)
