@@ -74,27 +74,37 @@ __device__ __forceinline__ float qg_byte_f(uint32_t x, int i) {
 }
 
 // ---- W dequantisation from raw super-blocks in shared memory --------------
-// Q4_K (BlockQ4K::to_float): stage c of a super-block holds values
-// [64c, 64c + 64): sub-block 2c (low nibbles of qs[32c .. 32c + 32)) and
-// 2c + 1 (high nibbles). K half hh = sub-block 2c + hh: value l is
-// d * sc * q_l - dmin * m (the products d * sc and dmin * m rounded in f32
-// as candle does; the last step fused), rounded to f16 in pairs.
-__device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, uint4 hd, int c, int hh, uint32_t (&o)[16]) {
+// A stage of a super-block holds 64 values; DW / 4 dequantising warps share
+// it per tensor-memory lane quarter, each taking VPT = 64 / (DW / 4)
+// consecutive values (part kp: values kp VPT .. kp VPT + VPT - 1).
+
+// Q4_K (BlockQ4K::to_float): stage c holds values [64c, 64c + 64):
+// sub-block 2c (low nibbles of qs[32c .. 32c + 32)) and 2c + 1 (high
+// nibbles). Value l of sub-block j is d * sc_j * q_l - dmin * m_j (the
+// products d * sc and dmin * m rounded in f32 as candle does; the last step
+// fused), rounded to f16 in pairs.
+template <int QG_VPT>
+__device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, uint4 hd, int c, int kp,
+                                           uint32_t (&o)[QG_VPT / 2]) {
+  const int off = kp * QG_VPT, nib = off >> 5, l0 = off & 31;
   uint8_t sc8[12];
   const uint32_t sw[3] = {hd.y, hd.z, hd.w};
 #pragma unroll
   for (int i = 0; i < 12; i++) sc8[i] = (uint8_t)(sw[i >> 2] >> (8 * (i & 3)));
   int sc, mn;
-  q4k_scale_min(sc8, 2 * c + hh, sc, mn);
+  q4k_scale_min(sc8, 2 * c + nib, sc, mn);
   const float d = h2f((uint16_t)(hd.x & 0xffffu)), dmin = h2f((uint16_t)(hd.x >> 16));
   const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
   const uint64_t dd = f2_pack(d1, d1), mm = f2_pack(-m1, -m1), bias = f2_pack(-8388608.f, -8388608.f);
-  const uint4 q0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c);
-  const uint4 q1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * c);
-  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  uint32_t qw[QG_VPT / 4];
 #pragma unroll
-  for (int w = 0; w < 8; w++) {
-    const uint32_t x = (qw[w] >> (4 * hh)) & 0x0F0F0F0Fu;
+  for (int i = 0; i < QG_VPT / 16; i++) {
+    const uint4 q = *reinterpret_cast<const uint4*>(blk + 16 + 32 * c + l0 + 16 * i);
+    qw[4 * i] = q.x; qw[4 * i + 1] = q.y; qw[4 * i + 2] = q.z; qw[4 * i + 3] = q.w;
+  }
+#pragma unroll
+  for (int w = 0; w < QG_VPT / 4; w++) {
+    const uint32_t x = (qw[w] >> (4 * nib)) & 0x0F0F0F0Fu;
 #pragma unroll
     for (int i = 0; i < 2; i++) {
       const uint64_t n = f2_add(f2_pack(qg_byte_f(x, 2 * i), qg_byte_f(x, 2 * i + 1)), bias);
@@ -105,27 +115,31 @@ __device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, uint4 hd, int c, 
 
 // Q6_K (BlockQ6K::to_float; device body: ql 128, qh 64, i8 scales 16, d from
 // the row's f16 array): stage t = 2n + hq holds values 128n + 64hq + [0, 64);
-// K half h: value 32h + l takes ql[64n + 32h + l] nibble hq and
+// value 32h + l of the stage takes ql[64n + 32h + l] nibble hq and
 // qh[32n + l] bits 4hq + 2h, scale sc[4t + 2h + l / 16]; (d * sc) * (q - 32).
-__device__ __forceinline__ void qg_deq_q6k(const uint8_t* body, float d, int t, int h, uint32_t (&o)[16]) {
-  const int n = t >> 1, hq = t & 1;
-  const uint4 l0 = *reinterpret_cast<const uint4*>(body + 64 * n + 32 * h);
-  const uint4 l1 = *reinterpret_cast<const uint4*>(body + 64 * n + 32 * h + 16);
-  const uint4 h0 = *reinterpret_cast<const uint4*>(body + 128 + 32 * n);
-  const uint4 h1 = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + 16);
-  const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-  const uint32_t sc2 = *reinterpret_cast<const uint16_t*>(body + 192 + 4 * t + 2 * h);
-  const float s0 = __fmul_rn(d, (float)(int8_t)(sc2 & 0xffu)), s1 = __fmul_rn(d, (float)(int8_t)(sc2 >> 8));
-  const uint64_t bias = f2_pack(-8388640.f, -8388640.f);  // -(2^23 + 32)
-  const uint64_t ss0 = f2_pack(s0, s0), ss1 = f2_pack(s1, s1);
+template <int QG_VPT>
+__device__ __forceinline__ void qg_deq_q6k(const uint8_t* body, float d, int t, int kp,
+                                           uint32_t (&o)[QG_VPT / 2]) {
+  const int n = t >> 1, hq = t & 1, off = kp * QG_VPT, h = off >> 5, l0 = off & 31;
+  uint32_t lw[QG_VPT / 4], hw[QG_VPT / 4];
 #pragma unroll
-  for (int w = 0; w < 8; w++) {
+  for (int i = 0; i < QG_VPT / 16; i++) {
+    const uint4 a = *reinterpret_cast<const uint4*>(body + 64 * n + 32 * h + l0 + 16 * i);
+    const uint4 b = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + l0 + 16 * i);
+    lw[4 * i] = a.x; lw[4 * i + 1] = a.y; lw[4 * i + 2] = a.z; lw[4 * i + 3] = a.w;
+    hw[4 * i] = b.x; hw[4 * i + 1] = b.y; hw[4 * i + 2] = b.z; hw[4 * i + 3] = b.w;
+  }
+  const int8_t* sc = reinterpret_cast<const int8_t*>(body + 192 + 4 * t + 2 * h + (l0 >> 4));
+  const uint64_t bias = f2_pack(-8388640.f, -8388640.f);  // -(2^23 + 32)
+#pragma unroll
+  for (int w = 0; w < QG_VPT / 4; w++) {
+    const float s = __fmul_rn(d, (float)sc[w >> 2]);
+    const uint64_t ss = f2_pack(s, s);
     const uint32_t x = ((lw[w] >> (4 * hq)) & 0x0F0F0F0Fu) | (((hw[w] >> (4 * hq + 2 * h)) & 0x03030303u) << 4);
 #pragma unroll
     for (int i = 0; i < 2; i++) {
       const uint64_t q = f2_add(f2_pack(qg_byte_f(x, 2 * i), qg_byte_f(x, 2 * i + 1)), bias);
-      o[2 * w + i] = f2_to_h2(f2_mul(w < 4 ? ss0 : ss1, q));
+      o[2 * w + i] = f2_to_h2(f2_mul(ss, q));
     }
   }
 }
@@ -150,8 +164,10 @@ __device__ __forceinline__ int qg_find_seg(const QgParams& p, int n, int& local)
 }
 
 // Grid: x = 128-row weight tiles, y = token tiles (p.ntok tokens), z = K
-// splits (p.kb_split super-blocks each).
-__global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__ QgMaps maps, const QgParams p) {
+// splits (p.kb_split super-blocks each). DW dequantising warps.
+template <int DW>
+__global__ void __launch_bounds__(32 * (3 + DW), 1) k_qgemm(const __grid_constant__ QgMaps maps, const QgParams p) {
+  constexpr int QG_KPARTS = DW / 4, QG_VPT = 64 / QG_KPARTS;
   extern __shared__ uint8_t qg_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // 1024-byte aligned tiles (the swizzle pattern repeats every 1024 bytes)
@@ -174,12 +190,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
   const int nk = 4 * nblk;
   if (tid == 0) {
     for (int s = 0; s < QG_STAGES; s++) {
-      mbar_init(&full[s], 1 + QG_DEQ_WARPS);  // token copy (arrive + tx) and the dequantising warps
+      mbar_init(&full[s], 1 + DW);  // token copy (arrive + tx) and the dequantising warps
       mbar_init(&empty[s], 1);                // tcgen05.commit after the stage's MMAs
     }
     for (int r = 0; r < QG_RAW_SLOTS; r++) {
       mbar_init(&rfull[r], 1);                // the raw loader's arrival + tx
-      mbar_init(&rempty[r], QG_DEQ_WARPS);    // every dequantising warp done with the slot
+      mbar_init(&rempty[r], DW);    // every dequantising warp done with the slot
     }
     mbar_init(accb, 1);
     fence_mbar_init();
@@ -273,8 +289,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
         qg_wait(&rfull[b % QG_RAW_SLOTS], (uint32_t)((b / QG_RAW_SLOTS) & 1), p.err);
     }
   } else {
-    // ---- W dequantisers: warp -> tensor-memory lane quarter q, K half hh ----
-    const int q = warp & 3, hh = (warp - 3) >> 2;
+    // ---- W dequantisers: warp -> tensor-memory lane quarter q, K part kp ----
+    const int q = warp & 3, kp = (warp - 3) >> 2;
     const int r = 32 * q + lane, n = n0 + r;
     int nl;
     const int si = qg_find_seg(p, n, nl);
@@ -295,34 +311,34 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
         if (q6d) d6 = h2f(__ldg(q6d + kb0 + b));
         else hd = *reinterpret_cast<const uint4*>(row);
       }
-      uint32_t o[16];
+      uint32_t o[QG_VPT / 2];
       if (si < 0) {
 #pragma unroll
-        for (int i = 0; i < 16; i++) o[i] = 0u;
+        for (int i = 0; i < QG_VPT / 2; i++) o[i] = 0u;
       } else if (wtype == GGML_Q4_K) {
-        qg_deq_q4k(row, hd, c, hh, o);
+        qg_deq_q4k<QG_VPT>(row, hd, c, kp, o);
       } else {
-        qg_deq_q6k(row, d6, c, hh, o);
+        qg_deq_q6k<QG_VPT>(row, d6, c, kp, o);
       }
       __syncwarp();
       if (lane == 0 && c == 3) mbar_arrive1(&rempty[rs]);  // the raw slot's last stage has been read
       // the MMAs of the stage that last used these columns have completed
       if (kc >= QG_STAGES && !qg_wait_warp(&empty[s], (uint32_t)((kc / QG_STAGES - 1) & 1), p.err)) break;
       tc_fence_after();
-      qg_tmem_st16(t_a + lane_base + 32 * s + 16 * hh, o);
+      const uint32_t ta = t_a + lane_base + 32 * s + (QG_VPT / 2) * kp;
+      qg_tmem_st(ta, o);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive1(&full[s]);
     }
-    // ---- epilogue: this warp's 32 weight rows x token half hh ----
+    // ---- epilogue: this warp's 32 weight rows x every QG_KPARTS-th group of 8 tokens ----
     const bool acc_ok = qg_wait_warp(accb, 0, p.err);
     tc_fence_after();
     if (acc_ok) {
       float* out = p.out + (size_t)blockIdx.z * p.split_stride;
-      const int half = ntok >> 1;
 #pragma unroll 1
-      for (int c0 = hh * half; c0 < (hh + 1) * half; c0 += 8) {
+      for (int c0 = 8 * kp; c0 < ntok; c0 += 8 * QG_KPARTS) {
         float v[8];
         qg_tmem_ld8(taddr + lane_base + (uint32_t)c0, v);
         if (n < p.n) {
@@ -330,8 +346,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1) k_qgemm(const __grid_constant__
           for (int j = 0; j < 8; j++) {
             const int t = t0 + c0 + j;
             if (t < p.m) {
-              float* o = out + (size_t)t * p.ldo + n;
-              *o = p.add ? __fadd_rn(v[j], *o) : v[j];
+              float* o2 = out + (size_t)t * p.ldo + n;
+              *o2 = p.add ? __fadd_rn(v[j], *o2) : v[j];
             }
           }
         }
@@ -723,7 +739,9 @@ int qgemm_run(const QgJob& j, cudaStream_t s, QgSplit* split) {
   int dev = 0;
   ARMAI_CUDA(cudaGetDevice(&dev));
   if (attr_dev != dev) {
-    ARMAI_CUDA(cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ARMAI_CUDA(cudaFuncSetAttribute(k_qgemm<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)qg_smem_bytes(QG_TOK_MAX)));
+    ARMAI_CUDA(cudaFuncSetAttribute(k_qgemm<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)qg_smem_bytes(QG_TOK_MAX)));
     ARMAI_CUDA(cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev));
     attr_dev = dev;
@@ -762,8 +780,13 @@ int qgemm_run(const QgJob& j, cudaStream_t s, QgSplit* split) {
   p.tmem_cols = 32;
   while (p.tmem_cols < p.acc_cols + 32 * QG_STAGES) p.tmem_cols <<= 1;
   const uint32_t smem = qg_smem_bytes(p.ntok);
+  // few tokens: 8 dequantising warps, two CTAs per SM hide each other's
+  // latency; wide token tiles: 16 warps, one CTA per SM (shared memory)
+  const bool wide = p.ntok > 64;
+  auto kern = wide ? k_qgemm<16> : k_qgemm<8>;
+  const int threads = 32 * (3 + (wide ? 16 : 8));
   int occ = 1;
-  ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k_qgemm, QG_THREADS, smem));
+  ARMAI_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, threads, smem));
   occ = std::max(1, std::min(occ, 512 / p.tmem_cols));
   const int tiles_n = (p.n + QG_W - 1) / QG_W, tiles_t = (j.m + p.ntok - 1) / p.ntok;
   const int ctas = tiles_n * tiles_t, slots = n_sms * occ, nb = j.k / QK_K;
@@ -794,7 +817,7 @@ int qgemm_run(const QgJob& j, cudaStream_t s, QgSplit* split) {
     p.split_stride = part;
   }
   const dim3 grid((unsigned)tiles_n, (unsigned)tiles_t, (unsigned)splits);
-  ARMAI_CUDA(qg_launch(k_qgemm, grid, dim3(QG_THREADS), smem, s, j.pdl != 0, maps, p));
+  ARMAI_CUDA(qg_launch(kern, grid, dim3(threads), smem, s, j.pdl != 0, maps, p));
   if (split) {
     *split = QgSplit{j.ws, splits, part, p.n};
   } else if (!direct) {

@@ -15,9 +15,9 @@
 //     16 .. 128 token rows (or two whole tiles) into shared memory as the MMA
 //     B operand.
 //   * W: raw super-blocks streamed into shared memory by TMA (32-row boxes of
-//     one super-block per segment, a 2-slot ring), dequantised by eight warps
-//     (BlockQ4K / BlockQ6K::to_float; one thread per weight row and 32 K
-//     values per stage) straight into tensor memory as f16 — the MMA's A
+//     one super-block per segment, a 2-slot ring), dequantised by 8 or 16
+//     warps (BlockQ4K / BlockQ6K::to_float; one thread per weight row and 32
+//     or 16 K values per stage) straight into tensor memory as f16 — the A
 //     operand — so the weights never pass through shared memory as f16.
 //   * tcgen05.mma (kind::f16, f32 accumulate) issued by one thread; the
 //     128-row x tokens f32 accumulator in tensor memory, read back with
@@ -31,12 +31,14 @@
 // rounding of the dequantised weights and of q * d (2^-11 relative) and the
 // f32 summation order.
 //
-// Roles (352 threads): warp 0 lane 0 streams token tiles (cp.async.bulk),
-// warp 1 allocates tensor memory and one lane issues the MMAs, warp 2 lane 0
-// streams raw weight super-blocks (TMA), warps 3-10 dequantise (warp w owns
-// tensor-memory lanes 32 * (w % 4) .. + 31 and K half (w - 3) / 4 of each
-// stage) and then run the epilogue (token half (w - 3) / 4). Every wait is
-// bounded and sets an error flag; tensor memory is always released.
+// Roles (32 x (3 + DW) threads, DW = 8 dequantising warps for up to 64
+// tokens per tile, 16 above): warp 0 lane 0 streams token tiles
+// (cp.async.bulk), warp 1 allocates tensor memory and one lane issues the
+// MMAs, warp 2 lane 0 streams raw weight super-blocks (TMA), warps 3 ..
+// 2 + DW dequantise (warp w owns tensor-memory lanes 32 * (w % 4) .. + 31 and
+// K part (w - 3) / 4 of each stage) and then run the epilogue (every
+// (DW / 4)-th group of 8 tokens). Every wait is bounded and sets an error
+// flag; tensor memory is always released.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -53,8 +55,6 @@ constexpr int QG_W = 128;                 // weight rows per tile (MMA M, tensor
 constexpr int QG_K = 64;                  // K per stage: one 128-byte row of f16
 constexpr int QG_STAGES = 4;
 constexpr int QG_TOK_MAX = 256;           // tokens per tile (MMA N; 16 .. 128 in steps of 16, or 256)
-constexpr int QG_DEQ_WARPS = 8;
-constexpr int QG_THREADS = 32 * (3 + QG_DEQ_WARPS);
 constexpr uint32_t QG_TILE_BYTES = 128u * 128u;          // one 128-token x 64-K activation tile (16 KB)
 // Raw weight super-blocks in shared memory: per slot four 32-row groups of
 // one super-block each (Q4_K 144 B, Q6_K body 208 B per row)

@@ -131,6 +131,8 @@ struct armai_llama {
   size_t attn_smem = 0;
   int n_kernels_step = 0;
   cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t bgraph = nullptr;  // batched GEMM step for bgraph_n sequences
+  int bgraph_n = 0;
   int kv_len = 0;  // positions currently in the cache (host mirror)
   size_t device_bytes = 0;
   // persistent decode kernel
@@ -731,6 +733,11 @@ int check_device_error(armai_llama* m) {
 
 int ensure_prefill(armai_llama* m, int S) {
   if (S <= m->pf_cap) return ARMAI_OK;
+  if (m->bgraph) {  // it holds the buffers about to be replaced
+    cudaGraphExecDestroy(m->bgraph);
+    m->bgraph = nullptr;
+    m->bgraph_n = 0;
+  }
   int cap = std::max(S, 64);
   cap = ((cap + PREFILL_TILE - 1) / PREFILL_TILE) * PREFILL_TILE;
   cudaFree(m->pX); cudaFree(m->pQ); cudaFree(m->pY); cudaFree(m->pH);
@@ -979,7 +986,31 @@ int enqueue_batch_step_gemm(armai_llama* m, int n) {
 }
 
 int enqueue_batch_step(armai_llama* m, int n) {
-  if (m->batch_gemm != 1) return enqueue_batch_step_gemm(m, n);
+  if (m->batch_gemm != 1) {
+    if (!m->use_graph) return enqueue_batch_step_gemm(m, n);
+    // one graph per batch size, captured on first use (its buffers are
+    // allocated first; a later reallocation drops the graph)
+    ARMAI_TRY(ensure_prefill(m, std::max(n, 64)));
+    if (m->bgraph_n != n) {
+      if (m->bgraph) cudaGraphExecDestroy(m->bgraph);
+      m->bgraph = nullptr;
+      m->bgraph_n = 0;
+      cudaGraph_t gr = nullptr;
+      ARMAI_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+      const int erc = enqueue_batch_step_gemm(m, n);
+      const cudaError_t ec = cudaStreamEndCapture(m->stream, &gr);
+      if (erc != ARMAI_OK || ec != cudaSuccess) {
+        if (gr) cudaGraphDestroy(gr);
+        return erc != ARMAI_OK ? erc : cuda_fail(ec, "cudaStreamEndCapture", __FILE__, __LINE__);
+      }
+      const cudaError_t ce = cudaGraphInstantiate(&m->bgraph, gr, 0);
+      cudaGraphDestroy(gr);
+      if (ce != cudaSuccess) return cuda_fail(ce, "cudaGraphInstantiate", __FILE__, __LINE__);
+      m->bgraph_n = n;
+    }
+    ARMAI_CUDA(cudaGraphLaunch(m->bgraph, m->stream));
+    return ARMAI_OK;
+  }
   return m->batch_nb == BATCH_NB ? enqueue_batch_step_nb<BATCH_NB>(m, n)
                                  : enqueue_batch_step_nb<BATCH_NB_WIDE>(m, n);
 }
@@ -1134,6 +1165,7 @@ void free_model(armai_llama* m) {
   cudaSetDevice(m->device);
   if (m->stream) wait_done(m);
   if (m->graph) cudaGraphExecDestroy(m->graph);  // before the NCCL communicator it may hold
+  if (m->bgraph) cudaGraphExecDestroy(m->bgraph);
   if (m->comm && m->xchg && !m->broken) {
     // no rank may still write into this rank's exchange area: meet first
     float* one = nullptr;

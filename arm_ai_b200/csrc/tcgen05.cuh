@@ -124,6 +124,9 @@ __device__ __forceinline__ void qg_tmem_st8(uint32_t taddr, const uint32_t (&r)[
                : "memory");
 }
 
+__device__ __forceinline__ void qg_tmem_st(uint32_t taddr, const uint32_t (&r)[16]) { qg_tmem_st16(taddr, r); }
+__device__ __forceinline__ void qg_tmem_st(uint32_t taddr, const uint32_t (&r)[8]) { qg_tmem_st8(taddr, r); }
+
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
                : "memory");
