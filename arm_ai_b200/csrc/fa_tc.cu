@@ -74,10 +74,11 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
   const int kend = p.causal ? min(p.sk, qlast + 1) : p.sk;
   const int ntiles = (kend + FA_KT - 1) / FA_KT;
 
+  const bool tiled = p.qt != nullptr;
   if (tid == 0) {
-    mbar_init(qfull, 4);
+    mbar_init(qfull, tiled ? 1 : 4);
     for (int i = 0; i < 2; i++) {
-      mbar_init(&kvfull[i], 4);   // one arrival per loader warp
+      mbar_init(&kvfull[i], tiled ? 1 : 4);   // the bulk copies, or one arrival per loader warp
       mbar_init(&kvempty[i], 1);  // tcgen05.commit after the tile's P V
     }
     mbar_init(sbar, 1);
@@ -92,7 +93,21 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
   pdl_launch();
   pdl_wait();  // q / k / v come from the previous kernel; the output may be read by it
 
-  if (warp >= 8) {
+  if (warp >= 8 && tiled) {
+    // ---- tiles already in the staged layout: one bulk copy each ----
+    if (tid == FA_SOFTMAX_THREADS) {
+      const uint64_t keep = l2_evict_last_policy();  // K / V tiles serve every query tile of the group
+      mbar_arrive_tx(qfull, L::QB);
+      bulk_g2s(qs, p.qt + ((size_t)h * p.nqt + qt) * L::QB, L::QB, qfull, keep);
+      for (int j = 0; j < ntiles; j++) {
+        const int buf = j & 1;
+        if (j >= 2) qg_wait(&kvempty[buf], (uint32_t)(((j >> 1) - 1) & 1), p.err);
+        mbar_arrive_tx(&kvfull[buf], L::KB + L::VB);
+        bulk_g2s(ks + buf * L::KB, p.kt + ((size_t)kvh * p.nkt + j) * L::KB, L::KB, &kvfull[buf], keep);
+        bulk_g2s(vs + buf * L::VB, p.vt + ((size_t)kvh * p.nkt + j) * L::VB, L::VB, &kvfull[buf], keep);
+      }
+    }
+  } else if (warp >= 8) {
     // ---- loaders: f16, K-major, swizzled ----
     const int lt = tid - FA_SOFTMAX_THREADS;
     const TQ* qb = reinterpret_cast<const TQ*>(p.q) + b * p.q_bs + (int64_t)h * p.q_hs;

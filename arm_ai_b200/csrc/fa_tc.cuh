@@ -43,10 +43,33 @@ struct FaParams {
   float scale;
   int causal;
   uint32_t* err;
+  // Optional operand tiles (batch 1), already f16 in the layout the kernel
+  // stages (fa_tile_bytes): when qt is set, q / k / v above are not read and
+  // one bulk copy brings each tile.
+  const uint8_t* qt;     // [n_head][q tiles][hd / 64][128 rows][128 B]
+  const uint8_t* kt;     // [kv heads][key tiles][hd / 64][128 keys][128 B]
+  const uint8_t* vt;     // [kv heads][key tiles][2][hd rows][128 B]: V^T, 64 keys per 128-byte row
+  int nqt, nkt;          // q tiles per head, key tiles per kv head
 };
 
+// Bytes of one operand tile (128 rows or keys) of head dimension hd.
+inline size_t fa_tile_bytes(int hd) { return (size_t)hd * 256; }
+
+// Tiled operands: byte offset of element (row, d) of a Q or K tile (row =
+// query or key within the tile, d < hd), and of element (key, d) of a V^T
+// tile; 128-byte rows, 16-byte chunks XOR-swizzled by row & 7.
+__host__ __device__ inline uint32_t fa_qk_off(int row, int d) {
+  const int kb = d >> 6, c = (d & 63) >> 3;
+  return (uint32_t)(kb * 128 * 128 + row * 128 + ((c ^ (row & 7)) << 4) + 2 * (d & 7));
+}
+__host__ __device__ inline uint32_t fa_vt_off(int hd, int key, int d) {
+  const int kb = key >> 6, c = (key & 63) >> 3;
+  return (uint32_t)(kb * hd * 128 + d * 128 + ((c ^ (d & 7)) << 4) + 2 * (key & 7));
+}
+
 // Launch for head dim 64 or 128 and batch b (gridDim.z); q_f16 / kv_f16
-// select f16 inputs (else f32). Returns ARMAI_E_INVALID for other head dims.
+// select f16 inputs (else f32; ignored with tiles). Returns ARMAI_E_INVALID
+// for other head dims.
 int fa_tc_launch(const FaParams& p, int hd, int batch, bool q_f16, bool kv_f16, cudaStream_t s, bool pdl = false);
 
 }  // namespace armai

@@ -12,6 +12,7 @@
 #include "kquant.cuh"
 #include "llama_kernels.cuh"
 #include "tcgen05.cuh"
+#include "fa_tc.cuh"
 
 namespace armai {
 
@@ -509,7 +510,8 @@ __global__ void __launch_bounds__(256) k_row_act(const RowAct p) {
 // ---- q|k|v epilogue -------------------------------------------------------
 __global__ void k_qkv_post(const QgSplit g, int S, const int* __restrict__ pos, int qn, int kn, int hd,
                            int max_seq, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                           float* __restrict__ q_out, void* kc, void* vc, int kv_f16, int64_t slot_stride) {
+                           float* __restrict__ q_out, void* kc, void* vc, int kv_f16, int64_t slot_stride,
+                           const FaTilesOut tl) {
   pdl_launch();
   pdl_wait();
   const int t = blockIdx.y;
@@ -531,16 +533,28 @@ __global__ void k_qkv_post(const QgSplit g, int S, const int* __restrict__ pos, 
     // candle rope_i: (a*c - b*s, a*s + b*c), each op rounded
     const float o0 = __fsub_rn(__fmul_rn(d0, cs), __fmul_rn(d1, sn));
     const float o1 = __fadd_rn(__fmul_rn(d0, sn), __fmul_rn(d1, cs));
+    const int dd = rr % hd;
     if (r < qn) {
-      *reinterpret_cast<float2*>(q_out + (size_t)t * qn + r) = make_float2(o0, o1);
+      if (q_out) *reinterpret_cast<float2*>(q_out + (size_t)t * qn + r) = make_float2(o0, o1);
+      if (tl.q)
+        *reinterpret_cast<__half2*>(tl.q + ((size_t)(rr / hd) * tl.nqt + t / 128) * tl.tile + fa_qk_off(t & 127, dd)) =
+            __floats2half2_rn(o0, o1);
     } else {
-      const int kvh = rr / hd, dd = rr % hd;
+      const int kvh = rr / hd;
       store_kv(kc, kv_f16, t * slot_stride + ((int64_t)kvh * max_seq + p) * hd + dd, o0, o1);
+      if (tl.k)
+        *reinterpret_cast<__half2*>(tl.k + ((size_t)kvh * tl.nkt + p / 128) * tl.tile + fa_qk_off(p & 127, dd)) =
+            __floats2half2_rn(o0, o1);
     }
   } else {
     const int rv = r - qn - kn;
     const int kvh = rv / hd, dd = rv % hd;
     store_kv(vc, kv_f16, t * slot_stride + ((int64_t)kvh * max_seq + p) * hd + dd, d0, d1);
+    if (tl.v) {
+      uint8_t* vt = tl.v + ((size_t)kvh * tl.nkt + p / 128) * tl.tile;
+      *reinterpret_cast<__half*>(vt + fa_vt_off(hd, p & 127, dd)) = __float2half_rn(d0);
+      *reinterpret_cast<__half*>(vt + fa_vt_off(hd, p & 127, dd + 1)) = __float2half_rn(d1);
+    }
   }
 }
 
@@ -615,11 +629,13 @@ __global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ l
 // ---- launchers --------------------------------------------------------------
 int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int hd, int max_seq,
                     const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
-                    int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl) {
+                    int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl, const FaTilesOut* tiles) {
   if (S <= 0) return ARMAI_OK;
+  FaTilesOut tl{};
+  if (tiles) tl = *tiles;
   const dim3 grid((unsigned)((g.ld / 2 + 127) / 128), (unsigned)S);
   ARMAI_CUDA(qg_launch(k_qkv_post, grid, dim3(128), 0, s, pdl, g, S, pos, qn, kn, hd, max_seq, cos_t, sin_t,
-                       q_out, kc, vc, kv_f16, (int64_t)(kv_seq_stride * seq_step)));
+                       q_out, kc, vc, kv_f16, (int64_t)(kv_seq_stride * seq_step), tl));
   return ARMAI_OK;
 }
 

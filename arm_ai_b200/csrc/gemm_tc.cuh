@@ -163,9 +163,18 @@ int silu_act_launch(const QgSplit& g, int S, int F, uint8_t* a_tiles, cudaStream
 // pos[t] of sequence slot t * seq_step (kv_seq_stride elements between
 // slots; a prompt uses seq_step 0, a decode batch 1), as the matvec QKV
 // epilogue does.
+// With tiles, q, k and v are also written as the tensor-core attention's f16
+// operand tiles (fa_tc.cuh; positions pos[t] must lie in the key tiles, rows
+// of a tile that no token writes keep what they held); q_out may then be null.
+struct FaTilesOut {
+  uint8_t *q, *k, *v;
+  int nqt, nkt;   // q tiles per head, key tiles per kv head
+  int tile;       // bytes per tile
+};
 int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int hd, int max_seq,
                     const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
-                    int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl = false);
+                    int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl = false,
+                    const FaTilesOut* tiles = nullptr);
 // x[t][i] += g[t][i] (residual), i < n.
 int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream_t s);
 // For each of the S rows of logits[t][n]: token[t] = first index of the

@@ -100,6 +100,7 @@ struct armai_llama {
   int g_cols = 0;
   float* pWs = nullptr;        // GEMM split-K partials
   size_t ws_floats = 0;
+  uint8_t *pFq = nullptr, *pFk = nullptr, *pFv = nullptr;  // prompt attention operand tiles
   int prefill_gemm = 0;        // armai_llama_opts.prefill_gemm
   int batch_gemm = 0;          // armai_llama_opts.batch_gemm
   bool q80 = false;            // a matrix takes Q8_0 activations (Q4_0 / Q5_0 / Q8_0)
@@ -742,7 +743,9 @@ int ensure_prefill(armai_llama* m, int S) {
   cap = ((cap + PREFILL_TILE - 1) / PREFILL_TILE) * PREFILL_TILE;
   cudaFree(m->pX); cudaFree(m->pQ); cudaFree(m->pY); cudaFree(m->pH);
   cudaFree(m->p_pos); cudaFree(m->p_tok); cudaFree(m->pA); cudaFree(m->pG); cudaFree(m->pWs);
+  cudaFree(m->pFq); cudaFree(m->pFk); cudaFree(m->pFv);
   m->pX = m->pQ = m->pY = m->pH = m->pG = m->pWs = nullptr;
+  m->pFq = m->pFk = m->pFv = nullptr;
   m->pA = nullptr;
   m->pf_cap = 0;
   m->ws_floats = 0;
@@ -756,6 +759,17 @@ int ensure_prefill(armai_llama* m, int S) {
     // split-K partials: a few splits of long prompts, many of short ones
     m->ws_floats = (size_t)m->g_cols * (size_t)std::max(2 * cap, 2048);
     ARMAI_CUDA(cudaMalloc(&m->pWs, m->ws_floats * 4));
+    if (m->head_dim == 64 || m->head_dim == 128) {
+      // attention operand tiles; zeroed once so that the key rows past a
+      // prompt's end hold finite values (P = 0 there multiplies them)
+      const size_t tiles = (size_t)(cap + 127) / 128, tb = fa_tile_bytes(m->head_dim);
+      ARMAI_CUDA(cudaMalloc(&m->pFq, (size_t)m->n_head * tiles * tb));
+      ARMAI_CUDA(cudaMalloc(&m->pFk, (size_t)m->n_head_kv * tiles * tb));
+      ARMAI_CUDA(cudaMalloc(&m->pFv, (size_t)m->n_head_kv * tiles * tb));
+      ARMAI_CUDA(cudaMemset(m->pFq, 0, (size_t)m->n_head * tiles * tb));
+      ARMAI_CUDA(cudaMemset(m->pFk, 0, (size_t)m->n_head_kv * tiles * tb));
+      ARMAI_CUDA(cudaMemset(m->pFv, 0, (size_t)m->n_head_kv * tiles * tb));
+    }
   }
   ARMAI_CUDA(cudaMalloc(&m->pX, (size_t)cap * m->n_embd * 4));
   ARMAI_CUDA(cudaMalloc(&m->pQ, (size_t)cap * qn * 4));
@@ -804,21 +818,23 @@ int gemm_layer(armai_llama* m, const Layer& L, int l, int S, float* x, float* q,
   const bool pdl = m->use_pdl;
   QgSplit g;
   ARMAI_TRY(gemm_job(m, {&L.wq, &L.wk, &L.wv}, S, E, QG_PARTIAL, nullptr, 0, &g));
-  ARMAI_TRY(qkv_post_launch(g, S, pos, L.wq.rows, L.wk.rows, m->head_dim, m->max_seq, m->cos_t, m->sin_t, q,
-                            kv_seq_ptr(m, m->kc, l, seq), kv_seq_ptr(m, m->vc, l, seq), m->kv_f16,
-                            m->kv_seq_stride, seq_step, m->stream, pdl));
+  // a prompt (positions 0 .. S-1) with a tensor-core head dim: q / k / v also
+  // as the attention kernel's operand tiles
+  const bool fa = !seq_step && m->pFq;
+  const int ntl = (S + 127) / 128;
+  const FaTilesOut tl{m->pFq, m->pFk, m->pFv, ntl, ntl, (int)fa_tile_bytes(m->head_dim)};
+  ARMAI_TRY(qkv_post_launch(g, S, pos, L.wq.rows, L.wk.rows, m->head_dim, m->max_seq, m->cos_t, m->sin_t,
+                            fa ? nullptr : q, kv_seq_ptr(m, m->kc, l, seq), kv_seq_ptr(m, m->vc, l, seq),
+                            m->kv_f16, m->kv_seq_stride, seq_step, m->stream, pdl, fa ? &tl : nullptr));
   if (seq_step) {
     ARMAI_CUDA(launch_attn(m, l, q, y, pos, S, m->kv_seq_stride, seq));
-  } else if (m->head_dim == 64 || m->head_dim == 128) {
+  } else if (fa) {
     // the prompt's causal attention on the tensor cores (positions 0 .. S-1)
     FaParams a{};
-    a.q = q;
-    a.q_ts = QN;
-    a.q_hs = m->head_dim;
-    a.k = kv_seq_ptr(m, m->kc, l, seq);
-    a.v = kv_seq_ptr(m, m->vc, l, seq);
-    a.kv_ts = m->head_dim;
-    a.kv_hs = (int64_t)m->max_seq * m->head_dim;
+    a.qt = m->pFq;
+    a.kt = m->pFk;
+    a.vt = m->pFv;
+    a.nqt = a.nkt = ntl;
     a.o = y;
     a.o_ts = QN;
     a.o_hs = m->head_dim;
