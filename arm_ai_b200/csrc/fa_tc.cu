@@ -97,14 +97,16 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
     // ---- tiles already in the staged layout: one bulk copy each ----
     if (tid == FA_SOFTMAX_THREADS) {
       const uint64_t keep = l2_evict_last_policy();  // K / V tiles serve every query tile of the group
+      const int n_kv = p.n_head / p.group;
       mbar_arrive_tx(qfull, L::QB);
-      bulk_g2s(qs, p.qt + ((size_t)h * p.nqt + qt) * L::QB, L::QB, qfull, keep);
+      bulk_g2s(qs, p.qt + ((size_t)(b * p.n_head + h) * p.nqt + qt) * L::QB, L::QB, qfull, keep);
       for (int j = 0; j < ntiles; j++) {
         const int buf = j & 1;
         if (j >= 2) qg_wait(&kvempty[buf], (uint32_t)(((j >> 1) - 1) & 1), p.err);
         mbar_arrive_tx(&kvfull[buf], L::KB + L::VB);
-        bulk_g2s(ks + buf * L::KB, p.kt + ((size_t)kvh * p.nkt + j) * L::KB, L::KB, &kvfull[buf], keep);
-        bulk_g2s(vs + buf * L::VB, p.vt + ((size_t)kvh * p.nkt + j) * L::VB, L::VB, &kvfull[buf], keep);
+        const size_t kv_tile = (size_t)(b * n_kv + kvh) * p.nkt + j;
+        bulk_g2s(ks + buf * L::KB, p.kt + kv_tile * L::KB, L::KB, &kvfull[buf], keep);
+        bulk_g2s(vs + buf * L::VB, p.vt + kv_tile * L::VB, L::VB, &kvfull[buf], keep);
       }
     }
   } else if (warp >= 8) {
@@ -315,6 +317,67 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
     tc_fence_after();
     tmem_dealloc(taddr, FA_TMEM_COLS);
   }
+}
+
+// One CTA per (tile, head, batch): 128 rows of one head into its tile.
+template <typename T, int HD, bool TRANSPOSE>
+__global__ void __launch_bounds__(256) k_fa_tiles(const T* __restrict__ src, int64_t bs, int64_t ts, int64_t hs,
+                                                  int heads, int n_rows, uint8_t* __restrict__ dst) {
+  const int tile = blockIdx.x, h = blockIdx.y, b = blockIdx.z, ntiles = gridDim.x;
+  const T* sb = src + b * bs + (int64_t)h * hs;
+  uint8_t* out = dst + ((size_t)(b * heads + h) * ntiles + tile) * fa_tile_bytes(HD);
+  const int r0 = tile * 128;
+  if constexpr (!TRANSPOSE) {
+    for (int task = threadIdx.x; task < 128 * (HD / 8); task += blockDim.x) {
+      const int r = task / (HD / 8), c = task % (HD / 8);
+      uint32_t hv[4] = {0u, 0u, 0u, 0u};
+      if (r0 + r < n_rows) fa_ld8h(sb + (int64_t)(r0 + r) * ts + 8 * c, hv);
+      fa_st16(out + (c >> 3) * (128 * 128), r, c & 7, hv);
+    }
+  } else {
+  // V^T: the tile's rows staged as f16 [128][HD] (coalesced loads), then
+  // 8 keys x 1 dim per 16-byte chunk
+  __shared__ __align__(16) __half st[128 * HD];
+  for (int task = threadIdx.x; task < 128 * (HD / 8); task += blockDim.x) {
+    const int r = task / (HD / 8), c = task % (HD / 8);
+    uint32_t hv[4] = {0u, 0u, 0u, 0u};
+    if (r0 + r < n_rows) fa_ld8h(sb + (int64_t)(r0 + r) * ts + 8 * c, hv);
+    *reinterpret_cast<uint4*>(st + r * HD + 8 * c) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+  __syncthreads();
+  for (int task = threadIdx.x; task < HD * 16; task += blockDim.x) {
+    const int d = task % HD, g = task / HD;
+    uint32_t hv[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const __half2 t2 = __halves2half2(st[(8 * g + 2 * i) * HD + d], st[(8 * g + 2 * i + 1) * HD + d]);
+      hv[i] = *reinterpret_cast<const uint32_t*>(&t2);
+    }
+    fa_st16(out + (g >> 3) * (HD * 128), d, g & 7, hv);
+  }
+  }
+}
+
+int fa_tiles_launch(const void* src, bool f16, int64_t bs, int64_t ts, int64_t hs, int batch, int heads, int n_rows,
+                    int hd, bool transpose, uint8_t* dst, cudaStream_t s) {
+  if (n_rows <= 0 || batch <= 0 || heads <= 0) return ARMAI_OK;
+  const int64_t es = f16 ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(src) % 16) || (ts * es) % 16 || (hs * es) % 16 || (bs * es) % 16)
+    return fail(ARMAI_E_INVALID, "attention: rows must be 16-byte aligned");
+  const dim3 grid((unsigned)((n_rows + 127) / 128), (unsigned)heads, (unsigned)batch);
+#define FA_TILES(T, HDV)                                                                                        \
+  (transpose ? (k_fa_tiles<T, HDV, true><<<grid, 256, 0, s>>>((const T*)src, bs, ts, hs, heads, n_rows, dst))  \
+             : (k_fa_tiles<T, HDV, false><<<grid, 256, 0, s>>>((const T*)src, bs, ts, hs, heads, n_rows, dst)))
+  if (hd == 64) {
+    if (f16) FA_TILES(__half, 64); else FA_TILES(float, 64);
+  } else if (hd == 128) {
+    if (f16) FA_TILES(__half, 128); else FA_TILES(float, 128);
+  } else {
+    return fail(ARMAI_E_INVALID, "attention: tensor-core path needs head dim 64 or 128");
+  }
+#undef FA_TILES
+  ARMAI_CUDA(cudaGetLastError());
+  return ARMAI_OK;
 }
 
 namespace {

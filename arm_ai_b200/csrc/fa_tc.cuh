@@ -53,7 +53,7 @@ struct FaParams {
 };
 
 // Bytes of one operand tile (128 rows or keys) of head dimension hd.
-inline size_t fa_tile_bytes(int hd) { return (size_t)hd * 256; }
+__host__ __device__ inline size_t fa_tile_bytes(int hd) { return (size_t)hd * 256; }
 
 // Tiled operands: byte offset of element (row, d) of a Q or K tile (row =
 // query or key within the tile, d < hd), and of element (key, d) of a V^T
@@ -67,9 +67,17 @@ __host__ __device__ inline uint32_t fa_vt_off(int hd, int key, int d) {
   return (uint32_t)(kb * hd * 128 + d * 128 + ((c ^ (d & 7)) << 4) + 2 * (key & 7));
 }
 
+// Operand tiles from strided rows: src element (b, row, h, d) at
+// b*bs + row*ts + h*hs + d (f16 when f16, else f32), rows < n_rows (the
+// rest of the last tile is zero), into dst as [batch][heads][tiles][...]:
+// Q / K tiles, or V^T tiles when transpose. dst holds
+// batch * heads * ceil(n_rows / 128) * fa_tile_bytes(hd) bytes.
+int fa_tiles_launch(const void* src, bool f16, int64_t bs, int64_t ts, int64_t hs, int batch, int heads, int n_rows,
+                    int hd, bool transpose, uint8_t* dst, cudaStream_t s);
+
 // Launch for head dim 64 or 128 and batch b (gridDim.z); q_f16 / kv_f16
-// select f16 inputs (else f32; ignored with tiles). Returns ARMAI_E_INVALID
-// for other head dims.
+// select f16 inputs (else f32; ignored with tiles, whose index runs over
+// batch, then head, then tile). Returns ARMAI_E_INVALID for other head dims.
 int fa_tc_launch(const FaParams& p, int hd, int batch, bool q_f16, bool kv_f16, cudaStream_t s, bool pdl = false);
 
 }  // namespace armai

@@ -88,12 +88,18 @@ template <int QG_VPT>
 __device__ __forceinline__ void qg_deq_q4k(const uint8_t* blk, uint4 hd, int c, int kp,
                                            uint32_t (&o)[QG_VPT / 2]) {
   const int off = kp * QG_VPT, nib = off >> 5, l0 = off & 31;
-  uint8_t sc8[12];
-  const uint32_t sw[3] = {hd.y, hd.z, hd.w};
-#pragma unroll
-  for (int i = 0; i < 12; i++) sc8[i] = (uint8_t)(sw[i >> 2] >> (8 * (i & 3)));
+  // 6-bit scale and min of sub-block j = 2c + nib from the 12 scale bytes
+  // (header words y, z, w), as get_scale_min_k4, in registers
+  const int j = 2 * c + nib, j4 = (j & 3) * 8;
   int sc, mn;
-  q4k_scale_min(sc8, 2 * c + nib, sc, mn);
+  if (j < 4) {
+    sc = (int)((hd.y >> j4) & 63u);
+    mn = (int)((hd.z >> j4) & 63u);
+  } else {
+    const uint32_t s8 = (hd.w >> j4) & 0xffu, s0 = (hd.y >> j4) & 0xffu, s4 = (hd.z >> j4) & 0xffu;
+    sc = (int)((s8 & 0xFu) | ((s0 >> 6) << 4));
+    mn = (int)((s8 >> 4) | ((s4 >> 6) << 4));
+  }
   const float d = h2f((uint16_t)(hd.x & 0xffffu)), dmin = h2f((uint16_t)(hd.x >> 16));
   const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
   const uint64_t dd = f2_pack(d1, d1), mm = f2_pack(-m1, -m1), bias = f2_pack(-8388608.f, -8388608.f);

@@ -1018,25 +1018,36 @@ extern "C" int armai_dev_flash_attention_f16(const uint16_t* q, const uint16_t* 
                                              float* out, float scale, int64_t b, int64_t h, int64_t sq,
                                              int64_t sk, int64_t d, int causal, void* stream) {
   if (!b || !h || !sq) return ARMAI_OK;
-  if ((d == 64 || d == 128) && sk > 0) {  // tensor cores (f16 operands are the inputs' own type)
+  if ((d == 64 || d == 128) && sk > 0) {
+    // tensor cores (f16 operands are the inputs' own type): q, k and v^T
+    // rearranged into the kernel's operand tiles first (stream-ordered
+    // scratch from the library pool, freed after the launch)
+    const cudaStream_t s = (cudaStream_t)stream;
+    const size_t tb = fa_tile_bytes((int)d), nqt = (size_t)(sq + 127) / 128, nkt = (size_t)(sk + 127) / 128;
+    Scoped tq(s), tk(s), tv(s);
+    ARMAI_TRY(dalloc(tq, (size_t)b * h * nqt * tb));
+    ARMAI_TRY(dalloc(tk, (size_t)b * h * nkt * tb));
+    ARMAI_TRY(dalloc(tv, (size_t)b * h * nkt * tb));
+    ARMAI_TRY(fa_tiles_launch(q, true, h * sq * d, d, sq * d, (int)b, (int)h, (int)sq, (int)d, false, (uint8_t*)tq.p, s));
+    ARMAI_TRY(fa_tiles_launch(k, true, h * sk * d, d, sk * d, (int)b, (int)h, (int)sk, (int)d, false, (uint8_t*)tk.p, s));
+    ARMAI_TRY(fa_tiles_launch(v, true, h * sk * d, d, sk * d, (int)b, (int)h, (int)sk, (int)d, true, (uint8_t*)tv.p, s));
     FaParams p{};
-    p.q = q;
-    p.k = k;
-    p.v = v;
+    p.qt = (const uint8_t*)tq.p;
+    p.kt = (const uint8_t*)tk.p;
+    p.vt = (const uint8_t*)tv.p;
+    p.nqt = (int)nqt;
+    p.nkt = (int)nkt;
     p.o = out;
-    p.q_bs = p.o_bs = h * sq * d;
-    p.q_hs = p.o_hs = sq * d;
-    p.q_ts = p.o_ts = d;
-    p.kv_bs = h * sk * d;
-    p.kv_hs = sk * d;
-    p.kv_ts = d;
+    p.o_bs = h * sq * d;
+    p.o_hs = sq * d;
+    p.o_ts = d;
     p.sq = (int)sq;
     p.sk = (int)sk;
     p.n_head = (int)h;
     p.group = 1;
     p.scale = scale;
     p.causal = causal;
-    return fa_tc_launch(p, (int)d, (int)b, true, true, (cudaStream_t)stream);
+    return fa_tc_launch(p, (int)d, (int)b, true, true, s);
   }
   return launch_flash<__half>(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
                               reinterpret_cast<const __half*>(v), out, scale, b, h, sq, sk, d, causal,

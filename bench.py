@@ -484,7 +484,8 @@ def run_config5(d, peak_hbm):
                                                           S, S, D, 1, sp))
     fl = 4 * S * S * D * H / 2
     out["flash_attention_f16_h32_s2048_d128_causal"] = {"us": ms * 1e3, "tflops": fl / ms / 1e9, "bound": "tensor",
-                                                        "frac": fl / ms / 1e9 / tc_peak}
+                                                        "frac": fl / ms / 1e9 / tc_peak,
+                                                        "kernel": "k_fa_tc (tcgen05 kind::f16, P in tensor memory)"}
     return out
 
 
