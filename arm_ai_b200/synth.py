@@ -58,6 +58,9 @@ ARCHS = {
     "small": LlamaArch(4, 512, 1536, 8, 2, 4096, 10000.0, 1e-5, 4096),
     # head_dim 128 (the Mistral / Llama-3 attention shape) at CPU-checkable size
     "tiny128": LlamaArch(2, 512, 1024, 4, 2, 1000, 500000.0, 1e-5, 8192),
+    # tensor parallelism over 4 ranks: 16 / 4 query heads, 4 / 4 KV heads,
+    # 256 attn_output columns and 512 FFN rows per rank
+    "tp4": LlamaArch(2, 1024, 2048, 16, 4, 4096, 10000.0, 1e-5, 4096),
     # FFN 12288: 16 activation rows of ffn_down's K exceed shared memory, so
     # batched decode runs its 8-row kernels (as for 7B/8B models on one GPU)
     "wide": LlamaArch(1, 256, 12288, 4, 2, 1000, 10000.0, 1e-5, 4096),

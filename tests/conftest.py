@@ -42,6 +42,12 @@ def tied_model(built):
 
 
 @pytest.fixture(scope="session")
+def tp4_model(built):
+    from arm_ai_b200 import synth
+    return synth.model_path("tp4", seed=5)
+
+
+@pytest.fixture(scope="session")
 def hd128_model(built):
     from arm_ai_b200 import synth
     return synth.model_path("tiny128", seed=4)

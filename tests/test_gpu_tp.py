@@ -1,13 +1,14 @@
-"""Tensor parallelism on two GPUs (the Llama-3-8B sharding on the small
-test model: 8 query / 2 KV heads, FFN 1536, vocab 4096 split over 2 ranks).
+"""Tensor parallelism on two and four GPUs (the Llama-3-8B sharding on small
+test models: 2 ranks on 8 query / 2 KV heads, FFN 1536; 4 ranks on 16 query
+/ 4 KV heads, FFN 2048; vocab 4096 split over the ranks).
 
 Each rank holds half the heads, gate/up rows and vocab rows and a K-half of
 attn_output / ffn_down; the halves are summed through peer memory (the
 persistent decode kernel) or by NCCL (per-kernel chain, prefill, batched
 decode). Against the oracle: prompt logits (gathered from both ranks) within
 the model's flip bound and greedy tokens consistent with the oracle,
-identical on both ranks, for single-sequence and batched decode. Skipped
-with fewer than two GPUs.
+identical on every rank, for single-sequence and batched decode. Skipped
+with fewer GPUs than ranks.
 """
 import os
 import socket
@@ -63,21 +64,23 @@ def _rank(rank, world, port, path, prompt, q):
         dist.destroy_process_group()
 
 
-def test_tp2_matches_oracle(small_model):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_matches_oracle(request, world):
     torch = pytest.importorskip("torch")
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
     import ref
     from arm_ai_b200 import synth
     from parity import flip_bound, greedy_consistent, rel_maxabs
 
+    small_model = request.getfixturevalue("small_model" if world == 2 else "tp4_model")
     prompt = synth.prompt_tokens(13, 4096, 21)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, small_model, prompt, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, small_model, prompt, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
@@ -86,7 +89,7 @@ def test_tp2_matches_oracle(small_model):
     for r in res:
         assert not isinstance(r[1], str), r[1]
     bt = [r[2] for r in res]
-    assert bt[0] == bt[1]  # both ranks decode the same batch
+    assert all(b == bt[0] for b in bt)  # every rank decodes the same batch
     btol = 2 * flip_bound(small_model, lengths=(16, 24, 64))
     for (n, sd), toks in zip(BATCH_PROMPTS, bt[0]):
         assert len(toks) == 20
@@ -104,5 +107,6 @@ def test_tp2_matches_oracle(small_model):
             assert rel_maxabs(lg1, lo1) < bound, kernel
             assert greedy_consistent(small_model, prompt, toks, tol=2 * bound) is None, kernel
             assert rel_maxabs(lg2, lo2) < 1.5 * bound, kernel  # GEMM prefill: f16 operands
-        assert res[0][1][kernel][2] == res[1][1][kernel][2]  # both ranks decode the same tokens
-        assert res[0][1][kernel][1] == res[1][1][kernel][1]
+        for r in res[1:]:  # every rank decodes the same tokens
+            assert r[1][kernel][2] == res[0][1][kernel][2]
+            assert r[1][kernel][1] == res[0][1][kernel][1]
