@@ -43,13 +43,22 @@ __device__ __forceinline__ void fa_ld8h(const __half* p, uint32_t (&h)[4]) {
 __device__ __forceinline__ float fa_ldf(const float* p) { return *p; }
 __device__ __forceinline__ float fa_ldf(const __half* p) { return __half2float(*p); }
 
+// 2^x by the special-function unit's approximation (ex2.approx, relative
+// error about 2^-22; results below the normal range flush to 0): the
+// probabilities are rounded to f16 next, and a flushed one is 0 in f16 too.
+__device__ __forceinline__ float fa_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 16-byte chunk c of row r of a K-major, 128-byte-swizzled block.
 __device__ __forceinline__ void fa_st16(uint8_t* blk, int r, int c, const uint32_t (&h)[4]) {
   *reinterpret_cast<uint4*>(blk + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
 template <typename TQ, typename TKV, int HD>
-__global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
+__global__ void __launch_bounds__(FA_THREADS, HD == 64 ? 2 : 1) k_fa_tc(const FaParams p) {
   using L = FaLayout<HD>;
   extern __shared__ uint8_t fa_raw[];
   const uint32_t raw_addr = smem_u32(fa_raw);
@@ -239,9 +248,10 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
       mt = fmaxf(mt, xch[(1 - hf) * 128 + row]);
       const float m_new = fmaxf(m_run, mt);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_use);
+      const float alpha = m_run == -INFINITY ? 0.f : fa_exp2(m_run - m_use);
       // pass 2: P = exp2(s' - m') as f16 over the S columns this thread has
-      // read (P column 64h + c holds keys 64h + 2c, + 1), the rounded P's sum
+      // read (P column 64h + c holds keys 64h + 2c, + 1), and P's row sum in
+      // f32 (of the values before their f16 rounding)
       float lsum = 0.f;
 #pragma unroll 1
       for (int c = 0; c < 64; c += 16) {
@@ -250,10 +260,10 @@ __global__ void __launch_bounds__(FA_THREADS, 2) k_fa_tc(const FaParams p) {
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 16; e += 2) {
-          const float p0 = k0 + c + e < klim ? exp2f(__fmul_rn(v[e], sl2) - m_use) : 0.f;
-          const float p1 = k0 + c + e + 1 < klim ? exp2f(__fmul_rn(v[e + 1], sl2) - m_use) : 0.f;
+          const float p0 = k0 + c + e < klim ? fa_exp2(__fmul_rn(v[e], sl2) - m_use) : 0.f;
+          const float p1 = k0 + c + e + 1 < klim ? fa_exp2(__fmul_rn(v[e + 1], sl2) - m_use) : 0.f;
           const __half2 hp = __floats2half2_rn(p0, p1);
-          lsum += __low2float(hp) + __high2float(hp);
+          lsum += p0 + p1;
           pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
         }
         qg_tmem_st8(sh + (uint32_t)(c >> 1), pk);
