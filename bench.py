@@ -50,7 +50,113 @@ def parse():
     p.add_argument("--no-config3", action="store_true", help="skip the Mistral-7B long-context (config 3) figures")
     p.add_argument("--no-config4", action="store_true", help="skip the Llama-3-8B tensor-parallel (config 4) figures")
     p.add_argument("--no-config5", action="store_true", help="skip the primitive sweep (config 5) figures")
+    p.add_argument("--trace-decode", action="store_true",
+                   help="print the per-phase timeline of one persistent-kernel decode step (globaltimer "
+                        "stamps per CTA, armai_llama_trace_decode) after a 32-token prompt, instead of the bench")
+    p.add_argument("--profile", default=None, choices=sorted(PROFILE_CASES),
+                   help="run one case for a profiler instead of the bench: once untimed, then once between "
+                        "cudaProfilerStart / Stop (ncu --profile-from-start off captures only that run)")
     return p.parse_args()
+
+
+def _profile_case(name):
+    """The cases the committed ncu summaries under profiles/ were captured on."""
+    import ctypes
+    import torch
+    from arm_ai_b200 import native, synth
+    from arm_ai_b200._lib import load_cuda
+    path = synth.model_path(ARCH, seed=0)
+    if name == "prefill512":  # one 512-token prompt through the tensor-core GEMMs and attention
+        m = native.llama_candle_load_op(path, prefill_gemm=2, max_seq_len=2048)
+        prompt = synth.prompt_tokens(512, 32000, 11)
+        run = lambda: native.llama_forward(m, prompt, 0, want_logits=False)
+    elif name == "batch16":  # 16 one-token prompts, then batched GEMM decode steps
+        m = native.llama_candle_load_op(path, max_batch=16, max_seq_len=1024, batch_gemm=2)
+        prompts = [synth.prompt_tokens(1, 32000, 50 + i) for i in range(16)]
+        run = lambda: native.llama_generate_batch(m, prompts, 3)
+    elif name == "decode":  # one persistent-kernel decode step after a 32-token prompt
+        m = native.llama_candle_load_op(path, max_seq_len=1024)
+        native.llama_forward(m, synth.prompt_tokens(PROMPT, 32000, 3), 0, want_logits=False)
+        pos = [PROMPT]
+        def run():
+            native.llama_forward(m, [5], pos[0], want_logits=False)
+            pos[0] += 1
+    else:  # config-5 primitives through the device-pointer entry points
+        lib = load_cuda()
+        dev = torch.device("cuda:0")
+        P = lambda t: ctypes.c_void_p(t.data_ptr())
+        if name == "attn2048":
+            H, S, D = 32, 2048, 128
+            q, k, v = (torch.rand(1, H, S, D, device=dev).half() * 2 - 1 for _ in range(3))
+            o = torch.empty(1, H, S, D, device=dev)
+            run = lambda: lib.armai_dev_flash_attention_f16(P(q), P(k), P(v), P(o), ctypes.c_float(D ** -0.5), 1, H,
+                                                            S, S, D, 1, None)
+        else:  # int8m512
+            M, K = 512, 4096
+            a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device=dev)
+            w = torch.randint(-127, 128, (K, K), dtype=torch.int8, device=dev)
+            o = torch.empty(M, K, dtype=torch.int32, device=dev)
+            run = lambda: lib.armai_dev_int8_matmul_s32(P(a), P(w), P(o), M, K, K, None)
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+
+
+PROFILE_CASES = ("prefill512", "batch16", "decode", "attn2048", "int8m512")
+
+
+def _trace_decode():
+    """Per-phase timeline of one decode step: per phase kind, the median over
+    layers of (the phase's median end over CTAs - the previous phase's),
+    the phase's own median duration and its activation-build time; then one
+    middle layer's slot medians relative to the phase start (slots: 1
+    activation built, 2 done, 4 first stage ready, 5 first stage computed,
+    6 first input pass, 7 rms scale known)."""
+    import numpy as np
+    from arm_ai_b200 import native, synth
+    m = native.llama_candle_load_op(synth.model_path(ARCH, seed=0), max_seq_len=1024)
+    native.llama_forward(m, synth.prompt_tokens(PROMPT, m.info().n_vocab, 3), 0, want_logits=False)
+    for i in range(8):
+        native.llama_forward(m, [5 + i], PROMPT + i, want_logits=False)
+    for _ in range(2):
+        tr = native.llama_trace_decode(m).astype(np.int64)
+    nph, nct, _ = tr.shape
+    t0 = tr[nph - 1, :, 0][tr[nph - 1, :, 0] > 0].min()
+    names = ["QKV", "ATTN", "WO", "GATEUP", "DOWN"]
+    nl = (nph - 2) // 5
+    med = lambda a: float(np.median(a)) if len(a) else float("nan")
+    end = {}
+    rows = {}
+    for i in range(nph - 1):
+        ok = (tr[i, :, 0] > 0) & (tr[i, :, 2] > 0)
+        if not ok.any():
+            continue
+        st, en = med(tr[i, ok, 0]) - t0, med(tr[i, ok, 2]) - t0
+        a = ok & (tr[i, :, 1] > 0)
+        act = med(tr[i, a, 1] - tr[i, a, 0]) if a.any() else 0.0
+        end[i] = en
+        kind = names[i % 5] if i < 5 * nl else "HEAD"
+        rows.setdefault(kind, []).append((en - end.get(i - 1, 0.0), en - st, act))
+    total = (tr[nph - 1, :, 1].max() - t0) / 1e3
+    print(f"decode step: {nph - 1} phases on {nct} CTAs, {total:.1f} us (trace build; globaltimer 256 ns resolution)")
+    print("| phase | n | span us (median) | own us | activation build us |")
+    print("|---|---|---|---|---|")
+    for kind, v in rows.items():
+        a = np.array(v) / 1e3
+        print(f"| {kind} | {len(v)} | {np.median(a[:, 0]):.2f} | {np.median(a[:, 1]):.2f} | {np.median(a[:, 2]):.2f} |")
+    lm = nl // 2
+    print(f"layer {lm}, slot medians relative to the phase start (us):")
+    for i in range(5 * lm, 5 * lm + 5):
+        s0 = tr[i, :, 0]
+        ok = s0 > 0
+        cells = []
+        for j in (6, 7, 1, 4, 5, 2):
+            okj = ok & (tr[i, :, j] > 0)
+            cells.append(f"s{j} {(med(tr[i, okj, j]) - med(s0[ok])) / 1e3:.2f}" if okj.any() else f"s{j} -")
+        print(f"  {names[i % 5]:6s} " + "  ".join(cells))
 
 
 class Dist:
@@ -602,6 +708,12 @@ def run_armai(args, d):
 
 def main():
     args = parse()
+    if args.profile:
+        _profile_case(args.profile)
+        return
+    if args.trace_decode:
+        _trace_decode()
+        return
     d = Dist()
     try:
         if args.impl == "reference":
