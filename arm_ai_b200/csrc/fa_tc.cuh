@@ -7,15 +7,17 @@
 // flash_attention_f32_op (native/arm_ai_nif/src/shape_ops.rs:464-558),
 // computed with an online softmax over key tiles.
 //
-// One CTA = 128 queries of one head (tensor-memory lanes). Per key tile of
-// 128: S = Q K^T by tcgen05.mma (kind::f16, f32 in tensor memory), the
-// softmax warps (thread = query row) read S with tcgen05.ld, keep the running
-// max / sum in f32, write P = exp(S - max) as f16 back into the same tensor
-// memory columns, rescale the f32 output accumulator in tensor memory when
-// the max moves, and O += P V is a second MMA with P as the A operand from
-// tensor memory and V^T from shared memory. Q, K and V (f32 or f16 in
-// global memory) are converted to f16 and written K-major, 128-byte
-// swizzled, by four loader warps, two key/value tiles ahead.
+// One CTA = 128 queries of one head (tensor-memory lanes), one CTA per SM.
+// Per key tile of 128: S = Q K^T by tcgen05.mma (kind::f16, f32 into one of
+// two S buffers in tensor memory); eight softmax warps (two per row: each
+// half the keys) read S with tcgen05.ld, keep the running max / sum in f32,
+// write P = exp(S - max) as f16 back into the same tensor-memory columns,
+// rescale the f32 output accumulator in tensor memory when the max moves;
+// O += P V is a second MMA with P as the A operand from tensor memory and
+// V^T from shared memory. One thread streams the f16 operand tiles (already
+// in the K-major, 128-byte-swizzled layout) by bulk copy, two K and two V^T
+// tiles deep, and issues the MMAs: the next tile's S runs while the softmax
+// warps work on this one.
 //
 // Precision: f16 operands (2^-11 relative) and f32 accumulation; the
 // reference computes in f32. Every wait is bounded and sets an error flag.
@@ -31,25 +33,20 @@
 namespace armai {
 
 struct FaParams {
-  const void* q;         // q[b][t][h][d]: element (b, t, h, d) at b*q_bs + t*q_ts + h*q_hs + d
-  int64_t q_bs, q_ts, q_hs;
-  const void* k;         // k/v: (b, key, kvh, d) at b*kv_bs + key*kv_ts + kvh*kv_hs + d
-  const void* v;
-  int64_t kv_bs, kv_ts, kv_hs;
-  float* o;              // f32 output, strides as q
+  // Operand tiles, f16 in the layout the kernel stages, indexed over batch,
+  // then head, then tile (fa_tiles_launch writes them from strided rows; the
+  // prompt's q/k/v epilogue writes them directly).
+  const uint8_t* qt;     // [batch][n_head][q tiles][hd / 64][128 rows][128 B]
+  const uint8_t* kt;     // [batch][kv heads][key tiles][hd / 64][128 keys][128 B]
+  const uint8_t* vt;     // [batch][kv heads][key tiles][2][hd rows][128 B]: V^T, 64 keys per 128-byte row
+  int nqt, nkt;          // q tiles per head, key tiles per kv head
+  float* o;              // f32 output: element (b, t, h, d) at b*o_bs + t*o_ts + h*o_hs + d
   int64_t o_bs, o_ts, o_hs;
   int sq, sk;            // queries, keys (causal: query i sees keys 0 .. i)
   int n_head, group;     // heads; query heads per key/value head
   float scale;
   int causal;
-  uint32_t* err;
-  // Optional operand tiles (batch 1), already f16 in the layout the kernel
-  // stages (fa_tile_bytes): when qt is set, q / k / v above are not read and
-  // one bulk copy brings each tile.
-  const uint8_t* qt;     // [n_head][q tiles][hd / 64][128 rows][128 B]
-  const uint8_t* kt;     // [kv heads][key tiles][hd / 64][128 keys][128 B]
-  const uint8_t* vt;     // [kv heads][key tiles][2][hd rows][128 B]: V^T, 64 keys per 128-byte row
-  int nqt, nkt;          // q tiles per head, key tiles per kv head
+  uint32_t* err;         // device error word (null: the module's own)
 };
 
 // Bytes of one operand tile (128 rows or keys) of head dimension hd.
@@ -75,9 +72,8 @@ __host__ __device__ inline uint32_t fa_vt_off(int hd, int key, int d) {
 int fa_tiles_launch(const void* src, bool f16, int64_t bs, int64_t ts, int64_t hs, int batch, int heads, int n_rows,
                     int hd, bool transpose, uint8_t* dst, cudaStream_t s);
 
-// Launch for head dim 64 or 128 and batch b (gridDim.z); q_f16 / kv_f16
-// select f16 inputs (else f32; ignored with tiles, whose index runs over
-// batch, then head, then tile). Returns ARMAI_E_INVALID for other head dims.
-int fa_tc_launch(const FaParams& p, int hd, int batch, bool q_f16, bool kv_f16, cudaStream_t s, bool pdl = false);
+// Launch for head dim 64 or 128 and batch b (gridDim.z). Returns
+// ARMAI_E_INVALID for other head dims.
+int fa_tc_launch(const FaParams& p, int hd, int batch, cudaStream_t s, bool pdl = false);
 
 }  // namespace armai

@@ -445,24 +445,24 @@ struct RowAct {
   uint8_t* a_tiles;  // null: no tiles (ACT_RESID only)
 };
 
-// One CTA (256 threads) per token row: the row's values (ACT_X: x;
+// One CTA per token row (one warp per 256-value block, at least 8 warps): the row's values (ACT_X: x;
 // ACT_RESID: x + the split sums, stored back; ACT_SILU: silu(gate) * up from
 // the split sums), optionally rms-normalised with gamma, as activation tiles.
 // The norm follows candle's rms_norm with per-block partial sums added in
 // block order (as the decode kernels).
 template <int KIND>
-__global__ void __launch_bounds__(256) k_row_act(const RowAct p) {
+__global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
   pdl_launch();
   pdl_wait();
   __shared__ float part[64];  // K <= 16384
   __shared__ float s_rms;
-  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const int k = p.k, nb = k / QK_K, nkc = k / QG_K;
   uint8_t* tbase = p.a_tiles ? p.a_tiles + (size_t)(row / 128) * nkc * QG_TILE_BYTES : nullptr;
   const int r = row % 128;
   const float* xr = KIND == ACT_X ? p.x + (size_t)row * k : p.xo + (size_t)row * k;
   const bool norm = p.gamma != nullptr && tbase != nullptr;
-  for (int j = warp; j < nb; j += 8) {
+  for (int j = warp; j < nb; j += nw) {
     const int col = j * QK_K + 8 * lane;
     float v[8];
     if (KIND == ACT_X) {
@@ -502,7 +502,7 @@ __global__ void __launch_bounds__(256) k_row_act(const RowAct p) {
   }
   __syncthreads();
   const float rms = s_rms;
-  for (int j = warp; j < nb; j += 8) {
+  for (int j = warp; j < nb; j += nw) {
     const int col = j * QK_K + 8 * lane;
     float v[8], g[8];
     qg_ld8(xr + col, v);  // ACT_RESID: this thread's own stores above
@@ -645,6 +645,9 @@ int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int
   return ARMAI_OK;
 }
 
+// One warp per 256-value block of a row (8 .. 32 warps).
+static unsigned row_threads(int k) { return 32u * (unsigned)std::min(32, std::max(8, k / QK_K)); }
+
 int resid_act_launch(const QgSplit& g, float* x, int S, int n, const float* gamma, float eps, uint8_t* a_tiles,
                      cudaStream_t s, bool pdl) {
   if (n % QK_K || n / QK_K > 64) return fail(ARMAI_E_INVALID, "resid_act: n must be a multiple of 256, at most 16384");
@@ -656,7 +659,7 @@ int resid_act_launch(const QgSplit& g, float* x, int S, int n, const float* gamm
   p.k = n;
   p.g = g;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_RESID>, dim3(S), dim3(256), 0, s, pdl, p));
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_RESID>, dim3(S), dim3(row_threads(n)), 0, s, pdl, p));
   return ARMAI_OK;
 }
 
@@ -667,7 +670,7 @@ int silu_act_launch(const QgSplit& g, int S, int F, uint8_t* a_tiles, cudaStream
   p.k = F;
   p.g = g;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_SILU>, dim3(S), dim3(256), 0, s, pdl, p));
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_SILU>, dim3(S), dim3(row_threads(F)), 0, s, pdl, p));
   return ARMAI_OK;
 }
 
@@ -693,7 +696,7 @@ int qgemm_act_launch(const float* x, const float* gamma, float eps, int m, int k
   p.eps = eps;
   p.k = k;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_X>, dim3(m), dim3(256), 0, s, pdl, p));
+  ARMAI_CUDA(qg_launch(k_row_act<ACT_X>, dim3(m), dim3(row_threads(k)), 0, s, pdl, p));
   return ARMAI_OK;
 }
 

@@ -844,7 +844,7 @@ int gemm_layer(armai_llama* m, const Layer& L, int l, int S, float* x, float* q,
     a.scale = (float)(1.0 / sqrt((double)m->head_dim));
     a.causal = 1;
     a.err = m->d_err;
-    ARMAI_TRY(fa_tc_launch(a, m->head_dim, 1, false, m->kv_f16 != 0, m->stream, pdl));
+    ARMAI_TRY(fa_tc_launch(a, m->head_dim, 1, m->stream, pdl));
   } else {
     for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
       const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);

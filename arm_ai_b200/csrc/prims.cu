@@ -1047,7 +1047,7 @@ extern "C" int armai_dev_flash_attention_f16(const uint16_t* q, const uint16_t* 
     p.group = 1;
     p.scale = scale;
     p.causal = causal;
-    return fa_tc_launch(p, (int)d, (int)b, true, true, s);
+    return fa_tc_launch(p, (int)d, (int)b, s);
   }
   return launch_flash<__half>(reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
                               reinterpret_cast<const __half*>(v), out, scale, b, h, sq, sk, d, causal,
