@@ -591,16 +591,17 @@ __global__ void k_qg_finish(const float* __restrict__ ws, int splits, size_t spl
   }
 }
 
-// token[t] = argmax of logits row t (am_better order), pos[t] += 1. Each
+// token[t] = argmax of logits row t (am_better order), pos[t] += 1; the
+// winner's value and index also into best_val / best_idx when given. Each
 // thread scans a strided slice, 4 loads in flight.
-__global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ logits, int n, uint32_t* token,
-                                                     int* pos) {
+__global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ logits, int n, int ld, uint32_t* token,
+                                                     int* pos, float* best_val, int* best_idx) {
   pdl_launch();
   pdl_wait();
   __shared__ float sv[32];
   __shared__ int si[32];
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
-  const float* row = logits + (size_t)t * n;
+  const float* row = logits + (size_t)t * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   int i = tid;
@@ -629,6 +630,10 @@ __global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ l
       if (am_better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
     token[t] = (uint32_t)(bi == 0x7fffffff ? 0 : bi);
     pos[t] += 1;
+    if (best_val) {
+      best_val[t] = bv;
+      best_idx[t] = bi;
+    }
   }
 }
 
@@ -680,9 +685,10 @@ int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream
   return ARMAI_OK;
 }
 
-int row_argmax_launch(const float* logits, int S, int n, uint32_t* token, int* pos, cudaStream_t s, bool pdl) {
+int row_argmax_launch(const float* logits, int S, int n, int ld, uint32_t* token, int* pos, cudaStream_t s, bool pdl,
+                      float* best_val, int* best_idx) {
   if (S <= 0) return ARMAI_OK;
-  ARMAI_CUDA(qg_launch(k_row_argmax, dim3(S), dim3(1024), 0, s, pdl, logits, n, token, pos));
+  ARMAI_CUDA(qg_launch(k_row_argmax, dim3(S), dim3(1024), 0, s, pdl, logits, n, ld, token, pos, best_val, best_idx));
   return ARMAI_OK;
 }
 

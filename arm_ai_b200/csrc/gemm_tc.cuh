@@ -177,9 +177,11 @@ int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int
                     const FaTilesOut* tiles = nullptr);
 // x[t][i] += g[t][i] (residual), i < n.
 int resid_add_launch(float* x, const float* g, int S, int n, int ldg, cudaStream_t s);
-// For each of the S rows of logits[t][n]: token[t] = first index of the
-// largest value (the decode head's order), pos[t] += 1.
-int row_argmax_launch(const float* logits, int S, int n, uint32_t* token, int* pos, cudaStream_t s,
-                      bool pdl = false);
+// For each of the S rows of logits[t][0, n) (row stride ld): token[t] =
+// first index of the largest value (the decode head's order), pos[t] += 1;
+// with best_val / best_idx, also the winner's value and index (a tensor-
+// parallel rank's candidate for the merge across ranks).
+int row_argmax_launch(const float* logits, int S, int n, int ld, uint32_t* token, int* pos, cudaStream_t s,
+                      bool pdl = false, float* best_val = nullptr, int* best_idx = nullptr);
 
 }  // namespace armai

@@ -998,7 +998,12 @@ int enqueue_batch_step_gemm(armai_llama* m, int n) {
     ARMAI_TRY(gemm_layer(m, m->layers[l], l, n, m->x, m->q, m->y, m->d_pos, 1, 0, next));
   }
   ARMAI_TRY(gemm_job(m, {&m->output}, n, E, QG_STORE, m->logits, m->n_vocab));
-  return row_argmax_launch(m->logits, n, m->n_vocab, m->d_token, m->d_pos, m->stream, m->use_pdl);
+  if (m->tp == 1) return row_argmax_launch(m->logits, n, m->output.rows, m->n_vocab, m->d_token, m->d_pos, m->stream,
+                                           m->use_pdl);
+  // tensor parallel: this rank's vocab rows; the ranks' winners are merged
+  ARMAI_TRY(row_argmax_launch(m->logits, n, m->output.rows, m->n_vocab, m->d_token, m->d_pos, m->stream, m->use_pdl,
+                              m->best_val, m->best_idx));
+  return tp_head_merge(m, m->d_token, n);
 }
 
 int enqueue_batch_step(armai_llama* m, int n) {
@@ -1268,7 +1273,6 @@ int load_model(const char* path, const armai_llama_opts* opts, armai_llama** out
     // memory (decode_kernel 0), or the per-kernel chain through NCCL (1)
     m->use_pdl = false;
     m->prefill_gemm = 2;
-    m->batch_gemm = 1;  // the batched GEMM step runs on one GPU
   }
   m->n_layer = (int)block_count;
   m->n_embd = (int)embd;

@@ -64,10 +64,11 @@ typedef struct armai_llama_opts {
                            at least 64 tokens, dp4a matvec below (default);
                            1 = always the dp4a matvec; 2 = always the GEMM */
   int32_t batch_gemm;   /* batched decode steps (armai_llama_generate_batch):
-                           0 = tensor-core GEMM for Q4_K / Q6_K models on one
-                           GPU, integer matvec otherwise (default); 1 = always
-                           the integer matvec (token for token the
-                           single-sequence chain); 2 = the GEMM where available */
+                           0 = tensor-core GEMM for Q4_K / Q6_K models (also
+                           tensor parallel), integer matvec otherwise
+                           (default); 1 = always the integer matvec (token for
+                           token the single-sequence chain); 2 = the GEMM
+                           where available */
   int32_t reserved[5];
 } armai_llama_opts;
 
