@@ -108,21 +108,34 @@ def _profile_case(name):
 PROFILE_CASES = ("prefill512", "batch16", "decode", "attn2048", "int8m512")
 
 
-def _trace_decode():
+def _trace_decode(d):
     """Per-phase timeline of one decode step: per phase kind, the median over
     layers of (the phase's median end over CTAs - the previous phase's),
     the phase's own median duration and its activation-build time; then one
     middle layer's slot medians relative to the phase start (slots: 1
     activation built, 2 done, 4 first stage ready, 5 first stage computed,
-    6 first input pass, 7 rms scale known)."""
+    6 first input pass, 7 rms scale known). One GPU: TinyLlama (config 1);
+    under torchrun: Llama-3-8B tensor parallel over the ranks (config 4),
+    every rank printing its own timeline."""
     import numpy as np
-    from arm_ai_b200 import native, synth
-    m = native.llama_candle_load_op(synth.model_path(ARCH, seed=0), max_seq_len=1024)
+    from arm_ai_b200 import native, synth, tp
+    if d.world > 1:
+        arch = "llama-3-8b"
+        if d.rank == 0:
+            synth.model_path(arch, seed=0)
+        d.barrier()
+        uid = tp.share_unique_id(d.rank)
+        m = tp.load_tp(synth.model_path(arch, seed=0), d.local, d.world, d.rank, uid, max_seq_len=1024)
+    else:
+        m = native.llama_candle_load_op(synth.model_path(ARCH, seed=0), max_seq_len=1024)
     native.llama_forward(m, synth.prompt_tokens(PROMPT, m.info().n_vocab, 3), 0, want_logits=False)
     for i in range(8):
         native.llama_forward(m, [5 + i], PROMPT + i, want_logits=False)
     for _ in range(2):
         tr = native.llama_trace_decode(m).astype(np.int64)
+    m.close()
+    out = []
+    print_ = out.append
     nph, nct, _ = tr.shape
     t0 = tr[nph - 1, :, 0][tr[nph - 1, :, 0] > 0].min()
     names = ["QKV", "ATTN", "WO", "GATEUP", "DOWN"]
@@ -141,14 +154,14 @@ def _trace_decode():
         kind = names[i % 5] if i < 5 * nl else "HEAD"
         rows.setdefault(kind, []).append((en - end.get(i - 1, 0.0), en - st, act))
     total = (tr[nph - 1, :, 1].max() - t0) / 1e3
-    print(f"decode step: {nph - 1} phases on {nct} CTAs, {total:.1f} us (trace build; globaltimer 256 ns resolution)")
-    print("| phase | n | span us (median) | own us | activation build us |")
-    print("|---|---|---|---|---|")
+    print_(f"decode step: {nph - 1} phases on {nct} CTAs, {total:.1f} us (trace build; globaltimer 256 ns resolution)")
+    print_("| phase | n | span us (median) | own us | activation build us |")
+    print_("|---|---|---|---|---|")
     for kind, v in rows.items():
         a = np.array(v) / 1e3
-        print(f"| {kind} | {len(v)} | {np.median(a[:, 0]):.2f} | {np.median(a[:, 1]):.2f} | {np.median(a[:, 2]):.2f} |")
+        print_(f"| {kind} | {len(v)} | {np.median(a[:, 0]):.2f} | {np.median(a[:, 1]):.2f} | {np.median(a[:, 2]):.2f} |")
     lm = nl // 2
-    print(f"layer {lm}, slot medians relative to the phase start (us):")
+    print_(f"layer {lm}, slot medians relative to the phase start (us):")
     for i in range(5 * lm, 5 * lm + 5):
         s0 = tr[i, :, 0]
         ok = s0 > 0
@@ -156,7 +169,9 @@ def _trace_decode():
         for j in (6, 7, 1, 4, 5, 2):
             okj = ok & (tr[i, :, j] > 0)
             cells.append(f"s{j} {(med(tr[i, okj, j]) - med(s0[ok])) / 1e3:.2f}" if okj.any() else f"s{j} -")
-        print(f"  {names[i % 5]:6s} " + "  ".join(cells))
+        print_(f"  {names[i % 5]:6s} " + "  ".join(cells))
+    text = "\n".join(out)
+    print((f"rank {d.rank} of {d.world}:\n" if d.world > 1 else "") + text, flush=True)
 
 
 class Dist:
@@ -711,10 +726,13 @@ def main():
     if args.profile:
         _profile_case(args.profile)
         return
-    if args.trace_decode:
-        _trace_decode()
-        return
     d = Dist()
+    if args.trace_decode:
+        try:
+            _trace_decode(d)
+        finally:
+            d.close()
+        return
     try:
         if args.impl == "reference":
             run_reference(args, d)
