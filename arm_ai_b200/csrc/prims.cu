@@ -109,10 +109,13 @@ __device__ __forceinline__ int warp_isum(int v) {
 // ---------------------------------------------------------------------------
 // P1/P2/P4: s8 x s8 -> s32 (dp4a), optional f32 scale epilogue
 // (shape_ops.rs:1205: (acc as f32) * act_scale * w_scales[j]).
-// CTA: 8 warps x 4 weight rows, MT activation rows staged through smem in
-// 2048-byte K chunks. Weight rows stream from HBM once per MT tile.
+// CTA: 8 warps x RW weight rows, MT activation rows staged through smem in
+// 2048-byte K chunks. Weight rows stream from HBM once per MT tile; two rows
+// per warp give 2 x (number of SMs) CTAs on 4096-row matrices, and the K loop
+// keeps two 16-byte loads per row in flight.
 // ---------------------------------------------------------------------------
 constexpr int I8_KC = 2048;
+constexpr int I8_RW = 2;  // weight rows per warp
 
 template <int MT>
 __global__ void __launch_bounds__(256) k_int8_gemm(const int8_t* __restrict__ a,
@@ -122,11 +125,11 @@ __global__ void __launch_bounds__(256) k_int8_gemm(const int8_t* __restrict__ a,
                                                    const float* w_scales, int m, int n, int k) {
   __shared__ __align__(16) int8_t As[MT][I8_KC];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int row0 = blockIdx.x * 32 + warp * 4;
+  const int row0 = blockIdx.x * (8 * I8_RW) + warp * I8_RW;
   const int m0 = blockIdx.y * MT;
-  int acc[4][MT];
+  int acc[I8_RW][MT];
 #pragma unroll
-  for (int r = 0; r < 4; r++)
+  for (int r = 0; r < I8_RW; r++)
 #pragma unroll
     for (int t = 0; t < MT; t++) acc[r][t] = 0;
   for (int kc = 0; kc < k; kc += I8_KC) {
@@ -139,17 +142,18 @@ __global__ void __launch_bounds__(256) k_int8_gemm(const int8_t* __restrict__ a,
       *reinterpret_cast<int4*>(&As[t][c]) = v;
     }
     __syncthreads();
+#pragma unroll 2
     for (int c = lane * 16; c < klen; c += 512) {
-      int4 wv[4];
+      int4 wv[I8_RW];
 #pragma unroll
-      for (int r = 0; r < 4; r++)
-        wv[r] = (row0 + r < n) ? *reinterpret_cast<const int4*>(w + (size_t)(row0 + r) * k + kc + c)
+      for (int r = 0; r < I8_RW; r++)
+        wv[r] = (row0 + r < n) ? __ldg(reinterpret_cast<const int4*>(w + (size_t)(row0 + r) * k + kc + c))
                                : make_int4(0, 0, 0, 0);
 #pragma unroll
       for (int t = 0; t < MT; t++) {
         const int4 av = *reinterpret_cast<const int4*>(&As[t][c]);
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < I8_RW; r++) {
           int s = acc[r][t];
           s = __dp4a(wv[r].x, av.x, s);
           s = __dp4a(wv[r].y, av.y, s);
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(256) k_int8_gemm(const int8_t* __restrict__ a,
     }
   }
 #pragma unroll
-  for (int r = 0; r < 4; r++)
+  for (int r = 0; r < I8_RW; r++)
 #pragma unroll
     for (int t = 0; t < MT; t++) {
       const int s = warp_isum(acc[r][t]);
@@ -199,11 +203,12 @@ int launch_int8_gemm(const int8_t* a, const int8_t* w, int32_t* o32, float* of32
   const bool aligned = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w)) & 15) == 0;
   if (m >= I8_TC_MIN_M && aligned && m <= INT32_MAX && n <= INT32_MAX && k <= INT32_MAX)
     return launch_int8_gemm_tc(a, w, o32, of32, act_scales, per_token, act_scale, w_scales, m, n, k, s);
+  const unsigned rows_per_cta = 8 * I8_RW;
   if (m <= 4) {
-    dim3 g((unsigned)((n + 31) / 32), (unsigned)m);
+    dim3 g((unsigned)((n + rows_per_cta - 1) / rows_per_cta), (unsigned)m);
     k_int8_gemm<1><<<g, 256, 0, s>>>(a, w, o32, of32, act_scales, per_token, act_scale, w_scales, (int)m, (int)n, (int)k);
   } else {
-    dim3 g((unsigned)((n + 31) / 32), (unsigned)((m + 15) / 16));
+    dim3 g((unsigned)((n + rows_per_cta - 1) / rows_per_cta), (unsigned)((m + 15) / 16));
     k_int8_gemm<16><<<g, 256, 0, s>>>(a, w, o32, of32, act_scales, per_token, act_scale, w_scales, (int)m, (int)n, (int)k);
   }
   ARMAI_CUDA(cudaGetLastError());
