@@ -413,25 +413,37 @@ __device__ __forceinline__ void qg_ld8(const float* p, float (&v)[8]) {
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-// The split sums of 8 consecutive columns, added in split order.
+// The split sums of 8 consecutive columns of two column sets (offsets oa,
+// ob; ob < 0: one set), each added in split order. All loads of a batch of
+// splits are issued before the first add, so a row kernel waits for one
+// memory round trip per batch rather than one per split (B splits per batch:
+// 8 for one set, 4 for two).
+template <int B>
+__device__ __forceinline__ void qg_split_sum8x2(const QgSplit& g, size_t oa, long long ob, float (&va)[8],
+                                                float (&vb)[8]) {
+  for (int sp0 = 0; sp0 < g.splits; sp0 += B) {
+    float wa[B][8], wb[B][8];
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if (sp0 + u < g.splits) {
+        qg_ld8(g.ws + (size_t)(sp0 + u) * g.stride + oa, wa[u]);
+        if (ob >= 0) qg_ld8(g.ws + (size_t)(sp0 + u) * g.stride + (size_t)ob, wb[u]);
+      }
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if (sp0 + u < g.splits) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          va[i] = sp0 + u == 0 ? wa[u][i] : __fadd_rn(va[i], wa[u][i]);
+          if (ob >= 0) vb[i] = sp0 + u == 0 ? wb[u][i] : __fadd_rn(vb[i], wb[u][i]);
+        }
+      }
+  }
+}
+template <int B>
 __device__ __forceinline__ void qg_split_sum8(const QgSplit& g, size_t off, float (&v)[8]) {
-  qg_ld8(g.ws + off, v);
-  int sp = 1;
-  for (; sp + 4 <= g.splits; sp += 4) {  // four partials in flight
-    float w[4][8];
-#pragma unroll
-    for (int u = 0; u < 4; u++) qg_ld8(g.ws + (size_t)(sp + u) * g.stride + off, w[u]);
-#pragma unroll
-    for (int u = 0; u < 4; u++)
-#pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], w[u][i]);
-  }
-  for (; sp < g.splits; sp++) {
-    float w[8];
-    qg_ld8(g.ws + (size_t)sp * g.stride + off, w);
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], w[i]);
-  }
+  float unused[8];
+  qg_split_sum8x2<B>(g, off, -1, v, unused);
 }
 
 enum { ACT_X = 0, ACT_RESID = 1, ACT_SILU = 2 };
@@ -445,13 +457,19 @@ struct RowAct {
   uint8_t* a_tiles;  // null: no tiles (ACT_RESID only)
 };
 
-// One CTA per token row (one warp per 256-value block, at least 8 warps): the row's values (ACT_X: x;
-// ACT_RESID: x + the split sums, stored back; ACT_SILU: silu(gate) * up from
-// the split sums), optionally rms-normalised with gamma, as activation tiles.
-// The norm follows candle's rms_norm with per-block partial sums added in
-// block order (as the decode kernels).
-template <int KIND>
-__global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
+// Token row blockIdx.x, one warp per 256-value block: the row's values
+// (ACT_X: x; ACT_RESID: x + the split sums, stored back; ACT_SILU:
+// silu(gate) * up from the split sums), optionally rms-normalised with gamma,
+// as activation tiles. ACT_X / ACT_RESID: one CTA per row (the norm needs the
+// whole row). ACT_SILU (no norm): blockIdx.y picks
+// the row's blocks [y * warps, (y + 1) * warps). The norm follows candle's
+// rms_norm with per-block partial sums added in block order (as the decode
+// kernels). B: split partials loaded per round trip — 8 for few rows (a
+// decode batch: latency; a warp's first block also stays in registers across
+// the norm's barrier), 2 for many (a prompt: registers, occupancy; every
+// block is read again after the barrier).
+template <int KIND, int B>
+__global__ void __launch_bounds__(512) k_row_act(const RowAct p) {
   pdl_launch();
   pdl_wait();
   __shared__ float part[64];  // K <= 16384
@@ -461,16 +479,20 @@ __global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
   uint8_t* tbase = p.a_tiles ? p.a_tiles + (size_t)(row / 128) * nkc * QG_TILE_BYTES : nullptr;
   const int r = row % 128;
   const float* xr = KIND == ACT_X ? p.x + (size_t)row * k : p.xo + (size_t)row * k;
-  const bool norm = p.gamma != nullptr && tbase != nullptr;
-  for (int j = warp; j < nb; j += nw) {
+  const bool norm = KIND != ACT_SILU && p.gamma != nullptr && tbase != nullptr;
+  constexpr bool KEEP = B >= 8;
+  const int j0 = KIND == ACT_SILU ? (int)blockIdx.y * nw : 0, j1 = KIND == ACT_SILU ? min(nb, j0 + nw) : nb;
+  float keep[8], g0[8];
+  for (int j = j0 + warp; j < j1; j += nw) {
     const int col = j * QK_K + 8 * lane;
     float v[8];
+    if (KEEP && norm && j == warp) qg_ld8(p.gamma + col, g0);  // used after the barrier
     if (KIND == ACT_X) {
       qg_ld8(xr + col, v);
     } else if (KIND == ACT_RESID) {
       float x0[8];
-      qg_split_sum8(p.g, (size_t)row * p.g.ld + col, v);
       qg_ld8(xr + col, x0);
+      qg_split_sum8<B>(p.g, (size_t)row * p.g.ld + col, v);
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fadd_rn(v[i], x0[i]);
       float* xw = p.xo + (size_t)row * k + col;
@@ -478,8 +500,7 @@ __global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
       *reinterpret_cast<float4*>(xw + 4) = make_float4(v[4], v[5], v[6], v[7]);
     } else {
       float u[8];
-      qg_split_sum8(p.g, (size_t)row * p.g.ld + col, v);
-      qg_split_sum8(p.g, (size_t)row * p.g.ld + k + col, u);
+      qg_split_sum8x2<(B > 1 ? B / 2 : 1)>(p.g, (size_t)row * p.g.ld + col, (long long)((size_t)row * p.g.ld + k + col), v, u);
 #pragma unroll
       for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], __fadd_rn(1.0f, expf(-v[i]))), u[i]);
     }
@@ -489,6 +510,10 @@ __global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       if (lane == 0) part[j] = ss;
+      if (KEEP && j == warp) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) keep[i] = v[i];
+      }
     } else if (tbase) {
       qg_act_block(v, lane, j, r, tbase);
     }
@@ -505,8 +530,13 @@ __global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
   for (int j = warp; j < nb; j += nw) {
     const int col = j * QK_K + 8 * lane;
     float v[8], g[8];
-    qg_ld8(xr + col, v);  // ACT_RESID: this thread's own stores above
-    qg_ld8(p.gamma + col, g);
+    if (KEEP && j == warp) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) { v[i] = keep[i]; g[i] = g0[i]; }
+    } else {
+      qg_ld8(xr + col, v);  // ACT_RESID: this thread's own stores above
+      qg_ld8(p.gamma + col, g);
+    }
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fdiv_rn(v[i], rms), g[i]);
     qg_act_block(v, lane, j, r, tbase);
@@ -514,6 +544,7 @@ __global__ void __launch_bounds__(1024) k_row_act(const RowAct p) {
 }
 
 // ---- q|k|v epilogue -------------------------------------------------------
+template <int B>
 __global__ void k_qkv_post(const QgSplit g, int S, const int* __restrict__ pos, int qn, int kn, int hd,
                            int max_seq, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                            float* __restrict__ q_out, void* kc, void* vc, int kv_f16, int64_t slot_stride,
@@ -526,10 +557,20 @@ __global__ void k_qkv_post(const QgSplit g, int S, const int* __restrict__ pos, 
   if (t >= S || 2 * pr >= rows) return;
   const int r = 2 * pr;
   const float* w = g.ws + (size_t)t * g.ld + r;
-  float d0 = w[0], d1 = w[1];
-  for (int sp = 1; sp < g.splits; sp++) {
-    d0 = __fadd_rn(d0, w[(size_t)sp * g.stride]);
-    d1 = __fadd_rn(d1, w[(size_t)sp * g.stride + 1]);
+  // rows (q | k | v, multiples of head_dim) and the split stride are even,
+  // so each row pair is one aligned float2; a batch's loads in flight together
+  float d0 = 0.f, d1 = 0.f;
+  for (int sp0 = 0; sp0 < g.splits; sp0 += B) {
+    float2 pv[B];
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if (sp0 + u < g.splits) pv[u] = *reinterpret_cast<const float2*>(w + (size_t)(sp0 + u) * g.stride);
+#pragma unroll
+    for (int u = 0; u < B; u++)
+      if (sp0 + u < g.splits) {
+        d0 = sp0 + u == 0 ? pv[u].x : __fadd_rn(d0, pv[u].x);
+        d1 = sp0 + u == 0 ? pv[u].y : __fadd_rn(d1, pv[u].y);
+      }
   }
   const int p = pos[t], half = hd >> 1;
   if (r < qn + kn) {
@@ -577,16 +618,29 @@ __global__ void k_qg_finish(const float* __restrict__ ws, int splits, size_t spl
   const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= m || i >= ncols) return;
   const float* w = ws + (size_t)t * ldw + i;
-  float a = w[0];
-  for (int sp = 1; sp < splits; sp++) a = __fadd_rn(a, w[(size_t)sp * split_stride]);
+  const bool two = mode != QG_STORE && mode != QG_RESID;
+  float a = 0.f, u = 0.f;
+  for (int sp0 = 0; sp0 < splits; sp0 += 8) {  // a batch's loads in flight together
+    float pa[8], pu[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (sp0 + k < splits) {
+        pa[k] = w[(size_t)(sp0 + k) * split_stride];
+        if (two) pu[k] = w[(size_t)(sp0 + k) * split_stride + ncols];
+      }
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (sp0 + k < splits) {
+        a = sp0 + k == 0 ? pa[k] : __fadd_rn(a, pa[k]);
+        if (two) u = sp0 + k == 0 ? pu[k] : __fadd_rn(u, pu[k]);
+      }
+  }
   float* o = dst + (size_t)t * ldd + i;
   if (mode == QG_STORE) {
     *o = a;
   } else if (mode == QG_RESID) {
     *o = __fadd_rn(a, *o);
   } else {
-    float u = w[ncols];
-    for (int sp = 1; sp < splits; sp++) u = __fadd_rn(u, w[(size_t)sp * split_stride + ncols]);
     *o = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), u);
   }
 }
@@ -638,6 +692,10 @@ __global__ void __launch_bounds__(1024) k_row_argmax(const float* __restrict__ l
 }
 
 // ---- launchers --------------------------------------------------------------
+// Row counts up to this take the row kernels' many-loads-per-round-trip
+// variants (a decode batch); longer inputs the lighter ones (prompts).
+constexpr int QG_FEW_ROWS = 64;
+
 int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int hd, int max_seq,
                     const float* cos_t, const float* sin_t, float* q_out, void* kc, void* vc, int kv_f16,
                     int64_t kv_seq_stride, int seq_step, cudaStream_t s, bool pdl, const FaTilesOut* tiles) {
@@ -645,13 +703,15 @@ int qkv_post_launch(const QgSplit& g, int S, const int* pos, int qn, int kn, int
   FaTilesOut tl{};
   if (tiles) tl = *tiles;
   const dim3 grid((unsigned)((g.ld / 2 + 127) / 128), (unsigned)S);
-  ARMAI_CUDA(qg_launch(k_qkv_post, grid, dim3(128), 0, s, pdl, g, S, pos, qn, kn, hd, max_seq, cos_t, sin_t,
+  ARMAI_CUDA(qg_launch(S <= QG_FEW_ROWS ? k_qkv_post<8> : k_qkv_post<2>, grid, dim3(128), 0, s, pdl, g, S, pos, qn,
+                       kn, hd, max_seq, cos_t, sin_t,
                        q_out, kc, vc, kv_f16, (int64_t)(kv_seq_stride * seq_step), tl));
   return ARMAI_OK;
 }
 
-// One warp per 256-value block of a row (8 .. 32 warps).
-static unsigned row_threads(int k) { return 32u * (unsigned)std::min(32, std::max(8, k / QK_K)); }
+// One warp per 256-value block of a row (8 .. 16 warps; longer rows give a
+// warp several blocks).
+static unsigned row_threads(int k) { return 32u * (unsigned)std::min(16, std::max(8, k / QK_K)); }
 
 int resid_act_launch(const QgSplit& g, float* x, int S, int n, const float* gamma, float eps, uint8_t* a_tiles,
                      cudaStream_t s, bool pdl) {
@@ -664,7 +724,8 @@ int resid_act_launch(const QgSplit& g, float* x, int S, int n, const float* gamm
   p.k = n;
   p.g = g;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_RESID>, dim3(S), dim3(row_threads(n)), 0, s, pdl, p));
+  ARMAI_CUDA(qg_launch(S <= QG_FEW_ROWS ? k_row_act<ACT_RESID, 8> : k_row_act<ACT_RESID, 2>, dim3(S),
+                       dim3(row_threads(n)), 0, s, pdl, p));
   return ARMAI_OK;
 }
 
@@ -675,7 +736,9 @@ int silu_act_launch(const QgSplit& g, int S, int F, uint8_t* a_tiles, cudaStream
   p.k = F;
   p.g = g;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_SILU>, dim3(S), dim3(row_threads(F)), 0, s, pdl, p));
+  const int nb = F / QK_K, per = std::min(nb, 8);  // 8 blocks per CTA: no norm, so rows split freely
+  ARMAI_CUDA(qg_launch(S <= QG_FEW_ROWS ? k_row_act<ACT_SILU, 8> : k_row_act<ACT_SILU, 2>, dim3(S, (unsigned)((nb + per - 1) / per)), dim3(32u * per), 0, s, pdl,
+                       p));
   return ARMAI_OK;
 }
 
@@ -702,7 +765,7 @@ int qgemm_act_launch(const float* x, const float* gamma, float eps, int m, int k
   p.eps = eps;
   p.k = k;
   p.a_tiles = a_tiles;
-  ARMAI_CUDA(qg_launch(k_row_act<ACT_X>, dim3(m), dim3(row_threads(k)), 0, s, pdl, p));
+  ARMAI_CUDA(qg_launch(m <= QG_FEW_ROWS ? k_row_act<ACT_X, 8> : k_row_act<ACT_X, 2>, dim3(m), dim3(row_threads(k)), 0, s, pdl, p));
   return ARMAI_OK;
 }
 

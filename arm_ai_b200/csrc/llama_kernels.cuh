@@ -678,22 +678,27 @@ struct AttnParams {
   uint32_t* err;
 };
 
-constexpr int ATT_TILE = 32;     // positions per shared-memory tile
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_MAX_REP = 8;   // query heads per KV head
-constexpr int ATT_SPLITS = 16;   // split-K factor (fixed: the combine is unrolled over it)
+constexpr int ATT_SPLITS = 16;   // most context splits per (sequence, KV head): the partials' layout
+// Positions per shared-memory tile: 64 at head_dim 64, 32 at 128 (the same
+// 16 KB K tile either way).
+template <int HD>
+__host__ __device__ constexpr int att_tile() { return 4096 / HD; }
 
 // Shared memory of k_attn_decode<HD> (floats): q[rep][HD], K[TILE][HD+1],
 // V[TILE][HD], p[rep][TILE], corr/m/l[rep], combine weights[SPLITS][rep].
 __host__ __device__ inline size_t attn_smem_floats(int hd) {
-  return (size_t)ATT_MAX_REP * hd + (size_t)ATT_TILE * (hd + 1) + (size_t)ATT_TILE * hd +
-         (size_t)ATT_MAX_REP * ATT_TILE + 3 * ATT_MAX_REP + (size_t)ATT_SPLITS * ATT_MAX_REP + ATT_MAX_REP;
+  const size_t tile = (size_t)(4096 / hd);
+  return (size_t)ATT_MAX_REP * hd + tile * (hd + 1) + tile * hd + (size_t)ATT_MAX_REP * tile + 3 * ATT_MAX_REP +
+         (size_t)ATT_SPLITS * ATT_MAX_REP + ATT_MAX_REP;
 }
 
 template <int HD, typename KV>
 __device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, float* Vs, const KV* vbase) {
   // n rows of HD values; K rows padded to HD+1 floats (conflict-free column reads)
   constexpr int V4 = HD / 4;
+#pragma unroll 4
   for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
     const int t = i / V4, c = (i % V4) * 4;
     float4 kv, vv;
@@ -717,24 +722,29 @@ __device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, f
 }
 
 // Split-K GQA flash-decode. grid (n_kv, ATT_SPLITS, NB), ATT_THREADS threads.
-// CTA (kvh, s, b) covers positions [t0, t1) of sequence b for the nrep query
-// heads sharing KV head kvh (repeat_kv: kvh = h / nrep), in tiles of 32:
-// scores s = (q . k) * scale with a lane per position, an online softmax per
-// head, o += p v with a thread per output dim. The last CTA of (b, kvh)
-// merges the splits in split order: y = sum_s o_s e^{m_s-M} / sum_s l_s e^{m_s-M}.
+// Sequence b's T positions are split over the fewest CTAs that keep one tile
+// (att_tile<HD>() positions) per CTA, at most ATT_SPLITS (longer contexts
+// give a CTA several tiles); CTAs past that count return at once. CTA
+// (kvh, s, b) covers positions [t0, t1) for the nrep query heads sharing KV
+// head kvh (repeat_kv: kvh = h / nrep): scores s = (q . k) * scale with a
+// lane per position (two heads per warp pass), an online softmax per head,
+// o += p v with a thread per output dim. The last CTA of (b, kvh) merges the
+// splits in split order: y = sum_s o_s e^{m_s-M} / sum_s l_s e^{m_s-M}.
 // For prefill the batch index runs over the prompt's tokens with a shared
 // cache (kv_seq_stride 0): token b attends positions 0..pos[b] (causal).
 template <int HD, typename KV>
 __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p) {
+  constexpr int TILE = att_tile<HD>();
+  constexpr int PPL = TILE / 32;                    // positions per lane
   extern __shared__ __align__(16) float sm[];
   const int kvh = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nrep = p.n_head / p.n_kv;
   float* qs = sm;                                   // [ATT_MAX_REP][HD]
   float* Ks = qs + ATT_MAX_REP * HD;                // [TILE][HD+1]
-  float* Vs = Ks + ATT_TILE * (HD + 1);             // [TILE][HD]
-  float* ps = Vs + ATT_TILE * HD;                   // [ATT_MAX_REP][TILE]
-  float* corr = ps + ATT_MAX_REP * ATT_TILE;        // [rep]
+  float* Vs = Ks + TILE * (HD + 1);                 // [TILE][HD]
+  float* ps = Vs + TILE * HD;                       // [ATT_MAX_REP][TILE]
+  float* corr = ps + ATT_MAX_REP * TILE;            // [rep]
   float* mrow = corr + ATT_MAX_REP;                 // [rep]
   float* lrow = mrow + ATT_MAX_REP;                 // [rep]
   float* wts = lrow + ATT_MAX_REP;                  // [SPLITS][rep]
@@ -743,7 +753,9 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   pdl_launch();
   pdl_wait();
   const int T = p.pos[b] + 1;
-  const int chunk = (T + ATT_SPLITS - 1) / ATT_SPLITS;
+  const int splits = min(ATT_SPLITS, (T + TILE - 1) / TILE);
+  if (s >= splits) return;
+  const int chunk = (T + splits - 1) / splits;
   const int t0 = min(T, s * chunk), t1 = min(T, t0 + chunk);
   const float* qb = p.q + (size_t)b * p.n_head * HD + (size_t)kvh * nrep * HD;
   for (int i = tid; i < nrep * HD / 4; i += blockDim.x)
@@ -756,59 +768,113 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   constexpr int DGROUPS = ATT_THREADS / HD;          // 2 for HD=64, 1 for HD=128
   constexpr int RPG = ATT_MAX_REP / DGROUPS;         // heads per thread
   const int d = tid % HD, rg = tid / HD;
+  const int nmine = min(RPG, nrep - rg * RPG);       // heads of this thread (may be <= 0)
   float o[RPG];
 #pragma unroll
   for (int i = 0; i < RPG; i++) o[i] = 0.f;
-  for (int tt0 = t0; tt0 < t1; tt0 += ATT_TILE) {
-    const int n = min(ATT_TILE, t1 - tt0);
+  for (int tt0 = t0; tt0 < t1; tt0 += TILE) {
+    const int n = min(TILE, t1 - tt0);
     __syncthreads();  // previous tile fully consumed (and q / m / l initialised)
     load_kv_tile<HD, KV>(kc + (size_t)tt0 * HD, n, Ks, Vs, vc + (size_t)tt0 * HD);
     __syncthreads();
-    for (int r = warp; r < nrep; r += ATT_THREADS / 32) {
-      float sc = -INFINITY;
-      if (lane < n) {
-        float acc = 0.f;
+    // scores and online softmax: warp per head pair (r, r + 4), lane per
+    // position(s) lane + 32 j; the two heads share each K element load
+    constexpr int NW = ATT_THREADS / 32;
+    for (int r = warp; r < nrep; r += 2 * NW) {
+      const int r2 = r + NW;
+      const bool two = r2 < nrep;
+      const float* qa = qs + r * HD;
+      const float* qb2 = qs + (two ? r2 : r) * HD;
+      float sc[PPL], sc2[PPL];
+#pragma unroll
+      for (int j = 0; j < PPL; j++) {
+        sc[j] = -INFINITY;
+        sc2[j] = -INFINITY;
+        if (lane + 32 * j < n) {
+          const float* kr = Ks + (lane + 32 * j) * (HD + 1);
+          float acc = 0.f, acc2 = 0.f;
 #pragma unroll 16
-        for (int dd = 0; dd < HD; dd++) acc += qs[r * HD + dd] * Ks[lane * (HD + 1) + dd];
-        sc = acc * p.scale;
+          for (int dd = 0; dd < HD; dd++) {
+            const float kv = kr[dd];
+            acc += qa[dd] * kv;
+            acc2 += qb2[dd] * kv;
+          }
+          sc[j] = acc * p.scale;
+          sc2[j] = acc2 * p.scale;
+        }
       }
-      float mt = sc;
+      float mt = sc[0], mt2 = sc2[0];
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-      const float mold = mrow[r];
-      const float mnew = fmaxf(mold, mt);
-      const float pe = lane < n ? expf(sc - mnew) : 0.f;
-      float ls = pe;
+      for (int j = 1; j < PPL; j++) {
+        mt = fmaxf(mt, sc[j]);
+        mt2 = fmaxf(mt2, sc2[j]);
+      }
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-      ps[r * ATT_TILE + lane] = pe;
+      for (int off = 16; off >= 1; off >>= 1) {
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+        mt2 = fmaxf(mt2, __shfl_xor_sync(0xffffffffu, mt2, off));
+      }
+      const float mold = mrow[r], mold2 = mrow[two ? r2 : r];
+      const float mnew = fmaxf(mold, mt), mnew2 = fmaxf(mold2, mt2);
+      float ls = 0.f, ls2 = 0.f;
+#pragma unroll
+      for (int j = 0; j < PPL; j++) {
+        const bool in = lane + 32 * j < n;
+        const float pe = in ? expf(sc[j] - mnew) : 0.f;
+        const float pe2 = in ? expf(sc2[j] - mnew2) : 0.f;
+        ls += pe;
+        ls2 += pe2;
+        ps[r * TILE + lane + 32 * j] = pe;
+        if (two) ps[r2 * TILE + lane + 32 * j] = pe2;
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        ls += __shfl_xor_sync(0xffffffffu, ls, off);
+        ls2 += __shfl_xor_sync(0xffffffffu, ls2, off);
+      }
       __syncwarp();
       if (lane == 0) {
         const float c = expf(mold - mnew);  // 0 on the first tile (mold = -inf)
         corr[r] = c;
         lrow[r] = lrow[r] * c + ls;
         mrow[r] = mnew;
+        if (two) {
+          const float c2 = expf(mold2 - mnew2);
+          corr[r2] = c2;
+          lrow[r2] = lrow[r2] * c2 + ls2;
+          mrow[r2] = mnew2;
+        }
       }
     }
     __syncthreads();
+    // o += p v: position outer, the thread's heads inner (one V load per
+    // position; each head's sum in position order)
+    const float* pr = ps + rg * RPG * TILE;
 #pragma unroll
-    for (int i = 0; i < RPG; i++) {
-      const int r = rg * RPG + i;
-      if (r < nrep) {
-        float acc = o[i] * corr[r];
-        for (int tt = 0; tt < n; tt++) acc += ps[r * ATT_TILE + tt] * Vs[tt * HD + d];
-        o[i] = acc;
-      }
+    for (int i = 0; i < RPG; i++)
+      if (i < nmine) o[i] *= corr[rg * RPG + i];
+    for (int tt = 0; tt < n; tt++) {
+      const float v = Vs[tt * HD + d];
+#pragma unroll
+      for (int i = 0; i < RPG; i++)
+        if (i < nmine) o[i] += pr[i * TILE + tt] * v;
     }
+  }
+  if (splits == 1) {  // the whole context in this CTA: y directly
+#pragma unroll
+    for (int i = 0; i < RPG; i++)
+      if (i < nmine) {
+        const int r = rg * RPG + i;
+        p.y[(size_t)b * p.n_head * HD + ((size_t)kvh * nrep + r) * HD + d] = o[i] / lrow[r];
+      }
+    return;
   }
   __syncthreads();
   // partial of this split: o[rep][HD], m[rep], l[rep]
   const size_t pbase = ((((size_t)b * p.n_kv + kvh) * ATT_SPLITS + s) * nrep) * (HD + 2);
 #pragma unroll
-  for (int i = 0; i < RPG; i++) {
-    const int r = rg * RPG + i;
-    if (r < nrep) p.part[pbase + (size_t)r * (HD + 2) + d] = o[i];
-  }
+  for (int i = 0; i < RPG; i++)
+    if (i < nmine) p.part[pbase + (size_t)(rg * RPG + i) * (HD + 2) + d] = o[i];
   if (tid < nrep) {
     p.part[pbase + (size_t)tid * (HD + 2) + HD] = mrow[tid];
     p.part[pbase + (size_t)tid * (HD + 2) + HD + 1] = lrow[tid];
@@ -817,14 +883,14 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   __syncthreads();
   if (tid == 0) {
     const unsigned prev = atomicAdd(&p.counters[b * p.n_kv + kvh], 1u);
-    s_last = (prev == (unsigned)ATT_SPLITS - 1);
+    s_last = (prev == (unsigned)splits - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const size_t base0 = (((size_t)b * p.n_kv + kvh) * ATT_SPLITS) * nrep * (HD + 2);
   // 1) (m, l) of every (split, head) -> smem; per-head max and weights
-  if (tid < ATT_SPLITS * nrep) {
+  if (tid < splits * nrep) {
     const int s2 = tid / nrep, r = tid % nrep;
     const size_t o2 = base0 + ((size_t)s2 * nrep + r) * (HD + 2);
     wts[s2 * ATT_MAX_REP + r] = __ldcg(p.part + o2 + HD);        // m
@@ -833,10 +899,10 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   __syncthreads();
   if (tid < nrep) {
     float M = -INFINITY;
-    for (int s2 = 0; s2 < ATT_SPLITS; s2++)
+    for (int s2 = 0; s2 < splits; s2++)
       if (ps[s2 * ATT_MAX_REP + tid] > 0.f) M = fmaxf(M, wts[s2 * ATT_MAX_REP + tid]);
     float Ls = 0.f;
-    for (int s2 = 0; s2 < ATT_SPLITS; s2++) {
+    for (int s2 = 0; s2 < splits; s2++) {
       const float l = ps[s2 * ATT_MAX_REP + tid];
       const float w = l > 0.f ? expf(wts[s2 * ATT_MAX_REP + tid] - M) : 0.f;
       wts[s2 * ATT_MAX_REP + tid] = w;
@@ -851,10 +917,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
     float ov[ATT_SPLITS];
 #pragma unroll
     for (int s2 = 0; s2 < ATT_SPLITS; s2++)
-      ov[s2] = __ldcg(p.part + base0 + ((size_t)s2 * nrep + r) * (HD + 2) + dd);
+      if (s2 < splits) ov[s2] = __ldcg(p.part + base0 + ((size_t)s2 * nrep + r) * (HD + 2) + dd);
     float O = 0.f;
 #pragma unroll
-    for (int s2 = 0; s2 < ATT_SPLITS; s2++) O += wts[s2 * ATT_MAX_REP + r] * ov[s2];
+    for (int s2 = 0; s2 < ATT_SPLITS; s2++)
+      if (s2 < splits) O += wts[s2 * ATT_MAX_REP + r] * ov[s2];
     p.y[(size_t)b * p.n_head * HD + ((size_t)kvh * nrep + r) * HD + dd] = O / Ltot[r];
   }
   if (tid == 0) p.counters[b * p.n_kv + kvh] = 0u;
