@@ -347,6 +347,30 @@ __device__ __forceinline__ void wait_words(const unsigned long long* p, uint32_t
       if ((uint32_t)w[e] != want || (uint32_t)w[e + 1] != want) ld_words2<SYS>(p + e, w[e], w[e + 1]);
   }
 }
+// N (even) consecutive words at each of two addresses, all carrying tag
+// `want`: both sets' loads are in flight together (one round trip for two
+// ranks' row sums instead of two).
+template <bool SYS, int N>
+__device__ __forceinline__ void wait_words_pair(const unsigned long long* pa, const unsigned long long* pb,
+                                                uint32_t want, unsigned long long (&wa)[N],
+                                                unsigned long long (&wb)[N], uint32_t* err, uint32_t limit) {
+#pragma unroll
+  for (int e = 0; e < N; e += 2) {
+    ld_words2<SYS>(pa + e, wa[e], wa[e + 1]);
+    ld_words2<SYS>(pb + e, wb[e], wb[e + 1]);
+  }
+  for (uint32_t it = 0;; ++it) {
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < N; e++) ok &= ((uint32_t)wa[e] == want) & ((uint32_t)wb[e] == want);
+    if (ok || !poll_continue(it, err, limit)) return;
+#pragma unroll
+    for (int e = 0; e < N; e += 2) {
+      if ((uint32_t)wa[e] != want || (uint32_t)wa[e + 1] != want) ld_words2<SYS>(pa + e, wa[e], wa[e + 1]);
+      if ((uint32_t)wb[e] != want || (uint32_t)wb[e + 1] != want) ld_words2<SYS>(pb + e, wb[e], wb[e + 1]);
+    }
+  }
+}
 // One word carrying tag `want`; its value.
 template <bool SYS>
 __device__ __forceinline__ float wait_word(const unsigned long long* p, uint32_t want, uint32_t* err,
@@ -378,7 +402,14 @@ __device__ __forceinline__ F8 mk_load_vals_ool(const MkParams& p, const MkPhase&
     const float4 a = xr[0], b = xr[1];
     float acc[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
     const unsigned long long* sl = p.xslot[p.tp_rank] + (size_t)par * p.tp * E + j * QK_K + 8 * lane;
-    for (int k = 0; k < p.tp; k++) {
+    int k = 0;
+    for (; k + 1 < p.tp; k += 2) {  // two ranks' slots per round trip, added in rank order
+      unsigned long long w[8], w2[8];
+      wait_words_pair<true, 8>(sl + (size_t)k * E, sl + (size_t)(k + 1) * E, want, w, w2, p.err, p.poll_limit);
+#pragma unroll
+      for (int e = 0; e < 8; e++) acc[e] = __fadd_rn(__fadd_rn(acc[e], word_val(w[e])), word_val(w2[e]));
+    }
+    if (k < p.tp) {
       unsigned long long w[8];
       wait_words<true, 8>(sl + (size_t)k * E, want, w, p.err, p.poll_limit);
 #pragma unroll
@@ -603,16 +634,39 @@ __device__ __forceinline__ void mk_advance(MkRun& run, int ns) {
   }
 }
 
+// The first one or two ring stages of this CTA's rows in phase ph (the
+// stages mk_chunks takes first), waited for before the phase's activation
+// build: the producer issued them phases earlier, and the wait and its
+// bookkeeping then overlap the wait for the phase's inputs instead of
+// following the activation build. Slot 10 / 11 of the trace: the wait's start
+// and its mbarrier polls.
+__device__ __forceinline__ bool mk_first_stages(const MkParams& p, const MkPhase& ph, int phase, int r0, int r1,
+                                                uint64_t* full, const MkRun& run, int cw, int lane) {
+  if (r0 >= r1) return true;
+  const int c1 = min(r0 + ph.chunk_rows, r1);
+  const bool two = ph.kind != PH_QKV && c1 < r1;
+  uint32_t iters = 0;
+  const bool tr = p.trace && cw == 0 && lane == 0;
+  if (tr) mk_stamp(p, phase, 10);
+  if (!mk_wait(&full[run.s], (uint32_t)run.par, p.err, tr ? &iters : nullptr)) return false;
+  if (tr) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * MK_TRACE_SLOTS + 11] = iters;
+  if (two) {
+    const bool wrap = run.s + 1 == p.ns;
+    if (!mk_wait(&full[wrap ? 0 : run.s + 1], (uint32_t)(run.par ^ (wrap ? 1 : 0)), p.err)) return false;
+  }
+  return true;
+}
+
 // All chunks of this CTA's rows in one matvec phase: wait for the stages,
 // compute, hand the stages back to the producer. Except for QKV (few rows
 // per CTA), chunks are taken two at a time and their units dealt over the
 // consumer warps as one list, so a phase whose rows arrive in several stages
 // does not serialise one unit per warp per stage.
+// Rows [r0, r1) come from phase_rows; the first chunk's stages were already
+// waited for (mk_first_stages) when first_waited is set.
 __device__ MkRun mk_chunks(const MkParams& p, const MkPhase& ph, int mode, int phase, int pos, uint32_t tag,
                            uint8_t* smem, uint64_t* full, uint64_t* empty, MkRun run, const ActQ8 act, int cw,
-                           int lane) {
-  int r0, r1;
-  phase_rows(ph, r0, r1);
+                           int lane, int r0, int r1, bool first_waited) {
   const MkCtx cx{p, ph, pos, phase, tag};
   const int nb = ph.nb;
   for (int c0 = r0; c0 < r1;) {
@@ -623,12 +677,10 @@ __device__ MkRun mk_chunks(const MkParams& p, const MkPhase& ph, int mode, int p
     mk_advance(run, p.ns);
     const int sB = run.s, pB = run.par;
     if (two) mk_advance(run, p.ns);
-    uint32_t iters = 0;
-    const bool tr = p.trace && c0 == r0 && cw == 0 && lane == 0;
-    if (tr) mk_stamp(p, phase, 10);
-    if (!mk_wait(&full[sA], (uint32_t)pA, p.err, tr ? &iters : nullptr)) return run;
-    if (tr) p.trace[((size_t)phase * gridDim.x + blockIdx.x) * MK_TRACE_SLOTS + 11] = iters;
-    if (two && !mk_wait(&full[sB], (uint32_t)pB, p.err)) return run;
+    if (!(first_waited && c0 == r0)) {
+      if (!mk_wait(&full[sA], (uint32_t)pA, p.err)) return run;
+      if (two && !mk_wait(&full[sB], (uint32_t)pB, p.err)) return run;
+    }
     if (c0 == r0 && cw == 0 && lane == 0) mk_stamp(p, phase, 4);
     Part pa[3], pb[3];
     mk_parts(ph, mode, c0, c1, pa);
@@ -1121,13 +1173,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
                              want, tag);
       }
     } else {
+      int r0, r1;
+      phase_rows(ph, r0, r1);
+      const bool staged = mk_first_stages(p, ph, i, r0, r1, full, run, cw, lane);
       mk_build_act(p, ph, i, smem, act, cw, lane, xrep, gbar, gcount & 1u, want);
       if (ph.gamma) gcount++;
       if (ctid == 0) mk_stamp(p, i, 1);
       // a wait that gives up flags the error and goes on (in bounds); all
       // warps leave at the next phase start
       const int mode = mode_of(ph.kind);
-      run = mk_chunks(p, ph, mode, i, s_pos, tag, smem, full, empty, run, act, cw, lane);
+      if (staged) run = mk_chunks(p, ph, mode, i, s_pos, tag, smem, full, empty, run, act, cw, lane, r0, r1, true);
     }
     if (ctid == 0) mk_stamp(p, i, 2);
   }

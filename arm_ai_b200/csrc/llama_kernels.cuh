@@ -686,38 +686,47 @@ constexpr int ATT_SPLITS = 16;   // most context splits per (sequence, KV head):
 template <int HD>
 __host__ __device__ constexpr int att_tile() { return 4096 / HD; }
 
-// Shared memory of k_attn_decode<HD> (floats): q[rep][HD], K[TILE][HD+1],
-// V[TILE][HD], p[rep][TILE], corr/m/l[rep], combine weights[SPLITS][rep].
+// Shared memory of k_attn_decode<HD> (floats): q[rep][HD], K[TILE][HD],
+// V[TILE][HD], p[rep][TILE], corr/m/l[rep], combine weights[SPLITS][rep]
+// (37.5 KB at either head_dim: six CTAs per SM).
 __host__ __device__ inline size_t attn_smem_floats(int hd) {
   const size_t tile = (size_t)(4096 / hd);
-  return (size_t)ATT_MAX_REP * hd + tile * (hd + 1) + tile * hd + (size_t)ATT_MAX_REP * tile + 3 * ATT_MAX_REP +
+  return (size_t)ATT_MAX_REP * hd + 2 * tile * hd + (size_t)ATT_MAX_REP * tile + 3 * ATT_MAX_REP +
          (size_t)ATT_SPLITS * ATT_MAX_REP + ATT_MAX_REP;
 }
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+
+// n rows of HD values of K and V into shared memory. K row t keeps its
+// 16-byte chunk c at c ^ (t & 7), so that float4 reads of one chunk by a lane
+// per row hit distinct banks. f32 caches: asynchronous 16-byte copies, every
+// copy of the tile in flight at once; f16 caches: loaded and widened by the
+// threads.
 template <int HD, typename KV>
 __device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, float* Vs, const KV* vbase) {
-  // n rows of HD values; K rows padded to HD+1 floats (conflict-free column reads)
   constexpr int V4 = HD / 4;
+  if constexpr (sizeof(KV) == 4) {
+    for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
+      const int t = i / V4, c = (i % V4) * 4;
+      cp_async16(Ks + t * HD + ((c >> 2) ^ (t & 7)) * 4, reinterpret_cast<const float*>(base) + (size_t)t * HD + c);
+      cp_async16(Vs + t * HD + c, reinterpret_cast<const float*>(vbase) + (size_t)t * HD + c);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  } else {
 #pragma unroll 4
-  for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
-    const int t = i / V4, c = (i % V4) * 4;
-    float4 kv, vv;
-    if constexpr (sizeof(KV) == 4) {
-      kv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + (size_t)t * HD + c);
-      vv = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(vbase) + (size_t)t * HD + c);
-    } else {
+    for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
+      const int t = i / V4, c = (i % V4) * 4;
       const uint2 kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + (size_t)t * HD + c);
       const uint2 vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(vbase) + (size_t)t * HD + c);
       const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kr.x));
       const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kr.y));
       const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vr.x));
       const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vr.y));
-      kv = make_float4(k0.x, k0.y, k1.x, k1.y);
-      vv = make_float4(v0.x, v0.y, v1.x, v1.y);
+      *reinterpret_cast<float4*>(Ks + t * HD + ((c >> 2) ^ (t & 7)) * 4) = make_float4(k0.x, k0.y, k1.x, k1.y);
+      *reinterpret_cast<float4*>(Vs + t * HD + c) = make_float4(v0.x, v0.y, v1.x, v1.y);
     }
-    float* kd = Ks + t * (HD + 1) + c;
-    kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-    *reinterpret_cast<float4*>(Vs + t * HD + c) = vv;
   }
 }
 
@@ -741,8 +750,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nrep = p.n_head / p.n_kv;
   float* qs = sm;                                   // [ATT_MAX_REP][HD]
-  float* Ks = qs + ATT_MAX_REP * HD;                // [TILE][HD+1]
-  float* Vs = Ks + TILE * (HD + 1);                 // [TILE][HD]
+  float* Ks = qs + ATT_MAX_REP * HD;                // [TILE][HD], chunk-swizzled
+  float* Vs = Ks + TILE * HD;                       // [TILE][HD]
   float* ps = Vs + TILE * HD;                       // [ATT_MAX_REP][TILE]
   float* corr = ps + ATT_MAX_REP * TILE;            // [rep]
   float* mrow = corr + ATT_MAX_REP;                 // [rep]
@@ -791,13 +800,22 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
         sc[j] = -INFINITY;
         sc2[j] = -INFINITY;
         if (lane + 32 * j < n) {
-          const float* kr = Ks + (lane + 32 * j) * (HD + 1);
+          const float4* kr = reinterpret_cast<const float4*>(Ks + (lane + 32 * j) * HD);
+          const int sw = lane & 7;  // the row's chunk swizzle
+          const float4* q4a = reinterpret_cast<const float4*>(qa);
+          const float4* q4b = reinterpret_cast<const float4*>(qb2);
           float acc = 0.f, acc2 = 0.f;
-#pragma unroll 16
-          for (int dd = 0; dd < HD; dd++) {
-            const float kv = kr[dd];
-            acc += qa[dd] * kv;
-            acc2 += qb2[dd] * kv;
+#pragma unroll 4
+          for (int d4 = 0; d4 < HD / 4; d4++) {  // dims in order: each sum as the sequential dot
+            const float4 kv = kr[d4 ^ sw], xa = q4a[d4], xb = q4b[d4];
+            acc = fmaf(xa.x, kv.x, acc);
+            acc = fmaf(xa.y, kv.y, acc);
+            acc = fmaf(xa.z, kv.z, acc);
+            acc = fmaf(xa.w, kv.w, acc);
+            acc2 = fmaf(xb.x, kv.x, acc2);
+            acc2 = fmaf(xb.y, kv.y, acc2);
+            acc2 = fmaf(xb.z, kv.z, acc2);
+            acc2 = fmaf(xb.w, kv.w, acc2);
           }
           sc[j] = acc * p.scale;
           sc2[j] = acc2 * p.scale;

@@ -165,14 +165,17 @@ def _trace_decode(d):
         a = np.array(v) / 1e3
         print_(f"| {kind} | {len(v)} | {np.median(a[:, 0]):.2f} | {np.median(a[:, 1]):.2f} | {np.median(a[:, 2]):.2f} |")
     lm = nl // 2
-    print_(f"layer {lm}, slot medians relative to the phase start (us):")
+    print_(f"layer {lm}, slot medians relative to the phase start (us; s3 = the producer issued the phase's "
+           f"first weight chunk, s10 = consumers start waiting for it; polls = that wait's mbarrier polls):")
     for i in range(5 * lm, 5 * lm + 5):
         s0 = tr[i, :, 0]
         ok = s0 > 0
         cells = []
-        for j in (6, 7, 1, 4, 5, 2):
+        for j in (3, 6, 7, 1, 10, 4, 5, 2):
             okj = ok & (tr[i, :, j] > 0)
-            cells.append(f"s{j} {(med(tr[i, okj, j]) - med(s0[ok])) / 1e3:.2f}" if okj.any() else f"s{j} -")
+            cells.append(f"s{j} {(med(tr[i, okj, j] - s0[okj])) / 1e3:.2f}" if okj.any() else f"s{j} -")
+        okp = ok & (tr[i, :, 10] > 0)
+        cells.append(f"polls {med(tr[i, okp, 11]):.0f}" if okp.any() else "polls -")
         print_(f"  {names[i % 5]:6s} " + "  ".join(cells))
     text = "\n".join(out)
     print((f"rank {d.rank} of {d.world}:\n" if d.world > 1 else "") + text, flush=True)
