@@ -1067,6 +1067,19 @@ __device__ void mk_attn_short(const MkParams& p, const MkPhase& ph, int phase, i
   if (tid == 0) mk_stamp(p, phase, 8);
 }
 
+// Asynchronous copy of a phase descriptor into shared memory by one warp
+// (8-byte pieces); the warp waits for it (cp.async.wait_all) before the sync
+// that publishes it.
+__device__ __forceinline__ void mk_fetch_phase(const MkPhase* src, MkPhase* dst, int lane) {
+  static_assert(sizeof(MkPhase) % 8 == 0, "phase descriptor copied in 8-byte pieces");
+  constexpr int W8 = (int)(sizeof(MkPhase) / 8);
+  for (int w = lane; w < W8; w += 32)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(reinterpret_cast<uint64_t*>(dst) + w)),
+                 "l"(reinterpret_cast<const uint64_t*>(src) + w)
+                 : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
@@ -1074,7 +1087,7 @@ template <int HD, typename KV>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_constant__ MkParams params) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_flag;
-  __shared__ __align__(16) MkPhase s_ph[2];
+  __shared__ __align__(16) MkPhase s_ph[3];  // phase i's descriptor in s_ph[i % 3]
   __shared__ int s_pos;  // position of this step's token (constant during the step)
   // The launch parameters live in shared memory for the whole step: read
   // through the constant cache, which shares its backing store with the
@@ -1116,32 +1129,41 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_mega(const __grid_cons
   // phase i's outputs carry tag gen + i + 1; its inputs gen + i
   const uint32_t gen = (uint32_t)(__ldcg(p.epoch) * (unsigned long long)(p.n_ph + 1));
 
+  // Phase descriptors live in shared memory, three deep: phases 0 and 1 are
+  // copied here; phase i + 2's is fetched asynchronously at the start of
+  // phase i (into the buffer of phase i - 1, which no warp reads once all
+  // passed phase i's start), so no phase start waits for a global load.
+  for (int i = 0; i < 2 && i < p.n_ph; i++) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph + i);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(&s_ph[i]);
+    for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
+  }
+  // The device error word as loaded at the previous phase start (consumer
+  // thread 0): checked one phase late, so its load never stalls a phase
+  // start. Every wait inside a phase checks the word itself.
+  uint32_t err_seen = 0u;
+
   for (int i = 0; i < p.n_ph; i++) {
-    // Copy the phase descriptor into shared memory (double-buffered by
-    // parity: no warp can still read phase i-1's copy once all passed the
-    // sync below); the sync also ends the CTA's previous phase, so the
-    // attention region is free for the rmsnorm weights staged next.
-    MkPhase& ph = s_ph[i & 1];
-    {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(p.ph + i);
-      uint32_t* dst = reinterpret_cast<uint32_t*>(&ph);
-      for (int w = ctid; w < (int)(sizeof(MkPhase) / 4); w += MK_CT) dst[w] = __ldg(src + w);
-    }
-    if (ctid == 0) s_flag = dev_failed(p.err);
+    // the sync below also ends the CTA's previous phase, so the attention
+    // region is free for the rmsnorm weights staged next
+    MkPhase& ph = s_ph[i % 3];
+    if (cw == 0) asm volatile("cp.async.wait_all;" ::: "memory");  // phase i + 1's descriptor
+    if (ctid == 0) s_flag = err_seen != 0u;
     named_sync(1, MK_CT);
     if (s_flag) {  // a wait gave up somewhere: all consumer warps leave together
       if (ctid == 0 && gissued > gcount) mk_drain(gbar, (gissued - 1u) & 1u);  // no copy left in flight
       return;
     }
+    if (ctid == 0) err_seen = *reinterpret_cast<const volatile uint32_t*>(p.err);
+    if (cw == 0 && i + 2 < p.n_ph) mk_fetch_phase(p.ph + i + 2, &s_ph[(i + 2) % 3], lane);
     // Stage the rmsnorm weights of the next phase (gate/up after attn_output,
     // q/k/v or the head after ffn_down; phase 0 its own) in the attention
     // region, idle until then, so the prologue reads them from shared memory.
     if (ctid == 0) {
       const int gi = i == 0 ? 0 : ((ph.kind == PH_WO || ph.kind == PH_DOWN) && i + 1 < p.n_ph ? i + 1 : -1);
-      const float* g = gi < 0 ? nullptr : reinterpret_cast<const float*>(
-                                              __ldg(reinterpret_cast<const unsigned long long*>(&p.ph[gi].gamma)));
+      const float* g = gi < 0 ? nullptr : s_ph[gi % 3].gamma;  // phase gi's descriptor is in place
       if (g) {
-        const uint32_t bytes = (uint32_t)__ldg(&p.ph[gi].K) * 4u;
+        const uint32_t bytes = (uint32_t)s_ph[gi % 3].K * 4u;
         fence_proxy_async();
         mbar_expect_tx(gbar, bytes);
         bulk_g2s(smem + p.off_att, g, bytes, gbar, l2_evict_first_policy());
