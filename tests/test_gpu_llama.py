@@ -55,17 +55,21 @@ def test_teacher_forced_decode_matches_oracle(tiny):
     check_errors(errs, flip_bound(path), min_tight_frac=0.25)
 
 
+@pytest.mark.parametrize("decode_kernel", [0, 1])
 @pytest.mark.parametrize("n_prompt,steps,check", [
     # the persistent kernel splits the context across CTAs every 128
-    # positions (head_dim 64): boundaries at 512 and 640 here
+    # positions (head_dim 64): boundaries at 512 and 640 here; the per-kernel
+    # chain's attention takes one CTA per 64 positions (9 .. 11 CTAs here)
     (450, 200, {0, 60, 61, 62, 63, 188, 189, 190, 199}),
-    # 16 splits of one tile each end at 2048; beyond, splits take two tiles
+    # persistent kernel: 16 splits of one tile each end at 2048, beyond them
+    # splits take two tiles; per-kernel chain: 16 CTAs of two to three
+    # 64-position tiles, and its prompt runs every context length below
     (2040, 16, set(range(16))),
 ])
-def test_long_context_decode_matches_oracle(tiny, n_prompt, steps, check):
+def test_long_context_decode_matches_oracle(tiny, n_prompt, steps, check, decode_kernel):
     # the integer (dp4a) prefill, so that only the decode attention is on trial
     path, _, orc = tiny
-    gpu = native.llama_candle_load_op(path, prefill_gemm=1)
+    gpu = native.llama_candle_load_op(path, prefill_gemm=1, decode_kernel=decode_kernel)
     prompt = synth.prompt_tokens(n_prompt, orc.n_vocab, 77)
     native.llama_forward(gpu, prompt, 0, want_logits=False)
     orc.forward(prompt, 0)
