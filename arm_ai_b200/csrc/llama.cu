@@ -332,10 +332,8 @@ cudaError_t launch_head(armai_llama* m, const Plan& pl, const float* x, const in
   return launch_mv<MODE_HEAD, NB>(m, pl, p, nrows);
 }
 
-// fresh_base: -1 for a decode step (only each row's own position was just
-// written), else the first position of the prompt whose rows were.
 cudaError_t launch_attn(armai_llama* m, int l, const float* q, float* y, const int* pos, int nb_tok,
-                        int64_t kv_seq_stride, int seq = 0, int fresh_base = -1) {
+                        int64_t kv_seq_stride, int seq = 0) {
   AttnParams a;
   a.q = q;
   a.kc = kv_seq_ptr(m, m->kc, l, seq);
@@ -352,7 +350,6 @@ cudaError_t launch_attn(armai_llama* m, int l, const float* q, float* y, const i
   a.counters = m->attn_cnt;
   a.y = y;
   a.err = m->d_err;
-  a.fresh_base = fresh_base;
   const dim3 grid(m->n_head_kv, ATT_SPLITS, nb_tok), block(ATT_THREADS);
   if (m->head_dim == 64)
     return m->kv_f16 ? launch_k(k_attn_decode<64, __half>, grid, block, m->attn_smem, m->stream, m->use_pdl, a)
@@ -851,7 +848,7 @@ int gemm_layer(armai_llama* m, const Layer& L, int l, int S, float* x, float* q,
   } else {
     for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
       const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
-      ARMAI_CUDA(launch_attn(m, l, q + (size_t)t0 * QN, y + (size_t)t0 * QN, pos + t0, n, 0, seq, 0));
+      ARMAI_CUDA(launch_attn(m, l, q + (size_t)t0 * QN, y + (size_t)t0 * QN, pos + t0, n, 0, seq));
     }
   }
   // x += W in (attn_output / ffn_down), then the next activation tiles;
@@ -908,7 +905,7 @@ int enqueue_prefill(armai_llama* m, const uint32_t* tokens, int S, int seq = 0) 
       ARMAI_CUDA(launch_qkv<1>(m, m->pl_qkv1, l, m->pX + t * E, m->pQ + t * QN, m->p_pos + t, 0, seq));
     for (int t0 = 0; t0 < S; t0 += ATTN_TOK_PER_LAUNCH) {
       const int n = std::min(ATTN_TOK_PER_LAUNCH, S - t0);
-      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0, seq, 0));
+      ARMAI_CUDA(launch_attn(m, l, m->pQ + t0 * QN, m->pY + t0 * QN, m->p_pos + t0, n, 0, seq));
     }
     t = 0;
     for (; t + PREFILL_TILE <= S; t += PREFILL_TILE)

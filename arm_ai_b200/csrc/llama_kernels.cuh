@@ -676,11 +676,6 @@ struct AttnParams {
   unsigned* counters;  // [NB][n_kv]
   float* y;            // [NB][n_head*hd]
   uint32_t* err;
-  // First cache position that the launch's predecessor may still be writing:
-  // -1 = each row's own position (a decode step appends one row per
-  // sequence), else this position (a prompt: its rows were just appended).
-  // Earlier positions are fetched before waiting for the predecessor.
-  int fresh_base;
 };
 
 constexpr int ATT_THREADS = 128;
@@ -709,21 +704,19 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 // per row hit distinct banks. f32 caches: asynchronous 16-byte copies, every
 // copy of the tile in flight at once; f16 caches: loaded and widened by the
 // threads.
-// Rows [r0, n) of the tile; f32 copies are only issued (load_kv_wait
-// completes them).
 template <int HD, typename KV>
-__device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, float* Vs, const KV* vbase,
-                                             int r0 = 0) {
+__device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, float* Vs, const KV* vbase) {
   constexpr int V4 = HD / 4;
   if constexpr (sizeof(KV) == 4) {
-    for (int i = r0 * V4 + (int)threadIdx.x; i < n * V4; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
       const int t = i / V4, c = (i % V4) * 4;
       cp_async16(Ks + t * HD + ((c >> 2) ^ (t & 7)) * 4, reinterpret_cast<const float*>(base) + (size_t)t * HD + c);
       cp_async16(Vs + t * HD + c, reinterpret_cast<const float*>(vbase) + (size_t)t * HD + c);
     }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
   } else {
 #pragma unroll 4
-    for (int i = r0 * V4 + (int)threadIdx.x; i < n * V4; i += blockDim.x) {
+    for (int i = threadIdx.x; i < n * V4; i += blockDim.x) {
       const int t = i / V4, c = (i % V4) * 4;
       const uint2 kr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(base) + (size_t)t * HD + c);
       const uint2 vr = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(vbase) + (size_t)t * HD + c);
@@ -735,10 +728,6 @@ __device__ __forceinline__ void load_kv_tile(const KV* base, int n, float* Ks, f
       *reinterpret_cast<float4*>(Vs + t * HD + c) = make_float4(v0.x, v0.y, v1.x, v1.y);
     }
   }
-}
-// Completes the calling thread's asynchronous tile copies.
-__device__ __forceinline__ void load_kv_wait() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // Split-K GQA flash-decode. grid (n_kv, ATT_SPLITS, NB), ATT_THREADS threads.
@@ -771,28 +760,19 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   float* Ltot = wts + ATT_SPLITS * ATT_MAX_REP;     // [rep]
   __shared__ int s_last;
   pdl_launch();
-  // The positions (pos) and the cache rows before the fresh ones were written
-  // by earlier launches, complete before this one's predecessor started: the
-  // context split and the first tile's settled rows need no wait.
+  pdl_wait();
   const int T = p.pos[b] + 1;
   const int splits = min(ATT_SPLITS, (T + TILE - 1) / TILE);
   if (s >= splits) return;
   const int chunk = (T + splits - 1) / splits;
   const int t0 = min(T, s * chunk), t1 = min(T, t0 + chunk);
-  const int64_t kvbase = (int64_t)b * p.kv_seq_stride + (int64_t)kvh * p.max_seq * HD;
-  const KV* kc = reinterpret_cast<const KV*>(p.kc) + kvbase;
-  const KV* vc = reinterpret_cast<const KV*>(p.vc) + kvbase;
-  int settled = 0;  // rows of the first tile copied before the wait
-  if (sizeof(KV) == 4 && t0 < t1) {  // f16 caches: widened by the threads, after the wait
-    const int fresh = p.fresh_base >= 0 ? p.fresh_base : T - 1;
-    settled = max(0, min(min(TILE, t1 - t0), fresh - t0));
-    if (settled > 0) load_kv_tile<HD, KV>(kc + (size_t)t0 * HD, settled, Ks, Vs, vc + (size_t)t0 * HD);
-  }
-  pdl_wait();
   const float* qb = p.q + (size_t)b * p.n_head * HD + (size_t)kvh * nrep * HD;
   for (int i = tid; i < nrep * HD / 4; i += blockDim.x)
     reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(qb)[i];
   if (tid < ATT_MAX_REP) { mrow[tid] = -INFINITY; lrow[tid] = 0.f; }
+  const int64_t kvbase = (int64_t)b * p.kv_seq_stride + (int64_t)kvh * p.max_seq * HD;
+  const KV* kc = reinterpret_cast<const KV*>(p.kc) + kvbase;
+  const KV* vc = reinterpret_cast<const KV*>(p.vc) + kvbase;
   // PV ownership: thread -> (dim d, group of heads)
   constexpr int DGROUPS = ATT_THREADS / HD;          // 2 for HD=64, 1 for HD=128
   constexpr int RPG = ATT_MAX_REP / DGROUPS;         // heads per thread
@@ -804,8 +784,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn_decode(const AttnParams p)
   for (int tt0 = t0; tt0 < t1; tt0 += TILE) {
     const int n = min(TILE, t1 - tt0);
     __syncthreads();  // previous tile fully consumed (and q / m / l initialised)
-    load_kv_tile<HD, KV>(kc + (size_t)tt0 * HD, n, Ks, Vs, vc + (size_t)tt0 * HD, tt0 == t0 ? settled : 0);
-    if constexpr (sizeof(KV) == 4) load_kv_wait();
+    load_kv_tile<HD, KV>(kc + (size_t)tt0 * HD, n, Ks, Vs, vc + (size_t)tt0 * HD);
     __syncthreads();
     // scores and online softmax: warp per head pair (r, r + 4), lane per
     // position(s) lane + 32 j; the two heads share each K element load
